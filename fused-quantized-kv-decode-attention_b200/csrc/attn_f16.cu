@@ -1,0 +1,334 @@
+// fp16-KV single-query decode attention (plain and GQA), sm_100a.
+//
+// Replaces the reference kernels decode_attn_fp16_mw_kernel
+// (kernels/decode_attn_fp16_mw.cu:6-49), decode_attn_gqa_kernel
+// (kernels/decode_attn_gqa.cu:8-55) and gqa_sk_partial_pa2
+// (kernels/decode_attn_gqa_sk_fast.cu:6-54) with one persistent kernel:
+//
+//  * A work unit is (sequence b, KV head kh, group of <= 8 query heads that
+//    share kh, split s).  Every K/V byte of the unit is read from HBM once and
+//    used by all heads of the group (the reference re-reads KV once per query
+//    head and relies on L2).
+//  * Warp 4 is the producer: one lane streams 64-key tiles of K and V into a
+//    STAGES-deep shared-memory ring with 3-D TMA tensor copies (128-byte
+//    swizzle, rows past N zero-filled by the TMA unit), completing on
+//    mbarriers.  It runs ahead across unit boundaries.
+//  * Warps 0-3 are consumers; each owns 16 keys of every tile.  Scores and
+//    P.V run on the tensor cores with mma.sync m16n8k16 (f16 in, f32
+//    accumulate): rows = query heads of the group (<= 8 valid), columns =
+//    keys for Q.K^T, and the probabilities are re-used from registers as the
+//    A operand of P.V (V fragments via ldmatrix.trans).  Tensor cores here
+//    remove the fp16->fp32 conversions and FMAs from the issue slots; the
+//    kernel stays HBM-bound.
+//  * Online softmax in the log2 domain (scores pre-multiplied by
+//    log2(e)/sqrt(D)), rescale only when a row maximum grows.
+//  * Unit epilogue: the 4 warps' (m, l, o) are merged through shared memory
+//    and written either as the fp16 output (one split) or as an fp32 partial
+//    (m in log2 units, l, unnormalised o) for the combine kernel.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace fqkv {
+namespace {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kTK = 64;            // keys per tile
+constexpr int kHalfBytes = kTK * 128;
+constexpr int kMergeHeads = 4;     // heads merged per epilogue pass
+
+template <int D>
+struct F16Cfg {
+  static constexpr int kHalves = D / 64;                 // 128-byte column blocks per row
+  static constexpr int kTileBytes = kHalves * kHalfBytes;  // K (or V) tile
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kStages = (D == 128) ? 3 : 4;
+  static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
+  static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
+  static constexpr size_t kMergeBytes =
+      size_t(kConsumerWarps) * (2 * 8 + kMergeHeads * D) * sizeof(float);
+  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kRingBytes + kBarBytes + kMergeBytes;
+};
+
+struct UnitCoord {
+  int b, kh, grp, s;
+};
+
+__device__ __forceinline__ UnitCoord decode_unit(const DecodeLaunch& a, int u) {
+  UnitCoord c;
+  c.grp = u % a.groups;
+  u /= a.groups;
+  c.s = u % a.S_eff;
+  u /= a.S_eff;
+  c.kh = u % a.Hkv;
+  c.b = u / a.Hkv;
+  return c;
+}
+
+// Byte offset of 16-byte chunk `chunk` (0 .. D/8-1) of tile row `row` in a
+// 128B-swizzled tile made of D/64 column blocks of [kTK rows x 128 B].
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return uint32_t((chunk >> 3) * kHalfBytes + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_constant__ DecodeLaunch a) {
+  using C = F16Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kRingBytes);
+  uint64_t* empty = full + C::kStages;
+  float* sm_m = reinterpret_cast<float*>(empty + C::kStages);  // [warps][8]
+  float* sm_l = sm_m + kConsumerWarps * 8;                     // [warps][8]
+  float* sm_o = sm_l + kConsumerWarps * 8;                     // [warps][kMergeHeads][D]
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtl wc{a.status, a.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kConsumerWarps && lane == 0) {
+    prefetch_tensormap(&a.tmK);
+    prefetch_tensormap(&a.tmV);
+  }
+  __syncthreads();
+  // Let the combine kernel (if any) get scheduled while this grid streams.
+  pdl_launch_dependents();
+
+  // ------------------------------------------------------------ producer
+  if (warp == kConsumerWarps) {
+    if (lane != 0 || a.debug_skip_loads) return;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+      const UnitCoord uc = decode_unit(a, u);
+      const int lo = uc.s * a.chunk;
+      const int hi = min(a.N, lo + a.chunk);
+      const int z = uc.b * a.Hkv + uc.kh;
+      for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
+        const int st = it % C::kStages;
+        if (it >= C::kStages) {
+          if (*reinterpret_cast<volatile int*>(&abort_flag) ||
+              !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+        }
+        mbar_arrive_expect_tx(&full[st], C::kStageBytes);
+        uint8_t* sk = smem + size_t(st) * C::kStageBytes;
+        uint8_t* sv = sk + C::kTileBytes;
+#pragma unroll
+        for (int h = 0; h < C::kHalves; ++h) tma_load_3d(sk + h * kHalfBytes, &a.tmK, 64 * h, k0, z, &full[st]);
+#pragma unroll
+        for (int h = 0; h < C::kHalves; ++h) tma_load_3d(sv + h * kHalfBytes, &a.tmV, 64 * h, k0, z, &full[st]);
+      }
+    }
+    if (!ok) {
+      // The consumers gave up: wait (bounded) for our own copies in flight so
+      // no TMA write lands in shared memory after the CTA has exited.
+      for (int j = (it > C::kStages ? it - C::kStages : 0); j < it; ++j)
+        mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, wc, kDevTimeoutDrain);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int g = lane >> 2;   // mma row (query head within the group)
+  const int t = lane & 3;
+  const int mi = lane >> 3;  // ldmatrix matrix index supplied by this lane
+  const int rr = lane & 7;   // ldmatrix row within that matrix
+  const int r0 = warp * 16;  // this warp's 16 keys within a tile
+  const uint32_t ring = smem_u32(smem);
+  const float csc = a.sm_scale_log2;
+  bool alive = true;
+  int it = 0;
+
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+    const UnitCoord uc = decode_unit(a, u);
+    const int lo = uc.s * a.chunk;
+    const int hi = min(a.N, lo + a.chunk);
+    const int h0 = uc.kh * a.G + uc.grp * a.GP;
+    const int gvalid = min(a.GP, a.G - uc.grp * a.GP);
+
+    // Q fragments (A operand rows = heads of the group; rows >= gvalid are 0).
+    uint32_t qa[D / 16][2];
+    {
+      const __half* qrow = static_cast<const __half*>(a.q) + (size_t(uc.b) * a.Hq + h0 + g) * D;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        if (g < gvalid) {
+          qa[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * t);
+          qa[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * t + 8);
+        } else {
+          qa[kk][0] = 0u;
+          qa[kk][1] = 0u;
+        }
+      }
+    }
+    float o[D / 8][4];
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
+      const int st = it % C::kStages;
+      if (alive) {
+        // warp-uniform decision: every lane waits, the warp proceeds only if all did
+        const bool ok = mbar_wait(&full[st], (it / C::kStages) & 1, wc, kDevTimeoutFull) &&
+                        !*reinterpret_cast<volatile int*>(&abort_flag);
+        alive = __all_sync(0xffffffffu, ok);
+        if (!alive && lane == 0) abort_flag = 1;
+      }
+      if (!alive) continue;
+      const uint32_t sk = ring + uint32_t(st) * C::kStageBytes;
+      const uint32_t sv = sk + C::kTileBytes;
+
+      // ---- S = Q K^T for this warp's 16 keys (two n8 tiles)
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int row = r0 + ((mi >> 1) << 3) + rr;
+        const int chunk = 2 * kk + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(sk + swz(row, chunk), b0, b1, b2, b3);
+        mma_16816(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+        mma_16816(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+      }
+
+      // ---- online softmax (log2 domain); row g, keys k0 + r0 + 8j + 2t + e
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = k0 + r0 + 8 * j + 2 * t + e;
+          const float v = (key < hi) ? sc[j][e] * csc : -INFINITY;
+          sc[j][e] = v;
+          mx = fmaxf(mx, v);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      if (__any_sync(0xffffffffu, m_new > m_run)) {
+        const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
+#pragma unroll
+        for (int j = 0; j < D / 8; ++j) {
+          o[j][0] *= alpha;
+          o[j][1] *= alpha;
+        }
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+      const float p00 = ex2(sc[0][0] - mu), p01 = ex2(sc[0][1] - mu);
+      const float p10 = ex2(sc[1][0] - mu), p11 = ex2(sc[1][1] - mu);
+      l_run += (p00 + p01) + (p10 + p11);
+      const uint32_t pa0 = pack_half2(p00, p01);
+      const uint32_t pa2 = pack_half2(p10, p11);
+
+      // ---- O += P V  (V^T fragments via ldmatrix.trans)
+#pragma unroll
+      for (int pp = 0; pp < D / 16; ++pp) {
+        const int row = r0 + ((mi & 1) << 3) + rr;
+        const int chunk = 2 * pp + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(sv + swz(row, chunk), b0, b1, b2, b3);
+        mma_16816(o[2 * pp], pa0, 0u, pa2, 0u, b0, b1);
+        mma_16816(o[2 * pp + 1], pa0, 0u, pa2, 0u, b2, b3);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+
+    // ---- unit epilogue: merge the 4 warps, write output or partial
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    if (t == 0) {
+      sm_m[warp * 8 + g] = m_run;
+      sm_l[warp * 8 + g] = l_run;
+    }
+    const int ct = threadIdx.x;  // 0 .. 127
+    const size_t row_base = size_t(uc.b) * a.Hq + h0;
+    for (int hp = 0; hp < gvalid; hp += kMergeHeads) {
+      const int gl = g - hp;
+      if (gl >= 0 && gl < kMergeHeads && g < gvalid) {
+#pragma unroll
+        for (int j = 0; j < D / 8; ++j) {
+          float2 v2 = make_float2(o[j][0], o[j][1]);
+          *reinterpret_cast<float2*>(&sm_o[(warp * kMergeHeads + gl) * D + 8 * j + 2 * t]) = v2;
+        }
+      }
+      named_bar_sync(1, 32 * kConsumerWarps);
+      const int nh = min(kMergeHeads, gvalid - hp);
+      for (int idx = ct; idx < nh * D; idx += 32 * kConsumerWarps) {
+        const int gl2 = idx / D, d = idx - gl2 * D;
+        const int gg = hp + gl2;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_m[w * 8 + gg]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float mw = sm_m[w * 8 + gg];
+          const float wt = (mw == -INFINITY) ? 0.f : ex2(mw - M);
+          L += wt * sm_l[w * 8 + gg];
+          O += wt * sm_o[(w * kMergeHeads + gl2) * D + d];
+        }
+        const size_t row = row_base + gg;
+        if (a.S_eff == 1) {
+          static_cast<__half*>(a.out)[row * D + d] = __float2half_rn(O / L);
+        } else {
+          const size_t slot = row * a.S + uc.s;
+          if (d == 0) {
+            a.part_m[slot] = M;
+            a.part_l[slot] = L;
+          }
+          a.part_o[slot * D + d] = O;
+        }
+      }
+      named_bar_sync(1, 32 * kConsumerWarps);
+    }
+  }
+}
+
+}  // namespace
+
+template <int D>
+static cudaError_t launch_f16(const DecodeLaunch& a, cudaStream_t stream) {
+  decode_f16_kernel<D><<<a.grid, kThreads, F16Cfg<D>::kSmemBytes, stream>>>(a);
+  return cudaGetLastError();
+}
+
+KernelShape decode_kernel_shape_f16(int D) {
+  return KernelShape{kThreads, D == 128 ? F16Cfg<128>::kSmemBytes : F16Cfg<64>::kSmemBytes};
+}
+
+cudaError_t decode_kernel_prepare_f16(int D, int* ctas_per_sm) {
+  const void* fn = D == 128 ? reinterpret_cast<const void*>(&decode_f16_kernel<128>)
+                            : reinterpret_cast<const void*>(&decode_f16_kernel<64>);
+  const size_t smem = decode_kernel_shape_f16(D).smem_bytes;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, kThreads, smem);
+}
+
+cudaError_t launch_decode_f16(const DecodeLaunch& a, cudaStream_t stream) {
+  return a.D == 128 ? launch_f16<128>(a, stream) : launch_f16<64>(a, stream);
+}
+
+}  // namespace fqkv

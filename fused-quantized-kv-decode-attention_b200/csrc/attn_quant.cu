@@ -1,0 +1,399 @@
+// int8-KV and int4-KV single-query decode attention, sm_100a.
+//
+// Replaces decode_attn_int8_mw_kernel (kernels/decode_attn_int8_mw.cu:6-51)
+// and decode_attn_int4_kernel (kernels/decode_attn_int4.cu:8-46); int4 is
+// generalised from the reference's D=64 to D in {64, 128}.
+//
+// Layout in HBM (exactly the reference's): codes [R, N, D] int8 or packed
+// [R, N, D/2] uint8 (element 2t in the low nibble), scales [R, N] fp16.
+//
+//  * Persistent, warp-specialised: warp 4 streams 8 KiB tiles of K and V codes
+//    plus the matching scale windows into a 4-stage ring with 1-D bulk copies
+//    (cp.async.bulk) completing on mbarriers.  A scale window starts at the
+//    16-byte boundary at or below the tile's first scale, so it may read up to
+//    15 bytes on either side of the scale array -- always inside the 16-byte
+//    blocks that hold the first / last scale, never used.
+//  * Each consumer warp owns a quarter of every tile.  A key row is split into
+//    16-byte chunks, one per lane (L = row_bytes/16 lanes per key), and every
+//    lane handles 4 keys per tile.
+//  * q . k on integer dot-product units: q is held as a 2-plane fixed-point
+//    number (q * 2^e = hi * 256 + lo, hi signed byte, lo unsigned byte, 14
+//    significant bits -- every fp16 q within 3 binades of max|q| is exact),
+//    codes enter dp4a directly (int4 nibbles as 16*code in signed bytes).
+//    The score is (integer dot) * k_scale * (log2(e) / sqrt(D)) / 2^e.
+//  * p . v in fp32 on CUDA cores: codes become floats through a byte-permute
+//    into the mantissa of 2^23 (exact), the V scale is folded into p.
+//  * Online softmax in the log2 domain, warp merge through shared memory,
+//    output fp16 or an fp32 split partial like the fp16 kernel.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace fqkv {
+namespace {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kStages = 4;
+constexpr int kTileBytes = 8192;
+
+template <bool kInt4, int D>
+struct QCfg {
+  static constexpr int kRowBytes = kInt4 ? D / 2 : D;
+  static constexpr int kTK = kTileBytes / kRowBytes;       // keys per tile
+  static constexpr int kL = kRowBytes / 16;                // lanes per key row
+  static constexpr int kKPS = 32 / kL;                     // keys per warp step
+  static constexpr int kDimsPerLane = kInt4 ? 32 : 16;
+  static constexpr int kScaleBytes = 2 * kTK + 32;         // scale window capacity
+  static constexpr int kStageBytes = 2 * kTileBytes + 2 * kScaleBytes;
+  static constexpr size_t kSmemBytes = 128 + size_t(kStages) * kStageBytes + 2 * kStages * sizeof(uint64_t) +
+                                       size_t(kConsumerWarps) * (2 + D) * sizeof(float);
+  static_assert(kTK == 4 * kConsumerWarps * kKPS, "each lane owns 4 keys per tile");
+};
+
+__device__ __forceinline__ float byte_to_float(uint32_t w_xor80, uint32_t sel) {
+  // result bytes: [w.b_sel, 0, 0, 0x4B] -> 2^23 + (code + 128)
+  return __int_as_float(static_cast<int>(__byte_perm(w_xor80, 0x4B000000u, 0x7540u | sel))) - 8388736.0f;
+}
+
+template <bool kInt4, int D>
+__global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_constant__ DecodeLaunch a) {
+  using C = QCfg<kInt4, D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * C::kStageBytes);
+  uint64_t* empty = full + kStages;
+  float* sm_ml = reinterpret_cast<float*>(empty + kStages);  // [warps][2]
+  float* sm_o = sm_ml + 2 * kConsumerWarps;                   // [warps][D]
+  __shared__ int abort_flag;
+  __shared__ int stage_off[kStages][2];                       // scale offsets (elements) in each window
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtl wc{a.status, a.timeout_ns};
+  const size_t row_stride = size_t(a.N) * C::kRowBytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // ------------------------------------------------------------ producer
+  if (warp == kConsumerWarps) {
+    if (lane != 0 || a.debug_skip_loads) return;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+      const int s = u % a.S_eff;
+      const int r = u / a.S_eff;  // row = b * Hkv + kh (Hq == Hkv here)
+      const int lo = s * a.chunk;
+      const int hi = min(a.N, lo + a.chunk);
+      const uint8_t* Kr = static_cast<const uint8_t*>(a.K) + size_t(r) * row_stride;
+      const uint8_t* Vr = static_cast<const uint8_t*>(a.V) + size_t(r) * row_stride;
+      const __half* Ksr = static_cast<const __half*>(a.Ks) + size_t(r) * a.N;
+      const __half* Vsr = static_cast<const __half*>(a.Vs) + size_t(r) * a.N;
+      for (int k0 = lo; k0 < hi; k0 += C::kTK, ++it) {
+        const int st = it % kStages;
+        if (it >= kStages) {
+          if (*reinterpret_cast<volatile int*>(&abort_flag) ||
+              !mbar_wait(&empty[st], ((it / kStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+        }
+        const int nk = min(C::kTK, hi - k0);
+        const uint32_t kv_bytes = uint32_t(nk) * C::kRowBytes;
+        const uintptr_t ka = reinterpret_cast<uintptr_t>(Ksr + k0);
+        const uintptr_t va = reinterpret_cast<uintptr_t>(Vsr + k0);
+        const uintptr_t ka0 = ka & ~uintptr_t(15), va0 = va & ~uintptr_t(15);
+        const uint32_t kwin = uint32_t(((ka + 2u * nk + 15u) & ~uintptr_t(15)) - ka0);
+        const uint32_t vwin = uint32_t(((va + 2u * nk + 15u) & ~uintptr_t(15)) - va0);
+        stage_off[st][0] = int(ka - ka0) >> 1;
+        stage_off[st][1] = int(va - va0) >> 1;
+        uint8_t* base = smem + size_t(st) * C::kStageBytes;
+        // expect_tx has release semantics: the stage_off stores above are
+        // visible to consumers that acquire the completed phase.
+        mbar_arrive_expect_tx(&full[st], 2 * kv_bytes + kwin + vwin);
+        bulk_g2s(base, Kr + size_t(k0) * C::kRowBytes, kv_bytes, &full[st]);
+        bulk_g2s(base + kTileBytes, Vr + size_t(k0) * C::kRowBytes, kv_bytes, &full[st]);
+        bulk_g2s(base + 2 * kTileBytes, reinterpret_cast<const void*>(ka0), kwin, &full[st]);
+        bulk_g2s(base + 2 * kTileBytes + C::kScaleBytes, reinterpret_cast<const void*>(va0), vwin, &full[st]);
+      }
+    }
+    if (!ok) {
+      for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
+        mbar_wait(&full[j % kStages], (j / kStages) & 1, wc, kDevTimeoutDrain);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int c = lane % C::kL;   // 16-byte chunk of the key row
+  const int j = lane / C::kL;   // key slot
+  const int kw = warp * (C::kTK / kConsumerWarps);
+  bool alive = true;
+  int it = 0;
+
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+    const int s = u % a.S_eff;
+    const int r = u / a.S_eff;
+    const int lo = s * a.chunk;
+    const int hi = min(a.N, lo + a.chunk);
+
+    // ---- q as 2-plane fixed point for this lane's dims.  e is chosen from
+    // max|q| over the whole row (lanes of one key slot cover all D dims) so
+    // that |q| * 2^e < 2^14; the score factor undoes 2^e (and the 16 of the
+    // int4 nibble-in-high-half trick).
+    float qv[C::kDimsPerLane];
+    float qscale_unit;
+    {
+      const __half* qrow = static_cast<const __half*>(a.q) + size_t(r) * D + c * C::kDimsPerLane;
+      float mq = 0.f;
+#pragma unroll
+      for (int d = 0; d < C::kDimsPerLane; ++d) {
+        qv[d] = __half2float(qrow[d]);
+        mq = fmaxf(mq, fabsf(qv[d]));
+      }
+#pragma unroll
+      for (int off = 1; off < C::kL; off <<= 1) mq = fmaxf(mq, __shfl_xor_sync(0xffffffffu, mq, off));
+      const int e = (mq > 0.f) ? 13 - ilogbf(mq) : 0;
+      const float two_e = ldexpf(1.f, e);
+#pragma unroll
+      for (int d = 0; d < C::kDimsPerLane; ++d) qv[d] = rintf(qv[d] * two_e);  // |.| <= 16384
+      qscale_unit = a.sm_scale_log2 * ldexpf(1.f, -e) * (kInt4 ? 0.0625f : 1.f);
+    }
+
+    // planes: int8 -> word w covers dims 4w..4w+3; int4 -> word w covers dims
+    // 8w..8w+7 split into even and odd dims (index 2w + parity).
+    uint32_t qh[kInt4 ? 8 : 4], ql[kInt4 ? 8 : 4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      if (kInt4) {
+#pragma unroll
+        for (int par = 0; par < 2; ++par) {
+          uint32_t hw = 0, lw = 0;
+#pragma unroll
+          for (int bb = 0; bb < 4; ++bb) {
+            const int qi = int(qv[8 * w + 2 * bb + par]);
+            hw |= (uint32_t(qi >> 8) & 0xFFu) << (8 * bb);
+            lw |= (uint32_t(qi) & 0xFFu) << (8 * bb);
+          }
+          qh[2 * w + par] = hw;
+          ql[2 * w + par] = lw;
+        }
+      } else {
+        uint32_t hw = 0, lw = 0;
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+          const int qi = int(qv[4 * w + bb]);
+          hw |= (uint32_t(qi >> 8) & 0xFFu) << (8 * bb);
+          lw |= (uint32_t(qi) & 0xFFu) << (8 * bb);
+        }
+        qh[w] = hw;
+        ql[w] = lw;
+      }
+    }
+
+    float o[C::kDimsPerLane];
+#pragma unroll
+    for (int d = 0; d < C::kDimsPerLane; ++d) o[d] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, lv_run = 0.f;
+
+    for (int k0 = lo; k0 < hi; k0 += C::kTK, ++it) {
+      const int st = it % kStages;
+      if (alive) {
+        bool ok = mbar_wait(&full[st], (it / kStages) & 1, wc, kDevTimeoutFull) &&
+                  !*reinterpret_cast<volatile int*>(&abort_flag);
+        alive = __all_sync(0xffffffffu, ok);
+        if (!alive && lane == 0) abort_flag = 1;
+      }
+      if (!alive) continue;
+      const uint8_t* base = smem + size_t(st) * C::kStageBytes;
+      const uint8_t* kt = base;
+      const uint8_t* vt = base + kTileBytes;
+      const __half* kst = reinterpret_cast<const __half*>(base + 2 * kTileBytes) + stage_off[st][0];
+      const __half* vst = reinterpret_cast<const __half*>(base + 2 * kTileBytes + C::kScaleBytes) + stage_off[st][1];
+
+      float sco[4];
+      int kl[4];
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        kl[sp] = kw + j + C::kKPS * sp;
+        const uint4 kv = *reinterpret_cast<const uint4*>(kt + kl[sp] * C::kRowBytes + 16 * c);
+        const uint32_t kw4[4] = {kv.x, kv.y, kv.z, kv.w};
+        int ah = 0, al = 0;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          if (kInt4) {
+            const uint32_t ev = (kw4[w] << 4) & 0xF0F0F0F0u;  // 16 * code of even dims
+            const uint32_t od = kw4[w] & 0xF0F0F0F0u;         // 16 * code of odd dims
+            ah = dp4a_ss(qh[2 * w], ev, ah);
+            ah = dp4a_ss(qh[2 * w + 1], od, ah);
+            al = dp4a_us(ql[2 * w], ev, al);
+            al = dp4a_us(ql[2 * w + 1], od, al);
+          } else {
+            ah = dp4a_ss(qh[w], kw4[w], ah);
+            al = dp4a_us(ql[w], kw4[w], al);
+          }
+        }
+        int acc = ah * 256 + al;
+#pragma unroll
+        for (int off = 1; off < C::kL; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        const int key = k0 + kl[sp];
+        sco[sp] = (key < hi) ? float(acc) * __half2float(kst[kl[sp]]) * qscale_unit : -INFINITY;
+      }
+      float mx = fmaxf(fmaxf(sco[0], sco[1]), fmaxf(sco[2], sco[3]));
+#pragma unroll
+      for (int off = C::kL; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_run, mx);
+      if (m_new > m_run) {  // warp-uniform
+        const float alpha = ex2(m_run - m_new);
+#pragma unroll
+        for (int d = 0; d < C::kDimsPerLane; ++d) o[d] *= alpha;
+        l_run *= alpha;
+        lv_run *= alpha;
+        m_run = m_new;
+      }
+      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        const bool valid = (k0 + kl[sp]) < hi;
+        const float p = ex2(sco[sp] - mu);
+        l_run += p;
+        const float pv = valid ? p * __half2float(vst[kl[sp]]) : 0.f;
+        const uint4 vv = *reinterpret_cast<const uint4*>(vt + kl[sp] * C::kRowBytes + 16 * c);
+        const uint32_t vw4[4] = {vv.x, vv.y, vv.z, vv.w};
+        if (kInt4) {
+          // nibble n of word w -> dim 8w + n, value (code + 8) after the xor
+          const float pv1 = pv * 0.0625f, pv2 = pv * 0.00390625f, pv3 = pv * 0.000244140625f,
+                      pv4 = pv * 1.52587890625e-05f;
+          lv_run += pv;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t x = vw4[w] ^ 0x88888888u;
+            const uint32_t y = x >> 20;
+            float* od = &o[8 * w];
+            od[0] = fmaf(pv, __int_as_float(int((x & 0xFu) | 0x4B000000u)) - 8388608.f, od[0]);
+            od[1] = fmaf(pv1, __int_as_float(int((x & 0xF0u) | 0x4B000000u)) - 8388608.f, od[1]);
+            od[2] = fmaf(pv2, __int_as_float(int((x & 0xF00u) | 0x4B000000u)) - 8388608.f, od[2]);
+            od[3] = fmaf(pv3, __int_as_float(int((x & 0xF000u) | 0x4B000000u)) - 8388608.f, od[3]);
+            od[4] = fmaf(pv4, __int_as_float(int((x & 0xF0000u) | 0x4B000000u)) - 8388608.f, od[4]);
+            od[5] = fmaf(pv, __int_as_float(int((y & 0xFu) | 0x4B000000u)) - 8388608.f, od[5]);
+            od[6] = fmaf(pv1, __int_as_float(int((y & 0xF0u) | 0x4B000000u)) - 8388608.f, od[6]);
+            od[7] = fmaf(pv2, __int_as_float(int((y & 0xF00u) | 0x4B000000u)) - 8388608.f, od[7]);
+          }
+        } else {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t x = vw4[w] ^ 0x80808080u;
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) o[4 * w + bb] = fmaf(pv, byte_to_float(x, uint32_t(bb)), o[4 * w + bb]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+
+    // ---- warp reduction over key slots, then merge the 4 warps
+    if (kInt4) {
+#pragma unroll
+      for (int d = 0; d < C::kDimsPerLane; ++d) o[d] = fmaf(-8.f, lv_run, o[d]);
+    }
+#pragma unroll
+    for (int off = C::kL; off < 32; off <<= 1) {
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
+#pragma unroll
+      for (int d = 0; d < C::kDimsPerLane; ++d) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
+    }
+    if (lane == 0) {
+      sm_ml[2 * warp] = m_run;
+      sm_ml[2 * warp + 1] = l_run;
+    }
+    if (j == 0) {
+#pragma unroll
+      for (int d = 0; d < C::kDimsPerLane; d += 4)
+        *reinterpret_cast<float4*>(&sm_o[warp * D + c * C::kDimsPerLane + d]) =
+            make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+    }
+    named_bar_sync(1, 32 * kConsumerWarps);
+    const int ct = threadIdx.x;
+    if (ct < D) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_ml[2 * w]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mw = sm_ml[2 * w];
+        const float wt = (mw == -INFINITY) ? 0.f : ex2(mw - M);
+        L += wt * sm_ml[2 * w + 1];
+        O += wt * sm_o[w * D + ct];
+      }
+      if (a.S_eff == 1) {
+        static_cast<__half*>(a.out)[size_t(r) * D + ct] = __float2half_rn(O / L);
+      } else {
+        const size_t slot = size_t(r) * a.S + s;
+        if (ct == 0) {
+          a.part_m[slot] = M;
+          a.part_l[slot] = L;
+        }
+        a.part_o[slot * D + ct] = O;
+      }
+    }
+    named_bar_sync(1, 32 * kConsumerWarps);
+  }
+}
+
+template <bool kInt4, int D>
+const void* qfn() {
+  return reinterpret_cast<const void*>(&decode_quant_kernel<kInt4, D>);
+}
+
+const void* quant_fn(bool int4, int D) {
+  if (int4) return D == 128 ? qfn<true, 128>() : qfn<true, 64>();
+  return D == 128 ? qfn<false, 128>() : qfn<false, 64>();
+}
+
+size_t quant_smem(bool int4, int D) {
+  if (int4) return D == 128 ? QCfg<true, 128>::kSmemBytes : QCfg<true, 64>::kSmemBytes;
+  return D == 128 ? QCfg<false, 128>::kSmemBytes : QCfg<false, 64>::kSmemBytes;
+}
+
+}  // namespace
+
+KernelShape decode_kernel_shape_quant(bool int4, int D) { return KernelShape{kThreads, quant_smem(int4, D)}; }
+
+cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm) {
+  const void* fn = quant_fn(int4, D);
+  const size_t smem = quant_smem(int4, D);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, kThreads, smem);
+}
+
+cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream) {
+  const bool int4 = a.fmt == KvFormat::I4;
+  const size_t smem = quant_smem(int4, a.D);
+  if (int4) {
+    if (a.D == 128) decode_quant_kernel<true, 128><<<a.grid, kThreads, smem, stream>>>(a);
+    else decode_quant_kernel<true, 64><<<a.grid, kThreads, smem, stream>>>(a);
+  } else {
+    if (a.D == 128) decode_quant_kernel<false, 128><<<a.grid, kThreads, smem, stream>>>(a);
+    else decode_quant_kernel<false, 64><<<a.grid, kThreads, smem, stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace fqkv

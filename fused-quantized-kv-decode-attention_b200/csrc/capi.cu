@@ -1,0 +1,397 @@
+// extern "C" entry points of libfqkv_b200.so (declared in include/fqkv_b200.h).
+//
+// Responsibilities: argument validation with the reference's error conditions
+// (before any CUDA call, so a bad call fails the same way with or without a
+// GPU), per-device one-time set-up (SM count, shared-memory opt-in, occupancy,
+// status-word address), TMA tensor-map encoding, the split-K plan, and the
+// launches.  No device memory is allocated here: split-K partials live in the
+// caller's workspace (or the caller's m/l/o scratch for gqa_sk_fast).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <mutex>
+
+#include "../../include/fqkv_b200.h"
+#include "kernels.h"
+
+// In-kernel status word (one per device image): written by a bounded wait that
+// gives up, read by fqkv_device_status().
+__device__ int g_fqkv_device_status;
+
+namespace {
+
+using fqkv::DecodeLaunch;
+using fqkv::KvFormat;
+
+thread_local char t_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(FQKV_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+std::atomic<unsigned long long> g_timeout_ns{2000ull * 1000ull * 1000ull};
+
+// ------------------------------------------------------------------ device state
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  std::once_flag once;
+  int err_code = FQKV_OK;
+  char err_msg[256] = "";
+  int sm_count = 0;
+  int* status = nullptr;
+  int occ_f16[2] = {0, 0};      // D = 64, 128
+  int occ_q[2][2] = {{0, 0}, {0, 0}};  // [int4][D==128]
+};
+DeviceState g_dev[kMaxDevices];
+
+void init_device(DeviceState& ds, int dev) {
+  auto bad = [&](int code, const char* msg) {
+    ds.err_code = code;
+    snprintf(ds.err_msg, sizeof(ds.err_msg), "%s", msg);
+  };
+  int major = 0, minor = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ds.sm_count, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
+  if (major != 10 || minor != 0) {
+    char m[128];
+    snprintf(m, sizeof(m), "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev, major, minor);
+    return bad(FQKV_ERR_UNSUPPORTED_DEVICE, m);
+  }
+  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status), g_fqkv_device_status);
+  if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_f16(i ? 128 : 64, &ds.occ_f16[i]);
+  for (int q = 0; q < 2 && e == cudaSuccess; ++q)
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i)
+      e = fqkv::decode_kernel_prepare_quant(q == 1, i ? 128 : 64, &ds.occ_q[q][i]);
+  if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int device_state(DeviceState** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FQKV_ERR_CUDA, "device index %d out of range", dev);
+  DeviceState& ds = g_dev[dev];
+  std::call_once(ds.once, init_device, std::ref(ds), dev);
+  if (ds.err_code != FQKV_OK) return fail(ds.err_code, "device init: %s", ds.err_msg);
+  *out = &ds;
+  return FQKV_OK;
+}
+
+// ------------------------------------------------------------------ tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// K or V viewed as [B*Hkv][N][D] fp16, box = 64 dims x 64 keys x 1, 128B swizzle.
+int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t D) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(BH)};
+  const cuuint64_t strides[2] = {cuuint64_t(D) * 2, cuuint64_t(N) * cuuint64_t(D) * 2};
+  const cuuint32_t box[3] = {64, 64, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  return FQKV_OK;
+}
+
+// ------------------------------------------------------------------ planning
+size_t partial_bytes(int64_t rows, int64_t S, int64_t D) {
+  const size_t ml = size_t(rows) * size_t(S) * sizeof(float);
+  const size_t ml_al = (ml + 255) & ~size_t(255);
+  return 2 * ml_al + size_t(rows) * size_t(S) * size_t(D) * sizeof(float);
+}
+
+void carve_partials(DecodeLaunch& a, void* ws, int64_t rows) {
+  const size_t ml = size_t(rows) * size_t(a.S) * sizeof(float);
+  const size_t ml_al = (ml + 255) & ~size_t(255);
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  a.part_m = reinterpret_cast<float*>(p);
+  a.part_l = reinterpret_cast<float*>(p + ml_al);
+  a.part_o = reinterpret_cast<float*>(p + 2 * ml_al);
+}
+
+int ctas_per_sm(const DeviceState& ds, KvFormat f, int D) {
+  const int i = D == 128 ? 1 : 0;
+  if (f == KvFormat::F16) return std::max(1, ds.occ_f16[i]);
+  return std::max(1, ds.occ_q[f == KvFormat::I4 ? 1 : 0][i]);
+}
+
+// Fills the geometry of `a` (fmt, B, Hq, Hkv, N, D set by the caller).
+// S_fixed > 0: use at most S_fixed splits (gqa_sk_fast).  Otherwise pick the
+// split count that minimises the modelled time, limited to what `ws_bytes`
+// can hold when `limit_ws`.
+void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_bytes, bool limit_ws) {
+  a.G = a.Hq / a.Hkv;
+  a.GP = std::min(a.G, 8);
+  a.groups = (a.G + a.GP - 1) / a.GP;
+  const int TK = fqkv::tile_keys(a.fmt, a.D);
+  const int64_t tiles = (int64_t(a.N) + TK - 1) / TK;
+  const int64_t units0 = int64_t(a.B) * a.Hkv * a.groups;
+  const int64_t C = int64_t(ds.sm_count) * ctas_per_sm(ds, a.fmt, a.D);
+  const int64_t rows = int64_t(a.B) * a.Hq;
+
+  auto geometry = [&](int64_t S, int64_t* chunk_tiles, int64_t* S_eff) {
+    *chunk_tiles = (tiles + S - 1) / S;
+    *S_eff = (tiles + *chunk_tiles - 1) / *chunk_tiles;
+  };
+  int64_t best_S = 1;
+  if (S_fixed > 0) {
+    // chunk = ceil(N/S) keys rounded up to whole tiles
+    const int64_t ck = (int64_t(a.N) + S_fixed - 1) / S_fixed;
+    const int64_t ct = (ck + TK - 1) / TK;
+    a.S = int(S_fixed);
+    a.chunk = int(ct * TK);
+    a.S_eff = int((tiles + ct - 1) / ct);
+  } else {
+    // Modelled time: every round of the persistent grid costs
+    // max(active CTAs, half the grid) x tiles per unit -- below about half of
+    // the CTAs the machine is no longer HBM-bound.  Splitting adds about one
+    // tile of epilogue / combine work per unit.
+    double best = 1e300;
+    const int64_t maxS = std::min<int64_t>(tiles, 256);
+    for (int64_t S = 1; S <= maxS; ++S) {
+      int64_t ct, se;
+      geometry(S, &ct, &se);
+      if (se != S) continue;
+      if (limit_ws && se > 1 && partial_bytes(rows, se, a.D) > ws_bytes) continue;
+      const int64_t U = units0 * se;
+      double cost = 0;
+      for (int64_t done = 0; done < U; done += C) {
+        const int64_t active = std::min(C, U - done);
+        cost += double(std::max<int64_t>(active, C / 2)) * double(ct + (se > 1 ? 1 : 0));
+      }
+      if (cost < best * 0.999) {
+        best = cost;
+        best_S = se;
+      }
+    }
+    int64_t ct, se;
+    geometry(best_S, &ct, &se);
+    a.S = int(se);
+    a.S_eff = int(se);
+    a.chunk = int(ct * TK);
+  }
+  const int64_t units = units0 * a.S_eff;
+  a.units = int(units);
+  a.grid = int(std::min<int64_t>(units, C));
+  a.sm_scale_log2 = float(1.4426950408889634 / std::sqrt(double(a.D)));
+  a.status = ds.status;
+  a.timeout_ns = g_timeout_ns.load();
+  a.debug_skip_loads = 0;
+}
+
+bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+int check_W(int64_t W) {
+  if (W != 2 && W != 4 && W != 8) return fail(FQKV_ERR_INVALID_ARGUMENT, "W: must be 2, 4 or 8 (got %lld)", (long long)W);
+  return FQKV_OK;
+}
+int check_D(int64_t D) {
+  if (D != 64 && D != 128) return fail(FQKV_ERR_INVALID_ARGUMENT, "D: head_dim must be 64 or 128 (got %lld)", (long long)D);
+  return FQKV_OK;
+}
+
+int launch(DecodeLaunch& a, cudaStream_t stream) {
+  cudaError_t e = a.fmt == KvFormat::F16 ? fqkv::launch_decode_f16(a, stream) : fqkv::launch_decode_quant(a, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launch");
+  if (a.S_eff > 1) {
+    e = fqkv::launch_combine(a, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  }
+  return FQKV_OK;
+}
+
+// Shared body of the four decode entry points (canonical GQA form).
+int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const void* Ks, const void* Vs, void* o,
+               int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, void* ws, size_t ws_bytes,
+               fqkv_stream_t stream) {
+  if (int rc = check_D(D)) return rc;
+  if (B < 0 || Hq < 1 || Hkv < 1 || N < 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "negative or zero size");
+  if (Hq % Hkv != 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "Hq (%lld) must be a multiple of Hkv (%lld)", (long long)Hq, (long long)Hkv);
+  if (B == 0) return FQKV_OK;
+  if (N == 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "N: the KV cache is empty (softmax over zero keys)");
+  if (!q || !K || !V || !o || (fmt != KvFormat::F16 && (!Ks || !Vs)))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (B * Hkv > INT32_MAX || N > INT32_MAX || B * Hq > INT32_MAX)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the 32-bit index range");
+  if (!aligned(K, 16) || !aligned(V, 16)) return fail(FQKV_ERR_MISALIGNED, "K/V must be 16-byte aligned");
+  if (!aligned(q, 4) || !aligned(o, 4)) return fail(FQKV_ERR_MISALIGNED, "q/out must be 4-byte aligned");
+  if ((Ks && !aligned(Ks, 2)) || (Vs && !aligned(Vs, 2))) return fail(FQKV_ERR_MISALIGNED, "scales must be 2-byte aligned");
+
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  DecodeLaunch a{};
+  a.fmt = fmt;
+  a.q = q; a.K = K; a.V = V; a.Ks = Ks; a.Vs = Vs; a.out = o;
+  a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
+  plan(a, *ds, 0, ws ? ws_bytes : 0, true);
+  if (int64_t(a.B) * a.Hkv * a.groups * a.S_eff > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "too many work units");
+  if (a.S_eff > 1) {
+    if (!aligned(ws, 16)) return fail(FQKV_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+    carve_partials(a, ws, int64_t(a.B) * a.Hq);
+  }
+  if (fmt == KvFormat::F16) {
+    if (int rc = make_kv_map(&a.tmK, K, B * Hkv, N, D)) return rc;
+    if (int rc = make_kv_map(&a.tmV, V, B * Hkv, N, D)) return rc;
+  }
+  return launch(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fqkv_last_error(void) { return t_err; }
+
+const char* fqkv_version(void) { return "fqkv_b200 0.1.0 (sm_100a)"; }
+
+void fqkv_set_wait_timeout_ms(uint32_t ms) { g_timeout_ns.store(uint64_t(ms) * 1000000ull); }
+
+int fqkv_device_status(int* status_out, int clear) {
+  if (!status_out) return fail(FQKV_ERR_INVALID_ARGUMENT, "status_out is null");
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  e = cudaMemcpy(status_out, ds->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (clear) {
+    e = cudaMemset(ds->status, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "clear status");
+  }
+  return FQKV_OK;
+}
+
+size_t fqkv_decode_workspace_bytes(int kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D) {
+  if (kv_format < 0 || kv_format > 2 || B <= 0 || Hq < 1 || Hkv < 1 || N < 1 || (D != 64 && D != 128) ||
+      Hq % Hkv != 0)
+    return 0;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != FQKV_OK) return 0;
+  DecodeLaunch a{};
+  a.fmt = static_cast<KvFormat>(kv_format);
+  a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
+  plan(a, *ds, 0, 0, false);
+  return a.S_eff > 1 ? partial_bytes(B * Hq, a.S_eff, D) : 0;
+}
+
+int fqkv_decode_attn_fp16_mw(const void* q, const void* K, const void* V, void* o, int64_t R, int64_t N,
+                             int64_t D, int64_t W, void* workspace, size_t workspace_bytes, fqkv_stream_t stream) {
+  if (int rc = check_W(W)) return rc;
+  return run_decode(KvFormat::F16, q, K, V, nullptr, nullptr, o, R, 1, 1, N, D, workspace, workspace_bytes, stream);
+}
+
+int fqkv_decode_attn_int8_mw(const void* q, const void* Kq, const void* Vq, const void* Ks, const void* Vs, void* o,
+                             int64_t R, int64_t N, int64_t D, int64_t W, void* workspace, size_t workspace_bytes,
+                             fqkv_stream_t stream) {
+  if (int rc = check_W(W)) return rc;
+  return run_decode(KvFormat::I8, q, Kq, Vq, Ks, Vs, o, R, 1, 1, N, D, workspace, workspace_bytes, stream);
+}
+
+int fqkv_decode_attn_int4(const void* q, const void* Kp, const void* Vp, const void* Ks, const void* Vs, void* o,
+                          int64_t R, int64_t N, int64_t D, int64_t W, void* workspace, size_t workspace_bytes,
+                          fqkv_stream_t stream) {
+  if (int rc = check_W(W)) return rc;
+  return run_decode(KvFormat::I4, q, Kp, Vp, Ks, Vs, o, R, 1, 1, N, D, workspace, workspace_bytes, stream);
+}
+
+int fqkv_decode_attn_gqa(const void* q, const void* K, const void* V, void* o, int64_t B, int64_t Hq, int64_t Hkv,
+                         int64_t N, int64_t D, int64_t W, void* workspace, size_t workspace_bytes,
+                         fqkv_stream_t stream) {
+  if (int rc = check_W(W)) return rc;
+  return run_decode(KvFormat::F16, q, K, V, nullptr, nullptr, o, B, Hq, Hkv, N, D, workspace, workspace_bytes,
+                    stream);
+}
+
+int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part, float* l_part, float* o_part,
+                     void* out, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, int64_t S, int64_t W, int64_t CW,
+                     fqkv_stream_t stream) {
+  if (int rc = check_W(W)) return rc;
+  if (CW != 4 && CW != 8) return fail(FQKV_ERR_INVALID_ARGUMENT, "CW: must be 4 or 8 (got %lld)", (long long)CW);
+  if (S < 1 || S > (1 << 20)) return fail(FQKV_ERR_INVALID_ARGUMENT, "S: split count must be in [1, 2^20] (got %lld)", (long long)S);
+  if (int rc = check_D(D)) return rc;
+  if (Hq < 1 || Hkv < 1 || N < 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "negative or zero size");
+  if (Hq % Hkv != 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "Hq (%lld) must be a multiple of Hkv (%lld)", (long long)Hq, (long long)Hkv);
+  if (N == 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "N: the KV cache is empty (softmax over zero keys)");
+  if (!q || !K || !V || !out || !m_part || !l_part || !o_part) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (N > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the 32-bit index range");
+  if (!aligned(K, 16) || !aligned(V, 16)) return fail(FQKV_ERR_MISALIGNED, "K/V must be 16-byte aligned");
+  if (!aligned(q, 4) || !aligned(out, 4)) return fail(FQKV_ERR_MISALIGNED, "q/out must be 4-byte aligned");
+  if (!aligned(m_part, 4) || !aligned(l_part, 4) || !aligned(o_part, 4)) return fail(FQKV_ERR_MISALIGNED, "partials must be 4-byte aligned");
+
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  DecodeLaunch a{};
+  a.fmt = KvFormat::F16;
+  a.q = q; a.K = K; a.V = V; a.out = out;
+  a.B = 1; a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
+  plan(a, *ds, S, 0, false);
+  a.part_m = m_part; a.part_l = l_part; a.part_o = o_part;
+  if (int rc = make_kv_map(&a.tmK, K, Hkv, N, D)) return rc;
+  if (int rc = make_kv_map(&a.tmV, V, Hkv, N, D)) return rc;
+  return launch(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+static int run_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int64_t D,
+                        fqkv_stream_t stream) {
+  if (rows < 0 || D < 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "rows must be >= 0 and D >= 1");
+  if (int4 && (D % 2)) return fail(FQKV_ERR_INVALID_ARGUMENT, "D: int4 packing needs an even head_dim (got %lld)", (long long)D);
+  if (D > (1 << 20)) return fail(FQKV_ERR_INVALID_ARGUMENT, "D too large");
+  if (rows == 0) return FQKV_OK;
+  if (!X || !codes || !scales) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(X, 2) || !aligned(scales, 2)) return fail(FQKV_ERR_MISALIGNED, "X/scales must be 2-byte aligned");
+  if (rows > (int64_t(1) << 40)) return fail(FQKV_ERR_INVALID_ARGUMENT, "too many rows");
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  cudaError_t e = fqkv::launch_quantize(int4, X, codes, scales, rows, int(D), reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  return FQKV_OK;
+}
+
+int fqkv_quantize_int8_per_token(const void* X, void* codes, void* scales, int64_t rows, int64_t D,
+                                 fqkv_stream_t stream) {
+  return run_quantize(false, X, codes, scales, rows, D, stream);
+}
+
+int fqkv_quantize_int4_per_token(const void* X, void* packed, void* scales, int64_t rows, int64_t D,
+                                 fqkv_stream_t stream) {
+  return run_quantize(true, X, packed, scales, rows, D, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// Internal interface between the C-ABI layer (capi.cu) and the kernel
+// translation units.  Host-only types: plain pointers, sizes and a stream.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace fqkv {
+
+enum class KvFormat : int { F16 = 0, I8 = 1, I4 = 2 };
+
+// Bytes of one key row of K (or V) in HBM.
+inline int64_t kv_row_bytes(KvFormat f, int64_t D) {
+  return f == KvFormat::F16 ? 2 * D : (f == KvFormat::I8 ? D : D / 2);
+}
+
+// Keys per pipeline stage (one tile).  The fp16 kernel uses 64-key tiles of
+// 128-byte swizzled rows; the quantized kernel uses 8 KiB tiles of K (and V).
+inline int tile_keys(KvFormat f, int64_t D) {
+  return f == KvFormat::F16 ? 64 : static_cast<int>(8192 / kv_row_bytes(f, D));
+}
+
+// One decode-attention launch, in the library's canonical form:
+//   q [B, Hq, D] fp16, K/V [B, Hkv, N, *], (scales [B, Hkv, N] fp16),
+//   out [B, Hq, D] fp16.  Query head h reads KV head h / G, G = Hq / Hkv.
+// A work unit is (b, kv head, head group, split); heads of one group share
+// every K/V byte the unit reads.
+struct DecodeLaunch {
+  KvFormat fmt;
+  const void* q;
+  const void* K;
+  const void* V;
+  const void* Ks;     // fp16 per-token scales (quantized formats)
+  const void* Vs;
+  void* out;
+  float* part_m;      // [B*Hq, S] (S > 1 only)
+  float* part_l;
+  float* part_o;      // [B*Hq, S, D]
+  int B, Hq, Hkv, N, D;
+  int G;              // Hq / Hkv
+  int GP;             // query heads handled by one unit (<= 8)
+  int groups;         // ceil(G / GP)
+  int S;              // splits (partial slots per row)
+  int S_eff;          // non-empty splits actually launched (<= S)
+  int chunk;          // keys per split, a multiple of the tile
+  int units;          // B * Hkv * groups * S_eff
+  int grid;           // persistent CTAs
+  float sm_scale_log2;                 // (1/sqrt(D)) * log2(e)
+  int* status;                         // device status word
+  unsigned long long timeout_ns;
+  int debug_skip_loads;                // test hook: producer issues nothing
+  CUtensorMap tmK, tmV;                // fp16 only
+};
+
+// Kernel resource queries and launches, per KV format (attn_f16.cu,
+// attn_quant.cu).  *_prepare sets the dynamic shared-memory opt-in for the
+// current device and returns how many CTAs of the kernel fit on one SM.
+struct KernelShape {
+  int threads;
+  size_t smem_bytes;
+};
+KernelShape decode_kernel_shape_f16(int D);
+cudaError_t decode_kernel_prepare_f16(int D, int* ctas_per_sm);
+cudaError_t launch_decode_f16(const DecodeLaunch& a, cudaStream_t stream);
+KernelShape decode_kernel_shape_quant(bool int4, int D);
+cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm);
+cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream);
+
+// Log-sum-exp merge of the S_eff partials of every row into out (fp16),
+// chained to the preceding launch by programmatic dependent launch.
+cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream);
+
+cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,
+                            cudaStream_t stream);
+
+}  // namespace fqkv

@@ -1,0 +1,286 @@
+"""PyTorch-facing operators: the reference extension's surface, on libfqkv_b200.
+
+Each function keeps the name, argument order, output and error behaviour of
+the reference operator it replaces (a ``RuntimeError`` whose message starts
+with the reference's ``TORCH_CHECK`` keyword: ``cuda``, ``fp16``, ``contig``,
+``D``, ``W``, ``CW``, ``int8``, ``packed uint8``, ``launch``), so
+``m.decode_attn_fp16_mw(q, K, V, W)`` call sites work unchanged.  The checks
+are a superset of the reference's (device, dtype, contiguity and shape are
+checked on every tensor of every op).
+
+Work is launched on the current torch CUDA stream of the input's device.
+There is no CPU path: inputs must be CUDA tensors and the native library must
+be built.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native
+
+__all__ = [
+    "decode_attn_fp16_mw",
+    "decode_attn_int8_mw",
+    "decode_attn_int4",
+    "decode_attn_gqa",
+    "gqa_sk_fast",
+    "qpt",
+    "quant_int4_per_token",
+    "workspace_bytes",
+]
+
+
+def _fail(op: str, key: str, detail: str) -> None:
+    raise RuntimeError(f"{key}: {op}: {detail}")
+
+
+def _require_cuda(op: str, *ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            _fail(op, "cuda", "all tensors must be CUDA tensors (there is no CPU path)")
+        if t.device != dev:
+            _fail(op, "cuda", "all tensors must be on the same device")
+    return dev
+
+
+def _require_dtype(op: str, key: str, dtype: torch.dtype, **ts: torch.Tensor) -> None:
+    for name, t in ts.items():
+        if t.dtype != dtype:
+            _fail(op, key, f"{name} must be {dtype} (got {t.dtype})")
+
+
+def _require_contig(op: str, **ts: torch.Tensor) -> None:
+    for name, t in ts.items():
+        if not t.is_contiguous():
+            _fail(op, "contig", f"{name} must be contiguous")
+
+
+def _require_shape(op: str, name: str, t: torch.Tensor, shape: tuple) -> None:
+    if tuple(t.shape) != tuple(shape):
+        _fail(op, "shape", f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+
+
+def _require_W(op: str, W: int) -> None:
+    if int(W) not in (2, 4, 8):
+        _fail(op, "W", f"W must be 2, 4 or 8 (got {W})")
+
+
+def _require_D(op: str, D: int) -> None:
+    if D not in (64, 128):
+        _fail(op, "D", f"head_dim must be 64 or 128 (got {D})")
+
+
+class _DeviceGuard:
+    """Make `dev` the current CUDA device for the C ABI call (cheap when it already is)."""
+
+    __slots__ = ("dev", "prev")
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.dev:
+            self.prev = cur
+            torch.cuda.set_device(self.dev)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def workspace_bytes(kv_format: str, B: int, Hq: int, Hkv: int, N: int, D: int) -> int:
+    """Split-K workspace the library would like for this shape on the current device."""
+    fmt = {"fp16": _native.KV_F16, "int8": _native.KV_INT8, "int4": _native.KV_INT4}[kv_format]
+    return int(_native.lib().fqkv_decode_workspace_bytes(fmt, B, Hq, Hkv, N, D))
+
+
+def _workspace(fmt: int, dev: torch.device, B: int, Hq: int, Hkv: int, N: int, D: int):
+    nbytes = int(_native.lib().fqkv_decode_workspace_bytes(fmt, B, Hq, Hkv, N, D))
+    if nbytes == 0:
+        return None, 0
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    return ws, nbytes
+
+
+def decode_attn_fp16_mw(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, W: int) -> torch.Tensor:
+    """fp16 single-query decode: q [R,D], K/V [R,N,D] -> o [R,D] (fp32 accumulation).
+
+    Replaces ``decode_attn_fp16_mw`` (kernels/decode_attn_fp16_mw.cu:50-63).
+    """
+    op = "decode_attn_fp16_mw"
+    dev = _require_cuda(op, q, K, V)
+    _require_dtype(op, "fp16", torch.float16, q=q, K=K, V=V)
+    _require_contig(op, q=q, K=K, V=V)
+    if K.dim() != 3:
+        _fail(op, "shape", "K must be [R, N, D]")
+    R, N, D = K.shape
+    _require_D(op, D)
+    _require_W(op, W)
+    _require_shape(op, "V", V, (R, N, D))
+    _require_shape(op, "q", q, (R, D))
+    o = torch.empty((R, D), dtype=torch.float16, device=dev)
+    with _DeviceGuard(dev):
+        ws, nb = _workspace(_native.KV_F16, dev, R, 1, 1, N, D) if R and N else (None, 0)
+        rc = _native.lib().fqkv_decode_attn_fp16_mw(
+            q.data_ptr(), K.data_ptr(), V.data_ptr(), o.data_ptr(), R, N, D, int(W),
+            ws.data_ptr() if ws is not None else None, nb, _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return o
+
+
+def _quant_decode(op: str, fmt: int, q, K, V, Ks, Vs, W, code_dtype, key, D_of_K):
+    dev = _require_cuda(op, q, K, V, Ks, Vs)
+    _require_dtype(op, key, code_dtype, K=K, V=V)
+    _require_dtype(op, "fp16", torch.float16, q=q, Ks=Ks, Vs=Vs)
+    _require_contig(op, q=q, K=K, V=V, Ks=Ks, Vs=Vs)
+    if K.dim() != 3:
+        _fail(op, "shape", "K must be [R, N, row_bytes]")
+    R, N, H = K.shape
+    D = D_of_K(H)
+    _require_D(op, D)
+    _require_W(op, W)
+    _require_shape(op, "V", V, (R, N, H))
+    _require_shape(op, "Ks", Ks, (R, N))
+    _require_shape(op, "Vs", Vs, (R, N))
+    _require_shape(op, "q", q, (R, D))
+    o = torch.empty((R, D), dtype=torch.float16, device=dev)
+    fn = _native.lib().fqkv_decode_attn_int8_mw if fmt == _native.KV_INT8 else _native.lib().fqkv_decode_attn_int4
+    with _DeviceGuard(dev):
+        ws, nb = _workspace(fmt, dev, R, 1, 1, N, D) if R and N else (None, 0)
+        rc = fn(q.data_ptr(), K.data_ptr(), V.data_ptr(), Ks.data_ptr(), Vs.data_ptr(), o.data_ptr(),
+                R, N, D, int(W), ws.data_ptr() if ws is not None else None, nb, _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return o
+
+
+def decode_attn_int8_mw(q, K, V, Ks, Vs, W):
+    """int8-KV decode: q [R,D] f16, K/V [R,N,D] int8, Ks/Vs [R,N] f16 -> o [R,D] f16.
+
+    Replaces ``decode_attn_int8_mw`` (kernels/decode_attn_int8_mw.cu:52-64).
+    """
+    return _quant_decode("decode_attn_int8_mw", _native.KV_INT8, q, K, V, Ks, Vs, W, torch.int8, "int8",
+                         lambda H: H)
+
+
+def decode_attn_int4(q, K, V, Ks, Vs, W):
+    """int4-KV decode: q [R,D] f16, K/V [R,N,D/2] uint8 (packed), Ks/Vs [R,N] f16 -> o [R,D].
+
+    Replaces ``decode_attn_int4`` (kernels/decode_attn_int4.cu:47-57); D may be
+    64 or 128 (the reference accepts only 64).
+    """
+    return _quant_decode("decode_attn_int4", _native.KV_INT4, q, K, V, Ks, Vs, W, torch.uint8,
+                         "packed uint8", lambda H: 2 * H)
+
+
+def decode_attn_gqa(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, W: int) -> torch.Tensor:
+    """GQA decode: q [B,Hq,D], K/V [B,Hkv,N,D] -> o [B,Hq,D]; head h reads KV head h // (Hq/Hkv).
+
+    Replaces ``decode_attn_gqa`` (kernels/decode_attn_gqa.cu:56-68).  Each KV
+    head is read once for all of its query heads.
+    """
+    op = "decode_attn_gqa"
+    dev = _require_cuda(op, q, K, V)
+    _require_dtype(op, "fp16", torch.float16, q=q, K=K, V=V)
+    _require_contig(op, q=q, K=K, V=V)
+    if q.dim() != 3 or K.dim() != 4:
+        _fail(op, "shape", "q must be [B, Hq, D] and K [B, Hkv, N, D]")
+    B, Hq, D = q.shape
+    _, Hkv, N, _ = K.shape
+    _require_D(op, D)
+    _require_W(op, W)
+    _require_shape(op, "K", K, (B, Hkv, N, D))
+    _require_shape(op, "V", V, (B, Hkv, N, D))
+    if Hkv < 1 or Hq % Hkv:
+        _fail(op, "shape", f"Hq ({Hq}) must be a multiple of Hkv ({Hkv})")
+    o = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
+    with _DeviceGuard(dev):
+        ws, nb = _workspace(_native.KV_F16, dev, B, Hq, Hkv, N, D) if B and N else (None, 0)
+        rc = _native.lib().fqkv_decode_attn_gqa(
+            q.data_ptr(), K.data_ptr(), V.data_ptr(), o.data_ptr(), B, Hq, Hkv, N, D, int(W),
+            ws.data_ptr() if ws is not None else None, nb, _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return o
+
+
+def gqa_sk_fast(q, K, V, m_part, l_part, o_part, o, S, W, CW) -> None:
+    """GQA split-K decode into caller buffers (batch 1).
+
+    q [Hq,D] f16, K/V [Hkv,N,D] f16, scratch m_part/l_part [Hq,S] f32,
+    o_part [Hq,S,D] f32, output o [Hq,D] f16.  Replaces ``gqa_sk_fast``
+    (kernels/decode_attn_gqa_sk_fast.cu:95-112).  Scratch contents afterwards
+    are unspecified.
+    """
+    op = "gqa_sk_fast"
+    dev = _require_cuda(op, q, K, V, m_part, l_part, o_part, o)
+    _require_dtype(op, "fp16", torch.float16, q=q, K=K, V=V, o=o)
+    _require_dtype(op, "f32", torch.float32, m_part=m_part, l_part=l_part, o_part=o_part)
+    _require_contig(op, q=q, K=K, V=V, m_part=m_part, l_part=l_part, o_part=o_part, o=o)
+    _require_W(op, W)
+    if int(CW) not in (4, 8):
+        _fail(op, "CW", f"CW must be 4 or 8 (got {CW})")
+    S = int(S)
+    if S < 1:
+        _fail(op, "S", f"S must be >= 1 (got {S})")
+    if q.dim() != 2 or K.dim() != 3:
+        _fail(op, "shape", "q must be [Hq, D] and K [Hkv, N, D]")
+    Hq, D = q.shape
+    Hkv, N, _ = K.shape
+    _require_D(op, D)
+    _require_shape(op, "K", K, (Hkv, N, D))
+    _require_shape(op, "V", V, (Hkv, N, D))
+    _require_shape(op, "m_part", m_part, (Hq, S))
+    _require_shape(op, "l_part", l_part, (Hq, S))
+    _require_shape(op, "o_part", o_part, (Hq, S, D))
+    _require_shape(op, "o", o, (Hq, D))
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_gqa_sk_fast(
+            q.data_ptr(), K.data_ptr(), V.data_ptr(), m_part.data_ptr(), l_part.data_ptr(), o_part.data_ptr(),
+            o.data_ptr(), Hq, Hkv, N, D, S, int(W), int(CW), _stream(dev))
+    _native.check(rc, f"launch: {op}")
+
+
+def _quantize(op: str, X: torch.Tensor, int4: bool):
+    dev = _require_cuda(op, X)
+    _require_dtype(op, "fp16", torch.float16, X=X)
+    _require_contig(op, X=X)
+    if X.dim() < 1:
+        _fail(op, "shape", "X must have a head_dim axis")
+    D = X.shape[-1]
+    if int4 and D % 2:
+        _fail(op, "D", f"int4 packing needs an even head_dim (got {D})")
+    rows = X.numel() // D if D else 0
+    codes = torch.empty(X.shape[:-1] + ((D // 2,) if int4 else (D,)),
+                        dtype=torch.uint8 if int4 else torch.int8, device=dev)
+    scales = torch.empty(X.shape[:-1], dtype=torch.float16, device=dev)
+    fn = _native.lib().fqkv_quantize_int4_per_token if int4 else _native.lib().fqkv_quantize_int8_per_token
+    with _DeviceGuard(dev):
+        rc = fn(X.data_ptr(), codes.data_ptr(), scales.data_ptr(), rows, D, _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return codes, scales
+
+
+def qpt(X: torch.Tensor):
+    """Per-token symmetric int8 quantizer: X [..., D] f16 -> (int8 [..., D], f16 scales [...]).
+
+    Bit-exact with the reference's ``qpt`` (notebook lines 236-238,
+    tests/test_kernels.py:32-34).
+    """
+    return _quantize("qpt", X, False)
+
+
+def quant_int4_per_token(X: torch.Tensor):
+    """Per-token symmetric int4 quantizer + packer: X [..., D] -> (uint8 [..., D/2], f16 [...]).
+
+    Bit-exact with the reference's ``quant_int4_per_token`` (notebook lines
+    292-299): element 2t in the low nibble of byte t.
+    """
+    return _quantize("quant_int4_per_token", X, True)

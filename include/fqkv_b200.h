@@ -1,0 +1,128 @@
+/*
+ * fqkv_b200.h -- C ABI of the B200 (sm_100a) fused single-query decode-attention
+ * library (libfqkv_b200.so).
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream, returns
+ * an fqkv_status_t, never allocates device memory, and launches asynchronously
+ * on `stream` (pass NULL for the legacy default stream).  All launches are
+ * stream-ordered and capturable in a CUDA graph.  On failure,
+ * fqkv_last_error() returns a message for the calling thread.
+ *
+ * Tensor layouts are the reference's (emirabayer/Fused-Quantized-KV-Decode-
+ * Attention); each entry point names the reference function it replaces as
+ * `reference: file:line`.  Element types:
+ *   f16  = IEEE binary16, i8 = int8 codes, u8 = packed int4 (two signed
+ *   nibbles per byte, element 2t in the low nibble), f32 = binary32.
+ * Softmax scale is 1/sqrt(D) in every attention entry point (as in the
+ * reference).  Accumulation is fp32; outputs are rounded once to f16.
+ *
+ * Alignment: K/V code or f16 tensors must start on a 16-byte boundary; q and
+ * out on a 4-byte boundary; scale arrays need only natural (2-byte)
+ * alignment.  The int8/int4 kernels read scales in 16-byte blocks and may
+ * touch up to 15 bytes before the first and after the last scale of an
+ * array, always inside the 16-byte blocks that hold those scales.
+ */
+#ifndef FQKV_B200_H_
+#define FQKV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t / CUstream. */
+typedef struct CUstream_st* fqkv_stream_t;
+
+typedef enum fqkv_status_t {
+  FQKV_OK = 0,
+  FQKV_ERR_INVALID_ARGUMENT = 1, /* bad size, head_dim, W / CW / S, or null pointer */
+  FQKV_ERR_MISALIGNED = 2,       /* a pointer violates the alignment rules above */
+  FQKV_ERR_CUDA = 3,             /* CUDA runtime / launch error (see fqkv_last_error) */
+  FQKV_ERR_UNSUPPORTED_DEVICE = 4, /* current device is not sm_100 */
+  FQKV_ERR_DEVICE_TIMEOUT = 5    /* a bounded in-kernel wait gave up (see fqkv_device_status) */
+} fqkv_status_t;
+
+/* KV storage formats for the workspace query. */
+typedef enum fqkv_kv_format_t { FQKV_KV_F16 = 0, FQKV_KV_INT8 = 1, FQKV_KV_INT4 = 2 } fqkv_kv_format_t;
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* fqkv_last_error(void);
+
+/* Library version string. */
+const char* fqkv_version(void);
+
+/* Reads (and, if clear != 0, resets) the in-kernel status word of the current
+ * device: 0 = healthy, otherwise the code of the first bounded wait that gave
+ * up (61 tile never arrived, 62 stage never freed, 63 copy drain failed).
+ * Synchronizes with the device. */
+int fqkv_device_status(int* status_out, int clear);
+
+/* Overrides the wall-clock limit of every in-kernel wait (milliseconds,
+ * default 2000).  Intended for tests of the failure path. */
+void fqkv_set_wait_timeout_ms(uint32_t ms);
+
+/* Bytes of optional workspace (split-K partials) that makes the single-block
+ * entry points below run with their preferred split count on the current
+ * device.  Passing less (or NULL) is valid: the split count is reduced to what
+ * fits, down to 1 (no workspace).  Rows are B*Hq (Hq = Hkv = 1 for the
+ * non-GQA entry points with B = R). */
+size_t fqkv_decode_workspace_bytes(int kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D);
+
+/* fp16 KV.  q [R,D] f16, K/V [R,N,D] f16 -> o [R,D] f16.  D in {64,128};
+ * W in {2,4,8} is accepted for compatibility (the kernel picks its own
+ * launch shape).
+ * reference: kernels/decode_attn_fp16_mw.cu:50 decode_attn_fp16_mw(q,K,V,W) */
+int fqkv_decode_attn_fp16_mw(const void* q, const void* K, const void* V, void* o, int64_t R, int64_t N,
+                             int64_t D, int64_t W, void* workspace, size_t workspace_bytes,
+                             fqkv_stream_t stream);
+
+/* int8 KV.  q [R,D] f16, Kq/Vq [R,N,D] i8, Ks/Vs [R,N] f16 -> o [R,D] f16.
+ * reference: kernels/decode_attn_int8_mw.cu:52 decode_attn_int8_mw(q,K,V,Ks,Vs,W) */
+int fqkv_decode_attn_int8_mw(const void* q, const void* Kq, const void* Vq, const void* Ks, const void* Vs,
+                             void* o, int64_t R, int64_t N, int64_t D, int64_t W, void* workspace,
+                             size_t workspace_bytes, fqkv_stream_t stream);
+
+/* int4 KV.  q [R,D] f16, Kp/Vp [R,N,D/2] u8, Ks/Vs [R,N] f16 -> o [R,D] f16.
+ * D in {64,128} (the reference supports D = 64 only).
+ * reference: kernels/decode_attn_int4.cu:47 decode_attn_int4(q,K,V,Ks,Vs,W) */
+int fqkv_decode_attn_int4(const void* q, const void* Kp, const void* Vp, const void* Ks, const void* Vs,
+                          void* o, int64_t R, int64_t N, int64_t D, int64_t W, void* workspace,
+                          size_t workspace_bytes, fqkv_stream_t stream);
+
+/* GQA fp16 KV.  q [B,Hq,D] f16, K/V [B,Hkv,N,D] f16 -> o [B,Hq,D] f16; query
+ * head h reads KV head h / (Hq/Hkv).  Hq must be a multiple of Hkv.
+ * reference: kernels/decode_attn_gqa.cu:56 decode_attn_gqa(q,K,V,W) */
+int fqkv_decode_attn_gqa(const void* q, const void* K, const void* V, void* o, int64_t B, int64_t Hq,
+                         int64_t Hkv, int64_t N, int64_t D, int64_t W, void* workspace,
+                         size_t workspace_bytes, fqkv_stream_t stream);
+
+/* GQA split-K (batch 1).  q [Hq,D] f16, K/V [Hkv,N,D] f16; caller-owned
+ * scratch m_part/l_part [Hq,S] f32, o_part [Hq,S,D] f32; out [Hq,D] f16.
+ * At most S splits are used (chunk = ceil(N/S) rounded up to 64 keys); the
+ * scratch contents after the call are unspecified.  W in {2,4,8}, CW in {4,8}
+ * are accepted for compatibility.
+ * reference: kernels/decode_attn_gqa_sk_fast.cu:95 gqa_sk_fast(q,K,V,m_part,l_part,o_part,o,S,W,CW) */
+int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part, float* l_part, float* o_part,
+                     void* out, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, int64_t S, int64_t W, int64_t CW,
+                     fqkv_stream_t stream);
+
+/* Per-token symmetric int8 quantizer, bit-exact with the reference's torch
+ * code.  X [rows,D] f16 -> codes [rows,D] i8, scales [rows] f16 (any D >= 1).
+ * reference: notebooks/integration_and_benchmarks.ipynb:236-238 qpt(X),
+ *            tests/test_kernels.py:32-34 */
+int fqkv_quantize_int8_per_token(const void* X, void* codes, void* scales, int64_t rows, int64_t D,
+                                 fqkv_stream_t stream);
+
+/* Per-token symmetric int4 quantizer + nibble packer, bit-exact.
+ * X [rows,D] f16 (D even) -> packed [rows,D/2] u8, scales [rows] f16.
+ * reference: notebooks/integration_and_benchmarks.ipynb:292-299 quant_int4_per_token(X) */
+int fqkv_quantize_int4_per_token(const void* X, void* packed, void* scales, int64_t rows, int64_t D,
+                                 fqkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FQKV_B200_H_ */

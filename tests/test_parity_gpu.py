@@ -1,0 +1,188 @@
+"""GPU parity: every attention entry point against the CPU oracle.
+
+Inputs are drawn on the CPU with ``torch.manual_seed`` (as the reference's
+tests do), copied to the GPU, and the library's output is compared with the
+float64 oracle at ``atol=2e-3, rtol=1e-2`` (the build's tolerance; the
+reference's own tests use 2e-2 .. 6e-2).  Quantized paths are compared with
+the oracle evaluated on the dequantised KV, codes coming from the library's
+own quantizer (which ``test_quantizer_gpu.py`` pins bit-exact).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _randn(*shape, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g, dtype=torch.float32).to(torch.float16)
+
+
+def _close(out: torch.Tensor, ref: np.ndarray):
+    got = out.float().cpu().numpy().astype(np.float64)
+    np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
+
+
+# ------------------------------------------------------------------ fp16 (K1)
+# reference tests: (B,N,W) in {(1,1024,8),(8,2048,4),(256,4096,8)} at D=64
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("R,N,W", [(1, 1024, 8), (8, 2048, 4), (256, 4096, 8), (3, 1, 2), (2, 3, 4),
+                                   (5, 100, 8), (4, 63, 8), (4, 64, 8), (4, 65, 8), (2, 16385, 8)])
+def test_fp16_mw(fqkv, R, N, W, D):
+    q, K, V = _randn(R, D, seed=1), _randn(R, N, D, seed=2), _randn(R, N, D, seed=3)
+    out = fqkv.decode_attn_fp16_mw(q.cuda(), K.cuda(), V.cuda(), W)
+    torch.cuda.synchronize()
+    assert out.shape == (R, D) and out.dtype == torch.float16
+    _close(out, oatt.decode_attention(q.numpy(), K.numpy(), V.numpy()))
+
+
+def test_fp16_mw_full_cfg1(fqkv):
+    """BASELINE config 1 at full size: B=8 x 32 heads, N=4096, D=128."""
+    R, N, D = 256, 4096, 128
+    q, K, V = _randn(R, D, seed=11), _randn(R, N, D, seed=12), _randn(R, N, D, seed=13)
+    out = fqkv.decode_attn_fp16_mw(q.cuda(), K.cuda(), V.cuda(), 8)
+    _close(out, oatt.decode_attention(q.numpy(), K.numpy(), V.numpy()))
+
+
+# ------------------------------------------------------------------ int8 (K2)
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("R,N,W", [(1, 1024, 8), (8, 2048, 4), (3, 1, 2), (2, 3, 4), (5, 100, 8),
+                                   (4, 64, 8), (4, 129, 8), (2, 5000, 8)])
+def test_int8_mw(fqkv, R, N, W, D):
+    q, K, V = _randn(R, D, seed=4), _randn(R, N, D, seed=5), _randn(R, N, D, seed=6)
+    Kq, Ks = fqkv.qpt(K.cuda())
+    Vq, Vs = fqkv.qpt(V.cuda())
+    out = fqkv.decode_attn_int8_mw(q.cuda(), Kq, Vq, Ks, Vs, W)
+    Kd = oq.dequantize_int8(Kq.cpu().numpy(), Ks.cpu().numpy())
+    Vd = oq.dequantize_int8(Vq.cpu().numpy(), Vs.cpu().numpy())
+    _close(out, oatt.decode_attention(q.numpy(), Kd, Vd))
+
+
+# ------------------------------------------------------------------ int4 (K3)
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("R,N,W", [(1, 1024, 8), (8, 2048, 2), (256, 4096, 8), (4, 3, 4), (3, 1, 2),
+                                   (5, 100, 8), (4, 257, 8)])
+def test_int4(fqkv, R, N, W, D):
+    q, K, V = _randn(R, D, seed=7), _randn(R, N, D, seed=8), _randn(R, N, D, seed=9)
+    Kp, Ks = fqkv.quant_int4_per_token(K.cuda())
+    Vp, Vs = fqkv.quant_int4_per_token(V.cuda())
+    out = fqkv.decode_attn_int4(q.cuda(), Kp, Vp, Ks, Vs, W)
+    Kd = oq.dequantize_int4(Kp.cpu().numpy(), Ks.cpu().numpy())
+    Vd = oq.dequantize_int4(Vp.cpu().numpy(), Vs.cpu().numpy())
+    _close(out, oatt.decode_attention(q.numpy(), Kd, Vd))
+
+
+def test_quantized_inputs_with_zero_tokens(fqkv):
+    """All-zero tokens quantize to scale 0 / codes 0 and contribute a zero key/value."""
+    R, N, D = 2, 70, 128
+    q, K, V = _randn(R, D, seed=20), _randn(R, N, D, seed=21), _randn(R, N, D, seed=22)
+    K[:, 5] = 0
+    V[:, 5] = 0
+    V[:, 66] = 0
+    for quant, dq, op in ((fqkv.qpt, oq.dequantize_int8, fqkv.decode_attn_int8_mw),
+                          (fqkv.quant_int4_per_token, oq.dequantize_int4, fqkv.decode_attn_int4)):
+        Kc, Ks = quant(K.cuda())
+        Vc, Vs = quant(V.cuda())
+        assert float(Ks[0, 5]) == 0.0
+        out = op(q.cuda(), Kc, Vc, Ks, Vs, 8)
+        ref = oatt.decode_attention(q.numpy(), dq(Kc.cpu().numpy(), Ks.cpu().numpy()),
+                                    dq(Vc.cpu().numpy(), Vs.cpu().numpy()))
+        _close(out, ref)
+
+
+# ------------------------------------------------------------------ GQA (K4)
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("B,Hq,Hkv,N", [(1, 32, 8, 1024), (16, 32, 8, 4096), (2, 32, 8, 37), (3, 32, 8, 1),
+                                        (2, 8, 8, 300), (2, 64, 8, 200), (1, 32, 2, 500), (2, 12, 4, 129),
+                                        (1, 32, 8, 16384)])
+def test_gqa(fqkv, B, Hq, Hkv, N, D):
+    q, K, V = _randn(B, Hq, D, seed=30), _randn(B, Hkv, N, D, seed=31), _randn(B, Hkv, N, D, seed=32)
+    out = fqkv.decode_attn_gqa(q.cuda(), K.cuda(), V.cuda(), 8)
+    assert out.shape == (B, Hq, D)
+    _close(out, oatt.decode_attention_gqa(q.numpy(), K.numpy(), V.numpy()))
+
+
+def test_gqa_bench_shape_sampled_rows(fqkv):
+    """The bench workload (B=64, Hq=32, Hkv=8, N=16384, D=128), checked on sampled sequences."""
+    B, Hq, Hkv, N, D = 64, 32, 8, 16384, 128
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, Hq, D, device="cuda", generator=gen, dtype=torch.float16)
+    K = torch.randn(B, Hkv, N, D, device="cuda", generator=gen, dtype=torch.float16)
+    V = torch.randn(B, Hkv, N, D, device="cuda", generator=gen, dtype=torch.float16)
+    out = fqkv.decode_attn_gqa(q, K, V, 8)
+    for b in (0, 17, 63):
+        ref = oatt.decode_attention_gqa(q[b:b + 1].cpu().numpy(), K[b:b + 1].cpu().numpy(),
+                                        V[b:b + 1].cpu().numpy())
+        _close(out[b:b + 1], ref)
+
+
+# ------------------------------------------------------------------ split-K (K5-K7)
+# the reference's six cases (tests/test_kernels.py:59) plus larger S / N
+@pytest.mark.parametrize("N,D,S,W,CW", [(1024, 64, 8, 8, 4), (4096, 128, 16, 8, 4), (16384, 64, 64, 8, 8),
+                                        (3, 128, 8, 4, 4), (1, 64, 4, 2, 4), (100, 64, 7, 4, 4),
+                                        (16384, 128, 64, 8, 8), (65536, 128, 128, 8, 8), (777, 128, 1, 8, 4)])
+def test_gqa_sk_fast(fqkv, N, D, S, W, CW):
+    Hq, Hkv = 32, 8
+    q, K, V = _randn(Hq, D, seed=40), _randn(Hkv, N, D, seed=41), _randn(Hkv, N, D, seed=42)
+    dev = "cuda"
+    mp = torch.empty(Hq, S, dtype=torch.float32, device=dev)
+    lp = torch.empty(Hq, S, dtype=torch.float32, device=dev)
+    op = torch.empty(Hq, S, D, dtype=torch.float32, device=dev)
+    out = torch.empty(Hq, D, dtype=torch.float16, device=dev)
+    fqkv.gqa_sk_fast(q.cuda(), K.cuda(), V.cuda(), mp, lp, op, out, S, W, CW)
+    _close(out, oatt.decode_attention_gqa(q.numpy()[None], K.numpy()[None], V.numpy()[None])[0])
+
+
+# ------------------------------------------------------------------ properties
+def test_split_count_does_not_change_the_result(fqkv):
+    """Same op with no workspace (one split) and with the preferred split-K plan."""
+    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 128
+    q, K, V = (_randn(B, Hq, D, seed=50).cuda(), _randn(B, Hkv, N, D, seed=51).cuda(),
+               _randn(B, Hkv, N, D, seed=52).cuda())
+    lib = fqkv.native.lib()
+    out1 = torch.empty(B, Hq, D, dtype=torch.float16, device="cuda")
+    rc = lib.fqkv_decode_attn_gqa(q.data_ptr(), K.data_ptr(), V.data_ptr(), out1.data_ptr(), B, Hq, Hkv, N, D, 8,
+                                  None, 0, torch.cuda.current_stream().cuda_stream)
+    fqkv.native.check(rc, "gqa")
+    nb = fqkv.workspace_bytes("fp16", B, Hq, Hkv, N, D)
+    assert nb > 0
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    out2 = torch.empty_like(out1)
+    rc = lib.fqkv_decode_attn_gqa(q.data_ptr(), K.data_ptr(), V.data_ptr(), out2.data_ptr(), B, Hq, Hkv, N, D, 8,
+                                  ws.data_ptr(), nb, torch.cuda.current_stream().cuda_stream)
+    fqkv.native.check(rc, "gqa")
+    torch.testing.assert_close(out1.float(), out2.float(), atol=1e-3, rtol=1e-3)
+
+
+def test_cuda_graph_capture_and_side_stream(fqkv):
+    B, Hq, Hkv, N, D = 2, 32, 8, 4096, 128
+    q, K, V = (_randn(B, Hq, D, seed=60).cuda(), _randn(B, Hkv, N, D, seed=61).cuda(),
+               _randn(B, Hkv, N, D, seed=62).cuda())
+    ref = fqkv.decode_attn_gqa(q, K, V, 8)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        side = fqkv.decode_attn_gqa(q, K, V, 8)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.testing.assert_close(side, ref, atol=0, rtol=0)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        cap = fqkv.decode_attn_gqa(q, K, V, 8)
+    g.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(cap, ref, atol=0, rtol=0)
+
+
+def test_device_status_clean_after_suite(fqkv):
+    import ctypes
+    st = ctypes.c_int(-1)
+    fqkv.native.check(fqkv.native.lib().fqkv_device_status(ctypes.byref(st), 0), "status")
+    assert st.value == 0
