@@ -10,7 +10,7 @@ The directory name is not a Python identifier, so import it with
 """
 from __future__ import annotations
 
-from . import _native
+from . import _native, sharding
 from .ops import (
     decode_attn_fp16_mw,
     decode_attn_gqa,
@@ -34,6 +34,7 @@ __all__ = [
     "build",
     "library_path",
     "native",
+    "sharding",
 ]
 
 native = _native
