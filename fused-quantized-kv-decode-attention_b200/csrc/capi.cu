@@ -274,6 +274,11 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
 
 }  // namespace
 
+namespace fqkv {
+// Records `msg` as the calling thread's fqkv_last_error() text; returns `code`.
+int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace fqkv
+
 extern "C" {
 
 const char* fqkv_last_error(void) { return t_err; }

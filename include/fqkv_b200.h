@@ -5,7 +5,8 @@
  * Every entry point takes raw device pointers, sizes and a CUDA stream, returns
  * an fqkv_status_t, never allocates device memory, and launches asynchronously
  * on `stream` (pass NULL for the legacy default stream).  All launches are
- * stream-ordered and capturable in a CUDA graph.  On failure,
+ * stream-ordered; the entry points whose buffers all come from the caller are
+ * capturable in a CUDA graph.  On failure,
  * fqkv_last_error() returns a message for the calling thread.
  *
  * Tensor layouts are the reference's (emirabayer/Fused-Quantized-KV-Decode-
@@ -107,6 +108,22 @@ int fqkv_decode_attn_gqa(const void* q, const void* K, const void* V, void* o, i
 int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part, float* l_part, float* o_part,
                      void* out, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, int64_t S, int64_t W, int64_t CW,
                      fqkv_stream_t stream);
+
+/* Split-K GQA decode that allocates nothing: same inputs, output and result as
+ * fqkv_gqa_sk_fast, but the per-split partials live in a 4 MiB array that the
+ * library keeps in device memory (one per GPU, held until exit) instead of in
+ * caller scratch.  For callers that may not allocate device memory at the
+ * call site (a serving runtime's enqueue/plugin hook that owns all device
+ * memory, a decode loop that must not stall on cudaMalloc, a C host with no
+ * allocator).  Limit: 2*pad256(4*Hq*S) + 4*Hq*S*D bytes must fit in 4 MiB
+ * (e.g. Hq=32, D=128 allows S <= 252), else FQKV_ERR_INVALID_ARGUMENT and
+ * nothing is launched.  The first call on a device (with it current) looks up
+ * the array's device address once; make it before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race on it.
+ * No counterpart in the reference. */
+int fqkv_gqa_sk_fast_static_scratch(const void* q, const void* K, const void* V, void* out, int64_t Hq,
+                                    int64_t Hkv, int64_t N, int64_t D, int64_t S, int64_t W, int64_t CW,
+                                    fqkv_stream_t stream);
 
 /* Per-token symmetric int8 quantizer, bit-exact with the reference's torch
  * code.  X [rows,D] f16 -> codes [rows,D] i8, scales [rows] f16 (any D >= 1).
