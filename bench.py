@@ -206,7 +206,7 @@ class Case:
 
     def launch(self) -> None:
         """One decode call through the C ABI, no allocation, on the current stream."""
-        w, lib, s = self.w, self.lib, self.stream.cuda_stream
+        w, lib, s = self.w, self.lib, torch.cuda.current_stream(self.dev).cuda_stream
         k = w["kind"]
         if k == "gqa":
             rc = lib.fqkv_decode_attn_gqa(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(), self.o.data_ptr(),
@@ -350,10 +350,22 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the per-GPU batch (sequences; 32 heads each for the row workloads)")
+    ap.add_argument("--no-clock-hold", action="store_true",
+                    help="do not keep the GPU loaded for clock sampling after the timed region (profiling runs)")
+    ap.add_argument("--eager", action="store_true",
+                    help="time K eager C-ABI calls instead of one CUDA-graph replay of K calls")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.batch is not None and w["kind"] != "sk":
+        if w["kind"] == "gqa":
+            w["B"] = args.batch
+        else:
+            w["R"] = 32 * args.batch
+        w["desc"] += f" [batch overridden to {args.batch}]"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -361,7 +373,9 @@ def main() -> int:
     config = {"workload": w["desc"], "global_batch": None, "seq_len": w["N"], "head_dim": w["D"],
               "parallelism": f"{world} GPU(s), sequences sharded, no data-path collective",
               "l2": "inputs larger than L2 per step (no flush needed)" if w["kind"] != "sk"
-              else "8 rotated KV sets (537 MB) > 4x L2"}
+              else "8 rotated KV sets (537 MB) > 4x L2",
+              "timing": "CUDA events around K eager C-ABI calls" if args.eager
+              else "CUDA events around one CUDA-graph replay of K C-ABI calls"}
     if w["kind"] == "gqa":
         config["global_batch"] = w["B"] * world
     elif w["kind"] == "sk":
@@ -418,16 +432,28 @@ def main() -> int:
         case.launch()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(case.stream)
-    for _ in range(args.steps):
-        case.launch()
-    ev1.record(case.stream)
+    if args.eager:
+        ev0.record()
+        for _ in range(args.steps):
+            case.launch()
+        ev1.record()
+    else:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=torch.cuda.Stream(dev)):
+            for _ in range(args.steps):
+                case.launch()
+        graph.replay()  # untimed: first replay uploads the graph
+        torch.cuda.synchronize(dev)
+        barrier()
+        ev0.record()
+        graph.replay()
+        ev1.record()
     torch.cuda.synchronize(dev)
     barrier()
     ms_total = ev0.elapsed_time(ev1)
     # keep the GPU loaded until the clock sampler has seen at least ~1 s of this kernel
     t_loaded = time.time() - sampler.t0
-    while t_loaded < 1.2:
+    while t_loaded < 1.2 and not args.no_clock_hold:
         for _ in range(50):
             case.launch()
         torch.cuda.synchronize(dev)

@@ -169,43 +169,37 @@ void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_byt
     *chunk_tiles = (tiles + S - 1) / S;
     *S_eff = (tiles + *chunk_tiles - 1) / *chunk_tiles;
   };
+  // Modelled time: every round of the persistent grid costs
+  // max(active CTAs, 3/4 of the grid) x tiles per unit -- with fewer CTAs than
+  // that the machine stops being HBM-bound -- and splitting adds about one
+  // tile of epilogue / combine work per unit.  S_fixed > 0 (gqa_sk_fast) caps
+  // the split count at the caller's scratch capacity; otherwise the caller's
+  // workspace bytes cap it when `limit_ws`.
+  const int64_t floor_ctas = (3 * C) / 4;
+  const int64_t maxS = S_fixed > 0 ? std::min<int64_t>(tiles, S_fixed) : std::min<int64_t>(tiles, 256);
+  double best = 1e300;
   int64_t best_S = 1;
-  if (S_fixed > 0) {
-    // chunk = ceil(N/S) keys rounded up to whole tiles
-    const int64_t ck = (int64_t(a.N) + S_fixed - 1) / S_fixed;
-    const int64_t ct = (ck + TK - 1) / TK;
-    a.S = int(S_fixed);
-    a.chunk = int(ct * TK);
-    a.S_eff = int((tiles + ct - 1) / ct);
-  } else {
-    // Modelled time: every round of the persistent grid costs
-    // max(active CTAs, half the grid) x tiles per unit -- below about half of
-    // the CTAs the machine is no longer HBM-bound.  Splitting adds about one
-    // tile of epilogue / combine work per unit.
-    double best = 1e300;
-    const int64_t maxS = std::min<int64_t>(tiles, 256);
-    for (int64_t S = 1; S <= maxS; ++S) {
-      int64_t ct, se;
-      geometry(S, &ct, &se);
-      if (se != S) continue;
-      if (limit_ws && se > 1 && partial_bytes(rows, se, a.D) > ws_bytes) continue;
-      const int64_t U = units0 * se;
-      double cost = 0;
-      for (int64_t done = 0; done < U; done += C) {
-        const int64_t active = std::min(C, U - done);
-        cost += double(std::max<int64_t>(active, C / 2)) * double(ct + (se > 1 ? 1 : 0));
-      }
-      if (cost < best * 0.999) {
-        best = cost;
-        best_S = se;
-      }
-    }
+  for (int64_t S = 1; S <= maxS; ++S) {
     int64_t ct, se;
-    geometry(best_S, &ct, &se);
-    a.S = int(se);
-    a.S_eff = int(se);
-    a.chunk = int(ct * TK);
+    geometry(S, &ct, &se);
+    if (se != S) continue;
+    if (S_fixed <= 0 && limit_ws && se > 1 && partial_bytes(rows, se, a.D) > ws_bytes) continue;
+    const int64_t U = units0 * se;
+    double cost = 0;
+    for (int64_t done = 0; done < U; done += C) {
+      const int64_t active = std::min(C, U - done);
+      cost += double(std::max<int64_t>(active, floor_ctas)) * double(ct + (se > 1 ? 1 : 0));
+    }
+    if (cost < best * 0.999) {
+      best = cost;
+      best_S = se;
+    }
   }
+  int64_t ct, se;
+  geometry(best_S, &ct, &se);
+  a.S = S_fixed > 0 ? int(S_fixed) : int(se);   // partial-slot stride per row
+  a.S_eff = int(se);
+  a.chunk = int(ct * TK);
   const int64_t units = units0 * a.S_eff;
   a.units = int(units);
   a.grid = int(std::min<int64_t>(units, C));

@@ -101,8 +101,9 @@ int fqkv_decode_attn_gqa(const void* q, const void* K, const void* V, void* o, i
 
 /* GQA split-K (batch 1).  q [Hq,D] f16, K/V [Hkv,N,D] f16; caller-owned
  * scratch m_part/l_part [Hq,S] f32, o_part [Hq,S,D] f32; out [Hq,D] f16.
- * At most S splits are used (chunk = ceil(N/S) rounded up to 64 keys); the
- * scratch contents after the call are unspecified.  W in {2,4,8}, CW in {4,8}
+ * At most S splits are used: the library picks the count (<= S, whole
+ * 64-key tiles per split) that fills the GPU; the scratch contents after the
+ * call are unspecified.  W in {2,4,8}, CW in {4,8}
  * are accepted for compatibility.
  * reference: kernels/decode_attn_gqa_sk_fast.cu:95 gqa_sk_fast(q,K,V,m_part,l_part,o_part,o,S,W,CW) */
 int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part, float* l_part, float* o_part,
