@@ -56,13 +56,37 @@ struct QCfg {
   static_assert(kTK == 4 * kConsumerWarps * kKPS, "each lane owns 4 keys per tile");
 };
 
-__device__ __forceinline__ float byte_to_float(uint32_t w_xor80, uint32_t sel) {
-  // result bytes: [w.b_sel, 0, 0, 0x4B] -> 2^23 + (code + 128)
-  return __int_as_float(static_cast<int>(__byte_perm(w_xor80, 0x4B000000u, 0x7540u | sel))) - 8388736.0f;
+// fp32 accumulate of p (fp16) times both halves of an fp16 pair:
+// lo += p * v.lo, hi += p * v.hi, with the sm_100 mixed-precision FMA.
+__device__ __forceinline__ void fma_pair(float& lo, float& hi, uint32_t v2, uint16_t p) {
+  asm("{\n\t.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "fma.rn.f32.f16 %0, %3, a, %0;\n\tfma.rn.f32.f16 %1, %3, b, %1;\n\t}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(v2), "h"(p));
+}
+
+// exact fp16 pair subtraction (both operands are small integers in fp16)
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// dp4a with a signed-byte first operand and unsigned-byte second operand,
+// and with both unsigned.
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 template <bool kInt4, int D>
-__global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_constant__ DecodeLaunch a) {
+__global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = QCfg<kInt4, D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -173,6 +197,13 @@ __global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_con
       for (int d = 0; d < C::kDimsPerLane; ++d) qv[d] = rintf(qv[d] * two_e);  // |.| <= 16384
       qscale_unit = a.sm_scale_log2 * ldexpf(1.f, -e) * (kInt4 ? 0.0625f : 1.f);
     }
+    // int4 codes enter dp4a as unsigned (code + 8); remove 8 * sum(q) once.
+    int qbias = 0;
+    if (kInt4) {
+#pragma unroll
+      for (int d = 0; d < C::kDimsPerLane; ++d) qbias += int(qv[d]);
+      qbias *= 128;  // 8 * 16 (all int4 products carry a factor 16)
+    }
 
     // planes: int8 -> word w covers dims 4w..4w+3; int4 -> word w covers dims
     // 8w..8w+7 split into even and odd dims (index 2w + parity).
@@ -208,7 +239,7 @@ __global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_con
     float o[C::kDimsPerLane];
 #pragma unroll
     for (int d = 0; d < C::kDimsPerLane; ++d) o[d] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f, lv_run = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
 
     for (int k0 = lo; k0 < hi; k0 += C::kTK, ++it) {
       const int st = it % kStages;
@@ -232,22 +263,31 @@ __global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_con
         kl[sp] = kw + j + C::kKPS * sp;
         const uint4 kv = *reinterpret_cast<const uint4*>(kt + kl[sp] * C::kRowBytes + 16 * c);
         const uint32_t kw4[4] = {kv.x, kv.y, kv.z, kv.w};
-        int ah = 0, al = 0;
+        int acc;
+        if (kInt4) {
+          // (nibble ^ 8) = code + 8 in [0, 15]: even dims as bytes (code+8),
+          // odd dims in the high half of each byte as 16 * (code+8).
+          int ahe = 0, aho = 0, ale = 0, alo = 0;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          if (kInt4) {
-            const uint32_t ev = (kw4[w] << 4) & 0xF0F0F0F0u;  // 16 * code of even dims
-            const uint32_t od = kw4[w] & 0xF0F0F0F0u;         // 16 * code of odd dims
-            ah = dp4a_ss(qh[2 * w], ev, ah);
-            ah = dp4a_ss(qh[2 * w + 1], od, ah);
-            al = dp4a_us(ql[2 * w], ev, al);
-            al = dp4a_us(ql[2 * w + 1], od, al);
-          } else {
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t x = kw4[w] ^ 0x88888888u;
+            const uint32_t ev = x & 0x0F0F0F0Fu;
+            const uint32_t od = x & 0xF0F0F0F0u;
+            ahe = dp4a_su(qh[2 * w], ev, ahe);
+            aho = dp4a_su(qh[2 * w + 1], od, aho);
+            ale = dp4a_uu(ql[2 * w], ev, ale);
+            alo = dp4a_uu(ql[2 * w + 1], od, alo);
+          }
+          acc = (ahe * 16 + aho) * 256 + (ale * 16 + alo) - qbias;
+        } else {
+          int ah = 0, al = 0;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
             ah = dp4a_ss(qh[w], kw4[w], ah);
             al = dp4a_us(ql[w], kw4[w], al);
           }
+          acc = ah * 256 + al;
         }
-        int acc = ah * 256 + al;
 #pragma unroll
         for (int off = 1; off < C::kL; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
         const int key = k0 + kl[sp];
@@ -262,7 +302,6 @@ __global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_con
 #pragma unroll
         for (int d = 0; d < C::kDimsPerLane; ++d) o[d] *= alpha;
         l_run *= alpha;
-        lv_run *= alpha;
         m_run = m_new;
       }
       const float mu = (m_run == -INFINITY) ? 0.f : m_run;
@@ -274,31 +313,36 @@ __global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_con
         const float pv = valid ? p * __half2float(vst[kl[sp]]) : 0.f;
         const uint4 vv = *reinterpret_cast<const uint4*>(vt + kl[sp] * C::kRowBytes + 16 * c);
         const uint32_t vw4[4] = {vv.x, vv.y, vv.z, vv.w};
+        const uint16_t ph = __half_as_ushort(__float2half_rn(pv));
         if (kInt4) {
-          // nibble n of word w -> dim 8w + n, value (code + 8) after the xor
-          const float pv1 = pv * 0.0625f, pv2 = pv * 0.00390625f, pv3 = pv * 0.000244140625f,
-                      pv4 = pv * 1.52587890625e-05f;
-          lv_run += pv;
+          // nibble n of word w is dim 8w + n.  One LOP3 builds an fp16 pair
+          // 1024 + s*(code+8) for nibbles (n, n+4), s = 1 or 16; an exact
+          // fp16 subtraction leaves s*code; p/16 pairs with the s = 16 halves.
+          const uint16_t ph16 = __half_as_ushort(__float2half_rn(pv * 0.0625f));
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
-            const uint32_t x = vw4[w] ^ 0x88888888u;
-            const uint32_t y = x >> 20;
+            const uint32_t x = vw4[w];
+            const uint32_t y = x >> 8;
+            const uint32_t a04 = hsub2_u32((x & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
+            const uint32_t a15 = hsub2_u32((x & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
+            const uint32_t a26 = hsub2_u32((y & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
+            const uint32_t a37 = hsub2_u32((y & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
             float* od = &o[8 * w];
-            od[0] = fmaf(pv, __int_as_float(int((x & 0xFu) | 0x4B000000u)) - 8388608.f, od[0]);
-            od[1] = fmaf(pv1, __int_as_float(int((x & 0xF0u) | 0x4B000000u)) - 8388608.f, od[1]);
-            od[2] = fmaf(pv2, __int_as_float(int((x & 0xF00u) | 0x4B000000u)) - 8388608.f, od[2]);
-            od[3] = fmaf(pv3, __int_as_float(int((x & 0xF000u) | 0x4B000000u)) - 8388608.f, od[3]);
-            od[4] = fmaf(pv4, __int_as_float(int((x & 0xF0000u) | 0x4B000000u)) - 8388608.f, od[4]);
-            od[5] = fmaf(pv, __int_as_float(int((y & 0xFu) | 0x4B000000u)) - 8388608.f, od[5]);
-            od[6] = fmaf(pv1, __int_as_float(int((y & 0xF0u) | 0x4B000000u)) - 8388608.f, od[6]);
-            od[7] = fmaf(pv2, __int_as_float(int((y & 0xF00u) | 0x4B000000u)) - 8388608.f, od[7]);
+            fma_pair(od[0], od[4], a04, ph);
+            fma_pair(od[1], od[5], a15, ph16);
+            fma_pair(od[2], od[6], a26, ph);
+            fma_pair(od[3], od[7], a37, ph16);
           }
         } else {
+          // bytes (code + 128) become fp16 pairs 1024 + code + 128 with one
+          // byte-permute per pair; an exact fp16 subtraction leaves the code.
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
             const uint32_t x = vw4[w] ^ 0x80808080u;
-#pragma unroll
-            for (int bb = 0; bb < 4; ++bb) o[4 * w + bb] = fmaf(pv, byte_to_float(x, uint32_t(bb)), o[4 * w + bb]);
+            const uint32_t a01 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x5140u), 0x64806480u);
+            const uint32_t a23 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x7362u), 0x64806480u);
+            fma_pair(o[4 * w + 0], o[4 * w + 1], a01, ph);
+            fma_pair(o[4 * w + 2], o[4 * w + 3], a23, ph);
           }
         }
       }
@@ -307,10 +351,6 @@ __global__ void __launch_bounds__(kThreads) decode_quant_kernel(const __grid_con
     }
 
     // ---- warp reduction over key slots, then merge the 4 warps
-    if (kInt4) {
-#pragma unroll
-      for (int d = 0; d < C::kDimsPerLane; ++d) o[d] = fmaf(-8.f, lv_run, o[d]);
-    }
 #pragma unroll
     for (int off = C::kL; off < 32; off <<= 1) {
       l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
