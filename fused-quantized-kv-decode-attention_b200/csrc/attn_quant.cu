@@ -7,22 +7,27 @@
 // Layout in HBM (exactly the reference's): codes [R, N, D] int8 or packed
 // [R, N, D/2] uint8 (element 2t in the low nibble), scales [R, N] fp16.
 //
-//  * Persistent, warp-specialised: warp 4 streams 8 KiB tiles of K and V codes
-//    plus the matching scale windows into a 4-stage ring with 1-D bulk copies
-//    (cp.async.bulk) completing on mbarriers.  A scale window starts at the
-//    16-byte boundary at or below the tile's first scale, so it may read up to
-//    15 bytes on either side of the scale array -- always inside the 16-byte
-//    blocks that hold the first / last scale, never used.
+//  * Persistent, warp-specialised: warp 4 streams 16 KiB tiles of K and V
+//    codes plus the matching scale windows into a 3-stage ring with 1-D bulk
+//    copies (cp.async.bulk) completing on mbarriers.  A scale window starts at
+//    the 16-byte boundary at or below the tile's first scale, so it may read up
+//    to 15 bytes on either side of the scale array -- always inside the
+//    16-byte blocks that hold the first / last scale, never used.
 //  * Each consumer warp owns a quarter of every tile.  A key row is split into
-//    16-byte chunks, one per lane (L = row_bytes/16 lanes per key), and every
-//    lane handles 4 keys per tile.
+//    32-byte chunks, one per lane (L = row_bytes/32 lanes per key: 64 int4 or
+//    32 int8 dims per lane, so the per-key work -- score reduction, softmax,
+//    scale loads -- is shared by many elements), and every lane handles 4 keys
+//    per tile.  Full tiles skip the per-key bounds masks.
 //  * q . k on integer dot-product units: q is held as a 2-plane fixed-point
 //    number (q * 2^e = hi * 256 + lo, hi signed byte, lo unsigned byte, 14
-//    significant bits -- every fp16 q within 3 binades of max|q| is exact),
-//    codes enter dp4a directly (int4 nibbles as 16*code in signed bytes).
+//    significant bits -- every fp16 q within 3 binades of max|q| is exact).
+//    int8 codes enter dp4a directly; int4 nibbles enter as unsigned
+//    (code + 8) bytes after one xor-and, and the +8 is removed once per unit.
 //    The score is (integer dot) * k_scale * (log2(e) / sqrt(D)) / 2^e.
-//  * p . v in fp32 on CUDA cores: codes become floats through a byte-permute
-//    into the mantissa of 2^23 (exact), the V scale is folded into p.
+//  * p . v in fp32: codes become exact fp16 pairs (one byte-permute or one
+//    logic op per pair plus an exact fp16 subtraction) and are accumulated
+//    with the mixed-precision f16 x f16 + f32 FMA; the V scale is folded
+//    into p.
 //  * Online softmax in the log2 domain, warp merge through shared memory,
 //    output fp16 or an fp32 split partial like the fp16 kernel.
 #include <cuda_fp16.h>
@@ -30,6 +35,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include "device_common.cuh"
 #include "kernels.h"
@@ -39,16 +45,20 @@ namespace {
 
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
-constexpr int kStages = 4;
-constexpr int kTileBytes = 8192;
+constexpr int kTileBytes = 16384;
 
 template <bool kInt4, int D>
 struct QCfg {
+  // 3-stage ring of 16 KiB K + V tiles, 2 CTAs per SM (shared memory and
+  // the int4 register budget both allow two).
+  static constexpr int kStages = 3;
+  static constexpr int kMinBlocks = 2;
   static constexpr int kRowBytes = kInt4 ? D / 2 : D;
   static constexpr int kTK = kTileBytes / kRowBytes;       // keys per tile
-  static constexpr int kL = kRowBytes / 16;                // lanes per key row
+  static constexpr int kL = kRowBytes / 32;                // lanes per key row
   static constexpr int kKPS = 32 / kL;                     // keys per warp step
-  static constexpr int kDimsPerLane = kInt4 ? 32 : 16;
+  static constexpr int kDimsPerLane = kInt4 ? 64 : 32;
+  static constexpr int kWords = 8;                         // 32-bit words per lane chunk
   static constexpr int kScaleBytes = 2 * kTK + 32;         // scale window capacity
   static constexpr int kStageBytes = 2 * kTileBytes + 2 * kScaleBytes;
   static constexpr size_t kSmemBytes = 128 + size_t(kStages) * kStageBytes + 2 * kStages * sizeof(uint64_t) +
@@ -86,8 +96,10 @@ __device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
 }
 
 template <bool kInt4, int D>
-__global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_constant__ DecodeLaunch a) {
+__global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
+    decode_quant_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = QCfg<kInt4, D>;
+  constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * C::kStageBytes);
@@ -163,8 +175,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_
   }
 
   // ------------------------------------------------------------ consumers
-  const int c = lane % C::kL;   // 16-byte chunk of the key row
-  const int j = lane / C::kL;   // key slot
+  constexpr int kDPL = C::kDimsPerLane;
+  constexpr int kPW = kInt4 ? 16 : 8;  // q plane words per lane
+  const int c = lane % C::kL;          // 32-byte chunk of the key row
+  const int j = lane / C::kL;          // key slot
   const int kw = warp * (C::kTK / kConsumerWarps);
   bool alive = true;
   int it = 0;
@@ -176,16 +190,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_
     const int hi = min(a.N, lo + a.chunk);
 
     // ---- q as 2-plane fixed point for this lane's dims.  e is chosen from
-    // max|q| over the whole row (lanes of one key slot cover all D dims) so
-    // that |q| * 2^e < 2^14; the score factor undoes 2^e (and the 16 of the
-    // int4 nibble-in-high-half trick).
-    float qv[C::kDimsPerLane];
+    // max|q| over the whole row (the L lanes of one key slot cover all D dims)
+    // so that |q| * 2^e < 2^14; the score factor undoes 2^e (and the 16 of the
+    // int4 odd-nibble bytes).
+    uint32_t qh[kPW], ql[kPW];
     float qscale_unit;
+    int qbias = 0;
     {
-      const __half* qrow = static_cast<const __half*>(a.q) + size_t(r) * D + c * C::kDimsPerLane;
+      float qv[kDPL];
+      const __half* qrow = static_cast<const __half*>(a.q) + size_t(r) * D + c * kDPL;
       float mq = 0.f;
 #pragma unroll
-      for (int d = 0; d < C::kDimsPerLane; ++d) {
+      for (int d = 0; d < kDPL; ++d) {
         qv[d] = __half2float(qrow[d]);
         mq = fmaxf(mq, fabsf(qv[d]));
       }
@@ -194,52 +210,149 @@ __global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_
       const int e = (mq > 0.f) ? 13 - ilogbf(mq) : 0;
       const float two_e = ldexpf(1.f, e);
 #pragma unroll
-      for (int d = 0; d < C::kDimsPerLane; ++d) qv[d] = rintf(qv[d] * two_e);  // |.| <= 16384
+      for (int d = 0; d < kDPL; ++d) qv[d] = rintf(qv[d] * two_e);  // |.| <= 16384
       qscale_unit = a.sm_scale_log2 * ldexpf(1.f, -e) * (kInt4 ? 0.0625f : 1.f);
-    }
-    // int4 codes enter dp4a as unsigned (code + 8); remove 8 * sum(q) once.
-    int qbias = 0;
-    if (kInt4) {
-#pragma unroll
-      for (int d = 0; d < C::kDimsPerLane; ++d) qbias += int(qv[d]);
-      qbias *= 128;  // 8 * 16 (all int4 products carry a factor 16)
-    }
-
-    // planes: int8 -> word w covers dims 4w..4w+3; int4 -> word w covers dims
-    // 8w..8w+7 split into even and odd dims (index 2w + parity).
-    uint32_t qh[kInt4 ? 8 : 4], ql[kInt4 ? 8 : 4];
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
       if (kInt4) {
+        // int4 codes enter dp4a as unsigned (code + 8): remove 8 * 16 * sum(q)
 #pragma unroll
-        for (int par = 0; par < 2; ++par) {
+        for (int d = 0; d < kDPL; ++d) qbias += int(qv[d]);
+        qbias *= 128;
+      }
+      // planes: int8 -> word w covers dims 4w..4w+3; int4 -> word w covers
+      // dims 8w..8w+7 split into even and odd dims (index 2w + parity).
+#pragma unroll
+      for (int w = 0; w < C::kWords; ++w) {
+        if (kInt4) {
+#pragma unroll
+          for (int par = 0; par < 2; ++par) {
+            uint32_t hw = 0, lw = 0;
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+              const int qi = int(qv[8 * w + 2 * bb + par]);
+              hw |= (uint32_t(qi >> 8) & 0xFFu) << (8 * bb);
+              lw |= (uint32_t(qi) & 0xFFu) << (8 * bb);
+            }
+            qh[(2 * w + par) % kPW] = hw;
+            ql[(2 * w + par) % kPW] = lw;
+          }
+        } else {
           uint32_t hw = 0, lw = 0;
 #pragma unroll
           for (int bb = 0; bb < 4; ++bb) {
-            const int qi = int(qv[8 * w + 2 * bb + par]);
+            const int qi = int(qv[(4 * w + bb) % kDPL]);
             hw |= (uint32_t(qi >> 8) & 0xFFu) << (8 * bb);
             lw |= (uint32_t(qi) & 0xFFu) << (8 * bb);
           }
-          qh[2 * w + par] = hw;
-          ql[2 * w + par] = lw;
+          qh[w % kPW] = hw;
+          ql[w % kPW] = lw;
         }
-      } else {
-        uint32_t hw = 0, lw = 0;
-#pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-          const int qi = int(qv[4 * w + bb]);
-          hw |= (uint32_t(qi >> 8) & 0xFFu) << (8 * bb);
-          lw |= (uint32_t(qi) & 0xFFu) << (8 * bb);
-        }
-        qh[w] = hw;
-        ql[w] = lw;
       }
     }
 
-    float o[C::kDimsPerLane];
+    float o[kDPL];
 #pragma unroll
-    for (int d = 0; d < C::kDimsPerLane; ++d) o[d] = 0.f;
+    for (int d = 0; d < kDPL; ++d) o[d] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
+
+    // One tile of this warp's keys; kMask adds the per-key bound checks that
+    // only the last (partial) tile of a unit needs.
+    auto tile = [&](const uint8_t* base, int st, int k0, auto mask_tag) {
+      constexpr bool kMask = decltype(mask_tag)::value;
+      const uint8_t* kt = base;
+      const uint8_t* vt = base + kTileBytes;
+      const __half* kst = reinterpret_cast<const __half*>(base + 2 * kTileBytes) + stage_off[st][0];
+      const __half* vst = reinterpret_cast<const __half*>(base + 2 * kTileBytes + C::kScaleBytes) + stage_off[st][1];
+      float sco[4];
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        const int kl = kw + j + C::kKPS * sp;
+        const uint4 k0v = *reinterpret_cast<const uint4*>(kt + kl * C::kRowBytes + 32 * c);
+        const uint4 k1v = *reinterpret_cast<const uint4*>(kt + kl * C::kRowBytes + 32 * c + 16);
+        const uint32_t kwd[8] = {k0v.x, k0v.y, k0v.z, k0v.w, k1v.x, k1v.y, k1v.z, k1v.w};
+        int acc;
+        if (kInt4) {
+          int ahe = 0, aho = 0, ale = 0, alo = 0;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t x = kwd[w] ^ 0x88888888u;
+            const uint32_t ev = x & 0x0F0F0F0Fu;  // (code + 8) of even dims
+            const uint32_t od = x & 0xF0F0F0F0u;  // 16 * (code + 8) of odd dims
+            ahe = dp4a_su(qh[(2 * w) % kPW], ev, ahe);
+            aho = dp4a_su(qh[(2 * w + 1) % kPW], od, aho);
+            ale = dp4a_uu(ql[(2 * w) % kPW], ev, ale);
+            alo = dp4a_uu(ql[(2 * w + 1) % kPW], od, alo);
+          }
+          acc = (ahe * 16 + aho) * 256 + (ale * 16 + alo) - qbias;
+        } else {
+          int ah = 0, al = 0;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            ah = dp4a_ss(qh[w % kPW], kwd[w], ah);
+            al = dp4a_us(ql[w % kPW], kwd[w], al);
+          }
+          acc = ah * 256 + al;
+        }
+#pragma unroll
+        for (int off = 1; off < C::kL; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        const float sv = float(acc) * (__half2float(kst[kl]) * qscale_unit);
+        sco[sp] = (!kMask || (k0 + kl) < hi) ? sv : -INFINITY;
+      }
+      float mx = fmaxf(fmaxf(sco[0], sco[1]), fmaxf(sco[2], sco[3]));
+#pragma unroll
+      for (int off = C::kL; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_run, mx);
+      if (m_new > m_run) {  // warp-uniform
+        const float alpha = ex2(m_run - m_new);
+#pragma unroll
+        for (int d = 0; d < kDPL; ++d) o[d] *= alpha;
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        const int kl = kw + j + C::kKPS * sp;
+        const float p = ex2(sco[sp] - mu);
+        l_run += p;
+        float pv = p * __half2float(vst[kl]);
+        if (kMask) pv = ((k0 + kl) < hi) ? pv : 0.f;
+        const uint16_t ph = __half_as_ushort(__float2half_rn(pv));
+        const uint4 v0v = *reinterpret_cast<const uint4*>(vt + kl * C::kRowBytes + 32 * c);
+        const uint4 v1v = *reinterpret_cast<const uint4*>(vt + kl * C::kRowBytes + 32 * c + 16);
+        const uint32_t vwd[8] = {v0v.x, v0v.y, v0v.z, v0v.w, v1v.x, v1v.y, v1v.z, v1v.w};
+        if (kInt4) {
+          // nibble n of word w is dim 8w + n.  One logic op builds an fp16 pair
+          // 1024 + s*(code+8) for nibbles (n, n+4), s = 1 or 16; an exact fp16
+          // subtraction leaves s*code; p/16 pairs with the s = 16 halves.
+          const uint16_t ph16 = __half_as_ushort(__float2half_rn(pv * 0.0625f));
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t x = vwd[w];
+            const uint32_t y = x >> 8;
+            const uint32_t a04 = hsub2_u32((x & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
+            const uint32_t a15 = hsub2_u32((x & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
+            const uint32_t a26 = hsub2_u32((y & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
+            const uint32_t a37 = hsub2_u32((y & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
+            float* od = &o[(8 * w) % kDPL];
+            fma_pair(od[0], od[4], a04, ph);
+            fma_pair(od[1], od[5], a15, ph16);
+            fma_pair(od[2], od[6], a26, ph);
+            fma_pair(od[3], od[7], a37, ph16);
+          }
+        } else {
+          // bytes (code + 128) become fp16 pairs 1024 + code + 128 with one
+          // byte-permute per pair; an exact fp16 subtraction leaves the code.
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t x = vwd[w] ^ 0x80808080u;
+            const uint32_t a01 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x5140u), 0x64806480u);
+            const uint32_t a23 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x7362u), 0x64806480u);
+            fma_pair(o[(4 * w) % kDPL], o[(4 * w + 1) % kDPL], a01, ph);
+            fma_pair(o[(4 * w + 2) % kDPL], o[(4 * w + 3) % kDPL], a23, ph);
+          }
+        }
+      }
+    };
 
     for (int k0 = lo; k0 < hi; k0 += C::kTK, ++it) {
       const int st = it % kStages;
@@ -251,101 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_
       }
       if (!alive) continue;
       const uint8_t* base = smem + size_t(st) * C::kStageBytes;
-      const uint8_t* kt = base;
-      const uint8_t* vt = base + kTileBytes;
-      const __half* kst = reinterpret_cast<const __half*>(base + 2 * kTileBytes) + stage_off[st][0];
-      const __half* vst = reinterpret_cast<const __half*>(base + 2 * kTileBytes + C::kScaleBytes) + stage_off[st][1];
-
-      float sco[4];
-      int kl[4];
-#pragma unroll
-      for (int sp = 0; sp < 4; ++sp) {
-        kl[sp] = kw + j + C::kKPS * sp;
-        const uint4 kv = *reinterpret_cast<const uint4*>(kt + kl[sp] * C::kRowBytes + 16 * c);
-        const uint32_t kw4[4] = {kv.x, kv.y, kv.z, kv.w};
-        int acc;
-        if (kInt4) {
-          // (nibble ^ 8) = code + 8 in [0, 15]: even dims as bytes (code+8),
-          // odd dims in the high half of each byte as 16 * (code+8).
-          int ahe = 0, aho = 0, ale = 0, alo = 0;
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t x = kw4[w] ^ 0x88888888u;
-            const uint32_t ev = x & 0x0F0F0F0Fu;
-            const uint32_t od = x & 0xF0F0F0F0u;
-            ahe = dp4a_su(qh[2 * w], ev, ahe);
-            aho = dp4a_su(qh[2 * w + 1], od, aho);
-            ale = dp4a_uu(ql[2 * w], ev, ale);
-            alo = dp4a_uu(ql[2 * w + 1], od, alo);
-          }
-          acc = (ahe * 16 + aho) * 256 + (ale * 16 + alo) - qbias;
-        } else {
-          int ah = 0, al = 0;
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            ah = dp4a_ss(qh[w], kw4[w], ah);
-            al = dp4a_us(ql[w], kw4[w], al);
-          }
-          acc = ah * 256 + al;
-        }
-#pragma unroll
-        for (int off = 1; off < C::kL; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        const int key = k0 + kl[sp];
-        sco[sp] = (key < hi) ? float(acc) * __half2float(kst[kl[sp]]) * qscale_unit : -INFINITY;
-      }
-      float mx = fmaxf(fmaxf(sco[0], sco[1]), fmaxf(sco[2], sco[3]));
-#pragma unroll
-      for (int off = C::kL; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float m_new = fmaxf(m_run, mx);
-      if (m_new > m_run) {  // warp-uniform
-        const float alpha = ex2(m_run - m_new);
-#pragma unroll
-        for (int d = 0; d < C::kDimsPerLane; ++d) o[d] *= alpha;
-        l_run *= alpha;
-        m_run = m_new;
-      }
-      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
-#pragma unroll
-      for (int sp = 0; sp < 4; ++sp) {
-        const bool valid = (k0 + kl[sp]) < hi;
-        const float p = ex2(sco[sp] - mu);
-        l_run += p;
-        const float pv = valid ? p * __half2float(vst[kl[sp]]) : 0.f;
-        const uint4 vv = *reinterpret_cast<const uint4*>(vt + kl[sp] * C::kRowBytes + 16 * c);
-        const uint32_t vw4[4] = {vv.x, vv.y, vv.z, vv.w};
-        const uint16_t ph = __half_as_ushort(__float2half_rn(pv));
-        if (kInt4) {
-          // nibble n of word w is dim 8w + n.  One LOP3 builds an fp16 pair
-          // 1024 + s*(code+8) for nibbles (n, n+4), s = 1 or 16; an exact
-          // fp16 subtraction leaves s*code; p/16 pairs with the s = 16 halves.
-          const uint16_t ph16 = __half_as_ushort(__float2half_rn(pv * 0.0625f));
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t x = vw4[w];
-            const uint32_t y = x >> 8;
-            const uint32_t a04 = hsub2_u32((x & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
-            const uint32_t a15 = hsub2_u32((x & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
-            const uint32_t a26 = hsub2_u32((y & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
-            const uint32_t a37 = hsub2_u32((y & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
-            float* od = &o[8 * w];
-            fma_pair(od[0], od[4], a04, ph);
-            fma_pair(od[1], od[5], a15, ph16);
-            fma_pair(od[2], od[6], a26, ph);
-            fma_pair(od[3], od[7], a37, ph16);
-          }
-        } else {
-          // bytes (code + 128) become fp16 pairs 1024 + code + 128 with one
-          // byte-permute per pair; an exact fp16 subtraction leaves the code.
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t x = vw4[w] ^ 0x80808080u;
-            const uint32_t a01 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x5140u), 0x64806480u);
-            const uint32_t a23 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x7362u), 0x64806480u);
-            fma_pair(o[4 * w + 0], o[4 * w + 1], a01, ph);
-            fma_pair(o[4 * w + 2], o[4 * w + 3], a23, ph);
-          }
-        }
-      }
+      if (k0 + C::kTK <= hi) tile(base, st, k0, std::false_type{});
+      else tile(base, st, k0, std::true_type{});
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
@@ -355,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_
     for (int off = C::kL; off < 32; off <<= 1) {
       l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
 #pragma unroll
-      for (int d = 0; d < C::kDimsPerLane; ++d) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
+      for (int d = 0; d < kDPL; ++d) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
     }
     if (lane == 0) {
       sm_ml[2 * warp] = m_run;
@@ -363,9 +383,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_quant_kernel(const __grid_
     }
     if (j == 0) {
 #pragma unroll
-      for (int d = 0; d < C::kDimsPerLane; d += 4)
-        *reinterpret_cast<float4*>(&sm_o[warp * D + c * C::kDimsPerLane + d]) =
-            make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+      for (int d = 0; d < kDPL; d += 4)
+        *reinterpret_cast<float4*>(&sm_o[warp * D + c * kDPL + d]) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
     }
     named_bar_sync(1, 32 * kConsumerWarps);
     const int ct = threadIdx.x;

@@ -17,42 +17,65 @@
 namespace fqkv {
 namespace {
 
-__global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ pm, const float* __restrict__ pl,
-                                                      const float* __restrict__ po, __half* __restrict__ out,
-                                                      int rows, int D, int S, int S_eff) {
+constexpr int kCombineThreads = 512;
+
+// One CTA per row.  The split range is divided among kCombineThreads / D
+// thread groups (thread = one dim of one group), so the loads of different
+// splits are independent and in flight together; groups are reduced in
+// shared memory.
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ pm,
+                                                                  const float* __restrict__ pl,
+                                                                  const float* __restrict__ po,
+                                                                  __half* __restrict__ out, int D, int S, int S_eff) {
   pdl_wait_primary();
-  // one warp per row, each lane covers D/32 dims
-  const int warps = blockDim.x >> 5;
-  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const float* m = pm + size_t(row) * S;
-  const float* l = pl + size_t(row) * S;
+  __shared__ float red[kCombineThreads / 32];
+  __shared__ float sm_o[kCombineThreads];
+  __shared__ float sm_l[kCombineThreads / 64];
+  const size_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* m = pm + row * S;
+  const float* l = pl + row * S;
+
   float M = -INFINITY;
-  for (int s = lane; s < S_eff; s += 32) M = fmaxf(M, m[s]);
+  for (int s = tid; s < S_eff; s += kCombineThreads) M = fmaxf(M, m[s]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float L = 0.f;
-  float O[4] = {0.f, 0.f, 0.f, 0.f};
-  const int per = D / 32;
-  for (int s = 0; s < S_eff; ++s) {
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = red[0];
+#pragma unroll
+  for (int w = 1; w < kCombineThreads / 32; ++w) M = fmaxf(M, red[w]);
+
+  const int groups = kCombineThreads / D;
+  const int gi = tid / D, d = tid - gi * D;
+  float L = 0.f, O = 0.f;
+#pragma unroll 4
+  for (int s = gi; s < S_eff; s += groups) {
     const float ms = m[s];
     const float w = (ms == -INFINITY) ? 0.f : ex2(ms - M);
-    L += w * l[s];
-    const float* os = po + (size_t(row) * S + s) * D;
-    for (int e = 0; e < per; ++e) O[e] += w * os[lane + 32 * e];
+    L = fmaf(w, l[s], L);
+    O = fmaf(w, po[(row * S + s) * D + d], O);
   }
-  for (int e = 0; e < per; ++e) out[size_t(row) * D + lane + 32 * e] = __float2half_rn(O[e] / L);
+  sm_o[tid] = O;
+  if (d == 0) sm_l[gi] = L;
+  __syncthreads();
+  if (gi == 0) {
+    float Ls = 0.f, Os = 0.f;
+    for (int g = 0; g < groups; ++g) {
+      Ls += sm_l[g];
+      Os += sm_o[g * D + d];
+    }
+    out[row * D + d] = __float2half_rn(Os / Ls);
+  }
 }
 
 }  // namespace
 
 cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream) {
   const int rows = a.B * a.Hq;
-  const int warps = 4;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((rows + warps - 1) / warps);
-  cfg.blockDim = dim3(32 * warps);
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(kCombineThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -62,7 +85,7 @@ cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream) {
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, combine_kernel, static_cast<const float*>(a.part_m),
                             static_cast<const float*>(a.part_l), static_cast<const float*>(a.part_o),
-                            static_cast<__half*>(a.out), rows, a.D, a.S, a.S_eff);
+                            static_cast<__half*>(a.out), a.D, a.S, a.S_eff);
 }
 
 }  // namespace fqkv

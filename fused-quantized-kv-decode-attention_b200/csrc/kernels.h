@@ -17,9 +17,9 @@ inline int64_t kv_row_bytes(KvFormat f, int64_t D) {
 }
 
 // Keys per pipeline stage (one tile).  The fp16 kernel uses 64-key tiles of
-// 128-byte swizzled rows; the quantized kernel uses 8 KiB tiles of K (and V).
+// 128-byte swizzled rows; the quantized kernel uses 16 KiB tiles of K (and V).
 inline int tile_keys(KvFormat f, int64_t D) {
-  return f == KvFormat::F16 ? 64 : static_cast<int>(8192 / kv_row_bytes(f, D));
+  return f == KvFormat::F16 ? 64 : static_cast<int>(16384 / kv_row_bytes(f, D));
 }
 
 // One decode-attention launch, in the library's canonical form:
