@@ -352,6 +352,8 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (sequences; 32 heads each for the row workloads)")
+    ap.add_argument("--seq-len", type=int, default=None, help="override the context length N")
+    ap.add_argument("--head-dim", type=int, default=None, choices=[64, 128], help="override head_dim D")
     ap.add_argument("--no-clock-hold", action="store_true",
                     help="do not keep the GPU loaded for clock sampling after the timed region (profiling runs)")
     ap.add_argument("--eager", action="store_true",
@@ -366,6 +368,12 @@ def main() -> int:
         else:
             w["R"] = 32 * args.batch
         w["desc"] += f" [batch overridden to {args.batch}]"
+    if args.seq_len is not None:
+        w["N"] = args.seq_len
+        w["desc"] += f" [N overridden to {args.seq_len}]"
+    if args.head_dim is not None:
+        w["D"] = args.head_dim
+        w["desc"] += f" [D overridden to {args.head_dim}]"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

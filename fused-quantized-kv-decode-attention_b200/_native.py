@@ -33,6 +33,7 @@ SIGNATURES = {
     "fqkv_version": (ctypes.c_char_p, []),
     "fqkv_device_status": (_INT, [ctypes.POINTER(_INT), _INT]),
     "fqkv_set_wait_timeout_ms": (None, [ctypes.c_uint32]),
+    "fqkv_debug_skip_loads": (None, [_INT]),
     "fqkv_decode_workspace_bytes": (_SZ, [_INT, _I64, _I64, _I64, _I64, _I64]),
     "fqkv_decode_attn_fp16_mw": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "fqkv_decode_attn_int8_mw": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),

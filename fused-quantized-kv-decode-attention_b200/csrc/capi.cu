@@ -46,6 +46,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 std::atomic<unsigned long long> g_timeout_ns{2000ull * 1000ull * 1000ull};
+std::atomic<int> g_debug_skip_loads{0};
 
 // ------------------------------------------------------------------ device state
 constexpr int kMaxDevices = 64;
@@ -206,7 +207,7 @@ void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_byt
   a.sm_scale_log2 = float(1.4426950408889634 / std::sqrt(double(a.D)));
   a.status = ds.status;
   a.timeout_ns = g_timeout_ns.load();
-  a.debug_skip_loads = 0;
+  a.debug_skip_loads = g_debug_skip_loads.load();
 }
 
 bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
@@ -280,6 +281,8 @@ const char* fqkv_last_error(void) { return t_err; }
 const char* fqkv_version(void) { return "fqkv_b200 0.1.0 (sm_100a)"; }
 
 void fqkv_set_wait_timeout_ms(uint32_t ms) { g_timeout_ns.store(uint64_t(ms) * 1000000ull); }
+
+void fqkv_debug_skip_loads(int enable) { g_debug_skip_loads.store(enable ? 1 : 0); }
 
 int fqkv_device_status(int* status_out, int clear) {
   if (!status_out) return fail(FQKV_ERR_INVALID_ARGUMENT, "status_out is null");

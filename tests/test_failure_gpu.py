@@ -1,0 +1,55 @@
+"""Failure detection without a GPU fault.
+
+Every mbarrier wait in the decode kernels is bounded.  The test hook
+``fqkv_debug_skip_loads`` makes the producer warp issue no tile loads, so the
+consumers' waits for a tile run out after a short limit (a flag that nothing
+sets).  The kernel must unwind on its own, record status 61 in the device
+status word, and leave the CUDA context usable: the next normal launch
+returns correct results.  Nothing faults, traps or hangs."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+
+
+def _status(fqkv, clear=0):
+    st = ctypes.c_int(-1)
+    fqkv.native.check(fqkv.native.lib().fqkv_device_status(ctypes.byref(st), clear), "status")
+    return st.value
+
+
+@pytest.mark.parametrize("kind", ["gqa", "int8"])
+def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
+    lib = fqkv.native.lib()
+    g = torch.Generator().manual_seed(5)
+    B, Hq, Hkv, N, D = 2, 8, 2, 300, 128
+    q = torch.randn(B, Hq, D, generator=g).half().cuda()
+    K = torch.randn(B, Hkv, N, D, generator=g).half().cuda()
+    V = torch.randn(B, Hkv, N, D, generator=g).half().cuda()
+    assert _status(fqkv, clear=1) == 0
+    lib.fqkv_set_wait_timeout_ms(50)
+    lib.fqkv_debug_skip_loads(1)
+    try:
+        if kind == "gqa":
+            fqkv.decode_attn_gqa(q, K, V, 8)
+        else:
+            Kq, Ks = fqkv.qpt(K.view(B * Hkv, N, D))
+            Vq, Vs = fqkv.qpt(V.view(B * Hkv, N, D))
+            fqkv.decode_attn_int8_mw(q[:, :Hkv].reshape(B * Hkv, D).contiguous(), Kq, Vq, Ks, Vs, 8)
+        torch.cuda.synchronize()
+    finally:
+        lib.fqkv_debug_skip_loads(0)
+        lib.fqkv_set_wait_timeout_ms(2000)
+    assert _status(fqkv, clear=1) == 61          # a consumer's wait for a tile ran out
+    assert _status(fqkv) == 0
+    out = fqkv.decode_attn_gqa(q, K, V, 8)        # the context is still healthy
+    ref = oatt.decode_attention_gqa(q.cpu().numpy(), K.cpu().numpy(), V.cpu().numpy())
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-3, rtol=1e-2)
+    assert _status(fqkv) == 0
