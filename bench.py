@@ -51,6 +51,9 @@ WORKLOADS = {
                  desc="cfg3: int4-KV decode B=256 x 32 heads (R=8192), N=4096, D=128 (decode_attn_int4)"),
     "int4_b2048": dict(kind="int4", R=65536, N=4096, D=128,
                        desc="cfg3 sweep: int4-KV decode B=2048 x 32 heads, N=4096, D=128"),
+    "llama": dict(kind="llama", B=1, N=640, D=64, prompt=512, gen=128,
+                  desc="cfg5: Llama-3.2-1B-architecture greedy decode, random N(0,0.02) bf16 weights, fp16 KV, "
+                       "prompt 512 + 128 generated tokens"),
     "sk": dict(kind="sk", Hq=32, Hkv=8, N=16384, D=128, S=64,
                desc="cfg4: GQA split-K batch 1, Hq=32, Hkv=8, N=16384, D=128, S=64 (gqa_sk_fast), 8 rotated KV sets"),
 }
@@ -339,6 +342,96 @@ def cpu_reference_sample(w: dict, seconds: float) -> dict:
             "ms_per_call": per_call * 1e3}
 
 
+# ---------------------------------------------------------------------------- config 5 (end to end)
+def llama_1b_config():
+    from transformers import LlamaConfig
+    return LlamaConfig(vocab_size=128256, hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=64, max_position_embeddings=131072,
+                       rms_norm_eps=1e-5, rope_theta=500000.0, tie_word_embeddings=True, initializer_range=0.02,
+                       hidden_act="silu")
+
+
+def run_llama(args, w) -> int:
+    """Greedy decode tok/s: fqkv GraphDecoder vs transformers SDPA generate (the reference's stock path)
+    and transformers + the fqkv hook (the reference's live-model path), same random weights."""
+    from transformers import LlamaForCausalLM
+
+    pkg = importlib.import_module(PKG)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, P, T = w["B"], w["prompt"], w["gen"]
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(llama_1b_config()).to(torch.bfloat16).eval()
+    ids = torch.randint(0, model.config.vocab_size, (B, P), device=dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    # ---- ours: eager prefill + CUDA-graph decode steps
+    dec = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T)
+    dec.prefill(ids)
+    dec.capture()
+    best_pre, best_dec = 1e30, 1e30
+    for _ in range(max(1, args.warmup // 3) + 2):
+        e0, e1, e2 = ev(), ev(), ev()
+        e0.record()
+        dec.prefill(ids)
+        e1.record()
+        dec.generate(T - 1)
+        e2.record()
+        torch.cuda.synchronize(dev)
+        best_pre, best_dec = min(best_pre, e0.elapsed_time(e1)), min(best_dec, e1.elapsed_time(e2))
+    ours_tokens = torch.cat([dec.out_tokens[:, P:P + T]], dim=1).clone()
+    decode_tps = B * (T - 1) / (best_dec / 1e3)
+    e2e_tps = B * T / ((best_pre + best_dec) / 1e3)
+
+    # ---- stock transformers generate (SDPA) and the reference-style hook
+    def hf_generate_tps(impl):
+        model.config._attn_implementation = impl
+        with torch.no_grad():
+            model.generate(ids, max_new_tokens=8, do_sample=False, pad_token_id=0)
+            torch.cuda.synchronize(dev)
+            best = 1e30
+            for _ in range(2):
+                t0 = time.perf_counter()
+                out = model.generate(ids, max_new_tokens=T, do_sample=False, pad_token_id=0)
+                torch.cuda.synchronize(dev)
+                best = min(best, time.perf_counter() - t0)
+        model.config._attn_implementation = "sdpa"
+        return B * T / best, out[:, P:]
+    stock_tps, stock_tokens = hf_generate_tps("sdpa")
+    hook_tps, hook_tokens = hf_generate_tps(pkg.hf_integration.register())
+
+    # ---- agreement: teacher-forced SDPA logits on our sequence (first <= 4 sequences)
+    nb = min(B, 4)
+    seq = torch.cat([ids[:nb], ours_tokens[:nb]], dim=1)
+    with torch.no_grad():
+        ref_logits = model(seq).logits[:, P - 1:P - 1 + T].float()
+    agree = (ref_logits.argmax(-1) == ours_tokens[:nb]).float().mean().item()
+    # our own logits for the same steps (teacher forced by construction: same tokens)
+    dec_chk = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True)
+    dec_chk.prefill(ids)
+    ours_logits = [dec_chk.logits[:nb].clone()]
+    for _ in range(T - 1):
+        dec_chk.step()
+        ours_logits.append(dec_chk.logits[:nb].clone())
+    ours_logits = torch.stack(ours_logits, dim=1)
+    max_diff = (ours_logits - ref_logits).abs().max().item()
+    line = {"metric": METRIC, "workload": "llama", "value": round(decode_tps, 2), "unit": "tok/s",
+            "n_gpus": 1, "higher_is_better": True, "dtype": "bf16 weights, f16 KV", "data": "synthetic",
+            "config": {"workload": w["desc"], "global_batch": B, "prompt": P, "gen": T, "head_dim": 64,
+                       "kv_cache": "fp16, static, graph-captured decode step"},
+            "decode_tok_s": round(decode_tps, 2), "e2e_generate_tok_s": round(e2e_tps, 2),
+            "prefill_ms": round(best_pre, 3), "decode_ms_per_step": round(best_dec / (T - 1), 4),
+            "stock_sdpa_generate_tok_s": round(stock_tps, 2), "hf_hook_generate_tok_s": round(hook_tps, 2),
+            "speedup_vs_stock_generate": round(e2e_tps / stock_tps, 3),
+            "greedy_agreement_vs_sdpa_teacher_forced": round(agree, 4),
+            "max_logit_diff_vs_sdpa": round(max_diff, 5),
+            "token_match_stock_vs_ours": round((stock_tokens[:nb] == ours_tokens[:nb]).float().mean().item(), 4),
+            "impl": "ours"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------------------- main
 def main() -> int:
     ap = argparse.ArgumentParser()
@@ -375,6 +468,10 @@ def main() -> int:
         w["D"] = args.head_dim
         w["desc"] += f" [D overridden to {args.head_dim}]"
 
+    if w["kind"] == "llama":
+        if args.batch is not None:
+            w["B"] = args.batch
+        return run_llama(args, w)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

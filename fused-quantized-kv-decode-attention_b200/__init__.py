@@ -10,10 +10,11 @@ The directory name is not a Python identifier, so import it with
 """
 from __future__ import annotations
 
-from . import _native, sharding
+from . import _native, hf_integration, sharding
 from .ops import (
     decode_attn_fp16_mw,
     decode_attn_gqa,
+    decode_attn_gqa_kvcache,
     decode_attn_int4,
     decode_attn_int8_mw,
     gqa_sk_fast,
@@ -27,6 +28,7 @@ __all__ = [
     "decode_attn_int8_mw",
     "decode_attn_int4",
     "decode_attn_gqa",
+    "decode_attn_gqa_kvcache",
     "gqa_sk_fast",
     "qpt",
     "quant_int4_per_token",
@@ -35,6 +37,7 @@ __all__ = [
     "library_path",
     "native",
     "sharding",
+    "hf_integration",
 ]
 
 native = _native

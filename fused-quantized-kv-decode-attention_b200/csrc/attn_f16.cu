@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   __syncthreads();
   // Let the combine kernel (if any) get scheduled while this grid streams.
   pdl_launch_dependents();
+  // Valid keys: the launch's N, or the device-side length of a growing cache.
+  const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
 
   // ------------------------------------------------------------ producer
   if (warp == kConsumerWarps) {
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
     for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
       const UnitCoord uc = decode_unit(a, u);
       const int lo = uc.s * a.chunk;
-      const int hi = min(a.N, lo + a.chunk);
+      const int hi = min(n_valid, lo + a.chunk);
       const int z = uc.b * a.Hkv + uc.kh;
       for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
         const int st = it % C::kStages;
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
     const UnitCoord uc = decode_unit(a, u);
     const int lo = uc.s * a.chunk;
-    const int hi = min(a.N, lo + a.chunk);
+    const int hi = min(n_valid, lo + a.chunk);
     const int h0 = uc.kh * a.G + uc.grp * a.GP;
     const int gvalid = min(a.GP, a.G - uc.grp * a.GP);
 

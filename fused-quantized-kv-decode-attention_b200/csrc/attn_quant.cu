@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtl wc{a.status, a.timeout_ns};
-  const size_t row_stride = size_t(a.N) * C::kRowBytes;
+  const size_t row_stride = size_t(a.kv_stride) * C::kRowBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -124,6 +124,8 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
   }
   __syncthreads();
   pdl_launch_dependents();
+  // Valid keys: the launch's N, or the device-side length of a growing cache.
+  const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
 
   // ------------------------------------------------------------ producer
   if (warp == kConsumerWarps) {
@@ -134,11 +136,11 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       const int s = u % a.S_eff;
       const int r = u / a.S_eff;  // row = b * Hkv + kh (Hq == Hkv here)
       const int lo = s * a.chunk;
-      const int hi = min(a.N, lo + a.chunk);
+      const int hi = min(n_valid, lo + a.chunk);
       const uint8_t* Kr = static_cast<const uint8_t*>(a.K) + size_t(r) * row_stride;
       const uint8_t* Vr = static_cast<const uint8_t*>(a.V) + size_t(r) * row_stride;
-      const __half* Ksr = static_cast<const __half*>(a.Ks) + size_t(r) * a.N;
-      const __half* Vsr = static_cast<const __half*>(a.Vs) + size_t(r) * a.N;
+      const __half* Ksr = static_cast<const __half*>(a.Ks) + size_t(r) * a.kv_stride;
+      const __half* Vsr = static_cast<const __half*>(a.Vs) + size_t(r) * a.kv_stride;
       for (int k0 = lo; k0 < hi; k0 += C::kTK, ++it) {
         const int st = it % kStages;
         if (it >= kStages) {
@@ -187,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
     const int s = u % a.S_eff;
     const int r = u / a.S_eff;
     const int lo = s * a.chunk;
-    const int hi = min(a.N, lo + a.chunk);
+    const int hi = min(n_valid, lo + a.chunk);
 
     // ---- q as 2-plane fixed point for this lane's dims.  e is chosen from
     // max|q| over the whole row (the L lanes of one key slot cover all D dims)

@@ -115,12 +115,13 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// K or V viewed as [B*Hkv][N][D] fp16, box = 64 dims x 64 keys x 1, 128B swizzle.
-int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t D) {
+// K or V viewed as [B*Hkv][N][D] fp16 with `stride` keys between consecutive
+// (b, kv head) rows, box = 64 dims x 64 keys x 1, 128B swizzle.
+int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t D, int64_t stride) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   const cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(BH)};
-  const cuuint64_t strides[2] = {cuuint64_t(D) * 2, cuuint64_t(N) * cuuint64_t(D) * 2};
+  const cuuint64_t strides[2] = {cuuint64_t(D) * 2, cuuint64_t(stride) * cuuint64_t(D) * 2};
   const cuuint32_t box[3] = {64, 64, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
@@ -232,9 +233,12 @@ int launch(DecodeLaunch& a, cudaStream_t stream) {
 }
 
 // Shared body of the four decode entry points (canonical GQA form).
+// kv_stride: keys between consecutive (b, kv head) rows (N for dense tensors,
+// the cache capacity for a KV cache); n_dev: optional device-side valid length.
 int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const void* Ks, const void* Vs, void* o,
                int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, void* ws, size_t ws_bytes,
-               fqkv_stream_t stream) {
+               fqkv_stream_t stream, int64_t kv_stride = -1, const int* n_dev = nullptr) {
+  if (kv_stride < 0) kv_stride = N;
   if (int rc = check_D(D)) return rc;
   if (B < 0 || Hq < 1 || Hkv < 1 || N < 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "negative or zero size");
   if (Hq % Hkv != 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "Hq (%lld) must be a multiple of Hkv (%lld)", (long long)Hq, (long long)Hkv);
@@ -254,6 +258,8 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
   a.fmt = fmt;
   a.q = q; a.K = K; a.V = V; a.Ks = Ks; a.Vs = Vs; a.out = o;
   a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
+  a.kv_stride = int(kv_stride);
+  a.n_dev = n_dev;
   plan(a, *ds, 0, ws ? ws_bytes : 0, true);
   if (int64_t(a.B) * a.Hkv * a.groups * a.S_eff > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "too many work units");
   if (a.S_eff > 1) {
@@ -261,8 +267,8 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
     carve_partials(a, ws, int64_t(a.B) * a.Hq);
   }
   if (fmt == KvFormat::F16) {
-    if (int rc = make_kv_map(&a.tmK, K, B * Hkv, N, D)) return rc;
-    if (int rc = make_kv_map(&a.tmV, V, B * Hkv, N, D)) return rc;
+    if (int rc = make_kv_map(&a.tmK, K, B * Hkv, N, D, kv_stride)) return rc;
+    if (int rc = make_kv_map(&a.tmV, V, B * Hkv, N, D, kv_stride)) return rc;
   }
   return launch(a, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -341,6 +347,22 @@ int fqkv_decode_attn_gqa(const void* q, const void* K, const void* V, void* o, i
                     stream);
 }
 
+int fqkv_decode_attn_gqa_kvcache(const void* q, const void* K, const void* V, void* o, int64_t B, int64_t Hq,
+                                 int64_t Hkv, int64_t max_len, int64_t D, int64_t n_host, const int32_t* seq_len_dev,
+                                 void* workspace, size_t workspace_bytes, fqkv_stream_t stream) {
+  if (max_len < 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "max_len must be >= 1");
+  if (!seq_len_dev && (n_host < 1 || n_host > max_len))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "n: valid length %lld outside [1, max_len=%lld]", (long long)n_host,
+                (long long)max_len);
+  if (max_len > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the 32-bit index range");
+  if (seq_len_dev && !aligned(seq_len_dev, 4)) return fail(FQKV_ERR_MISALIGNED, "seq_len must be 4-byte aligned");
+  // Host length: plan for exactly n keys.  Device length: plan for max_len and
+  // let the kernel stop at the length it reads.
+  const int64_t N = seq_len_dev ? max_len : n_host;
+  return run_decode(KvFormat::F16, q, K, V, nullptr, nullptr, o, B, Hq, Hkv, N, D, workspace, workspace_bytes,
+                    stream, max_len, reinterpret_cast<const int*>(seq_len_dev));
+}
+
 int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part, float* l_part, float* o_part,
                      void* out, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, int64_t S, int64_t W, int64_t CW,
                      fqkv_stream_t stream) {
@@ -363,10 +385,12 @@ int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part,
   a.fmt = KvFormat::F16;
   a.q = q; a.K = K; a.V = V; a.out = out;
   a.B = 1; a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
+  a.kv_stride = int(N);
+  a.n_dev = nullptr;
   plan(a, *ds, S, 0, false);
   a.part_m = m_part; a.part_l = l_part; a.part_o = o_part;
-  if (int rc = make_kv_map(&a.tmK, K, Hkv, N, D)) return rc;
-  if (int rc = make_kv_map(&a.tmV, V, Hkv, N, D)) return rc;
+  if (int rc = make_kv_map(&a.tmK, K, Hkv, N, D, N)) return rc;
+  if (int rc = make_kv_map(&a.tmV, V, Hkv, N, D, N)) return rc;
   return launch(a, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -39,6 +39,8 @@ struct DecodeLaunch {
   float* part_l;
   float* part_o;      // [B*Hq, S, D]
   int B, Hq, Hkv, N, D;
+  int kv_stride;      // keys between consecutive (b, kv head) rows in memory (>= N)
+  const int* n_dev;   // optional device-side valid length (<= N), read at kernel start
   int G;              // Hq / Hkv
   int GP;             // query heads handled by one unit (<= 8)
   int groups;         // ceil(G / GP)

@@ -1,0 +1,202 @@
+"""Model integration: the reference's Hugging Face hook and a graph-captured decode engine.
+
+* :func:`kernel_attention_forward` / :func:`register` -- drop-in for the
+  reference's ``kernel_attention_forward`` (notebook lines 1043-1066): an
+  attention function for ``transformers``' ``ALL_ATTENTION_FUNCTIONS`` that
+  sends decode steps (one query token) to :func:`ops.decode_attn_gqa` and
+  prefill to the library's own SDPA path of ``transformers``.  Like the
+  reference it casts q/K/V to fp16 and reads the whole (contiguous) cache
+  every step.
+
+* :class:`GraphDecoder` -- greedy decoding for a Llama-architecture
+  ``LlamaForCausalLM`` with a preallocated fp16 KV cache.  Prefill runs
+  eagerly (torch SDPA, causal); every decode step -- embeddings, RMSNorm,
+  projections, RoPE, the cache append, fused decode attention over the cache
+  (:func:`ops.decode_attn_gqa_kvcache` with the sequence length read on the
+  device), MLP, LM head and argmax -- is captured once in a CUDA graph and
+  replayed per token, so a step costs no Python or launch overhead.  The
+  model's weights may be bf16 or fp16; attention runs on the fp16 cache.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+HOOK_NAME = "fqkv_decode"
+
+__all__ = ["HOOK_NAME", "kernel_attention_forward", "register", "GraphDecoder"]
+
+
+def kernel_attention_forward(module, query, key, value, attention_mask=None, scaling=None, dropout=0.0, **kwargs):
+    """Attention function for ``ALL_ATTENTION_FUNCTIONS``.
+
+    query [B, Hq, q_len, D], key/value [B, Hkv, kv_len, D] -> ([B, q_len, Hq, D], None).
+    Decode (q_len == 1) runs :func:`ops.decode_attn_gqa`; prefill is handed to
+    ``transformers``' SDPA attention function, as in the reference.
+    """
+    q_len = query.shape[2]
+    if q_len != 1:
+        from transformers.integrations.sdpa_attention import sdpa_attention_forward
+        return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
+                                      **kwargs)
+    D = query.shape[-1]
+    if scaling is not None and not math.isclose(scaling, D ** -0.5, rel_tol=1e-6):
+        raise ValueError(f"fqkv decode attention uses scale 1/sqrt(D); got scaling={scaling}")
+    q = query[:, :, 0, :].to(torch.float16).contiguous()          # [B, Hq, D]
+    K = key.to(torch.float16).contiguous()                          # [B, Hkv, kv, D]
+    V = value.to(torch.float16).contiguous()
+    out = ops.decode_attn_gqa(q, K, V, 8)                           # [B, Hq, D]
+    return out.to(query.dtype).unsqueeze(1), None                   # [B, 1, Hq, D]
+
+
+def register(name: str = HOOK_NAME) -> str:
+    """Register :func:`kernel_attention_forward` under ``name`` in ``ALL_ATTENTION_FUNCTIONS``."""
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+    ALL_ATTENTION_FUNCTIONS.register(name, kernel_attention_forward)
+    return name
+
+
+class GraphDecoder:
+    """Greedy decode of a ``LlamaForCausalLM`` with a static fp16 KV cache and a CUDA-graph step.
+
+    Usage::
+
+        dec = GraphDecoder(model, batch=B, max_len=P + T)
+        first = dec.prefill(prompt_ids)          # [B] first generated token
+        tokens = dec.generate(T - 1)             # [B, T - 1] following tokens
+    """
+
+    def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False):
+        from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+
+        self._rope = apply_rotary_pos_emb
+        self.model = model
+        cfg = model.config
+        self.L = cfg.num_hidden_layers
+        self.Hq = cfg.num_attention_heads
+        self.Hkv = cfg.num_key_value_heads
+        self.D = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.Hq
+        self.B = batch
+        self.max_len = max_len
+        dev = next(model.parameters()).device
+        self.dev = dev
+        self.dtype = next(model.parameters()).dtype
+        self.kc = torch.zeros(self.L, batch, self.Hkv, max_len, self.D, dtype=torch.float16, device=dev)
+        self.vc = torch.zeros_like(self.kc)
+        self.pos = torch.zeros(1, dtype=torch.long, device=dev)      # position of the token fed to the step
+        self.nlen = torch.zeros(1, dtype=torch.int32, device=dev)    # valid cache length during the step
+        self.tok = torch.zeros(batch, dtype=torch.long, device=dev)  # token fed to the step
+        self.out_tokens = torch.zeros(batch, max_len, dtype=torch.long, device=dev)
+        self.attn_out = torch.empty(batch, self.Hq, self.D, dtype=torch.float16, device=dev)
+        nb = ops.workspace_bytes("fp16", batch, self.Hq, self.Hkv, max_len, self.D)
+        self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev) if nb else None
+        self.keep_logits = keep_logits
+        self.logits = torch.zeros(batch, cfg.vocab_size, dtype=torch.float32, device=dev) if keep_logits else None
+        self.graph = None
+        self.prompt_len = 0
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+        """Run the prompt [B, P], fill the cache, return the first generated token [B]."""
+        m = self.model.model
+        B, P = ids.shape
+        if B != self.B or P >= self.max_len:
+            raise ValueError("prompt does not fit the decoder's batch / max_len")
+        h = m.embed_tokens(ids)
+        position_ids = torch.arange(P, device=self.dev)[None].expand(B, P)
+        cos, sin = m.rotary_emb(h, position_ids=position_ids)
+        for li, layer in enumerate(m.layers):
+            attn = layer.self_attn
+            x = layer.input_layernorm(h)
+            q = attn.q_proj(x).view(B, P, self.Hq, self.D).transpose(1, 2)
+            k = attn.k_proj(x).view(B, P, self.Hkv, self.D).transpose(1, 2)
+            v = attn.v_proj(x).view(B, P, self.Hkv, self.D).transpose(1, 2)
+            q, k = self._rope(q, k, cos, sin)
+            self.kc[li, :, :, :P].copy_(k)
+            self.vc[li, :, :, :P].copy_(v)
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            h = h + attn.o_proj(o.transpose(1, 2).reshape(B, P, self.Hq * self.D))
+            h = h + layer.mlp(layer.post_attention_layernorm(h))
+        logits = self.model.lm_head(m.norm(h[:, -1:]))[:, -1].float()
+        first = logits.argmax(-1)
+        self.tok.copy_(first)
+        self.pos.fill_(P)
+        self.nlen.fill_(P + 1)
+        self.out_tokens[:, P].copy_(first)
+        self.prompt_len = P
+        if self.keep_logits:
+            self.logits.copy_(logits)
+        return first
+
+    # ------------------------------------------------------------------ decode step
+    def _step(self) -> None:
+        """Decode the token in ``self.tok`` at ``self.pos``; graph-capturable (no host sync)."""
+        m = self.model.model
+        B = self.B
+        h = m.embed_tokens(self.tok[:, None])                         # [B, 1, H]
+        position_ids = self.pos.expand(B)[:, None]
+        cos, sin = m.rotary_emb(h, position_ids=position_ids)
+        for li, layer in enumerate(m.layers):
+            attn = layer.self_attn
+            x = layer.input_layernorm(h)
+            q = attn.q_proj(x).view(B, 1, self.Hq, self.D).transpose(1, 2)
+            k = attn.k_proj(x).view(B, 1, self.Hkv, self.D).transpose(1, 2)
+            v = attn.v_proj(x).view(B, 1, self.Hkv, self.D).transpose(1, 2)
+            q, k = self._rope(q, k, cos, sin)
+            self.kc[li].index_copy_(2, self.pos, k.to(torch.float16))
+            self.vc[li].index_copy_(2, self.pos, v.to(torch.float16))
+            ops.decode_attn_gqa_kvcache(q[:, :, 0].to(torch.float16).contiguous(), self.kc[li], self.vc[li],
+                                        self.nlen, out=self.attn_out, workspace=self.ws)
+            o = self.attn_out.to(h.dtype).reshape(B, 1, self.Hq * self.D)
+            h = h + attn.o_proj(o)
+            h = h + layer.mlp(layer.post_attention_layernorm(h))
+        logits = self.model.lm_head(m.norm(h))[:, 0].float()
+        nxt = logits.argmax(-1)
+        if self.keep_logits:
+            self.logits.copy_(logits)
+        self.pos.add_(1)
+        self.nlen.add_(1)
+        self.out_tokens.index_copy_(1, self.pos, nxt[:, None])
+        self.tok.copy_(nxt)
+
+    @torch.no_grad()
+    def capture(self, warmup: int = 2) -> None:
+        """Capture one decode step in a CUDA graph (restores the decoder state afterwards)."""
+        state = [self.kc, self.vc, self.pos, self.nlen, self.tok, self.out_tokens]
+        if self.keep_logits:
+            state.append(self.logits)
+        saved = [t.clone() for t in state]
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        for dst, src in zip(state, saved):
+            dst.copy_(src)
+        torch.cuda.synchronize(self.dev)
+
+    @torch.no_grad()
+    def step(self) -> None:
+        if self.graph is None:
+            self._step()
+        else:
+            self.graph.replay()
+
+    @torch.no_grad()
+    def generate(self, steps: int) -> torch.Tensor:
+        """Decode ``steps`` more tokens after :meth:`prefill`; returns them as [B, steps]."""
+        P = self.prompt_len
+        if P + 1 + steps > self.max_len:
+            raise ValueError("generation exceeds max_len")
+        for _ in range(steps):
+            self.step()
+        return self.out_tokens[:, P + 1:P + 1 + steps]

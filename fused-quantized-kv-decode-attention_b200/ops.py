@@ -23,6 +23,7 @@ __all__ = [
     "decode_attn_int8_mw",
     "decode_attn_int4",
     "decode_attn_gqa",
+    "decode_attn_gqa_kvcache",
     "gqa_sk_fast",
     "qpt",
     "quant_int4_per_token",
@@ -209,6 +210,57 @@ def decode_attn_gqa(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, W: int) -
             ws.data_ptr() if ws is not None else None, nb, _stream(dev))
     _native.check(rc, f"launch: {op}")
     return o
+
+
+def decode_attn_gqa_kvcache(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, seq_len,
+                            out: torch.Tensor | None = None,
+                            workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """GQA decode over a preallocated fp16 KV cache (one model decode step).
+
+    q [B,Hq,D] f16; K/V [B,Hkv,max_len,D] f16 with positions [0, n) valid.
+    ``seq_len`` is an int (n) or a CUDA int32 tensor holding n, read on the
+    device -- with ``out`` and ``workspace`` preallocated the call allocates
+    nothing and can be captured in a CUDA graph that is replayed as the cache
+    grows.  ``workspace`` needs ``workspace_bytes("fp16", B, Hq, Hkv, max_len, D)``
+    bytes (device length) or the same with N = n (host length); too small
+    only reduces the split count.
+    """
+    op = "decode_attn_gqa_kvcache"
+    dev = _require_cuda(op, q, K, V)
+    _require_dtype(op, "fp16", torch.float16, q=q, K=K, V=V)
+    _require_contig(op, q=q, K=K, V=V)
+    if q.dim() != 3 or K.dim() != 4:
+        _fail(op, "shape", "q must be [B, Hq, D] and K [B, Hkv, max_len, D]")
+    B, Hq, D = q.shape
+    _, Hkv, max_len, _ = K.shape
+    _require_D(op, D)
+    _require_shape(op, "K", K, (B, Hkv, max_len, D))
+    _require_shape(op, "V", V, (B, Hkv, max_len, D))
+    if Hkv < 1 or Hq % Hkv:
+        _fail(op, "shape", f"Hq ({Hq}) must be a multiple of Hkv ({Hkv})")
+    if isinstance(seq_len, torch.Tensor):
+        if seq_len.device != dev or seq_len.dtype != torch.int32 or seq_len.numel() < 1:
+            _fail(op, "seq_len", "a tensor seq_len must be a CUDA int32 tensor on the inputs' device")
+        n_host, n_ptr, n_plan = 0, seq_len.data_ptr(), max_len
+    else:
+        n_host, n_ptr, n_plan = int(seq_len), None, int(seq_len)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
+    else:
+        _require_cuda(op, q, out)
+        _require_dtype(op, "fp16", torch.float16, out=out)
+        _require_contig(op, out=out)
+        _require_shape(op, "out", out, (B, Hq, D))
+    with _DeviceGuard(dev):
+        if workspace is None:
+            ws, nb = _workspace(_native.KV_F16, dev, B, Hq, Hkv, max(n_plan, 1), D) if B else (None, 0)
+        else:
+            ws, nb = workspace, workspace.numel() * workspace.element_size()
+        rc = _native.lib().fqkv_decode_attn_gqa_kvcache(
+            q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), B, Hq, Hkv, max_len, D, n_host, n_ptr,
+            ws.data_ptr() if ws is not None and nb else None, nb, _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return out
 
 
 def gqa_sk_fast(q, K, V, m_part, l_part, o_part, o, S, W, CW) -> None:

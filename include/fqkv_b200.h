@@ -106,6 +106,21 @@ int fqkv_decode_attn_gqa(const void* q, const void* K, const void* V, void* o, i
                          int64_t Hkv, int64_t N, int64_t D, int64_t W, void* workspace,
                          size_t workspace_bytes, fqkv_stream_t stream);
 
+/* GQA fp16 decode over a preallocated KV cache (the decode step of a model).
+ * q [B,Hq,D] f16; K/V [B,Hkv,max_len,D] f16 of which positions [0, n) are
+ * valid; out [B,Hq,D] f16.  n = *seq_len_dev when seq_len_dev != NULL (int32,
+ * read on the device, clamped to max_len -- so one launch, e.g. replayed from
+ * a CUDA graph, follows a growing cache), otherwise n = n_host.  Positions
+ * [n, max_len) must hold finite values (they are read and weighted by zero).
+ * Workspace: fqkv_decode_workspace_bytes(FQKV_KV_F16, B, Hq, Hkv, N, D) with
+ * N = max_len when seq_len_dev is used, else n_host.
+ * Extends decode_attn_gqa (reference: kernels/decode_attn_gqa.cu:56) to the
+ * static-cache layout used by the reference's live-model hook (nb:1043-1061). */
+int fqkv_decode_attn_gqa_kvcache(const void* q, const void* K, const void* V, void* o, int64_t B, int64_t Hq,
+                                 int64_t Hkv, int64_t max_len, int64_t D, int64_t n_host,
+                                 const int32_t* seq_len_dev, void* workspace, size_t workspace_bytes,
+                                 fqkv_stream_t stream);
+
 /* GQA split-K (batch 1).  q [Hq,D] f16, K/V [Hkv,N,D] f16; caller-owned
  * scratch m_part/l_part [Hq,S] f32, o_part [Hq,S,D] f32; out [Hq,D] f16.
  * At most S splits are used: the library picks the count (<= S, whole

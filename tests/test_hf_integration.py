@@ -1,0 +1,99 @@
+"""Model integration: the Hugging Face attention hook and the CUDA-graph decode engine.
+
+CPU tests check registration and the prefill hand-off (no GPU needed).  GPU
+tests run a small random-weight Llama-architecture model three ways --
+``transformers`` with SDPA (the reference's stock path), ``transformers``
+with the fqkv hook (the reference's live-model path), and :class:`GraphDecoder`
+(static cache, captured decode step) -- and compare them teacher-forced
+against SDPA logits on the same token sequence.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+
+def _tiny_config():
+    from transformers import LlamaConfig
+    return LlamaConfig(vocab_size=1000, hidden_size=512, intermediate_size=1024, num_hidden_layers=4,
+                       num_attention_heads=8, num_key_value_heads=2, head_dim=64, max_position_embeddings=2048,
+                       rms_norm_eps=1e-5, rope_theta=500000.0, tie_word_embeddings=True, initializer_range=0.02)
+
+
+def test_register_adds_hook(fqkv):
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+    name = fqkv.hf_integration.register()
+    assert name in ALL_ATTENTION_FUNCTIONS
+
+
+def test_prefill_is_handed_to_sdpa_on_any_device(fqkv):
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    class M(torch.nn.Module):
+        num_key_value_groups = 4
+        is_causal = True
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(2, 8, 5, 64, generator=g)
+    k = torch.randn(2, 2, 5, 64, generator=g)
+    v = torch.randn(2, 2, 5, 64, generator=g)
+    got, _ = fqkv.hf_integration.kernel_attention_forward(M(), q, k, v, None, scaling=0.125)
+    ref, _ = sdpa_attention_forward(M(), q, k, v, None, scaling=0.125)
+    torch.testing.assert_close(got, ref)
+
+
+def test_decode_on_cpu_tensors_has_no_fallback(fqkv):
+    q = torch.randn(1, 8, 1, 64)
+    k = torch.randn(1, 2, 7, 64)
+    with pytest.raises(RuntimeError, match="^cuda"):
+        fqkv.hf_integration.kernel_attention_forward(None, q, k, k, None, scaling=0.125)
+
+
+def _teacher_forced_logits(model, seq):
+    with torch.no_grad():
+        return model(seq).logits.float()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_graph_decoder_matches_sdpa_teacher_forced(fqkv, dtype):
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(_tiny_config()).to(dtype).eval()
+    model.config._attn_implementation = "sdpa"
+    B, P, T = 3, 37, 20
+    ids = torch.randint(0, 1000, (B, P), device="cuda")
+    dec = fqkv.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True)
+    first = dec.prefill(ids)
+    dec.capture()
+    steps_logits = [dec.logits.clone()]
+    for _ in range(T - 1):
+        dec.step()
+        steps_logits.append(dec.logits.clone())
+    toks = torch.cat([first[:, None], dec.out_tokens[:, P + 1:P + T]], dim=1)          # [B, T]
+    seq = torch.cat([ids, toks], dim=1)
+    ref = _teacher_forced_logits(model, seq)[:, P - 1:P - 1 + T]                        # logits that chose toks
+    ours = torch.stack(steps_logits, dim=1)
+    agree = (ref.argmax(-1) == toks).float().mean().item()
+    assert agree >= 0.9
+    err = (ours - ref).abs().max().item()
+    assert err <= 0.02 + 0.03 * ref.abs().max().item()
+
+
+@pytest.mark.gpu
+def test_hf_hook_generate_matches_sdpa(fqkv):
+    from transformers import LlamaForCausalLM
+    name = fqkv.hf_integration.register()
+    torch.manual_seed(1)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(_tiny_config()).half().eval()
+    ids = torch.randint(0, 1000, (2, 29), device="cuda")
+    try:
+        model.config._attn_implementation = name
+        with torch.no_grad():
+            out = model.generate(ids, max_new_tokens=12, do_sample=False, pad_token_id=0)
+    finally:
+        model.config._attn_implementation = "sdpa"
+    gen = out[:, 29:]
+    ref = _teacher_forced_logits(model, out)[:, 28:28 + 12].argmax(-1)
+    assert (ref == gen).float().mean().item() >= 0.9

@@ -186,3 +186,39 @@ def test_device_status_clean_after_suite(fqkv):
     st = ctypes.c_int(-1)
     fqkv.native.check(fqkv.native.lib().fqkv_device_status(ctypes.byref(st), 0), "status")
     assert st.value == 0
+
+
+# ------------------------------------------------------------------ KV-cache entry (model decode step)
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("B,Hq,Hkv,max_len,n", [(1, 32, 8, 640, 513), (4, 32, 8, 300, 1), (2, 16, 2, 5000, 4097),
+                                                (64, 32, 8, 640, 600)])
+def test_gqa_kvcache_host_and_device_length(fqkv, B, Hq, Hkv, max_len, n, D):
+    q = _randn(B, Hq, D, seed=70).cuda()
+    K = torch.zeros(B, Hkv, max_len, D, dtype=torch.float16, device="cuda")
+    V = torch.zeros_like(K)
+    K[:, :, :n] = _randn(B, Hkv, n, D, seed=71).cuda()
+    V[:, :, :n] = _randn(B, Hkv, n, D, seed=72).cuda()
+    ref = oatt.decode_attention_gqa(q.cpu().numpy(), K[:, :, :n].cpu().numpy(), V[:, :, :n].cpu().numpy())
+    _close(fqkv.decode_attn_gqa_kvcache(q, K, V, n), ref)
+    n_dev = torch.tensor([n], dtype=torch.int32, device="cuda")
+    _close(fqkv.decode_attn_gqa_kvcache(q, K, V, n_dev), ref)
+
+
+def test_gqa_kvcache_graph_follows_device_length(fqkv):
+    B, Hq, Hkv, max_len, D = 2, 32, 8, 1024, 64
+    q = _randn(B, Hq, D, seed=80).cuda()
+    K = _randn(B, Hkv, max_len, D, seed=81).cuda()
+    V = _randn(B, Hkv, max_len, D, seed=82).cuda()
+    n_dev = torch.tensor([100], dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hq, D, dtype=torch.float16, device="cuda")
+    ws = torch.empty(max(fqkv.workspace_bytes("fp16", B, Hq, Hkv, max_len, D), 1), dtype=torch.uint8, device="cuda")
+    fqkv.decode_attn_gqa_kvcache(q, K, V, n_dev, out=out, workspace=ws)   # first call: device set-up
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fqkv.decode_attn_gqa_kvcache(q, K, V, n_dev, out=out, workspace=ws)
+    for n in (100, 101, 513, 1024, 7):
+        n_dev.fill_(n)
+        g.replay()
+        torch.cuda.synchronize()
+        ref = oatt.decode_attention_gqa(q.cpu().numpy(), K[:, :, :n].cpu().numpy(), V[:, :, :n].cpu().numpy())
+        _close(out, ref)
