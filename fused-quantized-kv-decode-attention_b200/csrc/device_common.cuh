@@ -6,7 +6,7 @@
 //    false, so a broken pipeline ends the kernel instead of hanging the GPU.
 //  * TMA: 1-D bulk copies (cp.async.bulk) and 3-D tiled tensor copies
 //    (cp.async.bulk.tensor) into shared memory, completing on an mbarrier.
-//    No cluster multicast is used anywhere in this library.
+//    Every copy targets only the issuing CTA's own shared memory.
 //  * ldmatrix / mma.sync (f16 in, f32 accumulate) fragments, ex2.approx,
 //    dp4a, and programmatic-dependent-launch controls.
 #pragma once
