@@ -40,6 +40,11 @@ SIGNATURES = {
     "fqkv_decode_attn_int4": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "fqkv_decode_attn_gqa": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "fqkv_decode_attn_gqa_kvcache": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ, _P]),
+    "fqkv_decode_attn_gqa_int8": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
+    "fqkv_decode_attn_gqa_int8_kvcache": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P,
+                                                 _SZ, _P]),
+    "fqkv_quantize_int8_into_cache": (_INT, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
+    "fqkv_quantize_int4_into_cache": (_INT, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "fqkv_gqa_sk_fast": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "fqkv_gqa_sk_fast_static_scratch": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "fqkv_quantize_int8_per_token": (_INT, [_P, _P, _P, _I64, _I64, _P]),

@@ -59,6 +59,7 @@ struct DeviceState {
   int* status = nullptr;
   int occ_f16[2] = {0, 0};      // D = 64, 128
   int occ_q[2][2] = {{0, 0}, {0, 0}};  // [int4][D==128]
+  int occ_q8g[2] = {0, 0};      // int8 GQA, D = 64, 128
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -83,6 +84,7 @@ void init_device(DeviceState& ds, int dev) {
   for (int q = 0; q < 2 && e == cudaSuccess; ++q)
     for (int i = 0; i < 2 && e == cudaSuccess; ++i)
       e = fqkv::decode_kernel_prepare_quant(q == 1, i ? 128 : 64, &ds.occ_q[q][i]);
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_q8gqa(i ? 128 : 64, &ds.occ_q8g[i]);
   if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -150,6 +152,7 @@ void carve_partials(DecodeLaunch& a, void* ws, int64_t rows) {
 int ctas_per_sm(const DeviceState& ds, KvFormat f, int D) {
   const int i = D == 128 ? 1 : 0;
   if (f == KvFormat::F16) return std::max(1, ds.occ_f16[i]);
+  if (f == KvFormat::I8Gqa) return std::max(1, ds.occ_q8g[i]);
   return std::max(1, ds.occ_q[f == KvFormat::I4 ? 1 : 0][i]);
 }
 
@@ -158,6 +161,8 @@ int ctas_per_sm(const DeviceState& ds, KvFormat f, int D) {
 // split count that minimises the modelled time, limited to what `ws_bytes`
 // can hold when `limit_ws`.
 void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_bytes, bool limit_ws) {
+  // int8 codes shared by several query heads go to the tensor-core GQA kernel.
+  if (a.fmt == KvFormat::I8 && a.Hq != a.Hkv) a.fmt = KvFormat::I8Gqa;
   a.G = a.Hq / a.Hkv;
   a.GP = std::min(a.G, 8);
   a.groups = (a.G + a.GP - 1) / a.GP;
@@ -223,7 +228,9 @@ int check_D(int64_t D) {
 }
 
 int launch(DecodeLaunch& a, cudaStream_t stream) {
-  cudaError_t e = a.fmt == KvFormat::F16 ? fqkv::launch_decode_f16(a, stream) : fqkv::launch_decode_quant(a, stream);
+  cudaError_t e = a.fmt == KvFormat::F16     ? fqkv::launch_decode_f16(a, stream)
+                  : a.fmt == KvFormat::I8Gqa ? fqkv::launch_decode_q8gqa(a, stream)
+                                             : fqkv::launch_decode_quant(a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "launch");
   if (a.S_eff > 1) {
     e = fqkv::launch_combine(a, stream);
@@ -242,6 +249,8 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
   if (int rc = check_D(D)) return rc;
   if (B < 0 || Hq < 1 || Hkv < 1 || N < 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "negative or zero size");
   if (Hq % Hkv != 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "Hq (%lld) must be a multiple of Hkv (%lld)", (long long)Hq, (long long)Hkv);
+  if (fmt == KvFormat::I4 && Hq != Hkv)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "int4 KV supports one query head per KV head (Hq == Hkv)");
   if (B == 0) return FQKV_OK;
   if (N == 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "N: the KV cache is empty (softmax over zero keys)");
   if (!q || !K || !V || !o || (fmt != KvFormat::F16 && (!Ks || !Vs)))
@@ -361,6 +370,60 @@ int fqkv_decode_attn_gqa_kvcache(const void* q, const void* K, const void* V, vo
   const int64_t N = seq_len_dev ? max_len : n_host;
   return run_decode(KvFormat::F16, q, K, V, nullptr, nullptr, o, B, Hq, Hkv, N, D, workspace, workspace_bytes,
                     stream, max_len, reinterpret_cast<const int*>(seq_len_dev));
+}
+
+int fqkv_decode_attn_gqa_int8(const void* q, const void* Kq, const void* Vq, const void* Ks, const void* Vs, void* o,
+                              int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, void* workspace,
+                              size_t workspace_bytes, fqkv_stream_t stream) {
+  return run_decode(KvFormat::I8, q, Kq, Vq, Ks, Vs, o, B, Hq, Hkv, N, D, workspace, workspace_bytes, stream);
+}
+
+int fqkv_decode_attn_gqa_int8_kvcache(const void* q, const void* Kq, const void* Vq, const void* Ks, const void* Vs,
+                                      void* o, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
+                                      int64_t n_host, const int32_t* seq_len_dev, void* workspace,
+                                      size_t workspace_bytes, fqkv_stream_t stream) {
+  if (max_len < 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "max_len must be >= 1");
+  if (!seq_len_dev && (n_host < 1 || n_host > max_len))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "n: valid length %lld outside [1, max_len=%lld]", (long long)n_host,
+                (long long)max_len);
+  if (max_len > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the 32-bit index range");
+  if (seq_len_dev && !aligned(seq_len_dev, 4)) return fail(FQKV_ERR_MISALIGNED, "seq_len must be 4-byte aligned");
+  const int64_t N = seq_len_dev ? max_len : n_host;
+  return run_decode(KvFormat::I8, q, Kq, Vq, Ks, Vs, o, B, Hq, Hkv, N, D, workspace, workspace_bytes, stream,
+                    max_len, reinterpret_cast<const int*>(seq_len_dev));
+}
+
+static int run_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
+                             int64_t D, int64_t cap, int64_t pos_host, const int32_t* pos_dev,
+                             fqkv_stream_t stream) {
+  if (D != 64 && D != 128) return fail(FQKV_ERR_INVALID_ARGUMENT, "D: head_dim must be 64 or 128 (got %lld)", (long long)D);
+  if (groups < 0 || T < 0 || cap < 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "negative size or empty cache");
+  if (!pos_dev && (pos_host < 0 || pos_host + T > cap))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "pos: tokens [%lld, %lld) outside the cache capacity %lld",
+                (long long)pos_host, (long long)(pos_host + T), (long long)cap);
+  if (groups == 0 || T == 0) return FQKV_OK;
+  if (!X || !codes || !scales) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(X, 16)) return fail(FQKV_ERR_MISALIGNED, "X must be 16-byte aligned");
+  if (!aligned(codes, int4 ? 4 : 8) || !aligned(scales, 2)) return fail(FQKV_ERR_MISALIGNED, "cache misaligned");
+  if (pos_dev && !aligned(pos_dev, 4)) return fail(FQKV_ERR_MISALIGNED, "pos must be 4-byte aligned");
+  if (groups * T > (int64_t(1) << 40)) return fail(FQKV_ERR_INVALID_ARGUMENT, "too many tokens");
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  cudaError_t e = fqkv::launch_quantize_into(int4, X, codes, scales, groups, T, int(D), cap, pos_host,
+                                             reinterpret_cast<const int*>(pos_dev),
+                                             reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  return FQKV_OK;
+}
+
+int fqkv_quantize_int8_into_cache(const void* X, void* codes, void* scales, int64_t groups, int64_t T, int64_t D,
+                                  int64_t cap, int64_t pos_host, const int32_t* pos_dev, fqkv_stream_t stream) {
+  return run_quantize_into(false, X, codes, scales, groups, T, D, cap, pos_host, pos_dev, stream);
+}
+
+int fqkv_quantize_int4_into_cache(const void* X, void* packed, void* scales, int64_t groups, int64_t T, int64_t D,
+                                  int64_t cap, int64_t pos_host, const int32_t* pos_dev, fqkv_stream_t stream) {
+  return run_quantize_into(true, X, packed, scales, groups, T, D, cap, pos_host, pos_dev, stream);
 }
 
 int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part, float* l_part, float* o_part,

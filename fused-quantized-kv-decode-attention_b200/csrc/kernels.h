@@ -9,17 +9,19 @@
 
 namespace fqkv {
 
-enum class KvFormat : int { F16 = 0, I8 = 1, I4 = 2 };
+// I8Gqa: int8 codes with more than one query head per KV head (tensor-core
+// kernel); chosen by the planner, never passed in by callers.
+enum class KvFormat : int { F16 = 0, I8 = 1, I4 = 2, I8Gqa = 3 };
 
 // Bytes of one key row of K (or V) in HBM.
 inline int64_t kv_row_bytes(KvFormat f, int64_t D) {
-  return f == KvFormat::F16 ? 2 * D : (f == KvFormat::I8 ? D : D / 2);
+  return f == KvFormat::F16 ? 2 * D : ((f == KvFormat::I8 || f == KvFormat::I8Gqa) ? D : D / 2);
 }
 
 // Keys per pipeline stage (one tile).  The fp16 kernel uses 64-key tiles of
 // 128-byte swizzled rows; the quantized kernel uses 16 KiB tiles of K (and V).
 inline int tile_keys(KvFormat f, int64_t D) {
-  return f == KvFormat::F16 ? 64 : static_cast<int>(16384 / kv_row_bytes(f, D));
+  return (f == KvFormat::F16 || f == KvFormat::I8Gqa) ? 64 : static_cast<int>(16384 / kv_row_bytes(f, D));
 }
 
 // One decode-attention launch, in the library's canonical form:
@@ -69,6 +71,8 @@ cudaError_t launch_decode_f16(const DecodeLaunch& a, cudaStream_t stream);
 KernelShape decode_kernel_shape_quant(bool int4, int D);
 cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm);
 cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream);
+cudaError_t decode_kernel_prepare_q8gqa(int D, int* ctas_per_sm);
+cudaError_t launch_decode_q8gqa(const DecodeLaunch& a, cudaStream_t stream);
 
 // Log-sum-exp merge of the S_eff partials of every row into out (fp16),
 // chained to the preceding launch by programmatic dependent launch.
@@ -76,5 +80,10 @@ cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream);
 
 cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,
                             cudaStream_t stream);
+// Quantize groups x T tokens [groups, T, D] into a cache [groups, cap, D]
+// (int4: [groups, cap, D/2]) at positions pos .. pos+T-1 of every group, pos =
+// *pos_dev if given else pos_host; D in {64, 128}; X 16-byte aligned.
+cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
+                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, cudaStream_t stream);
 
 }  // namespace fqkv

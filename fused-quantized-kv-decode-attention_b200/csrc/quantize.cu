@@ -42,9 +42,19 @@ __device__ __forceinline__ __half quant_scale(float amax, bool any_nan) {
 }
 
 // Vectorised path: D in {64, 128, 256}; LPR = D/8 lanes per token.
+// Output placement: token `row` of the input (rows = groups x T tokens) goes
+// to output row (row / T) * cap + pos + row % T, where pos is *pos_dev when
+// given (a growing KV cache) else pos_host; tokens landing at or past `cap`
+// are not written.  The plain quantizer uses T = cap = rows, pos = 0.
+struct QuantPlace {
+  int64_t T, cap, pos_host;
+  const int* pos_dev;
+};
+
 template <bool kInt4, int D>
 __global__ void __launch_bounds__(256) quantize_vec_kernel(const __half* __restrict__ X, void* __restrict__ codes,
-                                                           __half* __restrict__ scales, int64_t rows) {
+                                                           __half* __restrict__ scales, int64_t rows,
+                                                           QuantPlace pl) {
   constexpr int LPR = D / 8;
   constexpr int RPW = 32 / LPR;
   constexpr int Q = kInt4 ? 7 : 127;
@@ -73,12 +83,15 @@ __global__ void __launch_bounds__(256) quantize_vec_kernel(const __half* __restr
   const __half sh = quant_scale<Q>(amax, nan);
   const float s = __half2float(sh);
   if (!active) return;
-  if (c == 0) scales[row] = sh;
+  const int64_t pos = (pl.pos_dev ? int64_t(*pl.pos_dev) : pl.pos_host) + row % pl.T;
+  if (pos < 0 || pos >= pl.cap) return;
+  const int64_t orow = (row / pl.T) * pl.cap + pos;
+  if (c == 0) scales[orow] = sh;
   if (kInt4) {
     uint32_t packed = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) packed |= (uint32_t(quant_code<Q>(xf[i], s)) & 0xFu) << (4 * i);
-    reinterpret_cast<uint32_t*>(codes)[(row * D) / 8 + c] = packed;
+    reinterpret_cast<uint32_t*>(codes)[(orow * D) / 8 + c] = packed;
   } else {
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
@@ -86,7 +99,7 @@ __global__ void __launch_bounds__(256) quantize_vec_kernel(const __half* __restr
       w0 |= (uint32_t(quant_code<Q>(xf[i], s)) & 0xFFu) << (8 * i);
       w1 |= (uint32_t(quant_code<Q>(xf[4 + i], s)) & 0xFFu) << (8 * i);
     }
-    reinterpret_cast<uint2*>(codes)[(row * D) / 8 + c] = make_uint2(w0, w1);
+    reinterpret_cast<uint2*>(codes)[(orow * D) / 8 + c] = make_uint2(w0, w1);
   }
 }
 
@@ -137,9 +150,10 @@ cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int
     const int lpr = D / 8;
     const int64_t threads_needed = rows * lpr;
     const int64_t blocks = (threads_needed + 255) / 256;
-    if (D == 64) quantize_vec_kernel<kInt4, 64><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows);
-    else if (D == 128) quantize_vec_kernel<kInt4, 128><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows);
-    else quantize_vec_kernel<kInt4, 256><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows);
+    const QuantPlace pl{rows, rows, 0, nullptr};
+    if (D == 64) quantize_vec_kernel<kInt4, 64><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else if (D == 128) quantize_vec_kernel<kInt4, 128><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<kInt4, 256><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
   } else {
     const int64_t blocks = (rows * 32 + 255) / 256;
     quantize_generic_kernel<kInt4><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, D);
@@ -148,6 +162,23 @@ cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int
 }
 
 }  // namespace
+
+cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
+                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, cudaStream_t stream) {
+  const __half* x = static_cast<const __half*>(X);
+  __half* sc = static_cast<__half*>(scales);
+  const int64_t rows = groups * T;
+  const QuantPlace pl{T, cap, pos_host, pos_dev};
+  const int64_t blocks = (rows * (D / 8) + 255) / 256;
+  if (D == 64) {
+    if (int4) quantize_vec_kernel<true, 64><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<false, 64><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+  } else {
+    if (int4) quantize_vec_kernel<true, 128><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<false, 128><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,
                             cudaStream_t stream) {

@@ -121,6 +121,25 @@ int fqkv_decode_attn_gqa_kvcache(const void* q, const void* K, const void* V, vo
                                  const int32_t* seq_len_dev, void* workspace, size_t workspace_bytes,
                                  fqkv_stream_t stream);
 
+/* GQA int8 KV.  q [B,Hq,D] f16, Kq/Vq [B,Hkv,N,D] i8, Ks/Vs [B,Hkv,N] f16 ->
+ * o [B,Hq,D] f16; query head h reads KV head h / (Hq/Hkv).  With Hq > Hkv the
+ * codes go through a tensor-core kernel that reads each KV head once for all
+ * its query heads; Hq == Hkv is fqkv_decode_attn_int8_mw.
+ * Combines decode_attn_int8_mw (reference: kernels/decode_attn_int8_mw.cu:52)
+ * with the head mapping of decode_attn_gqa (kernels/decode_attn_gqa.cu:56). */
+int fqkv_decode_attn_gqa_int8(const void* q, const void* Kq, const void* Vq, const void* Ks, const void* Vs,
+                              void* o, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, void* workspace,
+                              size_t workspace_bytes, fqkv_stream_t stream);
+
+/* GQA int8 decode over a preallocated int8 KV cache: codes [B,Hkv,max_len,D]
+ * i8, scales [B,Hkv,max_len] f16, positions [0, n) valid with n as in
+ * fqkv_decode_attn_gqa_kvcache (device-side or host length).  Workspace:
+ * fqkv_decode_workspace_bytes(FQKV_KV_INT8, B, Hq, Hkv, N, D) with the same N. */
+int fqkv_decode_attn_gqa_int8_kvcache(const void* q, const void* Kq, const void* Vq, const void* Ks,
+                                      const void* Vs, void* o, int64_t B, int64_t Hq, int64_t Hkv,
+                                      int64_t max_len, int64_t D, int64_t n_host, const int32_t* seq_len_dev,
+                                      void* workspace, size_t workspace_bytes, fqkv_stream_t stream);
+
 /* GQA split-K (batch 1).  q [Hq,D] f16, K/V [Hkv,N,D] f16; caller-owned
  * scratch m_part/l_part [Hq,S] f32, o_part [Hq,S,D] f32; out [Hq,D] f16.
  * At most S splits are used: the library picks the count (<= S, whole
@@ -160,6 +179,23 @@ int fqkv_quantize_int8_per_token(const void* X, void* codes, void* scales, int64
  * reference: notebooks/integration_and_benchmarks.ipynb:292-299 quant_int4_per_token(X) */
 int fqkv_quantize_int4_per_token(const void* X, void* packed, void* scales, int64_t rows, int64_t D,
                                  fqkv_stream_t stream);
+
+/* Quantize-on-append: X [groups,T,D] f16 (D in {64,128}, 16-byte aligned) is
+ * quantized exactly like fqkv_quantize_int8_per_token and written into a
+ * cache codes [groups,cap,D] i8 / scales [groups,cap] f16 at positions
+ * pos .. pos+T-1 of every group, pos = *pos_dev (device int32, for a decode
+ * step replayed from a CUDA graph) if non-NULL else pos_host.  Tokens that
+ * would land at or past cap are not written.
+ * reference: quantizer of notebooks/integration_and_benchmarks.ipynb:236-238,
+ * applied per appended token instead of to the whole cache. */
+int fqkv_quantize_int8_into_cache(const void* X, void* codes, void* scales, int64_t groups, int64_t T, int64_t D,
+                                  int64_t cap, int64_t pos_host, const int32_t* pos_dev, fqkv_stream_t stream);
+
+/* Same for the int4 cache: packed [groups,cap,D/2] u8, scales [groups,cap] f16.
+ * reference: notebooks/integration_and_benchmarks.ipynb:292-299 */
+int fqkv_quantize_int4_into_cache(const void* X, void* packed, void* scales, int64_t groups, int64_t T,
+                                  int64_t D, int64_t cap, int64_t pos_host, const int32_t* pos_dev,
+                                  fqkv_stream_t stream);
 
 #ifdef __cplusplus
 }
