@@ -367,7 +367,7 @@ def run_llama(args, w) -> int:
     ev = lambda: torch.cuda.Event(enable_timing=True)
 
     # ---- ours: eager prefill + CUDA-graph decode steps
-    dec = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T)
+    dec = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, kv_dtype=args.kv)
     dec.prefill(ids)
     dec.capture()
     best_pre, best_dec = 1e30, 1e30
@@ -408,7 +408,7 @@ def run_llama(args, w) -> int:
         ref_logits = model(seq).logits[:, P - 1:P - 1 + T].float()
     agree = (ref_logits.argmax(-1) == ours_tokens[:nb]).float().mean().item()
     # our own logits for the same steps (teacher forced by construction: same tokens)
-    dec_chk = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True)
+    dec_chk = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True, kv_dtype=args.kv)
     dec_chk.prefill(ids)
     ours_logits = [dec_chk.logits[:nb].clone()]
     for _ in range(T - 1):
@@ -417,9 +417,10 @@ def run_llama(args, w) -> int:
     ours_logits = torch.stack(ours_logits, dim=1)
     max_diff = (ours_logits - ref_logits).abs().max().item()
     line = {"metric": METRIC, "workload": "llama", "value": round(decode_tps, 2), "unit": "tok/s",
-            "n_gpus": 1, "higher_is_better": True, "dtype": "bf16 weights, f16 KV", "data": "synthetic",
+            "n_gpus": 1, "higher_is_better": True, "dtype": f"bf16 weights, {args.kv} KV", "data": "synthetic",
             "config": {"workload": w["desc"], "global_batch": B, "prompt": P, "gen": T, "head_dim": 64,
-                       "kv_cache": "fp16, static, graph-captured decode step"},
+                       "kv_cache": f"{args.kv}, static, graph-captured decode step"
+                       + (" (quantize-on-append)" if args.kv == "int8" else "")},
             "decode_tok_s": round(decode_tps, 2), "e2e_generate_tok_s": round(e2e_tps, 2),
             "prefill_ms": round(best_pre, 3), "decode_ms_per_step": round(best_dec / (T - 1), 4),
             "stock_sdpa_generate_tok_s": round(stock_tps, 2), "hf_hook_generate_tok_s": round(hook_tps, 2),
@@ -446,6 +447,7 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (sequences; 32 heads each for the row workloads)")
     ap.add_argument("--seq-len", type=int, default=None, help="override the context length N")
+    ap.add_argument("--kv", default="fp16", choices=["fp16", "int8"], help="KV cache type of the llama workload")
     ap.add_argument("--head-dim", type=int, default=None, choices=[64, 128], help="override head_dim D")
     ap.add_argument("--no-clock-hold", action="store_true",
                     help="do not keep the GPU loaded for clock sampling after the timed region (profiling runs)")

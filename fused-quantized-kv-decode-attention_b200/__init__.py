@@ -14,12 +14,15 @@ from . import _native, hf_integration, sharding
 from .ops import (
     decode_attn_fp16_mw,
     decode_attn_gqa,
+    decode_attn_gqa_int8,
+    decode_attn_gqa_int8_kvcache,
     decode_attn_gqa_kvcache,
     decode_attn_int4,
     decode_attn_int8_mw,
     gqa_sk_fast,
     qpt,
     quant_int4_per_token,
+    quantize_into_cache,
     workspace_bytes,
 )
 
@@ -29,6 +32,9 @@ __all__ = [
     "decode_attn_int4",
     "decode_attn_gqa",
     "decode_attn_gqa_kvcache",
+    "decode_attn_gqa_int8",
+    "decode_attn_gqa_int8_kvcache",
+    "quantize_into_cache",
     "gqa_sk_fast",
     "qpt",
     "quant_int4_per_token",

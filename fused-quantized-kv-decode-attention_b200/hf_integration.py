@@ -9,13 +9,15 @@
   every step.
 
 * :class:`GraphDecoder` -- greedy decoding for a Llama-architecture
-  ``LlamaForCausalLM`` with a preallocated fp16 KV cache.  Prefill runs
-  eagerly (torch SDPA, causal); every decode step -- embeddings, RMSNorm,
-  projections, RoPE, the cache append, fused decode attention over the cache
-  (:func:`ops.decode_attn_gqa_kvcache` with the sequence length read on the
-  device), MLP, LM head and argmax -- is captured once in a CUDA graph and
-  replayed per token, so a step costs no Python or launch overhead.  The
-  model's weights may be bf16 or fp16; attention runs on the fp16 cache.
+  ``LlamaForCausalLM`` with a preallocated KV cache, fp16 or int8.  Prefill
+  runs eagerly (torch SDPA, causal); every decode step -- embeddings, RMSNorm,
+  projections, RoPE, the cache append (int8: quantize-on-append of the new
+  token only, bit-exact with the reference quantizer), fused decode attention
+  over the cache with the sequence length read on the device
+  (:func:`ops.decode_attn_gqa_kvcache` / :func:`ops.decode_attn_gqa_int8_kvcache`),
+  MLP, LM head and argmax -- is captured once in a CUDA graph and replayed
+  per token, so a step costs no Python or launch overhead.  The model's
+  weights may be bf16 or fp16; attention runs on the fp16 / int8 cache.
 """
 from __future__ import annotations
 
@@ -70,7 +72,7 @@ class GraphDecoder:
         tokens = dec.generate(T - 1)             # [B, T - 1] following tokens
     """
 
-    def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False):
+    def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False, kv_dtype: str = "fp16"):
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
         self._rope = apply_rotary_pos_emb
@@ -85,14 +87,22 @@ class GraphDecoder:
         dev = next(model.parameters()).device
         self.dev = dev
         self.dtype = next(model.parameters()).dtype
-        self.kc = torch.zeros(self.L, batch, self.Hkv, max_len, self.D, dtype=torch.float16, device=dev)
+        if kv_dtype not in ("fp16", "int8"):
+            raise ValueError("kv_dtype must be 'fp16' or 'int8'")
+        self.kv_dtype = kv_dtype
+        cache_dtype = torch.float16 if kv_dtype == "fp16" else torch.int8
+        self.kc = torch.zeros(self.L, batch, self.Hkv, max_len, self.D, dtype=cache_dtype, device=dev)
         self.vc = torch.zeros_like(self.kc)
+        if kv_dtype == "int8":  # per-token fp16 scales of the int8 codes
+            self.ks = torch.zeros(self.L, batch, self.Hkv, max_len, dtype=torch.float16, device=dev)
+            self.vs = torch.zeros_like(self.ks)
+        self.pos32 = torch.zeros(1, dtype=torch.int32, device=dev)   # self.pos as int32 (append position)
         self.pos = torch.zeros(1, dtype=torch.long, device=dev)      # position of the token fed to the step
         self.nlen = torch.zeros(1, dtype=torch.int32, device=dev)    # valid cache length during the step
         self.tok = torch.zeros(batch, dtype=torch.long, device=dev)  # token fed to the step
         self.out_tokens = torch.zeros(batch, max_len, dtype=torch.long, device=dev)
         self.attn_out = torch.empty(batch, self.Hq, self.D, dtype=torch.float16, device=dev)
-        nb = ops.workspace_bytes("fp16", batch, self.Hq, self.Hkv, max_len, self.D)
+        nb = ops.workspace_bytes(kv_dtype, batch, self.Hq, self.Hkv, max_len, self.D)
         self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev) if nb else None
         self.keep_logits = keep_logits
         self.logits = torch.zeros(batch, cfg.vocab_size, dtype=torch.float32, device=dev) if keep_logits else None
@@ -117,8 +127,7 @@ class GraphDecoder:
             k = attn.k_proj(x).view(B, P, self.Hkv, self.D).transpose(1, 2)
             v = attn.v_proj(x).view(B, P, self.Hkv, self.D).transpose(1, 2)
             q, k = self._rope(q, k, cos, sin)
-            self.kc[li, :, :, :P].copy_(k)
-            self.vc[li, :, :, :P].copy_(v)
+            self._append(li, k, v, 0)
             o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
             h = h + attn.o_proj(o.transpose(1, 2).reshape(B, P, self.Hq * self.D))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
@@ -126,12 +135,36 @@ class GraphDecoder:
         first = logits.argmax(-1)
         self.tok.copy_(first)
         self.pos.fill_(P)
+        self.pos32.fill_(P)
         self.nlen.fill_(P + 1)
         self.out_tokens[:, P].copy_(first)
         self.prompt_len = P
         if self.keep_logits:
             self.logits.copy_(logits)
         return first
+
+    # ------------------------------------------------------------------ cache
+    def _append(self, li: int, k: torch.Tensor, v: torch.Tensor, pos) -> None:
+        """Write k/v [B, Hkv, T, D] at position ``pos`` (int, or the device tensor) of layer li."""
+        if self.kv_dtype == "fp16":
+            if isinstance(pos, int):
+                T = k.shape[2]
+                self.kc[li, :, :, pos:pos + T].copy_(k)
+                self.vc[li, :, :, pos:pos + T].copy_(v)
+            else:
+                self.kc[li].index_copy_(2, self.pos, k.to(torch.float16))
+                self.vc[li].index_copy_(2, self.pos, v.to(torch.float16))
+        else:
+            p = pos if isinstance(pos, int) else self.pos32
+            ops.quantize_into_cache(k.to(torch.float16).contiguous(), self.kc[li], self.ks[li], p)
+            ops.quantize_into_cache(v.to(torch.float16).contiguous(), self.vc[li], self.vs[li], p)
+
+    def _attend(self, li: int, q: torch.Tensor) -> None:
+        if self.kv_dtype == "fp16":
+            ops.decode_attn_gqa_kvcache(q, self.kc[li], self.vc[li], self.nlen, out=self.attn_out, workspace=self.ws)
+        else:
+            ops.decode_attn_gqa_int8_kvcache(q, self.kc[li], self.vc[li], self.ks[li], self.vs[li], self.nlen,
+                                             out=self.attn_out, workspace=self.ws)
 
     # ------------------------------------------------------------------ decode step
     def _step(self) -> None:
@@ -148,10 +181,8 @@ class GraphDecoder:
             k = attn.k_proj(x).view(B, 1, self.Hkv, self.D).transpose(1, 2)
             v = attn.v_proj(x).view(B, 1, self.Hkv, self.D).transpose(1, 2)
             q, k = self._rope(q, k, cos, sin)
-            self.kc[li].index_copy_(2, self.pos, k.to(torch.float16))
-            self.vc[li].index_copy_(2, self.pos, v.to(torch.float16))
-            ops.decode_attn_gqa_kvcache(q[:, :, 0].to(torch.float16).contiguous(), self.kc[li], self.vc[li],
-                                        self.nlen, out=self.attn_out, workspace=self.ws)
+            self._append(li, k, v, self.pos)
+            self._attend(li, q[:, :, 0].to(torch.float16).contiguous())
             o = self.attn_out.to(h.dtype).reshape(B, 1, self.Hq * self.D)
             h = h + attn.o_proj(o)
             h = h + layer.mlp(layer.post_attention_layernorm(h))
@@ -160,6 +191,7 @@ class GraphDecoder:
         if self.keep_logits:
             self.logits.copy_(logits)
         self.pos.add_(1)
+        self.pos32.add_(1)
         self.nlen.add_(1)
         self.out_tokens.index_copy_(1, self.pos, nxt[:, None])
         self.tok.copy_(nxt)
@@ -167,7 +199,9 @@ class GraphDecoder:
     @torch.no_grad()
     def capture(self, warmup: int = 2) -> None:
         """Capture one decode step in a CUDA graph (restores the decoder state afterwards)."""
-        state = [self.kc, self.vc, self.pos, self.nlen, self.tok, self.out_tokens]
+        state = [self.kc, self.vc, self.pos, self.pos32, self.nlen, self.tok, self.out_tokens]
+        if self.kv_dtype == "int8":
+            state += [self.ks, self.vs]
         if self.keep_logits:
             state.append(self.logits)
         saved = [t.clone() for t in state]

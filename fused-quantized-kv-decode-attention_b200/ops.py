@@ -24,6 +24,9 @@ __all__ = [
     "decode_attn_int4",
     "decode_attn_gqa",
     "decode_attn_gqa_kvcache",
+    "decode_attn_gqa_int8",
+    "decode_attn_gqa_int8_kvcache",
+    "quantize_into_cache",
     "gqa_sk_fast",
     "qpt",
     "quant_int4_per_token",
@@ -261,6 +264,107 @@ def decode_attn_gqa_kvcache(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, s
             ws.data_ptr() if ws is not None and nb else None, nb, _stream(dev))
     _native.check(rc, f"launch: {op}")
     return out
+
+
+def _seq_len_args(op, seq_len, dev, max_len):
+    if isinstance(seq_len, torch.Tensor):
+        if seq_len.device != dev or seq_len.dtype != torch.int32 or seq_len.numel() < 1:
+            _fail(op, "seq_len", "a tensor seq_len must be a CUDA int32 tensor on the inputs' device")
+        return 0, seq_len.data_ptr(), max_len
+    return int(seq_len), None, int(seq_len)
+
+
+def _check_int8_gqa(op, q, Kq, Vq, Ks, Vs):
+    dev = _require_cuda(op, q, Kq, Vq, Ks, Vs)
+    _require_dtype(op, "int8", torch.int8, Kq=Kq, Vq=Vq)
+    _require_dtype(op, "fp16", torch.float16, q=q, Ks=Ks, Vs=Vs)
+    _require_contig(op, q=q, Kq=Kq, Vq=Vq, Ks=Ks, Vs=Vs)
+    if q.dim() != 3 or Kq.dim() != 4:
+        _fail(op, "shape", "q must be [B, Hq, D] and Kq [B, Hkv, N, D]")
+    B, Hq, D = q.shape
+    _, Hkv, N, _ = Kq.shape
+    _require_D(op, D)
+    _require_shape(op, "Kq", Kq, (B, Hkv, N, D))
+    _require_shape(op, "Vq", Vq, (B, Hkv, N, D))
+    _require_shape(op, "Ks", Ks, (B, Hkv, N))
+    _require_shape(op, "Vs", Vs, (B, Hkv, N))
+    if Hkv < 1 or Hq % Hkv:
+        _fail(op, "shape", f"Hq ({Hq}) must be a multiple of Hkv ({Hkv})")
+    return dev, B, Hq, Hkv, N, D
+
+
+def decode_attn_gqa_int8(q, Kq, Vq, Ks, Vs) -> torch.Tensor:
+    """GQA decode over int8 KV: q [B,Hq,D] f16, Kq/Vq [B,Hkv,N,D] int8, Ks/Vs [B,Hkv,N] f16 -> [B,Hq,D].
+
+    int8 codes and scales as produced by :func:`qpt`; KV head h // (Hq/Hkv).
+    """
+    op = "decode_attn_gqa_int8"
+    dev, B, Hq, Hkv, N, D = _check_int8_gqa(op, q, Kq, Vq, Ks, Vs)
+    o = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
+    with _DeviceGuard(dev):
+        ws, nb = _workspace(_native.KV_INT8, dev, B, Hq, Hkv, N, D) if B and N else (None, 0)
+        rc = _native.lib().fqkv_decode_attn_gqa_int8(
+            q.data_ptr(), Kq.data_ptr(), Vq.data_ptr(), Ks.data_ptr(), Vs.data_ptr(), o.data_ptr(),
+            B, Hq, Hkv, N, D, ws.data_ptr() if ws is not None else None, nb, _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return o
+
+
+def decode_attn_gqa_int8_kvcache(q, Kq, Vq, Ks, Vs, seq_len, out=None, workspace=None) -> torch.Tensor:
+    """GQA decode over a preallocated int8 KV cache (codes [B,Hkv,max_len,D], scales [B,Hkv,max_len]).
+
+    ``seq_len``, ``out`` and ``workspace`` as in :func:`decode_attn_gqa_kvcache`.
+    """
+    op = "decode_attn_gqa_int8_kvcache"
+    dev, B, Hq, Hkv, max_len, D = _check_int8_gqa(op, q, Kq, Vq, Ks, Vs)
+    n_host, n_ptr, n_plan = _seq_len_args(op, seq_len, dev, max_len)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
+    else:
+        _require_shape(op, "out", out, (B, Hq, D))
+        _require_dtype(op, "fp16", torch.float16, out=out)
+    with _DeviceGuard(dev):
+        if workspace is None:
+            ws, nb = _workspace(_native.KV_INT8, dev, B, Hq, Hkv, max(n_plan, 1), D) if B else (None, 0)
+        else:
+            ws, nb = workspace, workspace.numel() * workspace.element_size()
+        rc = _native.lib().fqkv_decode_attn_gqa_int8_kvcache(
+            q.data_ptr(), Kq.data_ptr(), Vq.data_ptr(), Ks.data_ptr(), Vs.data_ptr(), out.data_ptr(),
+            B, Hq, Hkv, max_len, D, n_host, n_ptr, ws.data_ptr() if ws is not None and nb else None, nb,
+            _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return out
+
+
+def quantize_into_cache(X: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, pos, int4: bool = False) -> None:
+    """Quantize-on-append: X [..., T, D] f16 -> codes[..., pos:pos+T, :], scales[..., pos:pos+T] of a cache.
+
+    codes [..., cap, D] int8 (int4: [..., cap, D/2] uint8), scales [..., cap] f16;
+    bit-exact with :func:`qpt` / :func:`quant_int4_per_token`.  ``pos`` is an
+    int or a CUDA int32 tensor read on the device (graph-capturable append).
+    """
+    op = "quantize_into_cache"
+    dev = _require_cuda(op, X, codes, scales)
+    _require_dtype(op, "fp16", torch.float16, X=X, scales=scales)
+    _require_dtype(op, "packed uint8" if int4 else "int8", torch.uint8 if int4 else torch.int8, codes=codes)
+    _require_contig(op, X=X, codes=codes, scales=scales)
+    if X.dim() < 2 or codes.dim() != X.dim() or scales.dim() != X.dim() - 1:
+        _fail(op, "shape", "X [..., T, D], codes [..., cap, D or D/2], scales [..., cap]")
+    D, T, cap = X.shape[-1], X.shape[-2], codes.shape[-2]
+    G = X.numel() // (T * D) if T and D else 0
+    _require_D(op, D)
+    _require_shape(op, "codes", codes, tuple(X.shape[:-2]) + (cap, D // 2 if int4 else D))
+    _require_shape(op, "scales", scales, tuple(X.shape[:-2]) + (cap,))
+    if isinstance(pos, torch.Tensor):
+        if pos.device != dev or pos.dtype != torch.int32:
+            _fail(op, "pos", "a tensor pos must be a CUDA int32 tensor")
+        p_host, p_ptr = 0, pos.data_ptr()
+    else:
+        p_host, p_ptr = int(pos), None
+    fn = _native.lib().fqkv_quantize_int4_into_cache if int4 else _native.lib().fqkv_quantize_int8_into_cache
+    with _DeviceGuard(dev):
+        rc = fn(X.data_ptr(), codes.data_ptr(), scales.data_ptr(), G, T, D, cap, p_host, p_ptr, _stream(dev))
+    _native.check(rc, f"launch: {op}")
 
 
 def gqa_sk_fast(q, K, V, m_part, l_part, o_part, o, S, W, CW) -> None:

@@ -97,3 +97,31 @@ def test_hf_hook_generate_matches_sdpa(fqkv):
     gen = out[:, 29:]
     ref = _teacher_forced_logits(model, out)[:, 28:28 + 12].argmax(-1)
     assert (ref == gen).float().mean().item() >= 0.9
+
+
+@pytest.mark.gpu
+def test_graph_decoder_int8_cache_tracks_fp16_cache(fqkv):
+    """int8 KV (quantize-on-append in the captured step) against the fp16-cache decoder."""
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(2)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(_tiny_config()).half().eval()
+    B, P, T = 2, 41, 16
+    ids = torch.randint(0, 1000, (B, P), device="cuda")
+    outs = {}
+    for kv in ("fp16", "int8"):
+        dec = fqkv.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True, kv_dtype=kv)
+        dec.prefill(ids)
+        dec.capture()
+        logits = [dec.logits.clone()]
+        for _ in range(T - 1):
+            dec.step()
+            logits.append(dec.logits.clone())
+        outs[kv] = (torch.stack(logits, 1), dec.out_tokens[:, P:P + T].clone())
+    (l16, t16), (l8, t8) = outs["fp16"], outs["int8"]
+    # int8 KV perturbs attention by ~1 % (per-token quantization); the step must
+    # stay close to the fp16-cache step on the same model
+    assert (t16 == t8).float().mean().item() >= 0.75
+    first_div = int((t16 != t8).any(0).float().argmax()) if (t16 != t8).any() else T
+    err = (l8[:, :max(first_div, 1)] - l16[:, :max(first_div, 1)]).abs().max().item()
+    assert err <= 0.05 + 0.05 * l16.abs().max().item()

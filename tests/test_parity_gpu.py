@@ -222,3 +222,69 @@ def test_gqa_kvcache_graph_follows_device_length(fqkv):
         torch.cuda.synchronize()
         ref = oatt.decode_attention_gqa(q.cpu().numpy(), K[:, :, :n].cpu().numpy(), V[:, :, :n].cpu().numpy())
         _close(out, ref)
+
+
+# ------------------------------------------------------------------ int8-KV GQA (model int8 cache)
+def _int8_gqa_ref(q, Kf, Vf, n=None):
+    """Oracle on the reference quantizer's dequantised int8 KV (first n keys)."""
+    Kc, Ks = oq.quantize_int8_per_token(Kf)
+    Vc, Vs = oq.quantize_int8_per_token(Vf)
+    Kd, Vd = oq.dequantize_int8(Kc, Ks), oq.dequantize_int8(Vc, Vs)
+    if n is not None:
+        Kd, Vd = Kd[:, :, :n], Vd[:, :, :n]
+    return oatt.decode_attention_gqa(q, Kd, Vd)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("B,Hq,Hkv,N", [(1, 32, 8, 1024), (4, 32, 8, 513), (2, 64, 8, 77), (3, 8, 2, 1),
+                                        (1, 32, 8, 16384), (2, 12, 4, 300)])
+def test_gqa_int8(fqkv, B, Hq, Hkv, N, D):
+    q, K, V = _randn(B, Hq, D, seed=90), _randn(B, Hkv, N, D, seed=91), _randn(B, Hkv, N, D, seed=92)
+    Kq, Ks = fqkv.qpt(K.cuda())
+    Vq, Vs = fqkv.qpt(V.cuda())
+    out = fqkv.decode_attn_gqa_int8(q.cuda(), Kq, Vq, Ks, Vs)
+    _close(out, _int8_gqa_ref(q.numpy(), K.numpy(), V.numpy()))
+
+
+@pytest.mark.parametrize("int4", [False, True])
+def test_quantize_into_cache_bit_exact(fqkv, int4):
+    G, T, D, cap = 6, 37, 128, 100
+    X = _randn(G, T, D, seed=93)
+    codes = torch.zeros(G, cap, D // 2 if int4 else D, dtype=torch.uint8 if int4 else torch.int8, device="cuda")
+    scales = torch.zeros(G, cap, dtype=torch.float16, device="cuda")
+    fqkv.quantize_into_cache(X.cuda(), codes, scales, 10, int4=int4)
+    rc, rs = (oq.quantize_int4_per_token if int4 else oq.quantize_int8_per_token)(X.numpy())
+    assert np.array_equal(codes[:, 10:10 + T].cpu().numpy(), rc)
+    assert np.array_equal(scales[:, 10:10 + T].cpu().numpy().view(np.uint16), rs.view(np.uint16))
+    assert not codes[:, :10].any() and not codes[:, 10 + T:].any()
+    # device position, one token per group, graph-style append; a position past cap writes nothing
+    x1 = _randn(G, 1, D, seed=94).cuda()
+    pos = torch.tensor([99], dtype=torch.int32, device="cuda")
+    fqkv.quantize_into_cache(x1, codes, scales, pos, int4=int4)
+    r1c, r1s = (oq.quantize_int4_per_token if int4 else oq.quantize_int8_per_token)(x1.cpu().numpy())
+    assert np.array_equal(codes[:, 99:100].cpu().numpy(), r1c)
+    before = codes.clone()
+    pos.fill_(100)
+    fqkv.quantize_into_cache(x1, codes, scales, pos, int4=int4)
+    torch.cuda.synchronize()
+    assert torch.equal(before, codes)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,max_len,n,D", [(1, 32, 8, 640, 513, 64), (8, 32, 8, 640, 600, 64),
+                                                  (2, 32, 8, 4096, 4000, 128)])
+def test_gqa_int8_kvcache_append_and_device_length(fqkv, B, Hq, Hkv, max_len, n, D):
+    q = _randn(B, Hq, D, seed=95)
+    Kf, Vf = _randn(B, Hkv, n, D, seed=96), _randn(B, Hkv, n, D, seed=97)
+    Kq = torch.zeros(B, Hkv, max_len, D, dtype=torch.int8, device="cuda")
+    Vq = torch.zeros_like(Kq)
+    Ks = torch.zeros(B, Hkv, max_len, dtype=torch.float16, device="cuda")
+    Vs = torch.zeros_like(Ks)
+    fqkv.quantize_into_cache(Kf[:, :, :n - 1].contiguous().cuda(), Kq, Ks, 0)   # prefill
+    fqkv.quantize_into_cache(Vf[:, :, :n - 1].contiguous().cuda(), Vq, Vs, 0)
+    pos = torch.tensor([n - 1], dtype=torch.int32, device="cuda")                # one appended token
+    fqkv.quantize_into_cache(Kf[:, :, n - 1:].contiguous().cuda(), Kq, Ks, pos)
+    fqkv.quantize_into_cache(Vf[:, :, n - 1:].contiguous().cuda(), Vq, Vs, pos)
+    ref = _int8_gqa_ref(q.numpy(), Kf.numpy(), Vf.numpy())
+    _close(fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, n), ref)
+    n_dev = torch.tensor([n], dtype=torch.int32, device="cuda")
+    _close(fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, n_dev), ref)
