@@ -41,6 +41,9 @@ FALLBACK_HBM_GBS = 6650.0
 WORKLOADS = {
     "gqa": dict(kind="gqa", B=64, Hq=32, Hkv=8, N=16384, D=128,
                 desc="cfg4 batched: GQA fp16 decode B=64/GPU, Hq=32, Hkv=8, N=16384, D=128 (decode_attn_gqa)"),
+    "gqa_int8": dict(kind="gqa_int8", B=64, Hq=32, Hkv=8, N=16384, D=128,
+                     desc="cfg4 batched over an int8 KV cache: GQA int8 decode B=64/GPU, Hq=32, Hkv=8, N=16384, "
+                          "D=128 (decode_attn_gqa_int8)"),
     "fp16": dict(kind="fp16", R=256, N=4096, D=128,
                  desc="cfg1: fp16 decode B=8 x 32 heads (R=256), N=4096, D=128 (decode_attn_fp16_mw)"),
     "int8": dict(kind="int8", R=8192, N=4096, D=128,
@@ -52,8 +55,8 @@ WORKLOADS = {
     "int4_b2048": dict(kind="int4", R=65536, N=4096, D=128,
                        desc="cfg3 sweep: int4-KV decode B=2048 x 32 heads, N=4096, D=128"),
     "llama": dict(kind="llama", B=1, N=640, D=64, prompt=512, gen=128,
-                  desc="cfg5: Llama-3.2-1B-architecture greedy decode, random N(0,0.02) bf16 weights, fp16 KV, "
-                       "prompt 512 + 128 generated tokens"),
+                  desc="cfg5: Llama-3.2-1B-architecture greedy decode, random N(0,0.02) bf16 weights, "
+                       "prompt 512 + 128 generated tokens (KV cache type in config.kv_cache)"),
     "sk": dict(kind="sk", Hq=32, Hkv=8, N=16384, D=128, S=64,
                desc="cfg4: GQA split-K batch 1, Hq=32, Hkv=8, N=16384, D=128, S=64 (gqa_sk_fast), 8 rotated KV sets"),
 }
@@ -64,6 +67,8 @@ def algorithmic_bytes(w: dict) -> int:
     k = w["kind"]
     if k == "gqa":
         return 2 * w["B"] * w["Hkv"] * w["N"] * w["D"] * 2 + 2 * w["B"] * w["Hq"] * w["D"] * 2
+    if k == "gqa_int8":
+        return 2 * w["B"] * w["Hkv"] * w["N"] * (w["D"] + 2) + 2 * w["B"] * w["Hq"] * w["D"] * 2
     if k == "sk":
         return 2 * w["Hkv"] * w["N"] * w["D"] * 2 + 2 * w["Hq"] * w["D"] * 2
     R, N, D = w["R"], w["N"], w["D"]
@@ -72,6 +77,12 @@ def algorithmic_bytes(w: dict) -> int:
         return 2 * R * N * D * 2 + qo
     code = R * N * D if k == "int8" else R * N * D // 2
     return 2 * code + 2 * R * N * 2 + qo
+
+
+def path_dtype(kind: str) -> str:
+    """Arithmetic types of the path: KV storage type and the accumulation type."""
+    return {"int8": "i8 KV, f32 accumulate", "gqa_int8": "i8 KV, f32 accumulate",
+            "int4": "i4 KV, f32 accumulate"}.get(kind, "f16 KV, f32 accumulate")
 
 
 def measured_peak() -> tuple[float, str]:
@@ -163,6 +174,25 @@ class Case:
             self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
             self.nb = nb
             self.kernels_per_call = 1 + (1 if nb > 0 else 0)
+        elif k == "gqa_int8":
+            B, Hq, Hkv, N, D = w["B"], w["Hq"], w["Hkv"], w["N"], w["D"]
+            self.q = torch.randn(B, Hq, D, device=dev, generator=gen, dtype=torch.float16)
+            self.K = torch.empty(B, Hkv, N, D, device=dev, dtype=torch.int8)
+            self.V = torch.empty_like(self.K)
+            self.Ks = torch.empty(B, Hkv, N, device=dev, dtype=torch.float16)
+            self.Vs = torch.empty_like(self.Ks)
+            for b in range(B):  # quantize one sequence of fp16 at a time
+                for dst, sdst in ((self.K, self.Ks), (self.V, self.Vs)):
+                    x = torch.randn(Hkv, N, D, device=dev, generator=gen, dtype=torch.float16)
+                    c, sc = pkg.qpt(x)
+                    dst[b].copy_(c)
+                    sdst[b].copy_(sc)
+                    del x, c, sc
+            self.o = torch.empty(B, Hq, D, device=dev, dtype=torch.float16)
+            nb = pkg.workspace_bytes("int8", B, Hq, Hkv, N, D)
+            self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+            self.nb = nb
+            self.kernels_per_call = 1 + (1 if nb > 0 else 0)
         elif k == "sk":
             Hq, Hkv, N, D, S = w["Hq"], w["Hkv"], w["N"], w["D"], w["S"]
             self.sets = []
@@ -215,6 +245,11 @@ class Case:
             rc = lib.fqkv_decode_attn_gqa(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(), self.o.data_ptr(),
                                           w["B"], w["Hq"], w["Hkv"], w["N"], w["D"], 8,
                                           self.ws.data_ptr() if self.nb else None, self.nb, s)
+        elif k == "gqa_int8":
+            rc = lib.fqkv_decode_attn_gqa_int8(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(),
+                                               self.Ks.data_ptr(), self.Vs.data_ptr(), self.o.data_ptr(),
+                                               w["B"], w["Hq"], w["Hkv"], w["N"], w["D"],
+                                               self.ws.data_ptr() if self.nb else None, self.nb, s)
         elif k == "sk":
             q, K, V = self.sets[self.i % len(self.sets)]
             self.i += 1
@@ -242,6 +277,11 @@ def e2e_run(pkg, case: Case, steps: int, dev: torch.device) -> dict:
         host = [t.cpu().pin_memory() for t in (case.q, case.K, case.V)]
         dev_in = [torch.empty_like(t) for t in (case.q, case.K, case.V)]
         call = lambda: pkg.decode_attn_gqa(dev_in[0], dev_in[1], dev_in[2], 8)
+    elif k == "gqa_int8":
+        ts = (case.q, case.K, case.V, case.Ks, case.Vs)
+        host = [t.cpu().pin_memory() for t in ts]
+        dev_in = [torch.empty_like(t) for t in ts]
+        call = lambda: pkg.decode_attn_gqa_int8(*dev_in)
     elif k == "sk":
         q, K, V = case.sets[0]
         host = [t.cpu().pin_memory() for t in (q, K, V)]
@@ -291,6 +331,19 @@ def cpu_reference_setup(w: dict):
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
     k = w["kind"]
+    if k == "gqa_int8":
+        Hq, Hkv, N, D = w["Hq"], w["Hkv"], w["N"], w["D"]
+        q = torch.randn(Hq, D, generator=g).half()
+        Kc, Ks = oq.quantize_int8_per_token(torch.randn(Hkv, N, D, generator=g).half().numpy())
+        Vc, Vs = oq.quantize_int8_per_token(torch.randn(Hkv, N, D, generator=g).half().numpy())
+        G = Hq // Hkv
+
+        def call():
+            Kd = torch.from_numpy(oq.dequantize_int8(Kc, Ks)).half().repeat_interleave(G, 0)
+            Vd = torch.from_numpy(oq.dequantize_int8(Vc, Vs)).half().repeat_interleave(G, 0)
+            return oatt.sdpa_cpu_reference_path(q, Kd, Vd)
+        nbytes = 2 * Hkv * N * (D + 2) + 2 * Hq * D * 2
+        return call, nbytes, f"1 sequence (Hq={Hq}, Hkv={Hkv}, N={N}, D={D}, int8 KV dequantised) per call"
     if k in ("gqa", "sk"):
         Hq, Hkv, N, D = w["Hq"], w["Hkv"], w["N"], w["D"]
         q = torch.randn(Hq, D, generator=g).half()
@@ -433,6 +486,119 @@ def run_llama(args, w) -> int:
     return 0
 
 
+def run_llama_reference(args, w, rank: int) -> int:
+    """Reference arm of config 5: the stock transformers SDPA decode (the reference notebook's baseline
+    path) on the host cores, rank 0 only, on a bounded sample (1 sequence, prompt 512, 8 new tokens)."""
+    if rank != 0:
+        return 0
+    from transformers import LlamaForCausalLM
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    torch.manual_seed(0)
+    model = LlamaForCausalLM(llama_1b_config()).float().eval()
+    model.config._attn_implementation = "sdpa"
+    P, new = w["prompt"], 8
+    ids = torch.randint(0, model.config.vocab_size, (1, P))
+    with torch.no_grad():
+        model.generate(ids, max_new_tokens=2, do_sample=False, pad_token_id=0)
+        t0 = time.perf_counter()
+        model.generate(ids, max_new_tokens=new, do_sample=False, pad_token_id=0)
+        el = time.perf_counter() - t0
+    value = new / el
+    sample = f"1 sequence, prompt {P}, {new} generated tokens (prefill included), fp32 weights on CPU"
+    line = {"impl": "reference", "metric": METRIC, "workload": "llama", "value": round(value, 3), "unit": "tok/s",
+            "n_gpus": 1, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w["desc"], "global_batch": 1, "prompt": P, "gen": new},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": torch.get_num_threads(),
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
+    """Config 5 tensor-parallel over `world` GPUs by KV head (NCCL all-gather of the attention
+    outputs every layer, inside the captured decode step); same model and workload as run_llama.
+    Total work is fixed as the GPU count grows ("scaling": "strong")."""
+    import torch.distributed as dist
+    from transformers import LlamaForCausalLM
+
+    pkg = importlib.import_module(PKG)
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B, P, T = w["B"], w["prompt"], w["gen"]
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(llama_1b_config()).to(torch.bfloat16).eval()
+    for prm in model.parameters():          # identical replicated weights on every rank
+        dist.broadcast(prm.data, src=0)
+    ids = torch.randint(0, model.config.vocab_size, (B, P), device=dev)
+    dist.broadcast(ids, src=0)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    dec = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, kv_dtype=args.kv,
+                                          tp_group=dist.group.WORLD)
+    dec.prefill(ids)
+    dec.capture()
+    best_pre, best_dec = 1e30, 1e30
+    for _ in range(max(1, args.warmup // 3) + 2):
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+        e0, e1, e2 = ev(), ev(), ev()
+        e0.record()
+        dec.prefill(ids)
+        e1.record()
+        dec.generate(T - 1)
+        e2.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1), e1.elapsed_time(e2)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        best_pre, best_dec = min(best_pre, float(t[0])), min(best_dec, float(t[1]))
+    ours = dec.out_tokens[:, P:P + T].clone()
+    same = torch.tensor([1.0], device=dev)
+    ref_tok = ours.clone()
+    dist.broadcast(ref_tok, src=0)
+    same.fill_(float(torch.equal(ref_tok, ours)))
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    dec.release()
+    line = None
+    if rank == 0:
+        nb = min(B, 4)
+        # the 1-GPU decoder on the same replicated weights, and SDPA teacher-forced logits
+        one = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, kv_dtype=args.kv)
+        one.prefill(ids)
+        one.capture()
+        one.generate(T - 1)
+        one_tok = one.out_tokens[:, P:P + T].clone()
+        one.release()
+        seq = torch.cat([ids[:nb], ours[:nb]], dim=1)
+        with torch.no_grad():
+            ref_logits = model(seq).logits[:, P - 1:P - 1 + T].float()
+        agree = (ref_logits.argmax(-1) == ours[:nb]).float().mean().item()
+        decode_tps = B * (T - 1) / (best_dec / 1e3)
+        e2e_tps = B * T / ((best_pre + best_dec) / 1e3)
+        line = {"metric": METRIC, "workload": "llama", "value": round(decode_tps, 2), "unit": "tok/s",
+                "n_gpus": world, "higher_is_better": True, "scaling": "strong",
+                "dtype": f"bf16 weights, {args.kv} KV", "data": "synthetic",
+                "config": {"workload": w["desc"], "global_batch": B, "prompt": P, "gen": T, "head_dim": 64,
+                           "parallelism": f"tp{world} by KV head (q/k/v rows, KV cache, attention sharded; "
+                                          "NCCL all_gather_into_tensor of attention outputs per layer; "
+                                          "o_proj, MLP, LM head replicated)",
+                           "kv_cache": f"{args.kv}, static, graph-captured decode step (collectives in the graph)"},
+                "decode_tok_s": round(decode_tps, 2), "e2e_generate_tok_s": round(e2e_tps, 2),
+                "prefill_ms": round(best_pre, 3), "decode_ms_per_step": round(best_dec / (T - 1), 4),
+                "timing": "CUDA events, max over ranks",
+                "tokens_identical_on_all_ranks": bool(same.item() == 1.0),
+                "token_match_vs_1gpu_decoder": round((one_tok == ours).float().mean().item(), 4),
+                "greedy_agreement_vs_sdpa_teacher_forced": round(agree, 4),
+                "gpu_launches_note": "per step: one CUDA graph replay", "impl": "ours"}
+    dist.barrier(device_ids=[local_rank])
+    dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------------------- main
 def main() -> int:
     ap = argparse.ArgumentParser()
@@ -458,7 +624,7 @@ def main() -> int:
         args.warmup = 3
     w = dict(WORKLOADS[args.workload])
     if args.batch is not None and w["kind"] != "sk":
-        if w["kind"] == "gqa":
+        if w["kind"] in ("gqa", "gqa_int8"):
             w["B"] = args.batch
         else:
             w["R"] = 32 * args.batch
@@ -470,20 +636,22 @@ def main() -> int:
         w["D"] = args.head_dim
         w["desc"] += f" [D overridden to {args.head_dim}]"
 
-    if w["kind"] == "llama":
-        if args.batch is not None:
-            w["B"] = args.batch
-        return run_llama(args, w)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if w["kind"] == "llama":
+        if args.batch is not None:
+            w["B"] = args.batch
+        if args.impl == "reference":
+            return run_llama_reference(args, w, rank)
+        return run_llama_tp(args, w, world, rank, local_rank) if world > 1 else run_llama(args, w)
     config = {"workload": w["desc"], "global_batch": None, "seq_len": w["N"], "head_dim": w["D"],
               "parallelism": f"{world} GPU(s), sequences sharded, no data-path collective",
               "l2": "inputs larger than L2 per step (no flush needed)" if w["kind"] != "sk"
               else "8 rotated KV sets (537 MB) > 4x L2",
               "timing": "CUDA events around K eager C-ABI calls" if args.eager
               else "CUDA events around one CUDA-graph replay of K C-ABI calls"}
-    if w["kind"] == "gqa":
+    if w["kind"] in ("gqa", "gqa_int8"):
         config["global_batch"] = w["B"] * world
     elif w["kind"] == "sk":
         config["global_batch"] = world
@@ -506,7 +674,7 @@ def main() -> int:
         res = {"cores": torch.get_num_threads(), "sample": desc}
         line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": path_dtype(w["kind"]), "data": "synthetic",
                 "config": config,
                 "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": res["cores"], "kind": "port",
                                  "sample": res["sample"] + f"; {args.steps} timed steps of one call"},
@@ -605,7 +773,7 @@ def main() -> int:
         cpu = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in c.items() if k != "ms_per_call"}
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": config,
+            "vs_baseline": None, "dtype": path_dtype(w["kind"]), "data": "synthetic", "config": config,
             "us_per_call": round(ms_step * 1e3, 3), "pct_of_8TBps": round(100 * achieved / NOMINAL_HBM_GBS, 2),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps * case.kernels_per_call, "clocks": clocks, "impl": "ours"}

@@ -18,6 +18,13 @@
   MLP, LM head and argmax -- is captured once in a CUDA graph and replayed
   per token, so a step costs no Python or launch overhead.  The model's
   weights may be bf16 or fp16; attention runs on the fp16 / int8 cache.
+
+  With ``tp_group`` (a ``torch.distributed`` group, NCCL on GPUs) the decoder
+  is tensor-parallel by KV head: each rank keeps the q/k/v projection rows, the
+  KV cache and the attention of Hkv/world KV heads (and their query heads),
+  and the per-rank attention outputs are all-gathered every layer -- inside
+  the captured graph -- before the replicated output projection, MLP and LM
+  head, so every rank produces the same tokens.
 """
 from __future__ import annotations
 
@@ -27,6 +34,7 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
+from . import sharding
 
 HOOK_NAME = "fqkv_decode"
 
@@ -72,7 +80,8 @@ class GraphDecoder:
         tokens = dec.generate(T - 1)             # [B, T - 1] following tokens
     """
 
-    def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False, kv_dtype: str = "fp16"):
+    def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False, kv_dtype: str = "fp16",
+                 tp_group=None):
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
         self._rope = apply_rotary_pos_emb
@@ -83,6 +92,20 @@ class GraphDecoder:
         self.Hkv = cfg.num_key_value_heads
         self.D = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.Hq
         self.B = batch
+        # tensor parallelism by KV head: this rank's query / KV heads and projection rows
+        self.tp_group = tp_group
+        if tp_group is not None:
+            import torch.distributed as dist
+            self.world, self.rank = dist.get_world_size(tp_group), dist.get_rank(tp_group)
+        else:
+            self.world, self.rank = 1, 0
+        sharding.shard_kv_heads(self.Hq, self.Hkv, self.world, self.rank)  # validates divisibility
+        self.Hq_l, self.Hkv_l = self.Hq // self.world, self.Hkv // self.world
+        self.proj = None
+        if self.world > 1:
+            self.proj = [sharding.shard_attention_projections(layer.self_attn, self.Hq, self.Hkv, self.D,
+                                                              self.world, self.rank)
+                         for layer in model.model.layers]
         self.max_len = max_len
         dev = next(model.parameters()).device
         self.dev = dev
@@ -91,23 +114,47 @@ class GraphDecoder:
             raise ValueError("kv_dtype must be 'fp16' or 'int8'")
         self.kv_dtype = kv_dtype
         cache_dtype = torch.float16 if kv_dtype == "fp16" else torch.int8
-        self.kc = torch.zeros(self.L, batch, self.Hkv, max_len, self.D, dtype=cache_dtype, device=dev)
+        self.kc = torch.zeros(self.L, batch, self.Hkv_l, max_len, self.D, dtype=cache_dtype, device=dev)
         self.vc = torch.zeros_like(self.kc)
         if kv_dtype == "int8":  # per-token fp16 scales of the int8 codes
-            self.ks = torch.zeros(self.L, batch, self.Hkv, max_len, dtype=torch.float16, device=dev)
+            self.ks = torch.zeros(self.L, batch, self.Hkv_l, max_len, dtype=torch.float16, device=dev)
             self.vs = torch.zeros_like(self.ks)
         self.pos32 = torch.zeros(1, dtype=torch.int32, device=dev)   # self.pos as int32 (append position)
         self.pos = torch.zeros(1, dtype=torch.long, device=dev)      # position of the token fed to the step
         self.nlen = torch.zeros(1, dtype=torch.int32, device=dev)    # valid cache length during the step
         self.tok = torch.zeros(batch, dtype=torch.long, device=dev)  # token fed to the step
         self.out_tokens = torch.zeros(batch, max_len, dtype=torch.long, device=dev)
-        self.attn_out = torch.empty(batch, self.Hq, self.D, dtype=torch.float16, device=dev)
-        nb = ops.workspace_bytes(kv_dtype, batch, self.Hq, self.Hkv, max_len, self.D)
+        self.attn_out = torch.empty(batch, self.Hq_l, self.D, dtype=torch.float16, device=dev)
+        # all-gather staging of the per-rank attention outputs (world x [B, 1, Hq_l, D])
+        self.gather_buf = (torch.empty(self.world * batch, 1, self.Hq_l, self.D, dtype=torch.float16, device=dev)
+                           if self.world > 1 else None)
+        nb = ops.workspace_bytes(kv_dtype, batch, self.Hq_l, self.Hkv_l, max_len, self.D)
         self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev) if nb else None
         self.keep_logits = keep_logits
         self.logits = torch.zeros(batch, cfg.vocab_size, dtype=torch.float32, device=dev) if keep_logits else None
         self.graph = None
         self.prompt_len = 0
+
+    # ------------------------------------------------------------------ per-rank attention pieces
+    def _qkv(self, li: int, attn, x: torch.Tensor):
+        """This rank's q [B, Hq_l, T, D], k/v [B, Hkv_l, T, D] projections of x [B, T, H]."""
+        B, T = x.shape[0], x.shape[1]
+        if self.proj is None:
+            q, k, v = attn.q_proj(x), attn.k_proj(x), attn.v_proj(x)
+        else:
+            (wq, bq), (wk, bk), (wv, bv) = self.proj[li]
+            q, k, v = F.linear(x, wq, bq), F.linear(x, wk, bk), F.linear(x, wv, bv)
+        return (q.view(B, T, self.Hq_l, self.D).transpose(1, 2), k.view(B, T, self.Hkv_l, self.D).transpose(1, 2),
+                v.view(B, T, self.Hkv_l, self.D).transpose(1, 2))
+
+    def _heads(self, o: torch.Tensor, staging=None) -> torch.Tensor:
+        """Local attention output o [B, T, Hq_l, D] -> all heads [B, T, Hq*D] (all-gather when sharded)."""
+        B, T = o.shape[0], o.shape[1]
+        if self.world == 1:
+            return o.reshape(B, T, self.Hq * self.D)
+        if staging is None:
+            staging = torch.empty((self.world * B,) + tuple(o.shape[1:]), dtype=o.dtype, device=o.device)
+        return sharding.gather_heads(o.contiguous(), staging, self.world, self.tp_group)
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
@@ -123,13 +170,11 @@ class GraphDecoder:
         for li, layer in enumerate(m.layers):
             attn = layer.self_attn
             x = layer.input_layernorm(h)
-            q = attn.q_proj(x).view(B, P, self.Hq, self.D).transpose(1, 2)
-            k = attn.k_proj(x).view(B, P, self.Hkv, self.D).transpose(1, 2)
-            v = attn.v_proj(x).view(B, P, self.Hkv, self.D).transpose(1, 2)
+            q, k, v = self._qkv(li, attn, x)
             q, k = self._rope(q, k, cos, sin)
             self._append(li, k, v, 0)
             o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
-            h = h + attn.o_proj(o.transpose(1, 2).reshape(B, P, self.Hq * self.D))
+            h = h + attn.o_proj(self._heads(o.transpose(1, 2)))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         logits = self.model.lm_head(m.norm(h[:, -1:]))[:, -1].float()
         first = logits.argmax(-1)
@@ -177,14 +222,12 @@ class GraphDecoder:
         for li, layer in enumerate(m.layers):
             attn = layer.self_attn
             x = layer.input_layernorm(h)
-            q = attn.q_proj(x).view(B, 1, self.Hq, self.D).transpose(1, 2)
-            k = attn.k_proj(x).view(B, 1, self.Hkv, self.D).transpose(1, 2)
-            v = attn.v_proj(x).view(B, 1, self.Hkv, self.D).transpose(1, 2)
+            q, k, v = self._qkv(li, attn, x)
             q, k = self._rope(q, k, cos, sin)
             self._append(li, k, v, self.pos)
             self._attend(li, q[:, :, 0].to(torch.float16).contiguous())
-            o = self.attn_out.to(h.dtype).reshape(B, 1, self.Hq * self.D)
-            h = h + attn.o_proj(o)
+            o = self._heads(self.attn_out.view(B, 1, self.Hq_l, self.D), self.gather_buf)
+            h = h + attn.o_proj(o.to(h.dtype))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         logits = self.model.lm_head(m.norm(h))[:, 0].float()
         nxt = logits.argmax(-1)
@@ -217,6 +260,12 @@ class GraphDecoder:
         for dst, src in zip(state, saved):
             dst.copy_(src)
         torch.cuda.synchronize(self.dev)
+
+    def release(self) -> None:
+        """Drop the captured graph (required before destroying a process group whose collectives it holds)."""
+        if self.graph is not None:
+            self.graph.reset()
+            self.graph = None
 
     @torch.no_grad()
     def step(self) -> None:
