@@ -7,18 +7,26 @@
 // scales [B, Hkv, stride] fp16 (the reference quantizer's output, e.g. written
 // by fqkv_quantize_int8_into_cache), q/out [B, Hq, D] fp16.
 //
-//  * Same persistent, warp-specialised structure as the fp16 kernel: a unit is
-//    (sequence, KV head, group of <= 8 query heads, split), warp 4 streams
-//    64-key tiles of K and V codes plus their scale windows into a 4-stage ring
-//    with 1-D bulk copies.
-//  * Each consumer warp first turns its 16 keys of K and V codes into exact
-//    fp16 integers in a private 128B-swizzled buffer (byte-permute into the
-//    mantissa of 1024 + exact fp16 subtraction) and releases the stage, then
-//    runs the tensor-core math of the fp16 kernel on that buffer: S = Q K^T
-//    (ldmatrix + mma.sync f16 -> f32) scaled per key by its K scale, and
-//    O += (P * V scale) V (ldmatrix.trans).  The softmax denominator sums the
-//    unscaled P.  The KV bytes are read from HBM once for all heads of the
-//    group.
+//  * Persistent, warp-specialised: a unit is (sequence, KV head, group of <= 8
+//    query heads, split).  Warp 4 streams 64-key tiles of K and V codes with
+//    3-D TMA tensor copies (128-byte swizzle for D = 128, 64-byte for D = 64,
+//    keys past the end zero-filled) plus 16-byte-aligned windows of their
+//    fp16 scales into a ring of stages; each consumer warp takes 16 keys of a
+//    tile and reads every KV byte once for all heads of the group.
+//  * S = Q K^T on the integer tensor cores (mma m16n8k32 s8 x s8 -> s32)
+//    straight from the codes: q is held as a 2-plane fixed-point number per
+//    head (q * Qs = hi * 256 + lo, |q * Qs| <= 32639, Qs = 32639 / max|q|);
+//    rows 0-7 of the A operand carry the hi planes of the group's heads and
+//    rows 8-15 the lo planes, so one MMA yields both partial sums of a score.
+//    The head dimension is permuted (identically for q and K) so that each
+//    thread reads one contiguous D/4-byte span of a key row.
+//  * O^T += V^T (P * Vscale)^T on the fp16 tensor cores (m16n8k16): the A
+//    operand pairs one dimension of two consecutive keys, built in registers
+//    from the codes (byte permute, one three-input logic op giving the fp16
+//    value 1152 + code, one exact fp16 subtraction); the B operand is the fp16
+//    probabilities times the key's V scale, taken directly from the score
+//    accumulators.  Rows of O^T are head dimensions, columns the group's
+//    heads.  The softmax denominator sums the unscaled probabilities.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -35,19 +43,19 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
 constexpr int kTK = 64;
 constexpr int kMergeHeads = 4;
+constexpr int kQMax = 32639;  // |q * Qs| bound: hi = (v + 128) >> 8 stays in [-127, 127]
 
 template <int D>
 struct Q8Cfg {
   static constexpr int kTileBytes = kTK * D;            // K (or V) codes of one tile
   static constexpr int kScaleBytes = 2 * kTK + 32;      // 16B-aligned scale window
-  static constexpr int kStageBytes = 2 * kTileBytes + 2 * kScaleBytes;
-  static constexpr int kStages = 4;
-  static constexpr int kWarpBuf = 16 * D * 2;           // 16 keys x D fp16 (K or V)
+  static constexpr int kStageRaw = 2 * kTileBytes + 2 * kScaleBytes;
+  static constexpr int kStageBytes = (kStageRaw + 1023) & ~1023;  // tiles stay 1024-aligned (swizzle atom)
+  static constexpr int kStages = D == 128 ? 3 : 4;
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
-  static constexpr size_t kBufBytes = size_t(kConsumerWarps) * 2 * kWarpBuf;
   static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
   static constexpr size_t kMergeBytes = size_t(kConsumerWarps) * (2 * 8 + kMergeHeads * D) * sizeof(float);
-  static constexpr size_t kSmemBytes = 1024 + kBufBytes + kRingBytes + kBarBytes + kMergeBytes;
+  static constexpr size_t kSmemBytes = 1024 + kRingBytes + kBarBytes + kMergeBytes;
 };
 
 struct UnitCoord {
@@ -65,39 +73,50 @@ __device__ __forceinline__ UnitCoord decode_unit(const DecodeLaunch& a, int u) {
   return c;
 }
 
-// 16-byte chunk `chunk` (0 .. D/8-1) of row `row` (0..15) of a warp buffer made
-// of D/64 blocks of [16 rows x 128 B], 128B-swizzled within each block.
-__device__ __forceinline__ uint32_t swz16(int row, int chunk) {
-  return uint32_t((chunk >> 3) * 2048 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+// Byte offset of 16-byte chunk `c` of key row `row` inside a tile written by
+// the TMA copy (128-byte swizzle for 128-byte rows, 64-byte swizzle for
+// 64-byte rows; the tile starts 1024-aligned).
+template <int D>
+__device__ __forceinline__ uint32_t tile_off(int row, int c) {
+  if constexpr (D == 128) return uint32_t(row * 128 + ((c ^ (row & 7)) << 4));
+  else return uint32_t(row * 64 + ((c ^ ((row >> 1) & 3)) << 4));
 }
 
-__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
+// D(16x8, s32) += A(16x32, s8, row) * B(32x8, s8, col).
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// 16 int8 codes (one uint4) -> 16 exact fp16 values (two uint4, element order kept).
-__device__ __forceinline__ void codes16_to_half(const uint4 w, uint4& lo, uint4& hi) {
-  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
-  uint32_t out[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t x = in[i] ^ 0x80808080u;  // code + 128
-    out[2 * i] = hsub2_u32(__byte_perm(x, 0x64646464u, 0x5140u), 0x64806480u);
-    out[2 * i + 1] = hsub2_u32(__byte_perm(x, 0x64646464u, 0x7362u), 0x64806480u);
-  }
-  lo = make_uint4(out[0], out[1], out[2], out[3]);
-  hi = make_uint4(out[4], out[5], out[6], out[7]);
+// Exact fp16x2 {code of x's byte, code of y's byte} for the byte chosen by
+// `sel` ({x.b, x.b, y.b, y.b}): the logic op forms 0x64 | (code ^ 0x80) in each
+// half (the fp16 value 1152 + code), the subtraction removes 1152.
+__device__ __forceinline__ uint32_t code_pair(uint32_t x, uint32_t y, uint32_t sel) {
+  const uint32_t p = __byte_perm(x, y, sel);
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x9c;" : "=r"(r) : "r"(p), "r"(0x64806480u), "r"(0xFF00FF00u));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(r), "r"(0x64806480u));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
+         (uint32_t(d) << 24);
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_constant__ DecodeLaunch a) {
+__global__ void __launch_bounds__(kThreads, 3) decode_q8gqa_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = Q8Cfg<D>;
+  constexpr int KS = D / 32;        // integer MMA k-steps over the head dimension
+  constexpr int MT = D / 16;        // m-tiles of O^T (16 head dimensions each)
+  constexpr int TW = D / 32;        // 32-bit words of this thread's V slice of one key
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bufs = smem;                                   // [warp][K|V][16 x D fp16], 1 KiB aligned
-  uint8_t* ring = smem + C::kBufBytes;
+  uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::kRingBytes);
   uint64_t* empty = full + C::kStages;
   float* sm_m = reinterpret_cast<float*>(empty + C::kStages);
@@ -109,7 +128,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtl wc{a.status, a.timeout_ns};
-  const size_t row_stride = size_t(a.kv_stride) * D;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -118,6 +136,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
     }
     abort_flag = 0;
     fence_barrier_init();
+  }
+  if (warp == kConsumerWarps && lane == 0) {
+    prefetch_tensormap(&a.tmK);
+    prefetch_tensormap(&a.tmV);
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -132,11 +154,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
       const UnitCoord uc = decode_unit(a, u);
       const int lo = uc.s * a.chunk;
       const int hi = min(n_valid, lo + a.chunk);
-      const size_t r = size_t(uc.b) * a.Hkv + uc.kh;
-      const uint8_t* Kr = static_cast<const uint8_t*>(a.K) + r * row_stride;
-      const uint8_t* Vr = static_cast<const uint8_t*>(a.V) + r * row_stride;
-      const __half* Ksr = static_cast<const __half*>(a.Ks) + r * a.kv_stride;
-      const __half* Vsr = static_cast<const __half*>(a.Vs) + r * a.kv_stride;
+      const int z = uc.b * a.Hkv + uc.kh;
+      const __half* Ksr = static_cast<const __half*>(a.Ks) + size_t(z) * a.kv_stride;
+      const __half* Vsr = static_cast<const __half*>(a.Vs) + size_t(z) * a.kv_stride;
       for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
         const int st = it % C::kStages;
         if (it >= C::kStages) {
@@ -147,7 +167,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
           }
         }
         const int nk = min(kTK, hi - k0);
-        const uint32_t kv_bytes = uint32_t(nk) * D;
         const uintptr_t ka = reinterpret_cast<uintptr_t>(Ksr + k0);
         const uintptr_t va = reinterpret_cast<uintptr_t>(Vsr + k0);
         const uintptr_t ka0 = ka & ~uintptr_t(15), va0 = va & ~uintptr_t(15);
@@ -156,9 +175,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
         stage_off[st][0] = int(ka - ka0) >> 1;
         stage_off[st][1] = int(va - va0) >> 1;
         uint8_t* base = ring + size_t(st) * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[st], 2 * kv_bytes + kwin + vwin);
-        bulk_g2s(base, Kr + size_t(k0) * D, kv_bytes, &full[st]);
-        bulk_g2s(base + C::kTileBytes, Vr + size_t(k0) * D, kv_bytes, &full[st]);
+        mbar_arrive_expect_tx(&full[st], 2 * C::kTileBytes + kwin + vwin);
+        tma_load_3d(base, &a.tmK, 0, k0, z, &full[st]);
+        tma_load_3d(base + C::kTileBytes, &a.tmV, 0, k0, z, &full[st]);
         bulk_g2s(base + 2 * C::kTileBytes, reinterpret_cast<const void*>(ka0), kwin, &full[st]);
         bulk_g2s(base + 2 * C::kTileBytes + C::kScaleBytes, reinterpret_cast<const void*>(va0), vwin, &full[st]);
       }
@@ -173,12 +192,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
   // ------------------------------------------------------------ consumers
   const int g = lane >> 2;
   const int t = lane & 3;
-  const int mi = lane >> 3;
-  const int rr = lane & 7;
   const int r0 = warp * 16;
-  uint8_t* kbuf = bufs + size_t(warp) * 2 * C::kWarpBuf;
-  uint8_t* vbuf = kbuf + C::kWarpBuf;
-  const uint32_t kbuf_u = smem_u32(kbuf), vbuf_u = smem_u32(vbuf);
   const float csc = a.sm_scale_log2;
   bool alive = true;
   int it = 0;
@@ -190,23 +204,51 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
     const int h0 = uc.kh * a.G + uc.grp * a.GP;
     const int gvalid = min(a.GP, a.G - uc.grp * a.GP);
 
-    uint32_t qa[D / 16][2];
+    // ---- q of head g, dimensions [t*D/4, (t+1)*D/4), as two int8 planes
+    uint32_t qa[KS][4];
+    float hf;  // sm_scale_log2 / Qs of head g
     {
-      const __half* qrow = static_cast<const __half*>(a.q) + (size_t(uc.b) * a.Hq + h0 + g) * D;
+      float qf[D / 4];
+      if (g < gvalid) {
+        const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+            static_cast<const __half*>(a.q) + (size_t(uc.b) * a.Hq + h0 + g) * D + t * (D / 4));
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        if (g < gvalid) {
-          qa[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * t);
-          qa[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * t + 8);
-        } else {
-          qa[kk][0] = 0u;
-          qa[kk][1] = 0u;
+        for (int v = 0; v < D / 8; ++v) {
+          const uint32_t w = qrow[v];
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+          qf[2 * v] = f.x;
+          qf[2 * v + 1] = f.y;
         }
+      } else {
+#pragma unroll
+        for (int i = 0; i < D / 4; ++i) qf[i] = 0.f;
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < D / 4; ++i) amax = fmaxf(amax, fabsf(qf[i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const float Qs = amax > 0.f ? float(kQMax) / amax : 0.f;
+      hf = amax > 0.f ? csc * (amax / float(kQMax)) : 0.f;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        int hv[8], lv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int v = __float2int_rn(qf[8 * kk + i] * Qs);
+          hv[i] = (v + 128) >> 8;
+          lv[i] = v - hv[i] * 256;
+        }
+        qa[kk][0] = pack_s8x4(hv[0], hv[1], hv[2], hv[3]);
+        qa[kk][1] = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
+        qa[kk][2] = pack_s8x4(hv[4], hv[5], hv[6], hv[7]);
+        qa[kk][3] = pack_s8x4(lv[4], lv[5], lv[6], lv[7]);
       }
     }
-    float o[D / 8][4];
+
+    float o[MT][4];
 #pragma unroll
-    for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
 
     for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
@@ -218,28 +260,42 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
         if (!alive && lane == 0) abort_flag = 1;
       }
       if (!alive) continue;
-      const uint8_t* base = ring + size_t(st) * C::kStageBytes;
+      const uint8_t* kt = ring + size_t(st) * C::kStageBytes;
+      const uint8_t* vt = kt + C::kTileBytes;
 
-      // ---- this warp's 16 keys: codes -> exact fp16 in the private buffers
-      {
-        const uint8_t* kt = base + size_t(r0) * D;
-        const uint8_t* vt = base + C::kTileBytes + size_t(r0) * D;
-#pragma unroll 1
-        for (int i = 0; i < D / 32; ++i) {     // 512-byte blocks of the warp's 16 x D codes
-          const int off = 512 * i + 16 * lane;  // byte offset: row off / D, column off % D
-          const int row = off / D, col = off % D;
-          uint4 lo4, hi4;
-          codes16_to_half(*reinterpret_cast<const uint4*>(kt + off), lo4, hi4);
-          *reinterpret_cast<uint4*>(kbuf + swz16(row, col / 8)) = lo4;
-          *reinterpret_cast<uint4*>(kbuf + swz16(row, col / 8 + 1)) = hi4;
-          codes16_to_half(*reinterpret_cast<const uint4*>(vt + off), lo4, hi4);
-          *reinterpret_cast<uint4*>(vbuf + swz16(row, col / 8)) = lo4;
-          *reinterpret_cast<uint4*>(vbuf + swz16(row, col / 8 + 1)) = hi4;
+      // ---- fragments of this warp's 16 keys (rows r0 .. r0 + 15 of the tile)
+      uint32_t kb[2][2 * KS];  // key r0 + 8j + g: this thread's D/4 bytes
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int row = r0 + 8 * j + g;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          const uint4 w = *reinterpret_cast<const uint4*>(kt + tile_off<D>(row, (D / 64) * t + c));
+          kb[j][4 * c + 0] = w.x;
+          kb[j][4 * c + 1] = w.y;
+          kb[j][4 * c + 2] = w.z;
+          kb[j][4 * c + 3] = w.w;
         }
       }
-      // per-key scales of the keys this thread's fragments cover
-      const __half* kst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes) + stage_off[st][0];
-      const __half* vst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes + C::kScaleBytes) + stage_off[st][1];
+      uint32_t vw[4][TW];  // keys r0 + {2t, 2t+1, 2t+8, 2t+9}, dimensions [g*D/8, (g+1)*D/8)
+#pragma unroll
+      for (int kq = 0; kq < 4; ++kq) {
+        const int row = r0 + 2 * t + (kq & 1) + 8 * (kq >> 1);
+        if constexpr (D == 128) {
+          const uint4 w = *reinterpret_cast<const uint4*>(vt + tile_off<D>(row, g));
+          vw[kq][0] = w.x;
+          vw[kq][1] = w.y;
+          vw[kq][2] = w.z;
+          vw[kq][3] = w.w;
+        } else {
+          const uint2 w = *reinterpret_cast<const uint2*>(vt + tile_off<D>(row, g >> 1) + 8 * (g & 1));
+          vw[kq][0] = w.x;
+          vw[kq][1] = w.y;
+        }
+      }
+      const __half* kst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes) + stage_off[st][0];
+      const __half* vst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes + C::kScaleBytes) +
+                          stage_off[st][1];
       float ks[2][2], vs[2][2];
 #pragma unroll
       for (int j = 0; j < 2; ++j)
@@ -249,20 +305,18 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
           vs[j][e] = __half2float(vst[r0 + 8 * j + 2 * t + e]);
         }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);  // the stage is no longer read by this warp
+      if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
 
-      // ---- S = Q K^T
-      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      // ---- S = Q K^T in integers: hi plane of head g in c0/c1, lo plane in c2/c3
+      int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const int row = ((mi >> 1) << 3) + rr;
-        const int chunk = 2 * kk + (mi & 1);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(kbuf_u + swz16(row, chunk), b0, b1, b2, b3);
-        mma_16816(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
-        mma_16816(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+      for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          mma_s8_16832(acc[j], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], kb[j][2 * kk], kb[j][2 * kk + 1]);
       }
 
+      float sc[2][2];
       float mx = -INFINITY;
       bool valid[2][2];
 #pragma unroll
@@ -270,9 +324,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           valid[j][e] = (k0 + r0 + 8 * j + 2 * t + e) < hi;
-          const float v = valid[j][e] ? sc[j][e] * ks[j][e] * csc : -INFINITY;
-          sc[j][e] = v;
-          mx = fmaxf(mx, v);
+          const float s = float(acc[j][e] * 256 + acc[j][2 + e]) * (ks[j][e] * hf);
+          sc[j][e] = valid[j][e] ? s : -INFINITY;
+          mx = fmaxf(mx, sc[j][e]);
         }
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -280,38 +334,43 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
       const float m_new = fmaxf(m_run, mx);
       if (__any_sync(0xffffffffu, m_new > m_run)) {
         const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
-#pragma unroll
-        for (int j = 0; j < D / 8; ++j) {
-          o[j][0] *= alpha;
-          o[j][1] *= alpha;
-        }
         l_run *= alpha;
         m_run = m_new;
+        // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
+        const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * t) * 4);
+        const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4);
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          o[i][0] *= a_lo;
+          o[i][1] *= a_hi;
+          o[i][2] *= a_lo;
+          o[i][3] *= a_hi;
+        }
       }
       const float mu = (m_run == -INFINITY) ? 0.f : m_run;
       float p[2][2];
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) p[j][e] = ex2(sc[j][e] - mu);
+        for (int e = 0; e < 2; ++e) p[j][e] = valid[j][e] ? ex2(sc[j][e] - mu) : 0.f;
       l_run += (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
-      const uint32_t pa0 = pack_half2(valid[0][0] ? p[0][0] * vs[0][0] : 0.f, valid[0][1] ? p[0][1] * vs[0][1] : 0.f);
-      const uint32_t pa2 = pack_half2(valid[1][0] ? p[1][0] * vs[1][0] : 0.f, valid[1][1] ? p[1][1] * vs[1][1] : 0.f);
+      const uint32_t pb0 = pack_half2(valid[0][0] ? p[0][0] * vs[0][0] : 0.f, valid[0][1] ? p[0][1] * vs[0][1] : 0.f);
+      const uint32_t pb1 = pack_half2(valid[1][0] ? p[1][0] * vs[1][0] : 0.f, valid[1][1] ? p[1][1] * vs[1][1] : 0.f);
 
-      // ---- O += (P * vscale) V
+      // ---- O^T += V^T P^T; m-tile i rows g / g+8 are dimensions g*D/8 + i / g*D/8 + D/16 + i
 #pragma unroll
-      for (int pp = 0; pp < D / 16; ++pp) {
-        const int row = ((mi & 1) << 3) + rr;
-        const int chunk = 2 * pp + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(vbuf_u + swz16(row, chunk), b0, b1, b2, b3);
-        mma_16816(o[2 * pp], pa0, 0u, pa2, 0u, b0, b1);
-        mma_16816(o[2 * pp + 1], pa0, 0u, pa2, 0u, b2, b3);
+      for (int i = 0; i < MT; ++i) {
+        const int w0 = i >> 2, w1 = (MT + i) >> 2;              // words holding bytes i and D/16 + i
+        const uint32_t sel = uint32_t(i & 3) * 0x1111u + 0x4400u;  // {x.b, x.b, y.b, y.b}
+        const uint32_t a0 = code_pair(vw[0][w0], vw[1][w0], sel);
+        const uint32_t a1 = code_pair(vw[0][w1], vw[1][w1], sel);
+        const uint32_t a2 = code_pair(vw[2][w0], vw[3][w0], sel);
+        const uint32_t a3 = code_pair(vw[2][w1], vw[3][w1], sel);
+        mma_16816(o[i], a0, a1, a2, a3, pb0, pb1);
       }
-      __syncwarp();  // the buffers are rewritten by the next tile
     }
 
-    // ---- unit epilogue (as in the fp16 kernel)
+    // ---- unit epilogue: merge the 4 warps' (m, l, O) per head
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     if (t == 0) {
@@ -321,12 +380,19 @@ __global__ void __launch_bounds__(kThreads, 2) decode_q8gqa_kernel(const __grid_
     const int ct = threadIdx.x;
     const size_t row_base = size_t(uc.b) * a.Hq + h0;
     for (int hp = 0; hp < gvalid; hp += kMergeHeads) {
-      const int gl = g - hp;
-      if (gl >= 0 && gl < kMergeHeads && g < gvalid) {
 #pragma unroll
-        for (int j = 0; j < D / 8; ++j)
-          *reinterpret_cast<float2*>(&sm_o[(warp * kMergeHeads + gl) * D + 8 * j + 2 * t]) =
-              make_float2(o[j][0], o[j][1]);
+      for (int e = 0; e < 2; ++e) {
+        const int head = 2 * t + e;
+        const int gl = head - hp;
+        if (gl >= 0 && gl < kMergeHeads && head < gvalid) {
+          float* dst = &sm_o[(warp * kMergeHeads + gl) * D + g * (D / 8)];
+#pragma unroll
+          for (int i = 0; i < MT; i += 4) {
+            *reinterpret_cast<float4*>(dst + i) = make_float4(o[i][e], o[i + 1][e], o[i + 2][e], o[i + 3][e]);
+            *reinterpret_cast<float4*>(dst + MT + i) =
+                make_float4(o[i][2 + e], o[i + 1][2 + e], o[i + 2][2 + e], o[i + 3][2 + e]);
+          }
+        }
       }
       named_bar_sync(1, 32 * kConsumerWarps);
       const int nh = min(kMergeHeads, gvalid - hp);

@@ -133,6 +133,23 @@ int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64
   return FQKV_OK;
 }
 
+// int8 codes viewed as [B*Hkv][N][D] bytes with `stride` keys between
+// consecutive (b, kv head) rows; box = one 64-key tile of whole rows, swizzled
+// at the row width (128 B for D = 128, 64 B for D = 64).
+int make_kv_map_i8(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t D, int64_t stride) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(BH)};
+  const cuuint64_t strides[2] = {cuuint64_t(D), cuuint64_t(stride) * cuuint64_t(D)};
+  const cuuint32_t box[3] = {cuuint32_t(D), 64, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  return FQKV_OK;
+}
+
 // ------------------------------------------------------------------ planning
 size_t partial_bytes(int64_t rows, int64_t S, int64_t D) {
   const size_t ml = size_t(rows) * size_t(S) * sizeof(float);
@@ -275,9 +292,12 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
     if (!aligned(ws, 16)) return fail(FQKV_ERR_MISALIGNED, "workspace must be 16-byte aligned");
     carve_partials(a, ws, int64_t(a.B) * a.Hq);
   }
-  if (fmt == KvFormat::F16) {
+  if (a.fmt == KvFormat::F16) {
     if (int rc = make_kv_map(&a.tmK, K, B * Hkv, N, D, kv_stride)) return rc;
     if (int rc = make_kv_map(&a.tmV, V, B * Hkv, N, D, kv_stride)) return rc;
+  } else if (a.fmt == KvFormat::I8Gqa) {
+    if (int rc = make_kv_map_i8(&a.tmK, K, B * Hkv, N, D, kv_stride)) return rc;
+    if (int rc = make_kv_map_i8(&a.tmV, V, B * Hkv, N, D, kv_stride)) return rc;
   }
   return launch(a, reinterpret_cast<cudaStream_t>(stream));
 }

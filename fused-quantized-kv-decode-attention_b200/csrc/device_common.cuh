@@ -159,8 +159,7 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, u
                : "r"(addr));
 }
 
-// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col).  Rows 8..15 of A are
-// zero in every use here, so the caller passes a1 = a3 = 0.
+// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col).
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
   asm volatile(

@@ -55,7 +55,7 @@ struct DecodeLaunch {
   int* status;                         // device status word
   unsigned long long timeout_ns;
   int debug_skip_loads;                // test hook: producer issues nothing
-  CUtensorMap tmK, tmV;                // fp16 only
+  CUtensorMap tmK, tmV;                // tiled K/V maps (fp16, and int8 GQA)
 };
 
 // Kernel resource queries and launches, per KV format (attn_f16.cu,

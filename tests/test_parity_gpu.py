@@ -237,7 +237,8 @@ def _int8_gqa_ref(q, Kf, Vf, n=None):
 
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("B,Hq,Hkv,N", [(1, 32, 8, 1024), (4, 32, 8, 513), (2, 64, 8, 77), (3, 8, 2, 1),
-                                        (1, 32, 8, 16384), (2, 12, 4, 300)])
+                                        (1, 32, 8, 16384), (2, 12, 4, 300), (1, 128, 8, 200), (2, 16, 8, 130),
+                                        (1, 40, 8, 63)])
 def test_gqa_int8(fqkv, B, Hq, Hkv, N, D):
     q, K, V = _randn(B, Hq, D, seed=90), _randn(B, Hkv, N, D, seed=91), _randn(B, Hkv, N, D, seed=92)
     Kq, Ks = fqkv.qpt(K.cuda())
@@ -288,3 +289,20 @@ def test_gqa_int8_kvcache_append_and_device_length(fqkv, B, Hq, Hkv, max_len, n,
     _close(fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, n), ref)
     n_dev = torch.tensor([n], dtype=torch.int32, device="cuda")
     _close(fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, n_dev), ref)
+
+
+def test_gqa_int8_extreme_q_and_scales(fqkv):
+    """q with one huge element per head (fixed-point q planes lose the small ones
+    only below the tolerance), all-zero tokens (scale 0), a zero q head."""
+    B, Hq, Hkv, N, D = 2, 16, 4, 300, 128
+    q = _randn(B, Hq, D, seed=98)
+    q[:, :, 5] = 60.0
+    q[1, 3] = 0.0
+    K, V = _randn(B, Hkv, N, D, seed=99), _randn(B, Hkv, N, D, seed=100)
+    K[:, :, 7] = 0.0
+    V[:, :, 11] = 0.0
+    V[0, 1, 13] *= 100.0
+    Kq, Ks = fqkv.qpt(K.cuda())
+    Vq, Vs = fqkv.qpt(V.cuda())
+    out = fqkv.decode_attn_gqa_int8(q.cuda(), Kq, Vq, Ks, Vs)
+    _close(out, _int8_gqa_ref(q.numpy(), K.numpy(), V.numpy()))
