@@ -1,0 +1,658 @@
+// Quantized-KV decode attention on the tensor cores, sm_100a: int8 codes with
+// several query heads per KV head (a GQA model's int8 cache) and int4 codes.
+//
+// The reference has int8 KV for one query head per KV row
+// (decode_attn_int8_mw, kernels/decode_attn_int8_mw.cu:6-51), int4 KV for one
+// query head per row and D = 64 (decode_attn_int4, kernels/decode_attn_int4.cu:
+// 8-46) and GQA only for fp16 (decode_attn_gqa, kernels/decode_attn_gqa.cu:
+// 8-55).  Layout: codes [B, Hkv, stride, RB] (RB = D bytes for int8, D/2 for
+// int4: two signed nibbles per byte, element 2i in the low nibble, as the
+// reference packs them, notebook lines 292-299), per-token scales
+// [B, Hkv, stride] fp16, q/out [B, Hq, D] fp16.
+//
+//  * Persistent, warp-specialised: a unit is (sequence, KV head, group of <= 8
+//    query heads, split).  Warp 4 streams tiles of 4*KPW keys of K and V codes
+//    with 3-D TMA tensor copies (swizzled at the row width: 128, 64 or 32
+//    bytes; keys past the end zero-filled) plus 16-byte-aligned windows of
+//    their fp16 scales into a ring of stages; each consumer warp takes KPW keys
+//    of a tile and reads every KV byte once for all heads of the group.
+//  * S = Q K^T on the integer tensor cores (mma m16n8k32, s32 accumulate)
+//    straight from the codes: q is a 2-plane fixed-point number per head
+//    (q * Qs = hi * 256 + lo, |q * Qs| <= 32639, Qs = 32639 / max|q|); rows 0-7
+//    of the A operand carry the hi planes of the group's heads and rows 8-15
+//    the lo planes, so one MMA gives both partial sums of a score.  int8 codes
+//    are the B operand as they are (s8).  int4 low nibbles enter as unsigned
+//    bytes code + 8 (one logic op per 4 codes; the + 8 is removed once per
+//    score with the head's 8 * sum(q) term), high nibbles as the signed bytes
+//    16 * code they already are in place (one mask).  The head dimension is
+//    permuted identically for q and K so that each thread reads one
+//    contiguous D/4-dimension span of a key row.
+//  * O^T += V^T (P * Vscale)^T on the fp16 tensor cores (m16n8k16): the A
+//    operand pairs one dimension of two consecutive keys, built in registers
+//    from the codes (a byte permute of the two keys' words, one three-input
+//    logic op forming an fp16 with the code in its mantissa, one exact fp16
+//    subtraction: int8 code, int4 code or 16 * code); the B operand is the
+//    fp16 probabilities times the key's V scale, taken directly from the score
+//    accumulators.  Rows of O^T are head dimensions, columns the group's
+//    heads.  The softmax denominator sums the unscaled probabilities.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace fqkv {
+namespace {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kQMax = 32639;  // |q * Qs| bound: hi = (v + 128) >> 8 stays in [-127, 127]
+
+template <int D, bool I4, bool G1>
+struct QtcCfg {
+  static constexpr int RB = I4 ? D / 2 : D;                   // bytes of one key row
+  static constexpr int KPW = (!I4 && D == 128) ? 16 : 32;      // keys per consumer warp per tile
+  static constexpr int TK = 4 * KPW;                           // keys per tile
+  static constexpr int kTileBytes = TK * RB;                   // K (or V) codes of one tile
+  static constexpr int kScaleBytes = 2 * TK + 32;              // 16B-aligned scale window
+  static constexpr int kStageRaw = 2 * kTileBytes + 2 * kScaleBytes;
+  static constexpr int kStageBytes = (kStageRaw + 1023) & ~1023;  // tiles stay 1024-aligned (swizzle atom)
+  static constexpr int kStages = (G1 || kStageBytes <= 10240) ? 4 : 3;
+  static constexpr int MH = G1 ? 1 : 4;                        // heads merged per epilogue pass
+  static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
+  static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
+  static constexpr size_t kMergeBytes = size_t(kConsumerWarps) * (2 * 8 + MH * D) * sizeof(float);
+  static constexpr size_t kSmemBytes = 1024 + kRingBytes + kBarBytes + kMergeBytes;
+  static_assert(TK == tile_keys(I4 ? KvFormat::I4Tc : KvFormat::I8Gqa, D), "planner tile size");
+  static_assert(!G1 || KPW % 16 == 0, "one-head variant works in 16-key blocks");
+};
+
+struct UnitCoord {
+  int b, kh, grp, s;
+};
+
+__device__ __forceinline__ UnitCoord decode_unit(const DecodeLaunch& a, int u) {
+  UnitCoord c;
+  c.grp = u % a.groups;
+  u /= a.groups;
+  c.s = u % a.S_eff;
+  u /= a.S_eff;
+  c.kh = u % a.Hkv;
+  c.b = u / a.Hkv;
+  return c;
+}
+
+// Byte offset of byte `b` of key row `row` inside a tile written by the TMA
+// copy with the swizzle of the row width (16-byte chunk index XOR the row's
+// position in the 1024-byte swizzle atom; the tile starts 1024-aligned).
+template <int RB>
+__device__ __forceinline__ uint32_t tile_off(int row, int b) {
+  const int c = b >> 4, w = b & 15;
+  if constexpr (RB == 128) return uint32_t(row * 128 + ((c ^ (row & 7)) << 4) + w);
+  else if constexpr (RB == 64) return uint32_t(row * 64 + ((c ^ ((row >> 1) & 3)) << 4) + w);
+  else return uint32_t(row * 32 + ((c ^ ((row >> 2) & 1)) << 4) + w);
+}
+
+// Loads N bytes (4, 8 or 16; N-aligned) from shared memory into words w[0..N/4).
+template <int N>
+__device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t* w) {
+  if constexpr (N == 16) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (N == 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+}
+
+// D(16x8, s32) += A(16x32, s8 or u8, row) * B(32x8, s8 or u8, col).
+template <bool kAUnsigned, bool kBUnsigned>
+__device__ __forceinline__ void mma_i8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  static_assert(!(kAUnsigned && kBUnsigned), "unused combination");
+  if constexpr (kBUnsigned) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else if constexpr (kAUnsigned) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// f(p) = B ? A : (p ^ A) bitwise, then an exact fp16x2 subtraction of A: with
+// p = {x.b, -, y.b, -} (byte b of the two keys' words) this turns the chosen
+// code field of each half into an exact fp16 (A holds 0x64 in the high byte of
+// each half, the field's sign-flip bit in the low byte; B marks constant bits).
+template <uint32_t A, uint32_t B>
+__device__ __forceinline__ uint32_t code_pair(uint32_t p) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x9c;" : "=r"(r) : "r"(p), "r"(A), "r"(B));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(r), "r"(A));
+  return r;
+}
+constexpr uint32_t kI8A = 0x64806480u, kI8B = 0xFF00FF00u;    // whole byte: int8 code
+constexpr uint32_t kLoA = 0x64086408u, kLoB = 0xFFF0FFF0u;    // low nibble: int4 code
+constexpr uint32_t kHiA = 0x64806480u, kHiB = 0xFF0FFF0Fu;    // high nibble: 16 * int4 code
+
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
+         (uint32_t(d) << 24);
+}
+
+// Position (0 .. D/4-1, within this thread's span of the head dimension) of
+// byte i (0..3) of operand half h (0: b0, 1: b1) of integer k-step kk.
+template <int D, bool I4>
+__device__ __forceinline__ constexpr int qk_dim(int kk, int h, int i) {
+  if constexpr (!I4) {
+    return 8 * kk + 4 * h + i;
+  } else {
+    constexpr int half = D / 64;  // low-nibble k-steps
+    return kk < half ? 16 * kk + 8 * h + 2 * i : 16 * (kk - half) + 8 * h + 2 * i + 1;
+  }
+}
+
+template <int D, bool I4, bool G1>
+__global__ void __launch_bounds__(kThreads, 3) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
+  using C = QtcCfg<D, I4, G1>;
+  constexpr int MH = C::MH;
+  constexpr int RB = C::RB;
+  constexpr int KPW = C::KPW;
+  constexpr int NJ = KPW / 8;          // score n-tiles (8 keys) per warp per tile
+  constexpr int KP = KPW / 16;         // P.V k-steps (16 keys) per warp per tile
+  constexpr int KS = D / 32;           // integer k-steps over the head dimension
+  constexpr int MT = D / 16;           // m-tiles of O^T
+  constexpr int KB = RB / 4;           // bytes of a K row this thread reads
+  constexpr int VB = RB / 8;           // bytes of a V row this thread reads
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::kRingBytes);
+  uint64_t* empty = full + C::kStages;
+  float* sm_m = reinterpret_cast<float*>(empty + C::kStages);
+  float* sm_l = sm_m + kConsumerWarps * 8;
+  float* sm_o = sm_l + kConsumerWarps * 8;
+  __shared__ int abort_flag;
+  __shared__ int stage_off[C::kStages][2];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtl wc{a.status, a.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kConsumerWarps && lane == 0) {
+    prefetch_tensormap(&a.tmK);
+    prefetch_tensormap(&a.tmV);
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
+
+  // ------------------------------------------------------------ producer
+  if (warp == kConsumerWarps) {
+    if (lane != 0 || a.debug_skip_loads) return;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+      const UnitCoord uc = decode_unit(a, u);
+      const int lo = uc.s * a.chunk;
+      const int hi = min(n_valid, lo + a.chunk);
+      const int z = uc.b * a.Hkv + uc.kh;
+      const __half* Ksr = static_cast<const __half*>(a.Ks) + size_t(z) * a.kv_stride;
+      const __half* Vsr = static_cast<const __half*>(a.Vs) + size_t(z) * a.kv_stride;
+      for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
+        const int st = it % C::kStages;
+        if (it >= C::kStages) {
+          if (*reinterpret_cast<volatile int*>(&abort_flag) ||
+              !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+        }
+        const int nk = min(C::TK, hi - k0);
+        const uintptr_t ka = reinterpret_cast<uintptr_t>(Ksr + k0);
+        const uintptr_t va = reinterpret_cast<uintptr_t>(Vsr + k0);
+        const uintptr_t ka0 = ka & ~uintptr_t(15), va0 = va & ~uintptr_t(15);
+        const uint32_t kwin = uint32_t(((ka + 2u * nk + 15u) & ~uintptr_t(15)) - ka0);
+        const uint32_t vwin = uint32_t(((va + 2u * nk + 15u) & ~uintptr_t(15)) - va0);
+        stage_off[st][0] = int(ka - ka0) >> 1;
+        stage_off[st][1] = int(va - va0) >> 1;
+        uint8_t* base = ring + size_t(st) * C::kStageBytes;
+        mbar_arrive_expect_tx(&full[st], 2 * C::kTileBytes + kwin + vwin);
+        tma_load_3d(base, &a.tmK, 0, k0, z, &full[st]);
+        tma_load_3d(base + C::kTileBytes, &a.tmV, 0, k0, z, &full[st]);
+        bulk_g2s(base + 2 * C::kTileBytes, reinterpret_cast<const void*>(ka0), kwin, &full[st]);
+        bulk_g2s(base + 2 * C::kTileBytes + C::kScaleBytes, reinterpret_cast<const void*>(va0), vwin, &full[st]);
+      }
+    }
+    if (!ok) {
+      for (int j = (it > C::kStages ? it - C::kStages : 0); j < it; ++j)
+        mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, wc, kDevTimeoutDrain);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  const int r0 = warp * KPW;
+  const float csc = a.sm_scale_log2;
+  // V rows are read in a t-parity-dependent key order where that avoids bank
+  // conflicts (rows of <= 64 bytes); the pair selector undoes the swap.
+  constexpr bool kSwap = RB <= 64;
+  const int vsw = kSwap ? (t & 1) : 0;
+  const uint32_t sel_base = vsw ? 0x0044u : 0x4400u;
+  bool alive = true;
+  int it = 0;
+
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+    const UnitCoord uc = decode_unit(a, u);
+    const int lo = uc.s * a.chunk;
+    const int hi = min(n_valid, lo + a.chunk);
+    const int h0 = uc.kh * a.G + uc.grp * a.GP;
+    const int gvalid = min(a.GP, a.G - uc.grp * a.GP);
+
+    // ---- q of head g, dimensions [t*D/4, (t+1)*D/4), as two int8 planes
+    uint32_t qa[KS][4];
+    float hf;       // sm_scale_log2 / Qs of head g (int4: / 16 more)
+    int qbias = 0;  // int4: 16 * 8 * sum of q * Qs over the low-nibble dimensions
+    {
+      float qf[D / 4];
+      if (G1 || g < gvalid) {
+        const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+            static_cast<const __half*>(a.q) + (size_t(uc.b) * a.Hq + h0 + (G1 ? 0 : g)) * D + t * (D / 4));
+#pragma unroll
+        for (int v = 0; v < D / 8; ++v) {
+          const uint32_t w = qrow[v];
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+          qf[2 * v] = f.x;
+          qf[2 * v + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < D / 4; ++i) qf[i] = 0.f;
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < D / 4; ++i) amax = fmaxf(amax, fabsf(qf[i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const float Qs = amax > 0.f ? float(kQMax) / amax : 0.f;
+      hf = amax > 0.f ? csc * (amax / float(kQMax)) * (I4 ? 0.0625f : 1.f) : 0.f;
+      int qi[D / 4];
+#pragma unroll
+      for (int i = 0; i < D / 4; ++i) qi[i] = __float2int_rn(qf[i] * Qs);
+      if constexpr (I4) {
+#pragma unroll
+        for (int i = 0; i < D / 4; i += 2) qbias += qi[i];
+        qbias += __shfl_xor_sync(0xffffffffu, qbias, 1);
+        qbias += __shfl_xor_sync(0xffffffffu, qbias, 2);
+        qbias *= 128;
+      }
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        int hv[8], lv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int v = qi[qk_dim<D, I4>(kk, i >> 2, i & 3)];
+          hv[i] = (v + 128) >> 8;
+          lv[i] = v - hv[i] * 256;
+        }
+        qa[kk][0] = pack_s8x4(hv[0], hv[1], hv[2], hv[3]);
+        qa[kk][1] = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
+        qa[kk][2] = pack_s8x4(hv[4], hv[5], hv[6], hv[7]);
+        qa[kk][3] = pack_s8x4(lv[4], lv[5], lv[6], lv[7]);
+        if constexpr (G1) {
+          // one head: q is the B operand of S^T = K Q^T, column 0 = hi plane, column 1 = lo plane
+          const uint32_t b0 = g == 0 ? qa[kk][0] : (g == 1 ? qa[kk][1] : 0u);
+          const uint32_t b1 = g == 0 ? qa[kk][2] : (g == 1 ? qa[kk][3] : 0u);
+          qa[kk][0] = b0;
+          qa[kk][1] = b1;
+        }
+      }
+    }
+
+    float o[MT][4];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
+      const int st = it % C::kStages;
+      if (alive) {
+        const bool ok = mbar_wait(&full[st], (it / C::kStages) & 1, wc, kDevTimeoutFull) &&
+                        !*reinterpret_cast<volatile int*>(&abort_flag);
+        alive = __all_sync(0xffffffffu, ok);
+        if (!alive && lane == 0) abort_flag = 1;
+      }
+      if (!alive) continue;
+      const uint8_t* kt = ring + size_t(st) * C::kStageBytes;
+      const uint8_t* vt = kt + C::kTileBytes;
+      const __half* kst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes) + stage_off[st][0];
+      const __half* vst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes + C::kScaleBytes) +
+                          stage_off[st][1];
+
+      // ---- scores of this warp's KPW keys (rows r0 ..) in integers.
+      // Several heads: S = Q K^T, n-tile j holds keys 8j + 2t + e of head g.
+      // One head (G1): S^T = K Q^T, m-tile j/2 holds keys 16(j/2) + g (+ 8) in
+      // lanes t == 0 (columns 0 / 1: hi / lo plane); sc[j][e] is key
+      // 16(j/2) + 8e + g for even j (odd j unused).
+      float sc[NJ][2];
+      bool valid[NJ][2];
+      float mx = -INFINITY;
+      if constexpr (G1) {
+#pragma unroll
+        for (int mt = 0; mt < KP; ++mt) {
+          uint32_t kw[2][KB / 4];  // keys r0 + 16mt + g and + 8
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+#pragma unroll
+            for (int c = 0; c < KB; c += 16)
+              lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + 16 * mt + 8 * e + g, t * KB + c), kw[e] + c / 4);
+          int acc[4] = {0, 0, 0, 0};
+          if constexpr (!I4) {
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+              const uint32_t af[4] = {kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1]};
+              mma_i8_16832<false, false>(acc, af, qa[kk][0], qa[kk][1]);
+            }
+          } else {
+            int acch[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int kk = 0; kk < KS / 2; ++kk) {
+              const uint32_t al[4] = {(kw[0][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu, (kw[1][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu,
+                                      (kw[0][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu,
+                                      (kw[1][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu};
+              const uint32_t ah[4] = {kw[0][2 * kk] & 0xF0F0F0F0u, kw[1][2 * kk] & 0xF0F0F0F0u,
+                                      kw[0][2 * kk + 1] & 0xF0F0F0F0u, kw[1][2 * kk + 1] & 0xF0F0F0F0u};
+              mma_i8_16832<true, false>(acc, al, qa[kk][0], qa[kk][1]);
+              mma_i8_16832<false, false>(acch, ah, qa[KS / 2 + kk][0], qa[KS / 2 + kk][1]);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] = 16 * acc[e] + acch[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = r0 + 16 * mt + 8 * e + g;
+            valid[2 * mt][e] = t == 0 && (k0 + key) < hi;
+            const int si = acc[2 * e] * 256 + acc[2 * e + 1] - (I4 ? qbias : 0);
+            const float s = float(si) * (__half2float(kst[key]) * hf);
+            sc[2 * mt][e] = valid[2 * mt][e] ? s : -INFINITY;
+            mx = fmaxf(mx, sc[2 * mt][e]);
+          }
+        }
+      } else {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        uint32_t kw[KB / 4];  // key r0 + 8j + g, bytes [t*KB, (t+1)*KB)
+#pragma unroll
+        for (int c = 0; c < KB; c += 16)
+          lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + 8 * j + g, t * KB + c), kw + c / 4);
+        int acc[4] = {0, 0, 0, 0};
+        if constexpr (!I4) {
+#pragma unroll
+          for (int kk = 0; kk < KS; ++kk) mma_i8_16832<false, false>(acc, qa[kk], kw[2 * kk], kw[2 * kk + 1]);
+        } else {
+          int acch[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int kk = 0; kk < KS / 2; ++kk) {
+            const uint32_t w0 = kw[2 * kk], w1 = kw[2 * kk + 1];
+            mma_i8_16832<false, true>(acc, qa[kk], (w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu);
+            mma_i8_16832<false, false>(acch, qa[KS / 2 + kk], w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u);
+          }
+          // 16 * (low sum - 8 sum q) + high sum (a multiple of 16); hf carries the 1/16
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] = 16 * acc[e] + acch[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = r0 + 8 * j + 2 * t + e;
+          valid[j][e] = (k0 + key) < hi;
+          const int si = I4 ? acc[e] * 256 + acc[2 + e] - qbias : acc[e] * 256 + acc[2 + e];
+          const float s = float(si) * (__half2float(kst[key]) * hf);
+          sc[j][e] = valid[j][e] ? s : -INFINITY;
+          mx = fmaxf(mx, sc[j][e]);
+        }
+      }
+      }
+      // ---- V fragments and scales, then release the stage
+      uint32_t vw[KP][4][VB / 4];  // per P.V k-step: keys {2t, 2t+1, 2t+8, 2t+9} (t-parity order)
+#pragma unroll
+      for (int kp = 0; kp < KP; ++kp)
+#pragma unroll
+        for (int kq = 0; kq < 4; ++kq) {
+          const int row = r0 + 16 * kp + 2 * t + ((kq & 1) ^ vsw) + 8 * (kq >> 1);
+          lds_words<VB>(vt + tile_off<RB>(row, g * VB), vw[kp][kq]);
+        }
+      float vs[NJ][2];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          if constexpr (G1) {
+            if (j % 2 == 0) vs[j][e] = __half2float(vst[r0 + 8 * j + 8 * e + g]);
+          } else {
+            vs[j][e] = __half2float(vst[r0 + 8 * j + 2 * t + e]);
+          }
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
+
+      // ---- online softmax per head g over the KPW keys
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if constexpr (G1) {  // one head: the maximum over every lane
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      }
+      const float m_new = fmaxf(m_run, mx);
+      if (__any_sync(0xffffffffu, m_new > m_run)) {
+        const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
+        l_run *= alpha;
+        m_run = m_new;
+        // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
+        const float a_lo = G1 ? alpha : __shfl_sync(0xffffffffu, alpha, (2 * t) * 4);
+        const float a_hi = G1 ? alpha : __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4);
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          o[i][0] *= a_lo;
+          o[i][1] *= a_hi;
+          o[i][2] *= a_lo;
+          o[i][3] *= a_hi;
+        }
+      }
+      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+      uint32_t pb[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        if (G1 && (j % 2) == 1) continue;
+        const float p0 = valid[j][0] ? ex2(sc[j][0] - mu) : 0.f;
+        const float p1 = valid[j][1] ? ex2(sc[j][1] - mu) : 0.f;
+        l_run += p0 + p1;
+        pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] : 0.f, valid[j][1] ? p1 * vs[j][1] : 0.f);
+      }
+      if constexpr (G1) {
+        // P^T fragments of each 16-key block: lane (g, t) needs keys 2t, 2t+1 (b0) and
+        // 2t+8, 2t+9 (b1); key k (k' = k + 8) sits in lane 4k, packed {k, k'}.
+#pragma unroll
+        for (int mt = 0; mt < KP; ++mt) {
+          const uint32_t s1 = __shfl_sync(0xffffffffu, pb[2 * mt], 8 * t);
+          const uint32_t s2 = __shfl_sync(0xffffffffu, pb[2 * mt], 8 * t + 4);
+          pb[2 * mt] = __byte_perm(s1, s2, 0x5410u);
+          pb[2 * mt + 1] = __byte_perm(s1, s2, 0x7632u);
+        }
+      }
+
+      // ---- O^T += V^T P^T
+#pragma unroll
+      for (int kp = 0; kp < KP; ++kp) {
+        if constexpr (!I4) {
+          // m-tile i rows g / g+8: dimensions g*D/8 + i / g*D/8 + MT + i (bytes i / MT + i)
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            const int w0 = i >> 2, w1 = (MT + i) >> 2;
+            const uint32_t s0 = uint32_t(i & 3) * 0x1111u + sel_base;
+            const uint32_t s1 = uint32_t((MT + i) & 3) * 0x1111u + sel_base;
+            const uint32_t a0 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w0], vw[kp][1][w0], s0));
+            const uint32_t a1 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w1], vw[kp][1][w1], s1));
+            const uint32_t a2 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w0], vw[kp][3][w0], s0));
+            const uint32_t a3 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1));
+            mma_16816(o[i], a0, a1, a2, a3, pb[2 * kp], pb[2 * kp + 1]);
+          }
+        } else {
+          // m-tile i < MT/2 rows g / g+8: dimensions g*D/8 + 2i / g*D/8 + MT + 2i (low nibbles of
+          // bytes i / MT/2 + i); m-tile MT/2 + i: the high nibbles (+1), accumulating 16 * V.
+#pragma unroll
+          for (int i = 0; i < MT / 2; ++i) {
+            const int w0 = i >> 2, w1 = (MT / 2 + i) >> 2;
+            const uint32_t s0 = uint32_t(i & 3) * 0x1111u + sel_base;
+            const uint32_t s1 = uint32_t((MT / 2 + i) & 3) * 0x1111u + sel_base;
+            const uint32_t p0 = __byte_perm(vw[kp][0][w0], vw[kp][1][w0], s0);
+            const uint32_t p1 = __byte_perm(vw[kp][0][w1], vw[kp][1][w1], s1);
+            const uint32_t p2 = __byte_perm(vw[kp][2][w0], vw[kp][3][w0], s0);
+            const uint32_t p3 = __byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1);
+            mma_16816(o[i], code_pair<kLoA, kLoB>(p0), code_pair<kLoA, kLoB>(p1), code_pair<kLoA, kLoB>(p2),
+                      code_pair<kLoA, kLoB>(p3), pb[2 * kp], pb[2 * kp + 1]);
+            mma_16816(o[MT / 2 + i], code_pair<kHiA, kHiB>(p0), code_pair<kHiA, kHiB>(p1),
+                      code_pair<kHiA, kHiB>(p2), code_pair<kHiA, kHiB>(p3), pb[2 * kp], pb[2 * kp + 1]);
+          }
+        }
+      }
+    }
+
+    // ---- unit epilogue: merge the 4 warps' (m, l, O) per head
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    if constexpr (G1) {  // one head: the keys were spread over every lane
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 4);
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
+    }
+    if (t == 0) {
+      sm_m[warp * 8 + g] = m_run;
+      sm_l[warp * 8 + g] = l_run;
+    }
+    const int ct = threadIdx.x;
+    const size_t row_base = size_t(uc.b) * a.Hq + h0;
+    for (int hp = 0; hp < gvalid; hp += MH) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int head = 2 * t + e;
+        const int gl = head - hp;
+        if (gl >= 0 && gl < MH && head < gvalid) {
+          // this thread's dimensions g*D/8 .. g*D/8 + D/8 - 1 of the head
+          float val[D / 8];
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            if constexpr (!I4) {
+              val[i] = o[i][e];
+              val[MT + i] = o[i][2 + e];
+            } else {
+              const int ii = i % (MT / 2), hb = i / (MT / 2);
+              const float f = hb ? 0.0625f : 1.f;
+              val[2 * ii + hb] = o[i][e] * f;
+              val[MT + 2 * ii + hb] = o[i][2 + e] * f;
+            }
+          }
+          float* dst = &sm_o[(warp * MH + gl) * D + g * (D / 8)];
+#pragma unroll
+          for (int i = 0; i < D / 8; i += 4)
+            *reinterpret_cast<float4*>(dst + i) = make_float4(val[i], val[i + 1], val[i + 2], val[i + 3]);
+        }
+      }
+      named_bar_sync(1, 32 * kConsumerWarps);
+      const int nh = min(MH, gvalid - hp);
+      for (int idx = ct; idx < nh * D; idx += 32 * kConsumerWarps) {
+        const int gl2 = idx / D, d = idx - gl2 * D;
+        const int gg = hp + gl2;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_m[w * 8 + gg]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float mw = sm_m[w * 8 + gg];
+          const float wt = (mw == -INFINITY) ? 0.f : ex2(mw - M);
+          L += wt * sm_l[w * 8 + gg];
+          O += wt * sm_o[(w * MH + gl2) * D + d];
+        }
+        const size_t row = row_base + gg;
+        if (a.S_eff == 1) {
+          static_cast<__half*>(a.out)[row * D + d] = __float2half_rn(O / L);
+        } else {
+          const size_t slot = row * a.S + uc.s;
+          if (d == 0) {
+            a.part_m[slot] = M;
+            a.part_l[slot] = L;
+          }
+          a.part_o[slot * D + d] = O;
+        }
+      }
+      named_bar_sync(1, 32 * kConsumerWarps);
+    }
+  }
+}
+
+template <int D, bool I4, bool G1>
+cudaError_t prepare_one(int* ctas_per_sm) {
+  const void* fn = reinterpret_cast<const void*>(&decode_qtc_kernel<D, I4, G1>);
+  const size_t smem = QtcCfg<D, I4, G1>::kSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, kThreads, smem);
+}
+
+template <int D, bool I4, bool G1>
+void launch_one(const DecodeLaunch& a, cudaStream_t stream) {
+  decode_qtc_kernel<D, I4, G1><<<a.grid, kThreads, QtcCfg<D, I4, G1>::kSmemBytes, stream>>>(a);
+}
+
+}  // namespace
+
+// int8 codes reach this kernel only with several query heads per KV head
+// (the planner's I8Gqa); int4 codes only with one (the C ABI requires
+// Hq == Hkv for int4) and D = 128, which runs the one-head (S^T) variant.
+cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm) {
+  if (int4) {
+    if (D != 128) return cudaErrorInvalidValue;
+    return prepare_one<128, true, true>(ctas_per_sm);
+  }
+  return D == 128 ? prepare_one<128, false, false>(ctas_per_sm) : prepare_one<64, false, false>(ctas_per_sm);
+}
+
+cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream) {
+  const bool i4 = a.fmt == KvFormat::I4Tc;
+  if (i4 != (a.GP == 1) || (i4 && a.D != 128)) return cudaErrorInvalidValue;
+  if (i4) {
+    launch_one<128, true, true>(a, stream);
+  } else {
+    if (a.D == 128) launch_one<128, false, false>(a, stream);
+    else launch_one<64, false, false>(a, stream);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace fqkv

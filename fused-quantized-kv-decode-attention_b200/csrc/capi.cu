@@ -59,7 +59,7 @@ struct DeviceState {
   int* status = nullptr;
   int occ_f16[2] = {0, 0};      // D = 64, 128
   int occ_q[2][2] = {{0, 0}, {0, 0}};  // [int4][D==128]
-  int occ_q8g[2] = {0, 0};      // int8 GQA, D = 64, 128
+  int occ_qtc[2][2] = {{0, 0}, {0, 0}};  // tensor-core quantized kernel [int4][D==128]
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -84,7 +84,8 @@ void init_device(DeviceState& ds, int dev) {
   for (int q = 0; q < 2 && e == cudaSuccess; ++q)
     for (int i = 0; i < 2 && e == cudaSuccess; ++i)
       e = fqkv::decode_kernel_prepare_quant(q == 1, i ? 128 : 64, &ds.occ_q[q][i]);
-  for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_q8gqa(i ? 128 : 64, &ds.occ_q8g[i]);
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_qtc(false, i ? 128 : 64, &ds.occ_qtc[0][i]);
+  if (e == cudaSuccess) e = fqkv::decode_kernel_prepare_qtc(true, 128, &ds.occ_qtc[1][1]);
   if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -133,19 +134,23 @@ int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64
   return FQKV_OK;
 }
 
-// int8 codes viewed as [B*Hkv][N][D] bytes with `stride` keys between
-// consecutive (b, kv head) rows; box = one 64-key tile of whole rows, swizzled
-// at the row width (128 B for D = 128, 64 B for D = 64).
-int make_kv_map_i8(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t D, int64_t stride) {
+// Quantized codes viewed as [B*Hkv][N][rb] bytes (rb = 128, 64 or 32 bytes
+// per key row) with `stride` keys between consecutive (b, kv head) rows; box =
+// one tile of `tile` whole rows, swizzled at the row width.
+int make_kv_map_codes(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t rb, int64_t stride,
+                      int tile) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
-  const cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(BH)};
-  const cuuint64_t strides[2] = {cuuint64_t(D), cuuint64_t(stride) * cuuint64_t(D)};
-  const cuuint32_t box[3] = {cuuint32_t(D), 64, 1};
+  const cuuint64_t dims[3] = {cuuint64_t(rb), cuuint64_t(N), cuuint64_t(BH)};
+  const cuuint64_t strides[2] = {cuuint64_t(rb), cuuint64_t(stride) * cuuint64_t(rb)};
+  const cuuint32_t box[3] = {cuuint32_t(rb), cuuint32_t(tile), 1};
   const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = rb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : rb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                           : CU_TENSOR_MAP_SWIZZLE_32B;
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
   return FQKV_OK;
 }
@@ -169,7 +174,7 @@ void carve_partials(DecodeLaunch& a, void* ws, int64_t rows) {
 int ctas_per_sm(const DeviceState& ds, KvFormat f, int D) {
   const int i = D == 128 ? 1 : 0;
   if (f == KvFormat::F16) return std::max(1, ds.occ_f16[i]);
-  if (f == KvFormat::I8Gqa) return std::max(1, ds.occ_q8g[i]);
+  if (f == KvFormat::I8Gqa || f == KvFormat::I4Tc) return std::max(1, ds.occ_qtc[f == KvFormat::I4Tc ? 1 : 0][i]);
   return std::max(1, ds.occ_q[f == KvFormat::I4 ? 1 : 0][i]);
 }
 
@@ -179,7 +184,13 @@ int ctas_per_sm(const DeviceState& ds, KvFormat f, int D) {
 // can hold when `limit_ws`.
 void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_bytes, bool limit_ws) {
   // int8 codes shared by several query heads go to the tensor-core GQA kernel.
+  // int8 codes shared by several query heads, and int4 codes with D = 128, go
+  // to the tensor-core quantized kernel (measured on B200: int4 D = 128 817 vs
+  // 871 us on the CUDA-core kernel at config 3; at D = 64 the CUDA-core kernel
+  // is faster, 463 vs 578 us, its per-key softmax work being shared by fewer
+  // dimensions on the tensor-core path).
   if (a.fmt == KvFormat::I8 && a.Hq != a.Hkv) a.fmt = KvFormat::I8Gqa;
+  if (a.fmt == KvFormat::I4 && a.D == 128) a.fmt = KvFormat::I4Tc;
   a.G = a.Hq / a.Hkv;
   a.GP = std::min(a.G, 8);
   a.groups = (a.G + a.GP - 1) / a.GP;
@@ -246,7 +257,7 @@ int check_D(int64_t D) {
 
 int launch(DecodeLaunch& a, cudaStream_t stream) {
   cudaError_t e = a.fmt == KvFormat::F16     ? fqkv::launch_decode_f16(a, stream)
-                  : a.fmt == KvFormat::I8Gqa ? fqkv::launch_decode_q8gqa(a, stream)
+                  : (a.fmt == KvFormat::I8Gqa || a.fmt == KvFormat::I4Tc) ? fqkv::launch_decode_qtc(a, stream)
                                              : fqkv::launch_decode_quant(a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "launch");
   if (a.S_eff > 1) {
@@ -295,9 +306,11 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
   if (a.fmt == KvFormat::F16) {
     if (int rc = make_kv_map(&a.tmK, K, B * Hkv, N, D, kv_stride)) return rc;
     if (int rc = make_kv_map(&a.tmV, V, B * Hkv, N, D, kv_stride)) return rc;
-  } else if (a.fmt == KvFormat::I8Gqa) {
-    if (int rc = make_kv_map_i8(&a.tmK, K, B * Hkv, N, D, kv_stride)) return rc;
-    if (int rc = make_kv_map_i8(&a.tmV, V, B * Hkv, N, D, kv_stride)) return rc;
+  } else if (a.fmt == KvFormat::I8Gqa || a.fmt == KvFormat::I4Tc) {
+    const int64_t rb = fqkv::kv_row_bytes(a.fmt, D);
+    const int tk = fqkv::tile_keys(a.fmt, D);
+    if (int rc = make_kv_map_codes(&a.tmK, K, B * Hkv, N, rb, kv_stride, tk)) return rc;
+    if (int rc = make_kv_map_codes(&a.tmV, V, B * Hkv, N, rb, kv_stride, tk)) return rc;
   }
   return launch(a, reinterpret_cast<cudaStream_t>(stream));
 }

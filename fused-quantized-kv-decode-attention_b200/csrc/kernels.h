@@ -9,19 +9,25 @@
 
 namespace fqkv {
 
-// I8Gqa: int8 codes with more than one query head per KV head (tensor-core
-// kernel); chosen by the planner, never passed in by callers.
-enum class KvFormat : int { F16 = 0, I8 = 1, I4 = 2, I8Gqa = 3 };
+// I8Gqa / I4Tc: int8 codes with more than one query head per KV head, and
+// int4 codes, on the tensor-core quantized kernel (attn_qtc.cu); chosen by the
+// planner, never passed in by callers.
+enum class KvFormat : int { F16 = 0, I8 = 1, I4 = 2, I8Gqa = 3, I4Tc = 4 };
 
 // Bytes of one key row of K (or V) in HBM.
-inline int64_t kv_row_bytes(KvFormat f, int64_t D) {
+constexpr int64_t kv_row_bytes(KvFormat f, int64_t D) {
   return f == KvFormat::F16 ? 2 * D : ((f == KvFormat::I8 || f == KvFormat::I8Gqa) ? D : D / 2);
 }
 
 // Keys per pipeline stage (one tile).  The fp16 kernel uses 64-key tiles of
-// 128-byte swizzled rows; the quantized kernel uses 16 KiB tiles of K (and V).
-inline int tile_keys(KvFormat f, int64_t D) {
-  return (f == KvFormat::F16 || f == KvFormat::I8Gqa) ? 64 : static_cast<int>(16384 / kv_row_bytes(f, D));
+// 128-byte swizzled rows; the tensor-core quantized kernel 64 (int8, D = 128)
+// or 128 keys (16 or 32 per consumer warp); the CUDA-core quantized kernel
+// 16 KiB tiles of K (and V).
+constexpr int tile_keys(KvFormat f, int64_t D) {
+  return f == KvFormat::F16     ? 64
+         : f == KvFormat::I8Gqa ? (D == 128 ? 64 : 128)
+         : f == KvFormat::I4Tc  ? 128
+                                : static_cast<int>(16384 / kv_row_bytes(f, D));
 }
 
 // One decode-attention launch, in the library's canonical form:
@@ -71,8 +77,8 @@ cudaError_t launch_decode_f16(const DecodeLaunch& a, cudaStream_t stream);
 KernelShape decode_kernel_shape_quant(bool int4, int D);
 cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm);
 cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream);
-cudaError_t decode_kernel_prepare_q8gqa(int D, int* ctas_per_sm);
-cudaError_t launch_decode_q8gqa(const DecodeLaunch& a, cudaStream_t stream);
+cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm);
+cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream);
 
 // Log-sum-exp merge of the S_eff partials of every row into out (fp16),
 // chained to the preceding launch by programmatic dependent launch.
