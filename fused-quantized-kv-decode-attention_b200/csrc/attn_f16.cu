@@ -108,6 +108,9 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   __syncthreads();
   // Let the combine kernel (if any) get scheduled while this grid streams.
   pdl_launch_dependents();
+  // Launched with programmatic serialization: wait for the previous kernel on
+  // the stream (and its memory) before reading any input.
+  pdl_wait_primary();
   // Valid keys: the launch's N, or the device-side length of a growing cache.
   const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
 
@@ -312,7 +315,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
 
 template <int D>
 static cudaError_t launch_f16(const DecodeLaunch& a, cudaStream_t stream) {
-  decode_f16_kernel<D><<<a.grid, kThreads, F16Cfg<D>::kSmemBytes, stream>>>(a);
+  launch_pdl(decode_f16_kernel<D>, dim3(a.grid), dim3(kThreads), F16Cfg<D>::kSmemBytes, stream, a);
   return cudaGetLastError();
 }
 

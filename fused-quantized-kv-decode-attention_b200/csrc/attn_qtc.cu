@@ -208,6 +208,9 @@ __global__ void __launch_bounds__(kThreads, 3) decode_qtc_kernel(const __grid_co
   }
   __syncthreads();
   pdl_launch_dependents();
+  // Launched with programmatic serialization: wait for the previous kernel on
+  // the stream (and its memory) before reading any input.
+  pdl_wait_primary();
   const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
 
   // ------------------------------------------------------------ producer
@@ -627,7 +630,7 @@ cudaError_t prepare_one(int* ctas_per_sm) {
 
 template <int D, bool I4, bool G1>
 void launch_one(const DecodeLaunch& a, cudaStream_t stream) {
-  decode_qtc_kernel<D, I4, G1><<<a.grid, kThreads, QtcCfg<D, I4, G1>::kSmemBytes, stream>>>(a);
+  launch_pdl(decode_qtc_kernel<D, I4, G1>, dim3(a.grid), dim3(kThreads), QtcCfg<D, I4, G1>::kSmemBytes, stream, a);
 }
 
 }  // namespace

@@ -125,6 +125,9 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
   __syncthreads();
   pdl_launch_dependents();
   // Valid keys: the launch's N, or the device-side length of a growing cache.
+  // Launched with programmatic serialization: wait for the previous kernel on
+  // the stream (and its memory) before reading any input.
+  pdl_wait_primary();
   const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
 
   // ------------------------------------------------------------ producer
@@ -448,11 +451,11 @@ cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream) {
   const bool int4 = a.fmt == KvFormat::I4;
   const size_t smem = quant_smem(int4, a.D);
   if (int4) {
-    if (a.D == 128) decode_quant_kernel<true, 128><<<a.grid, kThreads, smem, stream>>>(a);
-    else decode_quant_kernel<true, 64><<<a.grid, kThreads, smem, stream>>>(a);
+    if (a.D == 128) launch_pdl(decode_quant_kernel<true, 128>, dim3(a.grid), dim3(kThreads), smem, stream, a);
+    else launch_pdl(decode_quant_kernel<true, 64>, dim3(a.grid), dim3(kThreads), smem, stream, a);
   } else {
-    if (a.D == 128) decode_quant_kernel<false, 128><<<a.grid, kThreads, smem, stream>>>(a);
-    else decode_quant_kernel<false, 64><<<a.grid, kThreads, smem, stream>>>(a);
+    if (a.D == 128) launch_pdl(decode_quant_kernel<false, 128>, dim3(a.grid), dim3(kThreads), smem, stream, a);
+    else launch_pdl(decode_quant_kernel<false, 64>, dim3(a.grid), dim3(kThreads), smem, stream, a);
   }
   return cudaGetLastError();
 }

@@ -27,6 +27,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
                                                                   const float* __restrict__ pl,
                                                                   const float* __restrict__ po,
                                                                   __half* __restrict__ out, int D, int S, int S_eff) {
+  pdl_launch_dependents();  // the next decode kernel may be scheduled now; it waits for this grid
   pdl_wait_primary();
   __shared__ float red[kCombineThreads / 32];
   __shared__ float sm_o[kCombineThreads];

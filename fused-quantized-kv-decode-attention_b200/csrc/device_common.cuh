@@ -12,8 +12,10 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 
 namespace fqkv {
 
@@ -114,6 +116,26 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait_primary() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Host side: launch `kernel` with programmatic stream serialization, so its
+// CTAs may be scheduled while the previous kernel on the stream finishes; the
+// kernel must execute pdl_wait_primary() before touching global memory that
+// earlier kernels may write.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- named barrier
