@@ -537,7 +537,7 @@ def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
     dist.broadcast(ids, src=0)
     ev = lambda: torch.cuda.Event(enable_timing=True)
     dec = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, kv_dtype=args.kv,
-                                          tp_group=dist.group.WORLD)
+                                          tp_group=dist.group.WORLD, tp_fused=args.tp_gather == "fused")
     dec.prefill(ids)
     dec.capture()
     best_pre, best_dec = 1e30, 1e30
@@ -582,8 +582,10 @@ def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
                 "dtype": f"bf16 weights, {args.kv} KV", "data": "synthetic",
                 "config": {"workload": w["desc"], "global_batch": B, "prompt": P, "gen": T, "head_dim": 64,
                            "parallelism": f"tp{world} by KV head (q/k/v rows, KV cache, attention sharded; "
-                                          "NCCL all_gather_into_tensor of attention outputs per layer; "
-                                          "o_proj, MLP, LM head replicated)",
+                                          + ("NCCL all_gather_into_tensor" if args.tp_gather == "nccl" else
+                                             "attention kernel stores its output to every rank over NVLink + "
+                                             "bounded arrival wait")
+                                          + " per layer; o_proj, MLP, LM head replicated)",
                            "kv_cache": f"{args.kv}, static, graph-captured decode step (collectives in the graph)"},
                 "decode_tok_s": round(decode_tps, 2), "e2e_generate_tok_s": round(e2e_tps, 2),
                 "prefill_ms": round(best_pre, 3), "decode_ms_per_step": round(best_dec / (T - 1), 4),
@@ -614,6 +616,8 @@ def main() -> int:
                     help="override the per-GPU batch (sequences; 32 heads each for the row workloads)")
     ap.add_argument("--seq-len", type=int, default=None, help="override the context length N")
     ap.add_argument("--kv", default="fp16", choices=["fp16", "int8"], help="KV cache type of the llama workload")
+    ap.add_argument("--tp-gather", default="nccl", choices=["nccl", "fused"],
+                    help="llama workload under torchrun: NCCL all-gather or the attention kernel's fused NVLink gather")
     ap.add_argument("--head-dim", type=int, default=None, choices=[64, 128], help="override head_dim D")
     ap.add_argument("--no-clock-hold", action="store_true",
                     help="do not keep the GPU loaded for clock sampling after the timed region (profiling runs)")

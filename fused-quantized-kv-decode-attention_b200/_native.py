@@ -19,6 +19,7 @@ ERR_MISALIGNED = 2
 ERR_CUDA = 3
 ERR_UNSUPPORTED_DEVICE = 4
 ERR_DEVICE_TIMEOUT = 5
+ERR_PEER = 6
 
 KV_F16, KV_INT8, KV_INT4 = 0, 1, 2
 
@@ -26,6 +27,15 @@ _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _SZ = ctypes.c_size_t
 _INT = ctypes.c_int
+
+TP_MAX_RANKS = 8
+
+
+class TpOut(ctypes.Structure):
+    """fqkv_tp_out_t: where a tensor-parallel decode call sends its output."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("dst_offset", ctypes.c_int64),
+                ("dst", ctypes.c_void_p * TP_MAX_RANKS), ("counters", ctypes.c_void_p * TP_MAX_RANKS)]
+
 
 # name -> (restype, argtypes); the same set of symbols the header declares.
 SIGNATURES = {
@@ -49,6 +59,14 @@ SIGNATURES = {
     "fqkv_gqa_sk_fast_static_scratch": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "fqkv_quantize_int8_per_token": (_INT, [_P, _P, _P, _I64, _I64, _P]),
     "fqkv_quantize_int4_per_token": (_INT, [_P, _P, _P, _I64, _I64, _P]),
+    "fqkv_decode_attn_kvcache_tp": (_INT, [ctypes.c_int32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P,
+                                           _P, _SZ, ctypes.POINTER(TpOut), _P]),
+    "fqkv_tp_arrivals": (_I64, [ctypes.c_int32, _I64, _I64, _I64, _I64, _I64, _SZ]),
+    "fqkv_tp_wait": (_INT, [_P, ctypes.c_int32, ctypes.c_uint64, _P, _P]),
+    "fqkv_ipc_alloc": (_INT, [_SZ, ctypes.POINTER(_P), _P]),
+    "fqkv_ipc_open": (_INT, [_P, ctypes.POINTER(_P)]),
+    "fqkv_ipc_close": (_INT, [_P]),
+    "fqkv_ipc_free": (_INT, [_P]),
 }
 
 

@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
         }
         const size_t row = row_base + gg;
         if (a.S_eff == 1) {
-          static_cast<__half*>(a.out)[row * D + d] = __float2half_rn(O / L);
+          store_out(a, row * D + d, O / L);
         } else {
           const size_t slot = row * a.S + uc.s;
           if (d == 0) {
@@ -308,6 +308,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
       }
       named_bar_sync(1, 32 * kConsumerWarps);
     }
+    if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
   }
 }
 

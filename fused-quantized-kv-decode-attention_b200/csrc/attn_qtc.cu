@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_qtc_kernel(const __grid_co
         }
         const size_t row = row_base + gg;
         if (a.S_eff == 1) {
-          static_cast<__half*>(a.out)[row * D + d] = __float2half_rn(O / L);
+          store_out(a, row * D + d, O / L);
         } else {
           const size_t slot = row * a.S + uc.s;
           if (d == 0) {
@@ -616,6 +616,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_qtc_kernel(const __grid_co
       }
       named_bar_sync(1, 32 * kConsumerWarps);
     }
+    if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
   }
 }
 

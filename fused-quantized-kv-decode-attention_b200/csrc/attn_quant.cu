@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         O += wt * sm_o[w * D + ct];
       }
       if (a.S_eff == 1) {
-        static_cast<__half*>(a.out)[size_t(r) * D + ct] = __float2half_rn(O / L);
+        store_out(a, size_t(r) * D + ct, O / L);
       } else {
         const size_t slot = size_t(r) * a.S + s;
         if (ct == 0) {
@@ -417,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       }
     }
     named_bar_sync(1, 32 * kConsumerWarps);
+    if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
   }
 }
 

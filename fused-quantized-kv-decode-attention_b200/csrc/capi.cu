@@ -272,7 +272,8 @@ int launch(DecodeLaunch& a, cudaStream_t stream) {
 // the cache capacity for a KV cache); n_dev: optional device-side valid length.
 int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const void* Ks, const void* Vs, void* o,
                int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, void* ws, size_t ws_bytes,
-               fqkv_stream_t stream, int64_t kv_stride = -1, const int* n_dev = nullptr) {
+               fqkv_stream_t stream, int64_t kv_stride = -1, const int* n_dev = nullptr,
+               const fqkv_tp_out_t* tp = nullptr) {
   if (kv_stride < 0) kv_stride = N;
   if (int rc = check_D(D)) return rc;
   if (B < 0 || Hq < 1 || Hkv < 1 || N < 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "negative or zero size");
@@ -281,7 +282,7 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
     return fail(FQKV_ERR_INVALID_ARGUMENT, "int4 KV supports one query head per KV head (Hq == Hkv)");
   if (B == 0) return FQKV_OK;
   if (N == 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "N: the KV cache is empty (softmax over zero keys)");
-  if (!q || !K || !V || !o || (fmt != KvFormat::F16 && (!Ks || !Vs)))
+  if (!q || !K || !V || (!o && !tp) || (fmt != KvFormat::F16 && (!Ks || !Vs)))
     return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
   if (B * Hkv > INT32_MAX || N > INT32_MAX || B * Hq > INT32_MAX)
     return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the 32-bit index range");
@@ -297,6 +298,15 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
   a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
   a.kv_stride = int(kv_stride);
   a.n_dev = n_dev;
+  if (tp) {
+    a.tp.world = tp->world;
+    a.tp.rank = tp->rank;
+    a.tp.dst_off = tp->dst_offset;
+    for (int p = 0; p < tp->world; ++p) {
+      a.tp.dst[p] = static_cast<__half_raw*>(tp->dst[p]);
+      a.tp.cnt[p] = tp->counters[p];
+    }
+  }
   plan(a, *ds, 0, ws ? ws_bytes : 0, true);
   if (int64_t(a.B) * a.Hkv * a.groups * a.S_eff > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "too many work units");
   if (a.S_eff > 1) {
@@ -514,6 +524,111 @@ int fqkv_quantize_int8_per_token(const void* X, void* codes, void* scales, int64
 int fqkv_quantize_int4_per_token(const void* X, void* packed, void* scales, int64_t rows, int64_t D,
                                  fqkv_stream_t stream) {
   return run_quantize(true, X, packed, scales, rows, D, stream);
+}
+
+
+// ------------------------------------------------------------------ tensor-parallel decode
+int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K, const void* V, const void* Ks,
+                                const void* Vs, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
+                                int64_t n_host, const int32_t* seq_len_dev, void* workspace, size_t workspace_bytes,
+                                const fqkv_tp_out_t* tp, fqkv_stream_t stream) {
+  if (kv_format != FQKV_KV_F16 && kv_format != FQKV_KV_INT8)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "kv_format: tensor-parallel decode takes FQKV_KV_F16 or FQKV_KV_INT8");
+  if (!tp) return fail(FQKV_ERR_INVALID_ARGUMENT, "tp: null tensor-parallel output descriptor");
+  if (tp->world < 2 || tp->world > FQKV_TP_MAX_RANKS || tp->rank < 0 || tp->rank >= tp->world)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "tp: world %d / rank %d outside 2..%d", int(tp->world), int(tp->rank),
+                FQKV_TP_MAX_RANKS);
+  if (tp->dst_offset < 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "tp: negative dst_offset");
+  for (int p = 0; p < tp->world; ++p) {
+    if (!tp->dst[p] || !tp->counters[p]) return fail(FQKV_ERR_INVALID_ARGUMENT, "tp: null buffer of rank %d", p);
+    if (!aligned(tp->dst[p], 16) || !aligned(tp->counters[p], 8))
+      return fail(FQKV_ERR_MISALIGNED, "tp: buffer of rank %d misaligned (dst 16 B, counters 8 B)", p);
+  }
+  if (max_len < 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "max_len must be >= 1");
+  if (!seq_len_dev && (n_host < 1 || n_host > max_len))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "n: valid length %lld outside [1, max_len=%lld]", (long long)n_host,
+                (long long)max_len);
+  if (max_len > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the 32-bit index range");
+  if (seq_len_dev && !aligned(seq_len_dev, 4)) return fail(FQKV_ERR_MISALIGNED, "seq_len must be 4-byte aligned");
+  const int64_t N = seq_len_dev ? max_len : n_host;
+  const KvFormat fmt = kv_format == FQKV_KV_F16 ? KvFormat::F16 : KvFormat::I8;
+  return run_decode(fmt, q, K, V, Ks, Vs, nullptr, B, Hq, Hkv, N, D, workspace, workspace_bytes, stream, max_len,
+                    reinterpret_cast<const int*>(seq_len_dev), tp);
+}
+
+int64_t fqkv_tp_arrivals(int32_t kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
+                         size_t workspace_bytes) {
+  if ((kv_format != FQKV_KV_F16 && kv_format != FQKV_KV_INT8) || B < 1 || Hq < 1 || Hkv < 1 || max_len < 1 ||
+      (D != 64 && D != 128) || Hq % Hkv != 0)
+    return -1;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != FQKV_OK) return -1;
+  DecodeLaunch a{};
+  a.fmt = kv_format == FQKV_KV_F16 ? KvFormat::F16 : KvFormat::I8;
+  a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(max_len); a.D = int(D);
+  plan(a, *ds, 0, workspace_bytes, true);
+  // unsplit: one arrival per unit (decode kernel epilogue); split: one per row (combine)
+  return a.S_eff == 1 ? int64_t(a.units) : B * Hq;
+}
+
+int fqkv_tp_wait(const unsigned long long* counters, int32_t world, uint64_t per_call, unsigned long long* sequence,
+                 fqkv_stream_t stream) {
+  if (!counters || !sequence) return fail(FQKV_ERR_INVALID_ARGUMENT, "null counters / sequence");
+  if (world < 1 || world > FQKV_TP_MAX_RANKS)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "world %d outside 1..%d", int(world), FQKV_TP_MAX_RANKS);
+  if (!aligned(counters, 8) || !aligned(sequence, 8)) return fail(FQKV_ERR_MISALIGNED, "counters / sequence: 8 B");
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  cudaError_t e = fqkv::launch_tp_wait(counters, int(world), per_call, sequence, ds->status, g_timeout_ns.load(),
+                                       reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tp wait launch");
+  return FQKV_OK;
+}
+
+int fqkv_ipc_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes == 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "ipc_alloc: bad argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "ipc_alloc: cudaMalloc");
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "ipc_alloc: zero fill / handle");
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return FQKV_OK;
+}
+
+int fqkv_ipc_open(const void* ipc_handle, void** dev_ptr) {
+  if (!dev_ptr || !ipc_handle) return fail(FQKV_ERR_INVALID_ARGUMENT, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FQKV_ERR_PEER, "ipc_open: %s", cudaGetErrorString(e));
+  }
+  *dev_ptr = p;
+  return FQKV_OK;
+}
+
+int fqkv_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) return fail(FQKV_ERR_INVALID_ARGUMENT, "ipc_close: null pointer");
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "ipc_close");
+  return FQKV_OK;
+}
+
+int fqkv_ipc_free(void* dev_ptr) {
+  if (!dev_ptr) return fail(FQKV_ERR_INVALID_ARGUMENT, "ipc_free: null pointer");
+  cudaError_t e = cudaFree(dev_ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "ipc_free");
+  return FQKV_OK;
 }
 
 }  // extern "C"

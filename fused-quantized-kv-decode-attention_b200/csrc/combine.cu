@@ -26,7 +26,8 @@ constexpr int kCombineThreads = 512;
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ pm,
                                                                   const float* __restrict__ pl,
                                                                   const float* __restrict__ po,
-                                                                  __half* __restrict__ out, int D, int S, int S_eff) {
+                                                                  __half* __restrict__ out, int D, int S, int S_eff,
+                                                                  const TpOut tp) {
   pdl_launch_dependents();  // the next decode kernel may be scheduled now; it waits for this grid
   pdl_wait_primary();
   __shared__ float red[kCombineThreads / 32];
@@ -66,7 +67,18 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
       Ls += sm_l[g];
       Os += sm_o[g * D + d];
     }
-    out[row * D + d] = __float2half_rn(Os / Ls);
+    const __half_raw h = __half_raw(__float2half_rn(Os / Ls));
+    if (tp.world == 0) {
+      reinterpret_cast<__half_raw*>(out)[row * D + d] = h;
+    } else {
+      for (int p = 0; p < tp.world; ++p) tp.dst[p][tp.dst_off + row * D + d] = h;
+    }
+  }
+  if (tp.world != 0) {  // tensor-parallel output: one arrival per row on every rank
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0)
+      for (int p = 0; p < tp.world; ++p) atomicAdd_system(tp.cnt[p] + tp.rank, 1ull);
   }
 }
 
@@ -86,7 +98,7 @@ cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream) {
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, combine_kernel, static_cast<const float*>(a.part_m),
                             static_cast<const float*>(a.part_l), static_cast<const float*>(a.part_o),
-                            static_cast<__half*>(a.out), a.D, a.S, a.S_eff);
+                            static_cast<__half*>(a.out), a.D, a.S, a.S_eff, a.tp);
 }
 
 }  // namespace fqkv

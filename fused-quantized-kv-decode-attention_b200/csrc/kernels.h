@@ -5,6 +5,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace fqkv {
@@ -29,6 +30,18 @@ constexpr int tile_keys(KvFormat f, int64_t D) {
          : f == KvFormat::I4Tc  ? 128
                                 : static_cast<int>(16384 / kv_row_bytes(f, D));
 }
+
+// Tensor-parallel output: instead of `out`, the final fp16 output is stored at
+// dst[p] + dst_off (+ the row offset) for every rank p < world, and each unit
+// of output counts one arrival on cnt[p][rank].  world == 0: plain output.
+constexpr int kTpMaxRanks = 8;
+struct TpOut {
+  int world;
+  int rank;
+  long long dst_off;
+  __half_raw* dst[kTpMaxRanks];
+  unsigned long long* cnt[kTpMaxRanks];
+};
 
 // One decode-attention launch, in the library's canonical form:
 //   q [B, Hq, D] fp16, K/V [B, Hkv, N, *], (scales [B, Hkv, N] fp16),
@@ -62,7 +75,32 @@ struct DecodeLaunch {
   unsigned long long timeout_ns;
   int debug_skip_loads;                // test hook: producer issues nothing
   CUtensorMap tmK, tmV;                // tiled K/V maps (fp16, and int8 GQA)
+  TpOut tp;                            // tensor-parallel output (tp.world == 0: write `out`)
 };
+
+#ifdef __CUDACC__
+// Final fp16 output element `idx` (row * D + d) of a launch.
+__device__ __forceinline__ void store_out(const DecodeLaunch& a, size_t idx, float v) {
+  const __half_raw h = __half_raw(__float2half_rn(v));
+  if (a.tp.world == 0) {
+    static_cast<__half_raw*>(a.out)[idx] = h;
+  } else {
+    for (int p = 0; p < a.tp.world; ++p) a.tp.dst[p][a.tp.dst_off + idx] = h;
+  }
+}
+
+// After the `nthreads` threads of named barrier `bar` have stored one unit of
+// final output: with tensor-parallel output, make the stores visible to the
+// other GPUs, then count the unit on every rank.
+__device__ __forceinline__ void signal_out(const DecodeLaunch& a, int tid, int bar, int nthreads) {
+  if (a.tp.world == 0) return;
+  __threadfence_system();
+  asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory");
+  if (tid == 0) {
+    for (int p = 0; p < a.tp.world; ++p) atomicAdd_system(a.tp.cnt[p] + a.tp.rank, 1ull);
+  }
+}
+#endif
 
 // Kernel resource queries and launches, per KV format (attn_f16.cu,
 // attn_quant.cu).  *_prepare sets the dynamic shared-memory opt-in for the
@@ -79,6 +117,10 @@ cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm);
 cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream);
 cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm);
 cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream);
+// Tensor-parallel arrival wait (tp.cu).
+cudaError_t launch_tp_wait(const unsigned long long* counters, int world, unsigned long long per_call,
+                           unsigned long long* sequence, int* status, unsigned long long timeout_ns,
+                           cudaStream_t stream);
 
 // Log-sum-exp merge of the S_eff partials of every row into out (fp16),
 // chained to the preceding launch by programmatic dependent launch.

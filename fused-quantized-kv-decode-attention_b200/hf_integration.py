@@ -24,7 +24,11 @@
   KV cache and the attention of Hkv/world KV heads (and their query heads),
   and the per-rank attention outputs are all-gathered every layer -- inside
   the captured graph -- before the replicated output projection, MLP and LM
-  head, so every rank produces the same tokens.
+  head, so every rank produces the same tokens.  The gather is NCCL's
+  ``all_gather_into_tensor``, or with ``tp_fused=True`` part of the attention
+  kernel itself: it stores its output into every rank's receive buffer over
+  NVLink and a bounded wait kernel precedes the output projection
+  (:mod:`tp_exchange`).
 """
 from __future__ import annotations
 
@@ -33,7 +37,7 @@ import math
 import torch
 import torch.nn.functional as F
 
-from . import ops
+from . import _native, ops
 from . import sharding
 
 HOOK_NAME = "fqkv_decode"
@@ -81,7 +85,7 @@ class GraphDecoder:
     """
 
     def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False, kv_dtype: str = "fp16",
-                 tp_group=None):
+                 tp_group=None, tp_fused: bool = False):
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
         self._rope = apply_rotary_pos_emb
@@ -130,6 +134,14 @@ class GraphDecoder:
                            if self.world > 1 else None)
         nb = ops.workspace_bytes(kv_dtype, batch, self.Hq_l, self.Hkv_l, max_len, self.D)
         self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev) if nb else None
+        # fused all-gather: receive buffers / counters of every rank mapped here
+        self.xchg = None
+        if tp_fused and self.world > 1:
+            from .tp_exchange import PeerExchange
+            self.xchg = PeerExchange(tp_group, self.L, batch, self.Hq_l, self.D, dev)
+            fmt = _native.KV_F16 if kv_dtype == "fp16" else _native.KV_INT8
+            self.xchg.set_plan(fmt, batch, self.Hq_l, self.Hkv_l, max_len, self.D,
+                               self.ws.numel() if self.ws is not None else 0)
         self.keep_logits = keep_logits
         self.logits = torch.zeros(batch, cfg.vocab_size, dtype=torch.float32, device=dev) if keep_logits else None
         self.graph = None
@@ -205,6 +217,12 @@ class GraphDecoder:
             ops.quantize_into_cache(v.to(torch.float16).contiguous(), self.vc[li], self.vs[li], p)
 
     def _attend(self, li: int, q: torch.Tensor) -> None:
+        if self.xchg is not None:  # output goes to every rank's receive buffer of layer li
+            ks = self.ks[li] if self.kv_dtype == "int8" else None
+            vs = self.vs[li] if self.kv_dtype == "int8" else None
+            ops.decode_attn_kvcache_tp(q, self.kc[li], self.vc[li], self.nlen, self.xchg.tp_out[li], ks, vs,
+                                       workspace=self.ws)
+            return
         if self.kv_dtype == "fp16":
             ops.decode_attn_gqa_kvcache(q, self.kc[li], self.vc[li], self.nlen, out=self.attn_out, workspace=self.ws)
         else:
@@ -226,7 +244,11 @@ class GraphDecoder:
             q, k = self._rope(q, k, cos, sin)
             self._append(li, k, v, self.pos)
             self._attend(li, q[:, :, 0].to(torch.float16).contiguous())
-            o = self._heads(self.attn_out.view(B, 1, self.Hq_l, self.D), self.gather_buf)
+            if self.xchg is not None:
+                self.xchg.wait()
+                o = self.xchg.gathered(li).permute(1, 0, 2, 3).reshape(B, 1, self.Hq * self.D)
+            else:
+                o = self._heads(self.attn_out.view(B, 1, self.Hq_l, self.D), self.gather_buf)
             h = h + attn.o_proj(o.to(h.dtype))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         logits = self.model.lm_head(m.norm(h))[:, 0].float()
@@ -262,10 +284,14 @@ class GraphDecoder:
         torch.cuda.synchronize(self.dev)
 
     def release(self) -> None:
-        """Drop the captured graph (required before destroying a process group whose collectives it holds)."""
+        """Drop the captured graph (required before destroying a process group whose collectives it holds)
+        and, with the fused all-gather, the exchange memory (collective: every rank calls it)."""
         if self.graph is not None:
             self.graph.reset()
             self.graph = None
+        if self.xchg is not None:
+            self.xchg.close()
+            self.xchg = None
 
     @torch.no_grad()
     def step(self) -> None:

@@ -14,6 +14,8 @@ be built.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _native
@@ -422,6 +424,53 @@ def _quantize(op: str, X: torch.Tensor, int4: bool):
         rc = fn(X.data_ptr(), codes.data_ptr(), scales.data_ptr(), rows, D, _stream(dev))
     _native.check(rc, f"launch: {op}")
     return codes, scales
+
+
+def decode_attn_kvcache_tp(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, seq_len, tp,
+                           Ks: torch.Tensor | None = None, Vs: torch.Tensor | None = None,
+                           workspace: torch.Tensor | None = None) -> None:
+    """Tensor-parallel decode step over this rank's KV cache, output sent to every rank.
+
+    As :func:`decode_attn_gqa_kvcache` (fp16 cache, ``Ks``/``Vs`` None) or
+    :func:`decode_attn_gqa_int8_kvcache` (int8 codes with their scales), but the
+    [B, Hq, D] output is stored into every rank's receive buffer described by
+    ``tp`` (a ``_native.TpOut``; see :class:`tp_exchange.PeerExchange`) and counted
+    on every rank's arrival counters.  Returns nothing: the gathered outputs are
+    read after :func:`tp_wait`.
+    """
+    op = "decode_attn_kvcache_tp"
+    if Ks is None:
+        dev = _require_cuda(op, q, K, V)
+        _require_dtype(op, "fp16", torch.float16, q=q, K=K, V=V)
+        _require_contig(op, q=q, K=K, V=V)
+        if q.dim() != 3 or K.dim() != 4:
+            _fail(op, "shape", "q must be [B, Hq, D] and K [B, Hkv, max_len, D]")
+        B, Hq, D = q.shape
+        _, Hkv, max_len, _ = K.shape
+        _require_D(op, D)
+        _require_shape(op, "K", K, (B, Hkv, max_len, D))
+        _require_shape(op, "V", V, (B, Hkv, max_len, D))
+        if Hkv < 1 or Hq % Hkv:
+            _fail(op, "shape", f"Hq ({Hq}) must be a multiple of Hkv ({Hkv})")
+        fmt = _native.KV_F16
+    else:
+        dev, B, Hq, Hkv, max_len, D = _check_int8_gqa(op, q, K, V, Ks, Vs)
+        fmt = _native.KV_INT8
+    n_host, n_ptr, _ = _seq_len_args(op, seq_len, dev, max_len)
+    nb = workspace.numel() if workspace is not None else 0
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_decode_attn_kvcache_tp(
+            fmt, q.data_ptr(), K.data_ptr(), V.data_ptr(), Ks.data_ptr() if Ks is not None else None,
+            Vs.data_ptr() if Vs is not None else None, B, Hq, Hkv, max_len, D, n_host, n_ptr,
+            workspace.data_ptr() if workspace is not None else None, nb, ctypes.byref(tp), _stream(dev))
+    _native.check(rc, f"launch: {op}")
+
+
+def tp_wait(counters_ptr: int, world: int, per_call: int, sequence_ptr: int, device: torch.device) -> None:
+    """Enqueue the bounded wait for every rank's tensor-parallel outputs of one call (see the C ABI)."""
+    with _DeviceGuard(device):
+        rc = _native.lib().fqkv_tp_wait(counters_ptr, world, per_call, sequence_ptr, _stream(device))
+    _native.check(rc, "launch: tp_wait")
 
 
 def qpt(X: torch.Tensor):

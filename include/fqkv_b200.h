@@ -3,8 +3,9 @@
  * library (libfqkv_b200.so).
  *
  * Every entry point takes raw device pointers, sizes and a CUDA stream, returns
- * an fqkv_status_t, never allocates device memory, and launches asynchronously
- * on `stream` (pass NULL for the legacy default stream).  All launches are
+ * an fqkv_status_t, never allocates device memory (the fqkv_ipc_* setup
+ * functions of the tensor-parallel exchange are the only exception), and
+ * launches asynchronously on `stream` (pass NULL for the legacy default stream).  All launches are
  * stream-ordered; the entry points whose buffers all come from the caller are
  * capturable in a CUDA graph.  On failure,
  * fqkv_last_error() returns a message for the calling thread.
@@ -42,7 +43,8 @@ typedef enum fqkv_status_t {
   FQKV_ERR_MISALIGNED = 2,       /* a pointer violates the alignment rules above */
   FQKV_ERR_CUDA = 3,             /* CUDA runtime / launch error (see fqkv_last_error) */
   FQKV_ERR_UNSUPPORTED_DEVICE = 4, /* current device is not sm_100 */
-  FQKV_ERR_DEVICE_TIMEOUT = 5    /* a bounded in-kernel wait gave up (see fqkv_device_status) */
+  FQKV_ERR_DEVICE_TIMEOUT = 5,   /* a bounded in-kernel wait gave up (see fqkv_device_status) */
+  FQKV_ERR_PEER = 6              /* tensor-parallel exchange: IPC mapping of a peer's buffer failed */
 } fqkv_status_t;
 
 /* KV storage formats for the workspace query. */
@@ -56,7 +58,8 @@ const char* fqkv_version(void);
 
 /* Reads (and, if clear != 0, resets) the in-kernel status word of the current
  * device: 0 = healthy, otherwise the code of the first bounded wait that gave
- * up (61 tile never arrived, 62 stage never freed, 63 copy drain failed).
+ * up (61 tile never arrived, 62 stage never freed, 63 copy drain failed,
+ * 64 a tensor-parallel peer's attention outputs never arrived).
  * Synchronizes with the device. */
 int fqkv_device_status(int* status_out, int clear);
 
@@ -196,6 +199,61 @@ int fqkv_quantize_int8_into_cache(const void* X, void* codes, void* scales, int6
 int fqkv_quantize_int4_into_cache(const void* X, void* packed, void* scales, int64_t groups, int64_t T,
                                   int64_t D, int64_t cap, int64_t pos_host, const int32_t* pos_dev,
                                   fqkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Tensor-parallel decode: attention fused with the all-gather of its outputs.
+ * No counterpart in the reference: its tensor-parallel end-to-end config
+ * all-gathers the attention outputs of every layer with NCCL.  Here the decode
+ * kernel that produces a rank's attention output (or the split-K combine, when
+ * the plan splits) stores it straight into every rank's receive buffer over
+ * NVLink and then counts one arrival per output unit on every rank's counter
+ * slot for this rank (system-scope atomic after a system fence);
+ * fqkv_tp_wait, enqueued before the consumer of the gathered outputs, waits
+ * (bounded) until every rank's arrivals for this call are in.  Counters only
+ * grow, so a whole decode step, collectives included, replays from one CUDA
+ * graph.  Receive buffers and counters live in memory from fqkv_ipc_alloc,
+ * mapped on the other ranks with fqkv_ipc_open. */
+#define FQKV_TP_MAX_RANKS 8
+
+typedef struct fqkv_tp_out {
+  int32_t world;       /* number of ranks (2 .. FQKV_TP_MAX_RANKS) */
+  int32_t rank;        /* this rank: its slice of every receive buffer, its counter slot */
+  int64_t dst_offset;  /* f16 elements from each dst[] to this rank's [B, Hq_local, D] slice */
+  void* dst[FQKV_TP_MAX_RANKS];                      /* receive buffers of ranks 0..world-1, mapped here */
+  unsigned long long* counters[FQKV_TP_MAX_RANKS];   /* arrival counters [world] of ranks 0..world-1, mapped here */
+} fqkv_tp_out_t;
+
+/* fqkv_decode_attn_gqa_kvcache (kv_format FQKV_KV_F16: Ks = Vs = NULL) or
+ * fqkv_decode_attn_gqa_int8_kvcache (FQKV_KV_INT8) for this rank's heads, with
+ * the output sent to every rank as described above instead of to an `o`
+ * tensor.  Each receive buffer must hold dst_offset + B*Hq*D f16 (16-byte
+ * aligned); every rank must make the same calls with the same sizes. */
+int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K, const void* V, const void* Ks,
+                                const void* Vs, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
+                                int64_t n_host, const int32_t* seq_len_dev, void* workspace, size_t workspace_bytes,
+                                const fqkv_tp_out_t* tp, fqkv_stream_t stream);
+
+/* Arrivals one call of fqkv_decode_attn_kvcache_tp with these sizes (and the
+ * same workspace size) counts on each counter slot; the waiter's per_call. */
+int64_t fqkv_tp_arrivals(int32_t kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
+                         size_t workspace_bytes);
+
+/* Waits on `stream` until counters[r] >= (*sequence + 1) * per_call for every
+ * rank r < world (counters and sequence: this rank's own device memory), then
+ * increments *sequence.  Bounded: after the wait limit it records status 64 in
+ * the device status word and returns (the call still completes). */
+int fqkv_tp_wait(const unsigned long long* counters, int32_t world, uint64_t per_call,
+                 unsigned long long* sequence, fqkv_stream_t stream);
+
+/* Exchange memory: `bytes` of zero-filled device memory on the current device
+ * and its 64-byte IPC handle (to send to the other ranks of the node). */
+int fqkv_ipc_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+/* Maps another rank's exchange memory (its 64-byte handle) on the current device. */
+int fqkv_ipc_open(const void* ipc_handle, void** dev_ptr);
+/* Unmaps memory from fqkv_ipc_open. */
+int fqkv_ipc_close(void* dev_ptr);
+/* Frees memory from fqkv_ipc_alloc (after every rank has closed its mapping). */
+int fqkv_ipc_free(void* dev_ptr);
 
 #ifdef __cplusplus
 }

@@ -2,12 +2,16 @@
 
 Each rank keeps the q/k/v rows, the KV cache and the attention of half the KV
 heads; the attention outputs are all-gathered every layer inside the captured
-decode step.  Checked against the 1-GPU decoder on the same weights: every rank
-emits the same tokens, and the per-step logits agree to fp16 rounding of the
-sharded projections.  Skipped with fewer than 2 GPUs.
+decode step, by NCCL or fused into the attention kernel (NVLink stores into
+every rank's receive buffer plus a bounded arrival wait).  Checked against
+the 1-GPU decoder on the same weights: every rank emits the same tokens, and
+the per-step logits agree to fp16 rounding of the sharded projections; the
+fused and NCCL gathers give bit-identical logits.  Skipped with fewer than 2
+GPUs.
 """
 from __future__ import annotations
 
+import ctypes
 import datetime
 import os
 
@@ -62,10 +66,17 @@ def _worker(rank: int, world: int, port: int, kv_dtype: str, q):
                                               tp_group=dist.group.WORLD)
         tp_logits, tp_tok = _decode(dec, ids, T)
         dec.release()
+        fused = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True, kv_dtype=kv_dtype,
+                                                tp_group=dist.group.WORLD, tp_fused=True)
+        fu_logits, fu_tok = _decode(fused, ids, T)
+        fused.release()
+        st = torch.zeros(1, dtype=torch.int32)
+        pkg.native.lib().fqkv_device_status(ctypes.cast(st.data_ptr(), ctypes.POINTER(ctypes.c_int)), 1)
         gathered = [torch.empty_like(tp_tok) for _ in range(world)]
         dist.all_gather(gathered, tp_tok)
         same = all(torch.equal(g, tp_tok) for g in gathered)
-        res = {"rank": rank, "same_tokens_all_ranks": same}
+        res = {"rank": rank, "same_tokens_all_ranks": same, "fused_equal": bool(torch.equal(fu_logits, tp_logits)),
+               "fused_tokens_equal": bool(torch.equal(fu_tok, tp_tok)), "device_status": int(st.item())}
         if rank == 0:
             one = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True, kv_dtype=kv_dtype)
             one_logits, one_tok = _decode(one, ids, T)
@@ -100,5 +111,7 @@ def test_tensor_parallel_decoder_matches_one_gpu(kv_dtype):
         assert p.exitcode == 0
     r0 = next(r for r in results if r["rank"] == 0)
     assert all(r["same_tokens_all_ranks"] for r in results)
+    assert all(r["fused_equal"] and r["fused_tokens_equal"] for r in results)
+    assert all(r["device_status"] == 0 for r in results)
     assert r0["match"] >= 0.75
     assert r0["max_logit_diff"] <= 0.02 + 0.01 * r0["logit_scale"]
