@@ -10,7 +10,7 @@ The directory name is not a Python identifier, so import it with
 """
 from __future__ import annotations
 
-from . import _native, hf_integration, sharding
+from . import _native, hf_integration, ops, sharding, tp_exchange
 from .ops import (
     decode_attn_fp16_mw,
     decode_attn_gqa,
@@ -19,10 +19,12 @@ from .ops import (
     decode_attn_gqa_kvcache,
     decode_attn_int4,
     decode_attn_int8_mw,
+    decode_attn_kvcache_tp,
     gqa_sk_fast,
     qpt,
     quant_int4_per_token,
     quantize_into_cache,
+    tp_wait,
     workspace_bytes,
 )
 
@@ -35,6 +37,8 @@ __all__ = [
     "decode_attn_gqa_int8",
     "decode_attn_gqa_int8_kvcache",
     "quantize_into_cache",
+    "decode_attn_kvcache_tp",
+    "tp_wait",
     "gqa_sk_fast",
     "qpt",
     "quant_int4_per_token",
@@ -44,6 +48,8 @@ __all__ = [
     "native",
     "sharding",
     "hf_integration",
+    "tp_exchange",
+    "ops",
 ]
 
 native = _native

@@ -53,3 +53,27 @@ def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
     ref = oatt.decode_attention_gqa(q.cpu().numpy(), K.cpu().numpy(), V.cpu().numpy())
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-3, rtol=1e-2)
     assert _status(fqkv) == 0
+
+
+def test_tensor_parallel_wait_times_out_on_missing_peer(fqkv):
+    """The arrival wait of the fused tensor-parallel gather is bounded: counters
+    that nothing advances (a peer that never sends) end the wait after the limit
+    with status 64; the sequence still advances and a later wait whose counts are
+    in returns clean."""
+    lib = fqkv.native.lib()
+    counters = torch.zeros(2, dtype=torch.int64, device="cuda")     # this rank's slots for 2 ranks
+    seq = torch.zeros(1, dtype=torch.int64, device="cuda")
+    dev = counters.device
+    assert _status(fqkv, clear=1) == 0
+    lib.fqkv_set_wait_timeout_ms(50)
+    try:
+        fqkv.ops.tp_wait(counters.data_ptr(), 2, 3, seq.data_ptr(), dev)   # needs 3 arrivals per rank
+        torch.cuda.synchronize()
+    finally:
+        lib.fqkv_set_wait_timeout_ms(2000)
+    assert _status(fqkv, clear=1) == 64
+    assert int(seq.item()) == 1
+    counters.fill_(6)                                                  # calls 1 and 2 complete
+    fqkv.ops.tp_wait(counters.data_ptr(), 2, 3, seq.data_ptr(), dev)
+    torch.cuda.synchronize()
+    assert _status(fqkv) == 0 and int(seq.item()) == 2
