@@ -306,3 +306,26 @@ def test_gqa_int8_extreme_q_and_scales(fqkv):
     Vq, Vs = fqkv.qpt(V.cuda())
     out = fqkv.decode_attn_gqa_int8(q.cuda(), Kq, Vq, Ks, Vs)
     _close(out, _int8_gqa_ref(q.numpy(), K.numpy(), V.numpy()))
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_int4_extreme_q_and_scales(fqkv, D):
+    """int4 with a dominant q element (the fixed-point q planes and the +8 nibble
+    bias correction at their extremes), a zero q row, zero tokens and a token
+    with a 100x larger scale."""
+    R, N = 6, 700
+    q = _randn(R, D, seed=101)
+    q[:, 3] = -60.0
+    q[2] = 0.0
+    q[4] *= 30.0
+    K, V = _randn(R, N, D, seed=102), _randn(R, N, D, seed=103)
+    K[:, 10] = 0.0
+    V[:, 20] = 0.0
+    V[1, 33] *= 100.0
+    K[3, 44] *= 100.0
+    Kp, Ks = fqkv.quant_int4_per_token(K.cuda())
+    Vp, Vs = fqkv.quant_int4_per_token(V.cuda())
+    out = fqkv.decode_attn_int4(q.cuda(), Kp, Vp, Ks, Vs, 8)
+    Kd = oq.dequantize_int4(Kp.cpu().numpy(), Ks.cpu().numpy())
+    Vd = oq.dequantize_int4(Vp.cpu().numpy(), Vs.cpu().numpy())
+    _close(out, oatt.decode_attention(q.numpy(), Kd, Vd))
