@@ -24,6 +24,7 @@ from .ops import (
     qpt,
     quant_int4_per_token,
     quantize_into_cache,
+    rope_qkv_append,
     tp_wait,
     workspace_bytes,
 )
@@ -37,6 +38,7 @@ __all__ = [
     "decode_attn_gqa_int8",
     "decode_attn_gqa_int8_kvcache",
     "quantize_into_cache",
+    "rope_qkv_append",
     "decode_attn_kvcache_tp",
     "tp_wait",
     "gqa_sk_fast",

@@ -527,6 +527,41 @@ int fqkv_quantize_int4_per_token(const void* X, void* packed, void* scales, int6
 }
 
 
+// ------------------------------------------------------------------ fused RoPE + append
+int fqkv_rope_qkv_append(int32_t kv_format, int32_t model_dtype, const void* qkv, int64_t qkv_row_stride,
+                         const void* cos_table, const void* sin_table, int64_t table_rows, int64_t pos_host,
+                         const int32_t* pos_dev, void* q_out, void* k_cache, void* v_cache, void* k_scales,
+                         void* v_scales, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t cap,
+                         fqkv_stream_t stream) {
+  if (kv_format != FQKV_KV_F16 && kv_format != FQKV_KV_INT8)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "kv_format: FQKV_KV_F16 or FQKV_KV_INT8");
+  if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (int rc = check_D(D)) return rc;
+  if (B < 0 || Hq < 1 || Hkv < 1 || cap < 1 || table_rows < 1 || Hq % Hkv != 0)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "bad sizes (B=%lld Hq=%lld Hkv=%lld cap=%lld table_rows=%lld)",
+                (long long)B, (long long)Hq, (long long)Hkv, (long long)cap, (long long)table_rows);
+  if (qkv_row_stride < (Hq + 2 * Hkv) * D)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "qkv_row_stride %lld < (Hq + 2 Hkv) D", (long long)qkv_row_stride);
+  if (!pos_dev && (pos_host < 0 || pos_host >= table_rows))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "pos %lld outside the rotary table (%lld rows)", (long long)pos_host,
+                (long long)table_rows);
+  if (B == 0) return FQKV_OK;
+  if (!qkv || !cos_table || !sin_table || !q_out || !k_cache || !v_cache ||
+      (kv_format == FQKV_KV_INT8 && (!k_scales || !v_scales)))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(qkv, 2) || !aligned(q_out, 2) || !aligned(k_cache, 2) || !aligned(v_cache, 2) ||
+      !aligned(cos_table, 2) || !aligned(sin_table, 2) || (pos_dev && !aligned(pos_dev, 4)))
+    return fail(FQKV_ERR_MISALIGNED, "rope_qkv_append: misaligned pointer");
+  if (B * (Hq + 2 * Hkv) > INT32_MAX / 32 || B * Hkv * cap > INT32_MAX * int64_t(64))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the index range");
+  cudaError_t e = fqkv::launch_rope_append(model_dtype == 1, kv_format == FQKV_KV_INT8, qkv, qkv_row_stride, cos_table,
+                                           sin_table, table_rows, pos_host, reinterpret_cast<const int*>(pos_dev), q_out,
+                                           k_cache, v_cache, k_scales, v_scales, int(B), int(Hq), int(Hkv), int(D),
+                                           int(cap), reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope_qkv_append launch");
+  return FQKV_OK;
+}
+
 // ------------------------------------------------------------------ tensor-parallel decode
 int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K, const void* V, const void* Ks,
                                 const void* Vs, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,

@@ -117,6 +117,11 @@ cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm);
 cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream);
 cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm);
 cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream);
+// Fused RoPE + q cast + KV append (quantize.cu).
+cudaError_t launch_rope_append(bool bf16, bool int8_cache, const void* qkv, int64_t qkv_stride, const void* cos_t,
+                               const void* sin_t, int64_t table_rows, int64_t pos_host, const int* pos_dev,
+                               void* q_out, void* k_cache, void* v_cache, void* k_scales, void* v_scales, int B,
+                               int Hq, int Hkv, int D, int cap, cudaStream_t stream);
 // Tensor-parallel arrival wait (tp.cu).
 cudaError_t launch_tp_wait(const unsigned long long* counters, int world, unsigned long long per_call,
                            unsigned long long* sequence, int* status, unsigned long long timeout_ns,

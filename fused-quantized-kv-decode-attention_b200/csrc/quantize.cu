@@ -16,6 +16,7 @@
 // does not depend on fast-math flags.
 //
 // HBM-bound: one 16-byte load per lane (8 elements), D/8 lanes per token.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -161,7 +162,141 @@ cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- RoPE + append
+// One decode step of a Llama-style attention block after its (fused) q/k/v
+// projection: rotary embedding of q and k exactly as transformers'
+// apply_rotary_pos_emb evaluates it in the model dtype T (fp16 or bf16):
+//   out_i = T( T(x_i * cos_i) + T(rot_i * sin_i) ),  rot = cat(-x[D/2:], x[:D/2])
+// (each product is exact in fp32 and rounded once to T, the sum is an fp32
+// add rounded to T -- torch's elementwise ops on T tensors), then the cast to
+// fp16 the attention takes (x.to(float16)).  q goes to q_out [B, Hq, D] fp16;
+// k (rotated) and v go to the cache at position pos: fp16 rows, or the
+// reference quantizer's int8 codes + fp16 scale of the fp16 row (bit-exact with
+// qpt).  One warp per head row; lane l holds elements l + 32m, so every
+// rotate-half partner (i, i + D/2) is in the same lane.
+template <typename T>
+__device__ __forceinline__ float to_f(T x);
+template <>
+__device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <typename T>
+__device__ __forceinline__ float round_t(float x);
+template <>
+__device__ __forceinline__ float round_t<__half>(float x) { return __half2float(__float2half_rn(x)); }
+template <>
+__device__ __forceinline__ float round_t<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+struct RopeAppendArgs {
+  const void* qkv;
+  int64_t qkv_stride;        // elements between consecutive sequences' rows
+  const void* cos_t;         // [table_rows, D] in T
+  const void* sin_t;
+  int64_t table_rows;
+  int64_t pos_host;
+  const int* pos_dev;
+  __half* q_out;             // [B, Hq, D]
+  void* k_cache;             // [B, Hkv, cap, D] f16 or i8
+  void* v_cache;
+  __half* k_scales;          // [B, Hkv, cap] (int8 cache)
+  __half* v_scales;
+  int B, Hq, Hkv, cap;
+};
+
+template <typename T, int D, bool kInt8>
+__global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendArgs a) {
+  constexpr int M = D / 32;  // elements per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int heads = a.Hq + 2 * a.Hkv;
+  if (row >= int64_t(a.B) * heads) return;
+  const int b = int(row / heads), slot = int(row % heads);
+  const int64_t pos = a.pos_dev ? int64_t(*a.pos_dev) : a.pos_host;
+  if (pos < 0 || pos >= a.table_rows) return;
+  const T* x = static_cast<const T*>(a.qkv) + b * a.qkv_stride + int64_t(slot) * D;
+  float v[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) v[m] = to_f<T>(x[lane + 32 * m]);
+  const bool is_v = slot >= a.Hq + a.Hkv;
+  if (!is_v) {
+    const T* c = static_cast<const T*>(a.cos_t) + pos * D;
+    const T* sn = static_cast<const T*>(a.sin_t) + pos * D;
+    float r[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int i = lane + 32 * m;
+      const float rot = m < M / 2 ? -v[m + M / 2] : v[m - M / 2];
+      r[m] = round_t<T>(round_t<T>(v[m] * to_f<T>(c[i])) + round_t<T>(rot * to_f<T>(sn[i])));
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) v[m] = r[m];
+  }
+  __half h[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) h[m] = __float2half_rn(v[m]);  // x.to(float16)
+  if (slot < a.Hq) {
+    __half* q = a.q_out + (int64_t(b) * a.Hq + slot) * D;
+#pragma unroll
+    for (int m = 0; m < M; ++m) q[lane + 32 * m] = h[m];
+    return;
+  }
+  if (pos >= a.cap) return;
+  const int kh = is_v ? slot - a.Hq - a.Hkv : slot - a.Hq;
+  const int64_t crow = (int64_t(b) * a.Hkv + kh) * a.cap + pos;
+  if constexpr (!kInt8) {
+    __half* dst = static_cast<__half*>(is_v ? a.v_cache : a.k_cache) + crow * D;
+#pragma unroll
+    for (int m = 0; m < M; ++m) dst[lane + 32 * m] = h[m];
+  } else {
+    float amax = 0.f;
+    bool nan = false;
+    float xf[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      xf[m] = __half2float(h[m]);
+      nan |= isnan(xf[m]);
+      amax = fmaxf(amax, fabsf(xf[m]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      nan |= __shfl_xor_sync(0xffffffffu, int(nan), off) != 0;
+    }
+    const __half sh = quant_scale<127>(amax, nan);
+    const float sc = __half2float(sh);
+    int8_t* dst = static_cast<int8_t*>(is_v ? a.v_cache : a.k_cache) + crow * D;
+#pragma unroll
+    for (int m = 0; m < M; ++m) dst[lane + 32 * m] = int8_t(quant_code<127>(xf[m], sc));
+    if (lane == 0) (is_v ? a.v_scales : a.k_scales)[crow] = sh;
+  }
+}
+
+template <typename T, int D>
+void launch_rope_append_t(const RopeAppendArgs& a, bool int8, cudaStream_t stream) {
+  const int64_t rows = int64_t(a.B) * (a.Hq + 2 * a.Hkv);
+  const unsigned blocks = unsigned((rows * 32 + 255) / 256);
+  if (int8) rope_append_kernel<T, D, true><<<blocks, 256, 0, stream>>>(a);
+  else rope_append_kernel<T, D, false><<<blocks, 256, 0, stream>>>(a);
+}
+
 }  // namespace
+
+cudaError_t launch_rope_append(bool bf16, bool int8_cache, const void* qkv, int64_t qkv_stride, const void* cos_t,
+                               const void* sin_t, int64_t table_rows, int64_t pos_host, const int* pos_dev,
+                               void* q_out, void* k_cache, void* v_cache, void* k_scales, void* v_scales, int B,
+                               int Hq, int Hkv, int D, int cap, cudaStream_t stream) {
+  const RopeAppendArgs a{qkv,     qkv_stride, cos_t,   sin_t,   table_rows,
+                         pos_host, pos_dev,   static_cast<__half*>(q_out), k_cache, v_cache,
+                         static_cast<__half*>(k_scales), static_cast<__half*>(v_scales), B, Hq, Hkv, cap};
+  if (bf16) {
+    if (D == 128) launch_rope_append_t<__nv_bfloat16, 128>(a, int8_cache, stream);
+    else launch_rope_append_t<__nv_bfloat16, 64>(a, int8_cache, stream);
+  } else {
+    if (D == 128) launch_rope_append_t<__half, 128>(a, int8_cache, stream);
+    else launch_rope_append_t<__half, 64>(a, int8_cache, stream);
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
                                  int D, int64_t cap, int64_t pos_host, const int* pos_dev, cudaStream_t stream) {

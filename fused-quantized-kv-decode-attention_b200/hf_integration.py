@@ -17,7 +17,12 @@
   (:func:`ops.decode_attn_gqa_kvcache` / :func:`ops.decode_attn_gqa_int8_kvcache`),
   MLP, LM head and argmax -- is captured once in a CUDA graph and replayed
   per token, so a step costs no Python or launch overhead.  The model's
-  weights may be bf16 or fp16; attention runs on the fp16 / int8 cache.
+  weights may be bf16 or fp16; attention runs on the fp16 / int8 cache.  With
+  the default rotary embedding the step's attention prologue is two kernels:
+  one GEMM against the concatenated q/k/v weights and
+  :func:`ops.rope_qkv_append` (RoPE of q and k from tables the model's own
+  rotary module filled, q cast to fp16, k/v appended or quantized into the
+  cache -- bit-exact with the HF ops it replaces, ``fused_rope=False``).
 
   With ``tp_group`` (a ``torch.distributed`` group, NCCL on GPUs) the decoder
   is tensor-parallel by KV head: each rank keeps the q/k/v projection rows, the
@@ -85,7 +90,7 @@ class GraphDecoder:
     """
 
     def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False, kv_dtype: str = "fp16",
-                 tp_group=None, tp_fused: bool = False):
+                 tp_group=None, tp_fused: bool = False, fused_rope: bool = True):
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
         self._rope = apply_rotary_pos_emb
@@ -144,6 +149,28 @@ class GraphDecoder:
                                self.ws.numel() if self.ws is not None else 0)
         self.keep_logits = keep_logits
         self.logits = torch.zeros(batch, cfg.vocab_size, dtype=torch.float32, device=dev) if keep_logits else None
+        # fused attention prologue: concatenated q/k/v weights + rotary tables of every position
+        rot = model.model.rotary_emb
+        self.rope_fused = (fused_rope and self.dtype in (torch.float16, torch.bfloat16) and self.D in (64, 128)
+                           and getattr(rot, "rope_type", "default") == "default"
+                           and float(getattr(rot, "attention_scaling", 1.0)) == 1.0)
+        if self.rope_fused:
+            self.wqkv, self.bqkv = [], []
+            for li, layer in enumerate(model.model.layers):
+                if self.proj is not None:
+                    parts = self.proj[li]
+                else:
+                    a = layer.self_attn
+                    parts = [(lin.weight.detach(), lin.bias.detach() if lin.bias is not None else None)
+                             for lin in (a.q_proj, a.k_proj, a.v_proj)]
+                self.wqkv.append(torch.cat([w for w, _ in parts], 0).contiguous())
+                self.bqkv.append(torch.cat([b for _, b in parts], 0).contiguous() if parts[0][1] is not None else None)
+            with torch.no_grad():
+                cos, sin = rot(torch.empty(1, 1, 1, dtype=self.dtype, device=dev),
+                               torch.arange(max_len, device=dev)[None])
+            self.cos_t = cos[0].contiguous()
+            self.sin_t = sin[0].contiguous()
+            self.q16 = torch.empty(batch, self.Hq_l, self.D, dtype=torch.float16, device=dev)
         self.graph = None
         self.prompt_len = 0
 
@@ -235,15 +262,24 @@ class GraphDecoder:
         m = self.model.model
         B = self.B
         h = m.embed_tokens(self.tok[:, None])                         # [B, 1, H]
-        position_ids = self.pos.expand(B)[:, None]
-        cos, sin = m.rotary_emb(h, position_ids=position_ids)
+        if not self.rope_fused:
+            position_ids = self.pos.expand(B)[:, None]
+            cos, sin = m.rotary_emb(h, position_ids=position_ids)
         for li, layer in enumerate(m.layers):
             attn = layer.self_attn
             x = layer.input_layernorm(h)
-            q, k, v = self._qkv(li, attn, x)
-            q, k = self._rope(q, k, cos, sin)
-            self._append(li, k, v, self.pos)
-            self._attend(li, q[:, :, 0].to(torch.float16).contiguous())
+            if self.rope_fused:
+                qkv = F.linear(x, self.wqkv[li], self.bqkv[li]).view(B, -1)
+                ks = self.ks[li] if self.kv_dtype == "int8" else None
+                vs = self.vs[li] if self.kv_dtype == "int8" else None
+                ops.rope_qkv_append(qkv, self.cos_t, self.sin_t, self.pos32, self.q16, self.kc[li], self.vc[li],
+                                    ks, vs)
+                self._attend(li, self.q16)
+            else:
+                q, k, v = self._qkv(li, attn, x)
+                q, k = self._rope(q, k, cos, sin)
+                self._append(li, k, v, self.pos)
+                self._attend(li, q[:, :, 0].to(torch.float16).contiguous())
             if self.xchg is not None:
                 self.xchg.wait()
                 o = self.xchg.gathered(li).permute(1, 0, 2, 3).reshape(B, 1, self.Hq * self.D)

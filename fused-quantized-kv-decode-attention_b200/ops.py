@@ -473,6 +473,61 @@ def tp_wait(counters_ptr: int, world: int, per_call: int, sequence_ptr: int, dev
     _native.check(rc, "launch: tp_wait")
 
 
+def rope_qkv_append(qkv: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor, pos,
+                    q_out: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
+                    Ks: torch.Tensor | None = None, Vs: torch.Tensor | None = None) -> None:
+    """Fused decode-step prologue: RoPE(q, k), q -> fp16, append k/v to the cache (see the C ABI).
+
+    qkv [B, W] (fp16 or bf16, W >= (Hq + 2 Hkv) D, contiguous rows) holds each
+    sequence's fused projection output [q heads | k heads | v heads];
+    cos_table / sin_table [rows, D] are the model's rotary tables (same dtype);
+    ``pos`` is an int or a CUDA int32 tensor (read on the device).  q_out
+    [B, Hq, D] fp16; K/V [B, Hkv, cap, D] fp16 cache, or int8 codes with
+    Ks/Vs [B, Hkv, cap] fp16 scales.  Bit-exact with transformers'
+    apply_rotary_pos_emb, ``.to(float16)`` and (int8) :func:`qpt` of the new token.
+    """
+    op = "rope_qkv_append"
+    dev = _require_cuda(op, qkv, cos_table, sin_table, q_out, K, V)
+    if qkv.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", "qkv must be fp16 or bf16")
+    _require_dtype(op, "model dtype", qkv.dtype, cos_table=cos_table, sin_table=sin_table)
+    _require_dtype(op, "fp16", torch.float16, q_out=q_out)
+    if qkv.dim() != 2 or qkv.stride(1) != 1 or q_out.dim() != 3 or K.dim() != 4:
+        _fail(op, "shape", "qkv [B, W] with contiguous rows, q_out [B, Hq, D], K [B, Hkv, cap, D]")
+    _require_contig(op, cos_table=cos_table, sin_table=sin_table, q_out=q_out, K=K, V=V)
+    B, Hq, D = q_out.shape
+    _, Hkv, cap, _ = K.shape
+    _require_D(op, D)
+    _require_shape(op, "V", V, (B, Hkv, cap, D))
+    if cos_table.dim() != 2 or cos_table.shape[1] != D or sin_table.shape != cos_table.shape:
+        _fail(op, "shape", "cos_table / sin_table must be [rows, D]")
+    if Ks is None:
+        _require_dtype(op, "fp16", torch.float16, K=K, V=V)
+        fmt = _native.KV_F16
+    else:
+        _require_dtype(op, "int8", torch.int8, K=K, V=V)
+        _require_dtype(op, "fp16", torch.float16, Ks=Ks, Vs=Vs)
+        _require_contig(op, Ks=Ks, Vs=Vs)
+        _require_shape(op, "Ks", Ks, (B, Hkv, cap))
+        _require_shape(op, "Vs", Vs, (B, Hkv, cap))
+        fmt = _native.KV_INT8
+    if qkv.shape[0] != B or qkv.shape[1] < (Hq + 2 * Hkv) * D:
+        _fail(op, "shape", f"qkv must be [B={B}, >= (Hq + 2 Hkv) D = {(Hq + 2 * Hkv) * D}]")
+    if isinstance(pos, torch.Tensor):
+        if pos.device != dev or pos.dtype != torch.int32 or pos.numel() < 1:
+            _fail(op, "pos", "a tensor pos must be a CUDA int32 tensor on the inputs' device")
+        pos_host, pos_ptr = 0, pos.data_ptr()
+    else:
+        pos_host, pos_ptr = int(pos), None
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_rope_qkv_append(
+            fmt, 1 if qkv.dtype == torch.bfloat16 else 0, qkv.data_ptr(), qkv.stride(0), cos_table.data_ptr(),
+            sin_table.data_ptr(), cos_table.shape[0], pos_host, pos_ptr, q_out.data_ptr(), K.data_ptr(),
+            V.data_ptr(), Ks.data_ptr() if Ks is not None else None, Vs.data_ptr() if Vs is not None else None,
+            B, Hq, Hkv, D, cap, _stream(dev))
+    _native.check(rc, f"launch: {op}")
+
+
 def qpt(X: torch.Tensor):
     """Per-token symmetric int8 quantizer: X [..., D] f16 -> (int8 [..., D], f16 scales [...]).
 

@@ -200,6 +200,31 @@ int fqkv_quantize_int4_into_cache(const void* X, void* packed, void* scales, int
                                   int64_t D, int64_t cap, int64_t pos_host, const int32_t* pos_dev,
                                   fqkv_stream_t stream);
 
+/* Fused decode-step prologue of a Llama-style attention block: rotary
+ * embedding of q and k, the fp16 cast of q, and the append of k and v to the
+ * KV cache, in one launch.  qkv [B, qkv_row_stride] in the model dtype
+ * (model_dtype 0 = f16, 1 = bf16) holds each sequence's fused projection
+ * output [q heads | k heads | v heads], D elements per head; cos_table /
+ * sin_table [table_rows, D] (model dtype) are the model's rotary tables.  At
+ * position pos = *pos_dev (device int32) if non-NULL else pos_host:
+ *   q_out [B,Hq,D] f16      <- fp16(rope(q))
+ *   K cache [B,Hkv,cap,D]   <- fp16(rope(k)) at pos (kv_format FQKV_KV_F16), or
+ *                              its int8 codes + f16 scale [B,Hkv,cap]
+ *                              (FQKV_KV_INT8, bit-exact with the reference
+ *                              quantizer), and V likewise from fp16(v).
+ * rope(x)_i = T(T(x_i*cos_i) + T(r_i*sin_i)), r = cat(-x[D/2:], x[:D/2]),
+ * T = rounding to the model dtype: bit-exact with transformers'
+ * apply_rotary_pos_emb followed by .to(float16).  Positions at or past cap (or
+ * the table) write nothing to the cache.  D in {64, 128}.
+ * reference: the live-model hook's per-step cache update
+ * (notebooks/integration_and_benchmarks.ipynb:1043-1061) with the quantizer of
+ * lines 236-238 applied to the new token only. */
+int fqkv_rope_qkv_append(int32_t kv_format, int32_t model_dtype, const void* qkv, int64_t qkv_row_stride,
+                         const void* cos_table, const void* sin_table, int64_t table_rows, int64_t pos_host,
+                         const int32_t* pos_dev, void* q_out, void* k_cache, void* v_cache, void* k_scales,
+                         void* v_scales, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t cap,
+                         fqkv_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Tensor-parallel decode: attention fused with the all-gather of its outputs.
  * No counterpart in the reference: its tensor-parallel end-to-end config

@@ -125,3 +125,70 @@ def test_graph_decoder_int8_cache_tracks_fp16_cache(fqkv):
     first_div = int((t16 != t8).any(0).float().argmax()) if (t16 != t8).any() else T
     err = (l8[:, :max(first_div, 1)] - l16[:, :max(first_div, 1)]).abs().max().item()
     assert err <= 0.05 + 0.05 * l16.abs().max().item()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("kv", ["fp16", "int8"])
+def test_rope_qkv_append_bit_exact(fqkv, dtype, kv):
+    """The fused prologue equals transformers' RoPE + .to(float16) + cache append / qpt, bit for bit."""
+    from transformers import LlamaForCausalLM
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    torch.manual_seed(4)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(_tiny_config()).to(dtype).eval()
+    rot = model.model.rotary_emb
+    B, Hq, Hkv, D, cap, pos = 3, 8, 2, 64, 50, 37
+    qkv = (torch.randn(B, (Hq + 2 * Hkv) * D, device="cuda") * 3).to(dtype)
+    cos_t, sin_t = rot(torch.empty(1, 1, 1, dtype=dtype, device="cuda"), torch.arange(cap, device="cuda")[None])
+    cos_t, sin_t = cos_t[0].contiguous(), sin_t[0].contiguous()
+    q_out = torch.empty(B, Hq, D, dtype=torch.float16, device="cuda")
+    cdt = torch.float16 if kv == "fp16" else torch.int8
+    K = torch.zeros(B, Hkv, cap, D, dtype=cdt, device="cuda")
+    V = torch.zeros_like(K)
+    Ks = torch.zeros(B, Hkv, cap, dtype=torch.float16, device="cuda") if kv == "int8" else None
+    Vs = torch.zeros_like(Ks) if kv == "int8" else None
+    posd = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    fqkv.rope_qkv_append(qkv, cos_t, sin_t, posd, q_out, K, V, Ks, Vs)
+    # reference: the HF ops the decoder used before
+    q = qkv[:, :Hq * D].view(B, 1, Hq, D).transpose(1, 2)
+    k = qkv[:, Hq * D:(Hq + Hkv) * D].view(B, 1, Hkv, D).transpose(1, 2)
+    v = qkv[:, (Hq + Hkv) * D:].view(B, 1, Hkv, D).transpose(1, 2)
+    cos, sin = rot(qkv[:, None], torch.full((B, 1), pos, device="cuda"))
+    qr, kr = apply_rotary_pos_emb(q, k, cos, sin)
+    assert torch.equal(q_out, qr[:, :, 0].to(torch.float16))
+    k16, v16 = kr[:, :, 0].to(torch.float16), v[:, :, 0].to(torch.float16)
+    if kv == "fp16":
+        assert torch.equal(K[:, :, pos], k16) and torch.equal(V[:, :, pos], v16)
+    else:
+        kc, ksc = fqkv.qpt(k16.contiguous())
+        vc, vsc = fqkv.qpt(v16.contiguous())
+        assert torch.equal(K[:, :, pos], kc) and torch.equal(V[:, :, pos], vc)
+        assert torch.equal(Ks[:, :, pos], ksc) and torch.equal(Vs[:, :, pos], vsc)
+    assert not K[:, :, :pos].any() and not K[:, :, pos + 1:].any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kv", ["fp16", "int8"])
+def test_graph_decoder_fused_prologue_equals_hf_ops(fqkv, kv):
+    """GraphDecoder with the fused RoPE/append prologue gives the same logits, bit for bit,
+    as with transformers' RoPE and separate cache writes."""
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(6)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(_tiny_config()).to(torch.bfloat16).eval()
+    B, P, T = 2, 29, 10
+    ids = torch.randint(0, 1000, (B, P), device="cuda")
+    res = {}
+    for fused in (False, True):
+        dec = fqkv.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True, kv_dtype=kv,
+                                               fused_rope=fused)
+        assert dec.rope_fused == fused
+        dec.prefill(ids)
+        dec.capture()
+        lg = [dec.logits.clone()]
+        for _ in range(T - 1):
+            dec.step()
+            lg.append(dec.logits.clone())
+        res[fused] = torch.stack(lg, 1)
+    assert torch.equal(res[False], res[True])
