@@ -60,7 +60,12 @@ struct QtcCfg {
   static constexpr int kScaleBytes = 2 * TK + 32;              // 16B-aligned scale window
   static constexpr int kStageRaw = 2 * kTileBytes + 2 * kScaleBytes;
   static constexpr int kStageBytes = (kStageRaw + 1023) & ~1023;  // tiles stay 1024-aligned (swizzle atom)
-  static constexpr int kStages = (G1 || kStageBytes <= 10240) ? 4 : 3;
+  // Resident CTAs per SM and ring depth, measured on B200: the kernel is
+  // issue-bound (consumers almost never wait for a tile), so the GQA variant
+  // runs 4 CTAs (20 warps) with a 2-stage ring (332.6 -> 323.7 us at B=64,
+  // N=16K, D=128); the one-head int4 variant keeps 3 CTAs and 4 stages.
+  static constexpr int kCtas = G1 ? 3 : 4;
+  static constexpr int kStages = G1 ? 4 : 2;
   static constexpr int MH = G1 ? 1 : 4;                        // heads merged per epilogue pass
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
   static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
@@ -168,7 +173,7 @@ __device__ __forceinline__ constexpr int qk_dim(int kk, int h, int i) {
 }
 
 template <int D, bool I4, bool G1>
-__global__ void __launch_bounds__(kThreads, 3) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
+__global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = QtcCfg<D, I4, G1>;
   constexpr int MH = C::MH;
   constexpr int RB = C::RB;
