@@ -23,8 +23,10 @@ from .ops import (
     gqa_sk_fast,
     qpt,
     quant_int4_per_token,
+    add_rmsnorm,
     quantize_into_cache,
     rope_qkv_append,
+    silu_mul,
     tp_wait,
     workspace_bytes,
 )
@@ -39,6 +41,8 @@ __all__ = [
     "decode_attn_gqa_int8_kvcache",
     "quantize_into_cache",
     "rope_qkv_append",
+    "add_rmsnorm",
+    "silu_mul",
     "decode_attn_kvcache_tp",
     "tp_wait",
     "gqa_sk_fast",

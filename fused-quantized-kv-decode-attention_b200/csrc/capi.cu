@@ -562,6 +562,37 @@ int fqkv_rope_qkv_append(int32_t kv_format, int32_t model_dtype, const void* qkv
   return FQKV_OK;
 }
 
+// ------------------------------------------------------------------ decode-step model helpers
+int fqkv_add_rmsnorm(int32_t model_dtype, void* h, const void* delta, const void* weight, void* y, int64_t rows,
+                     int64_t H, float eps, fqkv_stream_t stream) {
+  if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (rows < 0 || H < 1 || H > 8192) return fail(FQKV_ERR_INVALID_ARGUMENT, "rows/H: need rows >= 0, 1 <= H <= 8192");
+  if (rows > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "rows exceed the grid range");
+  if (rows == 0) return FQKV_OK;
+  if (!h || !weight || !y) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(h, 2) || !aligned(weight, 2) || !aligned(y, 2) || (delta && !aligned(delta, 2)))
+    return fail(FQKV_ERR_MISALIGNED, "add_rmsnorm: misaligned pointer");
+  cudaError_t e = fqkv::launch_add_rmsnorm(model_dtype == 1, h, delta, weight, y, rows, int(H), eps,
+                                           reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
+  return FQKV_OK;
+}
+
+int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, int64_t I, int64_t gu_row_stride,
+                  fqkv_stream_t stream) {
+  if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (rows < 0 || I < 1 || I > INT32_MAX || gu_row_stride < 2 * I)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "silu_mul: bad sizes (rows %lld, I %lld, stride %lld)", (long long)rows,
+                (long long)I, (long long)gu_row_stride);
+  if (rows == 0) return FQKV_OK;
+  if (!gu || !y) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(gu, 2) || !aligned(y, 2)) return fail(FQKV_ERR_MISALIGNED, "silu_mul: misaligned pointer");
+  cudaError_t e = fqkv::launch_silu_mul(model_dtype == 1, gu, y, rows, int(I), gu_row_stride,
+                                        reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
+  return FQKV_OK;
+}
+
 // ------------------------------------------------------------------ tensor-parallel decode
 int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K, const void* V, const void* Ks,
                                 const void* Vs, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,

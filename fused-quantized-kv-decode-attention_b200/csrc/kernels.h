@@ -122,6 +122,11 @@ cudaError_t launch_rope_append(bool bf16, bool int8_cache, const void* qkv, int6
                                const void* sin_t, int64_t table_rows, int64_t pos_host, const int* pos_dev,
                                void* q_out, void* k_cache, void* v_cache, void* k_scales, void* v_scales, int B,
                                int Hq, int Hkv, int D, int cap, cudaStream_t stream);
+// Decode-step model kernels (model_ops.cu).
+cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void* w, void* y, int64_t rows, int H,
+                               float eps, cudaStream_t stream);
+cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, int I, int64_t row_stride,
+                            cudaStream_t stream);
 // Tensor-parallel arrival wait (tp.cu).
 cudaError_t launch_tp_wait(const unsigned long long* counters, int world, unsigned long long per_call,
                            unsigned long long* sequence, int* status, unsigned long long timeout_ns,

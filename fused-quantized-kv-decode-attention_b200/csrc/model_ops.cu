@@ -1,0 +1,136 @@
+// Small fused kernels of the graph-captured Llama decode step around attention.
+//
+// A transformers decode step spends most of its non-GEMM time in the
+// elementwise and reduction kernels of LlamaRMSNorm (cast to fp32, pow, mean,
+// add eps, rsqrt, two multiplies, cast back) and of the SwiGLU MLP.  These
+// kernels do the same arithmetic in one launch each:
+//
+//  * add_rmsnorm: h <- T(h + delta) (optional), y <- T(w * T(h32 * rsqrt(mean(h32^2) + eps)))
+//    with T the model dtype (fp16 / bf16), exactly LlamaRMSNorm's sequence of
+//    roundings; only the order of the fp32 sum of squares differs from torch's
+//    reduction (the mean can differ in the last fp32 bit).
+//  * silu_mul: y <- T(T(silu(g)) * u) on a fused [gate | up] projection, with
+//    silu(x) = x / (1 + exp(-x)) in fp32 as torch evaluates it.
+//
+// One CTA per row for add_rmsnorm (hidden sizes up to 8192), a grid-stride
+// loop for silu_mul.  Both are HBM-bound and tiny; the point is the launch
+// count of a decode step.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+
+#include "kernels.h"
+
+namespace fqkv {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float ld<__half>(const __half* p, int64_t i) { return __half2float(p[i]); }
+template <>
+__device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) { return __bfloat162float(p[i]); }
+template <typename T>
+__device__ __forceinline__ T cvt(float x);
+template <>
+__device__ __forceinline__ __half cvt<__half>(float x) { return __float2half_rn(x); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <typename T>
+__device__ __forceinline__ float rnd(float x);
+template <>
+__device__ __forceinline__ float rnd<__half>(float x) { return __half2float(__float2half_rn(x)); }
+template <>
+__device__ __forceinline__ float rnd<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+constexpr int kNormThreads = 256;
+constexpr int kMaxPerThread = 32;  // hidden size <= 8192
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(T* __restrict__ h, const T* __restrict__ delta,
+                                                                   const T* __restrict__ w, T* __restrict__ y, int H,
+                                                                   float eps) {
+  const int64_t row = blockIdx.x;
+  T* hr = h + row * H;
+  const T* dr = delta ? delta + row * H : nullptr;
+  float v[kMaxPerThread];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxPerThread; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    if (i < H) {
+      float x = ld<T>(hr, i);
+      if (dr) {
+        x = rnd<T>(x + ld<T>(dr, i));  // the residual add, rounded to the model dtype
+        hr[i] = cvt<T>(x);
+      }
+      v[k] = x;
+      ss = fmaf(x, x, ss);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  __shared__ float part[kNormThreads / 32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormThreads / 32; ++k) tot += part[k];
+  const float r = rsqrtf(tot * (1.f / float(H)) + eps);
+  T* yr = y + row * H;
+#pragma unroll
+  for (int k = 0; k < kMaxPerThread; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    if (i < H) yr[i] = cvt<T>(ld<T>(w, i) * rnd<T>(v[k] * r));
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ y, int64_t rows,
+                                                       int I, int64_t row_stride) {
+  const int64_t n = rows * I;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / I;
+    const int c = int(idx - r * I);
+    const float g = ld<T>(gu, r * row_stride + c);
+    const float u = ld<T>(gu, r * row_stride + I + c);
+    const float s = rnd<T>(g / (1.f + expf(-g)));
+    y[idx] = cvt<T>(s * u);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void* w, void* y, int64_t rows, int H,
+                               float eps, cudaStream_t stream) {
+  if (H > kNormThreads * kMaxPerThread) return cudaErrorInvalidValue;
+  if (bf16)
+    add_rmsnorm_kernel<__nv_bfloat16><<<unsigned(rows), kNormThreads, 0, stream>>>(
+        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
+        static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), H, eps);
+  else
+    add_rmsnorm_kernel<__half><<<unsigned(rows), kNormThreads, 0, stream>>>(
+        static_cast<__half*>(h), static_cast<const __half*>(delta), static_cast<const __half*>(w),
+        static_cast<__half*>(y), H, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, int I, int64_t row_stride,
+                            cudaStream_t stream) {
+  const int64_t n = rows * I;
+  const unsigned blocks = unsigned(std::min<int64_t>((n + 255) / 256, 148 * 16));
+  if (bf16)
+    silu_mul_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gu),
+                                                               static_cast<__nv_bfloat16*>(y), rows, I, row_stride);
+  else
+    silu_mul_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(gu), static_cast<__half*>(y), rows,
+                                                        I, row_stride);
+  return cudaGetLastError();
+}
+
+}  // namespace fqkv

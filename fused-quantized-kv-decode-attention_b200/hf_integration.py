@@ -23,6 +23,11 @@
   :func:`ops.rope_qkv_append` (RoPE of q and k from tables the model's own
   rotary module filled, q cast to fp16, k/v appended or quantized into the
   cache -- bit-exact with the HF ops it replaces, ``fused_rope=False``).
+  With ``fused_model_ops`` (default) the residual adds and RMSNorms are one
+  :func:`ops.add_rmsnorm` launch each and the MLP is one GEMM against the
+  concatenated gate/up weights plus :func:`ops.silu_mul` and the down GEMM
+  (LlamaRMSNorm / SwiGLU arithmetic; only the fp32 sum of squares is
+  reduced in a different order).
 
   With ``tp_group`` (a ``torch.distributed`` group, NCCL on GPUs) the decoder
   is tensor-parallel by KV head: each rank keeps the q/k/v projection rows, the
@@ -90,7 +95,7 @@ class GraphDecoder:
     """
 
     def __init__(self, model, batch: int, max_len: int, keep_logits: bool = False, kv_dtype: str = "fp16",
-                 tp_group=None, tp_fused: bool = False, fused_rope: bool = True):
+                 tp_group=None, tp_fused: bool = False, fused_rope: bool = True, fused_model_ops: bool = True):
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
         self._rope = apply_rotary_pos_emb
@@ -171,6 +176,19 @@ class GraphDecoder:
             self.cos_t = cos[0].contiguous()
             self.sin_t = sin[0].contiguous()
             self.q16 = torch.empty(batch, self.Hq_l, self.D, dtype=torch.float16, device=dev)
+        # fused residual/RMSNorm and SwiGLU (same dtype conditions, LlamaRMSNorm / silu MLP)
+        H = cfg.hidden_size
+        self.model_fused = (fused_model_ops and self.rope_fused and H <= 8192
+                            and getattr(cfg, "hidden_act", "silu") == "silu"
+                            and all(hasattr(l.input_layernorm, "variance_epsilon") for l in model.model.layers))
+        if self.model_fused:
+            I = cfg.intermediate_size
+            self.wgu = [torch.cat([l.mlp.gate_proj.weight.detach(), l.mlp.up_proj.weight.detach()], 0).contiguous()
+                        for l in model.model.layers]
+            self.bgu = [torch.cat([l.mlp.gate_proj.bias.detach(), l.mlp.up_proj.bias.detach()], 0).contiguous()
+                        if l.mlp.gate_proj.bias is not None else None for l in model.model.layers]
+            self.xn = torch.empty(batch, H, dtype=self.dtype, device=dev)     # normed hidden state
+            self.act = torch.empty(batch, I, dtype=self.dtype, device=dev)   # silu(gate) * up
         self.graph = None
         self.prompt_len = 0
 
@@ -261,6 +279,9 @@ class GraphDecoder:
         """Decode the token in ``self.tok`` at ``self.pos``; graph-capturable (no host sync)."""
         m = self.model.model
         B = self.B
+        if self.model_fused:
+            self._step_fused()
+            return
         h = m.embed_tokens(self.tok[:, None])                         # [B, 1, H]
         if not self.rope_fused:
             position_ids = self.pos.expand(B)[:, None]
@@ -288,6 +309,44 @@ class GraphDecoder:
             h = h + attn.o_proj(o.to(h.dtype))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         logits = self.model.lm_head(m.norm(h))[:, 0].float()
+        nxt = logits.argmax(-1)
+        if self.keep_logits:
+            self.logits.copy_(logits)
+        self.pos.add_(1)
+        self.pos32.add_(1)
+        self.nlen.add_(1)
+        self.out_tokens.index_copy_(1, self.pos, nxt[:, None])
+        self.tok.copy_(nxt)
+
+    def _step_fused(self) -> None:
+        """The decode step with every launch of the block fused that can be (see the class docstring)."""
+        m = self.model.model
+        B = self.B
+        layers = m.layers
+        h = m.embed_tokens(self.tok).view(B, -1)                      # [B, H], residual stream (updated in place)
+        x = self.xn
+        ops.add_rmsnorm(h, None, layers[0].input_layernorm.weight, x, layers[0].input_layernorm.variance_epsilon)
+        for li, layer in enumerate(layers):
+            attn = layer.self_attn
+            qkv = F.linear(x, self.wqkv[li], self.bqkv[li])
+            ks = self.ks[li] if self.kv_dtype == "int8" else None
+            vs = self.vs[li] if self.kv_dtype == "int8" else None
+            ops.rope_qkv_append(qkv, self.cos_t, self.sin_t, self.pos32, self.q16, self.kc[li], self.vc[li], ks, vs)
+            self._attend(li, self.q16)
+            if self.xchg is not None:
+                self.xchg.wait()
+                o = self.xchg.gathered(li).permute(1, 0, 2, 3).reshape(B, self.Hq * self.D)
+            else:
+                o = self._heads(self.attn_out.view(B, 1, self.Hq_l, self.D), self.gather_buf).view(B, -1)
+            a = attn.o_proj(o.to(h.dtype))
+            ops.add_rmsnorm(h, a, layer.post_attention_layernorm.weight, x,
+                            layer.post_attention_layernorm.variance_epsilon)
+            gu = F.linear(x, self.wgu[li], self.bgu[li])
+            ops.silu_mul(gu, self.act)
+            d = layer.mlp.down_proj(self.act)
+            nrm = layers[li + 1].input_layernorm if li + 1 < len(layers) else m.norm
+            ops.add_rmsnorm(h, d, nrm.weight, x, nrm.variance_epsilon)
+        logits = self.model.lm_head(x).float()
         nxt = logits.argmax(-1)
         if self.keep_logits:
             self.logits.copy_(logits)

@@ -528,6 +528,48 @@ def rope_qkv_append(qkv: torch.Tensor, cos_table: torch.Tensor, sin_table: torch
     _native.check(rc, f"launch: {op}")
 
 
+def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, y: torch.Tensor,
+                eps: float) -> None:
+    """Residual add + RMSNorm in one launch: ``h += delta`` (if given, in place), ``y = rmsnorm(h) * weight``.
+
+    h, delta, y [rows, H] and weight [H] in the model dtype (fp16 / bf16),
+    contiguous; LlamaRMSNorm's arithmetic (fp32 inside, rounded to the model
+    dtype where transformers rounds).
+    """
+    op = "add_rmsnorm"
+    ts = dict(h=h, weight=weight, y=y) if delta is None else dict(h=h, delta=delta, weight=weight, y=y)
+    dev = _require_cuda(op, *ts.values())
+    if h.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", "h must be fp16 or bf16")
+    _require_dtype(op, "model dtype", h.dtype, **ts)
+    _require_contig(op, **ts)
+    H = h.shape[-1]
+    rows = h.numel() // H
+    if weight.numel() != H or y.shape != h.shape or (delta is not None and delta.shape != h.shape):
+        _fail(op, "shape", "h, delta, y [rows, H] and weight [H]")
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_add_rmsnorm(1 if h.dtype == torch.bfloat16 else 0, h.data_ptr(),
+                                            delta.data_ptr() if delta is not None else None, weight.data_ptr(),
+                                            y.data_ptr(), rows, H, float(eps), _stream(dev))
+    _native.check(rc, f"launch: {op}")
+
+
+def silu_mul(gu: torch.Tensor, y: torch.Tensor) -> None:
+    """SwiGLU on a fused [gate | up] projection: gu [rows, 2I] -> y [rows, I] = silu(gate) * up (model dtype)."""
+    op = "silu_mul"
+    dev = _require_cuda(op, gu, y)
+    if gu.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", "gu must be fp16 or bf16")
+    _require_dtype(op, "model dtype", gu.dtype, y=y)
+    _require_contig(op, y=y)
+    if gu.dim() != 2 or gu.stride(1) != 1 or y.dim() != 2 or gu.shape[0] != y.shape[0] or gu.shape[1] < 2 * y.shape[1]:
+        _fail(op, "shape", "gu [rows, >= 2I] with contiguous rows, y [rows, I]")
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_silu_mul(1 if gu.dtype == torch.bfloat16 else 0, gu.data_ptr(), y.data_ptr(),
+                                         y.shape[0], y.shape[1], gu.stride(0), _stream(dev))
+    _native.check(rc, f"launch: {op}")
+
+
 def qpt(X: torch.Tensor):
     """Per-token symmetric int8 quantizer: X [..., D] f16 -> (int8 [..., D], f16 scales [...]).
 

@@ -225,6 +225,22 @@ int fqkv_rope_qkv_append(int32_t kv_format, int32_t model_dtype, const void* qkv
                          void* v_scales, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t cap,
                          fqkv_stream_t stream);
 
+/* Decode-step helpers of the graph-captured Llama decoder (no counterpart in
+ * the reference, whose end-to-end path runs transformers' eager modules;
+ * they cut the launches of a step).  model_dtype 0 = f16, 1 = bf16.
+ * Residual add + RMSNorm of rows [rows, H] (H <= 8192):
+ *   if delta: h <- T(h + delta)   (in place)
+ *   y <- T(w * T(h * rsqrt(mean(h^2) + eps)))     (fp32 inside, T = model dtype)
+ * -- transformers' LlamaRMSNorm arithmetic (the fp32 sum of squares may be
+ * summed in a different order). */
+int fqkv_add_rmsnorm(int32_t model_dtype, void* h, const void* delta, const void* weight, void* y, int64_t rows,
+                     int64_t H, float eps, fqkv_stream_t stream);
+
+/* SwiGLU: y [rows, I] <- T(T(silu(g)) * u) with g = gu[:, :I], u = gu[:, I:2I]
+ * (row stride gu_row_stride elements), silu(x) = x / (1 + exp(-x)) in fp32. */
+int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, int64_t I, int64_t gu_row_stride,
+                  fqkv_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Tensor-parallel decode: attention fused with the all-gather of its outputs.
  * No counterpart in the reference: its tensor-parallel end-to-end config

@@ -192,3 +192,34 @@ def test_graph_decoder_fused_prologue_equals_hf_ops(fqkv, kv):
             lg.append(dec.logits.clone())
         res[fused] = torch.stack(lg, 1)
     assert torch.equal(res[False], res[True])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_graph_decoder_fused_model_ops_track_hf_modules(fqkv, dtype):
+    """The fused residual/RMSNorm + SwiGLU step against transformers' modules on
+    the same decoder: same tokens, logits within rounding (the RMSNorm sum of
+    squares and the concatenated gate/up GEMM reduce in a different order)."""
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(8)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(_tiny_config()).to(dtype).eval()
+    B, P, T = 2, 31, 12
+    ids = torch.randint(0, 1000, (B, P), device="cuda")
+    res = {}
+    for fused in (False, True):
+        dec = fqkv.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True,
+                                               fused_model_ops=fused)
+        assert dec.model_fused == fused
+        dec.prefill(ids)
+        dec.capture()
+        lg = [dec.logits.clone()]
+        for _ in range(T - 1):
+            dec.step()
+            lg.append(dec.logits.clone())
+        res[fused] = (torch.stack(lg, 1), dec.out_tokens[:, P:P + T].clone())
+    (l0, t0), (l1, t1) = res[False], res[True]
+    assert (t0 == t1).float().mean().item() >= 0.9
+    n_ok = int((t0 != t1).any(0).float().argmax()) if (t0 != t1).any() else T
+    err = (l1[:, :max(n_ok, 1)] - l0[:, :max(n_ok, 1)]).abs().max().item()
+    assert err <= 0.02 + 0.01 * l0.abs().max().item()
