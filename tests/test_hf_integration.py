@@ -223,3 +223,36 @@ def test_graph_decoder_fused_model_ops_track_hf_modules(fqkv, dtype):
     n_ok = int((t0 != t1).any(0).float().argmax()) if (t0 != t1).any() else T
     err = (l1[:, :max(n_ok, 1)] - l0[:, :max(n_ok, 1)]).abs().max().item()
     assert err <= 0.02 + 0.01 * l0.abs().max().item()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("H", [2048, 520])
+def test_add_rmsnorm_and_silu_mul_kernels(fqkv, dtype, H):
+    """Residual add bit-exact; RMSNorm within one unit in the last place of the
+    model dtype of transformers' LlamaRMSNorm (only the fp32 sum order differs);
+    SwiGLU bit-exact with torch's silu(g) * u.  H=520 takes the scalar path."""
+    from transformers.models.llama.modeling_llama import LlamaRMSNorm
+    torch.manual_seed(9)
+    rows = 7
+    h = (torch.randn(rows, H, device="cuda") * 2).to(dtype)
+    d = torch.randn(rows, H, device="cuda").to(dtype)
+    norm = LlamaRMSNorm(H, eps=1e-5).cuda().to(dtype)
+    with torch.no_grad():
+        norm.weight.copy_((1 + 0.1 * torch.randn(H, device="cuda")).to(dtype))
+        h_ref = h + d
+        y_ref = norm(h_ref)
+    y = torch.empty_like(h)
+    fqkv.add_rmsnorm(h, d, norm.weight.detach(), y, 1e-5)
+    assert torch.equal(h, h_ref)
+    ulp = torch.finfo(dtype).eps * y_ref.float().abs().clamp_min(torch.finfo(dtype).tiny)
+    assert ((y.float() - y_ref.float()).abs() <= ulp * 1.01).all()
+    assert (y == y_ref).float().mean().item() >= 0.97
+    y2 = torch.empty_like(h)
+    fqkv.add_rmsnorm(h, None, norm.weight.detach(), y2, 1e-5)   # plain norm of the updated stream
+    assert torch.equal(y2, y)
+    I = 300
+    gu = (torch.randn(rows, 2 * I, device="cuda") * 3).to(dtype)
+    out = torch.empty(rows, I, device="cuda", dtype=dtype)
+    fqkv.silu_mul(gu, out)
+    assert torch.equal(out, torch.nn.functional.silu(gu[:, :I]) * gu[:, I:])
