@@ -24,6 +24,7 @@ from .ops import (
     qpt,
     quant_int4_per_token,
     add_rmsnorm,
+    gemv,
     quantize_into_cache,
     rope_qkv_append,
     silu_mul,
@@ -42,6 +43,7 @@ __all__ = [
     "quantize_into_cache",
     "rope_qkv_append",
     "add_rmsnorm",
+    "gemv",
     "silu_mul",
     "decode_attn_kvcache_tp",
     "tp_wait",

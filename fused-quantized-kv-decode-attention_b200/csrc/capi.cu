@@ -593,6 +593,20 @@ int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, in
   return FQKV_OK;
 }
 
+int fqkv_gemv(int32_t model_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B, int64_t N,
+              int64_t K, fqkv_stream_t stream) {
+  if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (B < 1 || B > 4 || N < 1 || N > INT32_MAX / 2 || K < 256 || K % 256 != 0 || K > 16384)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "gemv: need 1 <= B <= 4, N >= 1, K a multiple of 256 in [256, 16384]");
+  if (!x || !W || !y) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(x, 16) || !aligned(W, 16) || !aligned(y, 2) || (bias && !aligned(bias, 2)))
+    return fail(FQKV_ERR_MISALIGNED, "gemv: x and W must be 16-byte aligned");
+  cudaError_t e = fqkv::launch_gemv(model_dtype == 1, x, W, bias, y, int(B), int(N), int(K),
+                                    reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+  return FQKV_OK;
+}
+
 // ------------------------------------------------------------------ tensor-parallel decode
 int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K, const void* V, const void* Ks,
                                 const void* Vs, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,

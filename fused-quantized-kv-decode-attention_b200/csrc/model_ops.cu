@@ -170,7 +170,124 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu,
   }
 }
 
+// Small-batch GEMV: y [B, N] = x [B, K] @ W[N, K]^T (+ bias), B <= 4, fp32
+// accumulation, output rounded to the model dtype.  A batch-1..4 decode step's
+// projections are weight-streaming GEMVs that cuBLAS's batch-1 kernels run far
+// below HBM speed.  One warp per weight row (two rows when K <= 2048); lanes
+// read 16-byte chunks 256 elements apart, x is staged in shared memory, every
+// lane keeps K/256 independent loads in flight.  K % 256 == 0, rows 16-byte
+// aligned.
+constexpr int kGemvWarps = 8;
+template <typename T, int B, int RPW>
+__global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const T* __restrict__ x, const T* __restrict__ W,
+                                                               const T* __restrict__ bias, T* __restrict__ y, int N,
+                                                               int K) {
+  extern __shared__ uint4 xs[];  // [B][K/8] chunks
+  const int kc = K / 8;
+  const int lane = threadIdx.x & 31;
+  const int warp_global = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
+  const int n0 = warp_global * RPW;
+  constexpr int U = 8;  // chunks per lane per pass: K = 2048 is one pass
+  uint4 wv[RPW][U];
+  // the first pass's weight loads are issued before x is staged, so the two
+  // memory round trips overlap
+  auto load_w = [&](int c) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int cc = c + 32 * u;
+        if (cc < kc && n0 + r < N) wv[r][u] = reinterpret_cast<const uint4*>(W + int64_t(n0 + r) * K)[cc];
+        else wv[r][u] = make_uint4(0, 0, 0, 0);
+      }
+  };
+  load_w(lane);
+  for (int i = threadIdx.x; i < B * kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
+  __syncthreads();
+  if (n0 >= N) return;
+  float acc[RPW][B];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
+  for (int c = lane; c < kc; c += 32 * U) {
+    if (c != lane) load_w(c);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int cc = c + 32 * u;
+      if (cc >= kc) continue;
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4 xv = xs[b * kc + cc];
+        const T* xp = reinterpret_cast<const T*>(&xv);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          const T* wp = reinterpret_cast<const T*>(&wv[r][u]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[r][b] = fmaf(ld<T>(wp, e), ld<T>(xp, e), acc[r][b]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float v = acc[r][b];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      acc[r][b] = v;
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      if (n0 + r >= N) break;
+      const float bv = bias ? ld<T>(bias, n0 + r) : 0.f;
+#pragma unroll
+      for (int b = 0; b < B; ++b) y[int64_t(b) * N + n0 + r] = cvt<T>(acc[r][b] + bv);
+    }
+  }
+}
+
+template <typename T, int B>
+cudaError_t launch_gemv_t(const void* x, const void* W, const void* bias, void* y, int N, int K, cudaStream_t stream) {
+  const size_t smem = size_t(B) * K * sizeof(T);
+  if (K <= 2048) {
+    constexpr int RPW = 2;
+    const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
+    auto fn = gemv_kernel<T, B, RPW>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(static_cast<const T*>(x), static_cast<const T*>(W),
+                                                 static_cast<const T*>(bias), static_cast<T*>(y), N, K);
+  } else {
+    constexpr int RPW = 1;
+    const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
+    auto fn = gemv_kernel<T, B, RPW>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(static_cast<const T*>(x), static_cast<const T*>(W),
+                                                 static_cast<const T*>(bias), static_cast<T*>(y), N, K);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_gemv_b(const void* x, const void* W, const void* bias, void* y, int B, int N, int K,
+                          cudaStream_t stream) {
+  switch (B) {
+    case 1: return launch_gemv_t<T, 1>(x, W, bias, y, N, K, stream);
+    case 2: return launch_gemv_t<T, 2>(x, W, bias, y, N, K, stream);
+    case 3: return launch_gemv_t<T, 3>(x, W, bias, y, N, K, stream);
+    default: return launch_gemv_t<T, 4>(x, W, bias, y, N, K, stream);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_gemv(bool bf16, const void* x, const void* W, const void* bias, void* y, int B, int N, int K,
+                        cudaStream_t stream) {
+  return bf16 ? launch_gemv_b<__nv_bfloat16>(x, W, bias, y, B, N, K, stream)
+              : launch_gemv_b<__half>(x, W, bias, y, B, N, K, stream);
+}
 
 cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void* w, void* y, int64_t rows, int H,
                                float eps, cudaStream_t stream) {

@@ -189,6 +189,10 @@ class GraphDecoder:
                         if l.mlp.gate_proj.bias is not None else None for l in model.model.layers]
             self.xn = torch.empty(batch, H, dtype=self.dtype, device=dev)     # normed hidden state
             self.act = torch.empty(batch, I, dtype=self.dtype, device=dev)   # silu(gate) * up
+            # batch <= 4: the q/k/v, o and down projections run on the library's GEMV (measured
+            # 1.5-2x faster than cuBLAS's batch-1..4 kernels on B200); gate/up and the LM head stay
+            # on cuBLAS, which streams those large matrices near HBM speed.
+            self.small_b = batch <= 4 and H % 256 == 0 and I % 256 == 0 and (self.Hq * self.D) % 256 == 0
         self.graph = None
         self.prompt_len = 0
 
@@ -328,7 +332,7 @@ class GraphDecoder:
         ops.add_rmsnorm(h, None, layers[0].input_layernorm.weight, x, layers[0].input_layernorm.variance_epsilon)
         for li, layer in enumerate(layers):
             attn = layer.self_attn
-            qkv = F.linear(x, self.wqkv[li], self.bqkv[li])
+            qkv = ops.gemv(x, self.wqkv[li], self.bqkv[li]) if self.small_b else F.linear(x, self.wqkv[li], self.bqkv[li])
             ks = self.ks[li] if self.kv_dtype == "int8" else None
             vs = self.vs[li] if self.kv_dtype == "int8" else None
             ops.rope_qkv_append(qkv, self.cos_t, self.sin_t, self.pos32, self.q16, self.kc[li], self.vc[li], ks, vs)
@@ -338,12 +342,21 @@ class GraphDecoder:
                 o = self.xchg.gathered(li).permute(1, 0, 2, 3).reshape(B, self.Hq * self.D)
             else:
                 o = self._heads(self.attn_out.view(B, 1, self.Hq_l, self.D), self.gather_buf).view(B, -1)
-            a = attn.o_proj(o.to(h.dtype))
+            o = o.to(h.dtype)
+            if self.small_b:
+                ob = attn.o_proj.bias.detach() if attn.o_proj.bias is not None else None
+                a = ops.gemv(o.contiguous(), attn.o_proj.weight.detach(), ob)
+            else:
+                a = attn.o_proj(o)
             ops.add_rmsnorm(h, a, layer.post_attention_layernorm.weight, x,
                             layer.post_attention_layernorm.variance_epsilon)
             gu = F.linear(x, self.wgu[li], self.bgu[li])
             ops.silu_mul(gu, self.act)
-            d = layer.mlp.down_proj(self.act)
+            if self.small_b:
+                db = layer.mlp.down_proj.bias.detach() if layer.mlp.down_proj.bias is not None else None
+                d = ops.gemv(self.act, layer.mlp.down_proj.weight.detach(), db)
+            else:
+                d = layer.mlp.down_proj(self.act)
             nrm = layers[li + 1].input_layernorm if li + 1 < len(layers) else m.norm
             ops.add_rmsnorm(h, d, nrm.weight, x, nrm.variance_epsilon)
         logits = self.model.lm_head(x).float()

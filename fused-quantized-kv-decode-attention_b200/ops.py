@@ -570,6 +570,30 @@ def silu_mul(gu: torch.Tensor, y: torch.Tensor) -> None:
     _native.check(rc, f"launch: {op}")
 
 
+def gemv(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = None,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """Small-batch projection y = x W^T (+ bias): x [B, K] (B <= 4), W [N, K], model dtype, fp32 accumulation."""
+    op = "gemv"
+    ts = dict(x=x, W=W) if bias is None else dict(x=x, W=W, bias=bias)
+    dev = _require_cuda(op, *ts.values())
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", "x must be fp16 or bf16")
+    _require_dtype(op, "model dtype", x.dtype, **ts)
+    _require_contig(op, **ts)
+    if x.dim() != 2 or W.dim() != 2 or x.shape[1] != W.shape[1] or (bias is not None and bias.shape != (W.shape[0],)):
+        _fail(op, "shape", "x [B, K], W [N, K], bias [N]")
+    B, K = x.shape
+    N = W.shape[0]
+    if out is None:
+        out = torch.empty(B, N, dtype=x.dtype, device=dev)
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_gemv(1 if x.dtype == torch.bfloat16 else 0, x.data_ptr(), W.data_ptr(),
+                                     bias.data_ptr() if bias is not None else None, out.data_ptr(), B, N, K,
+                                     _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return out
+
+
 def qpt(X: torch.Tensor):
     """Per-token symmetric int8 quantizer: X [..., D] f16 -> (int8 [..., D], f16 scales [...]).
 

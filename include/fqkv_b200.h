@@ -241,6 +241,12 @@ int fqkv_add_rmsnorm(int32_t model_dtype, void* h, const void* delta, const void
 int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, int64_t I, int64_t gu_row_stride,
                   fqkv_stream_t stream);
 
+/* Small-batch projection of a decode step: y [B,N] = x [B,K] W^T (+ bias [N])
+ * with W [N,K] row-major, all in the model dtype, fp32 accumulation, B in
+ * 1..4, K a multiple of 256, x / W / y 16-byte aligned. */
+int fqkv_gemv(int32_t model_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B, int64_t N,
+              int64_t K, fqkv_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Tensor-parallel decode: attention fused with the all-gather of its outputs.
  * No counterpart in the reference: its tensor-parallel end-to-end config

@@ -182,7 +182,7 @@ def test_graph_decoder_fused_prologue_equals_hf_ops(fqkv, kv):
     res = {}
     for fused in (False, True):
         dec = fqkv.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True, kv_dtype=kv,
-                                               fused_rope=fused)
+                                               fused_rope=fused, fused_model_ops=False)
         assert dec.rope_fused == fused
         dec.prefill(ids)
         dec.capture()
@@ -256,3 +256,18 @@ def test_add_rmsnorm_and_silu_mul_kernels(fqkv, dtype, H):
     out = torch.empty(rows, I, device="cuda", dtype=dtype)
     fqkv.silu_mul(gu, out)
     assert torch.equal(out, torch.nn.functional.silu(gu[:, :I]) * gu[:, I:])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("B,N,K", [(1, 300, 512), (2, 1000, 2048), (3, 77, 8192), (4, 2048, 2048), (1, 3, 256)])
+def test_gemv_matches_fp32_projection(fqkv, dtype, B, N, K):
+    """Small-batch GEMV: within one output rounding of the fp32 product (with bias)."""
+    torch.manual_seed(B * 1000 + N)
+    x = torch.randn(B, K, device="cuda").to(dtype)
+    W = (torch.randn(N, K, device="cuda") * 0.05).to(dtype)
+    b = torch.randn(N, device="cuda").to(dtype)
+    ref = x.float() @ W.float().t() + b.float()
+    got = fqkv.gemv(x, W, b).float()
+    tol = torch.finfo(dtype).eps * ref.abs() + 1e-4 * ref.abs().max()
+    assert ((got - ref).abs() <= tol).all()
