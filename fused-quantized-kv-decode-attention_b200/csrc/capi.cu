@@ -639,10 +639,12 @@ int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K,
 int64_t fqkv_tp_arrivals(int32_t kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
                          size_t workspace_bytes) {
   if ((kv_format != FQKV_KV_F16 && kv_format != FQKV_KV_INT8) || B < 1 || Hq < 1 || Hkv < 1 || max_len < 1 ||
-      (D != 64 && D != 128) || Hq % Hkv != 0)
+      (D != 64 && D != 128) || Hq % Hkv != 0) {
+    fail(FQKV_ERR_INVALID_ARGUMENT, "tp_arrivals: bad kv_format or sizes");
     return -1;
+  }
   DeviceState* ds = nullptr;
-  if (device_state(&ds) != FQKV_OK) return -1;
+  if (device_state(&ds) != FQKV_OK) return -1;  // device_state recorded the message
   DecodeLaunch a{};
   a.fmt = kv_format == FQKV_KV_F16 ? KvFormat::F16 : KvFormat::I8;
   a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(max_len); a.D = int(D);

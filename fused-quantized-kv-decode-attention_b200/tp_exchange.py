@@ -69,14 +69,23 @@ class PeerExchange:
             handles = [None] * self.world
             dist.all_gather_object(handles, bytes(handle), group=group)
             self.peers = []
-            for r, h in enumerate(handles):
-                if r == self.rank:
-                    self.peers.append(self.base)
-                    continue
-                p = ctypes.c_void_p()
-                buf = (ctypes.c_ubyte * 64).from_buffer_copy(h)
-                _check(lib.fqkv_ipc_open(buf, ctypes.byref(p)), f"ipc_open (rank {r})")
-                self.peers.append(int(p.value))
+            try:
+                for r, h in enumerate(handles):
+                    if r == self.rank:
+                        self.peers.append(self.base)
+                        continue
+                    p = ctypes.c_void_p()
+                    buf = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+                    _check(lib.fqkv_ipc_open(buf, ctypes.byref(p)), f"ipc_open (rank {r})")
+                    self.peers.append(int(p.value))
+            except Exception:
+                # undo this rank's mappings and memory; the other ranks' waits on this rank
+                # then end with device status 64 instead of hanging
+                for r, p in enumerate(self.peers):
+                    if r != self.rank:
+                        lib.fqkv_ipc_close(ctypes.c_void_p(p))
+                lib.fqkv_ipc_free(ctypes.c_void_p(self.base))
+                raise
         self.counters = self.base
         self.sequence = self.base + _ALIGN
         self.tp_out = []

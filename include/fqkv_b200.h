@@ -281,7 +281,8 @@ int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K,
                                 const fqkv_tp_out_t* tp, fqkv_stream_t stream);
 
 /* Arrivals one call of fqkv_decode_attn_kvcache_tp with these sizes (and the
- * same workspace size) counts on each counter slot; the waiter's per_call. */
+ * same workspace size) counts on each counter slot; the waiter's per_call.
+ * Returns -1 (message in fqkv_last_error) on bad arguments. */
 int64_t fqkv_tp_arrivals(int32_t kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
                          size_t workspace_bytes);
 
