@@ -225,6 +225,11 @@ void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_byt
       const int64_t active = std::min(C, U - done);
       cost += double(std::max<int64_t>(active, floor_ctas)) * double(ct + (se > 1 ? 1 : 0));
     }
+    // The combine kernel (its wait for the partial grid, the partials' round
+    // trip through L2) costs about three tile-rounds of the whole grid,
+    // measured on B200: e.g. B=64, Hkv=8, N=640, D=64 runs 20.4 us unsplit
+    // against 25.7 us in two splits.
+    if (se > 1) cost += 3.0 * double(C);
     if (cost < best * 0.999) {
       best = cost;
       best_S = se;
