@@ -598,17 +598,35 @@ int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, in
   return FQKV_OK;
 }
 
-int fqkv_gemv(int32_t model_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B, int64_t N,
-              int64_t K, fqkv_stream_t stream) {
+int fqkv_gemv(int32_t model_dtype, int32_t x_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B,
+              int64_t N, int64_t K, fqkv_stream_t stream) {
   if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (x_dtype != 0 && x_dtype != model_dtype)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "gemv: x_dtype is the model dtype or 0 (f16)");
   if (B < 1 || B > 4 || N < 1 || N > INT32_MAX / 2 || K < 256 || K % 256 != 0 || K > 16384)
     return fail(FQKV_ERR_INVALID_ARGUMENT, "gemv: need 1 <= B <= 4, N >= 1, K a multiple of 256 in [256, 16384]");
   if (!x || !W || !y) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
   if (!aligned(x, 16) || !aligned(W, 16) || !aligned(y, 2) || (bias && !aligned(bias, 2)))
     return fail(FQKV_ERR_MISALIGNED, "gemv: x and W must be 16-byte aligned");
-  cudaError_t e = fqkv::launch_gemv(model_dtype == 1, x, W, bias, y, int(B), int(N), int(K),
+  cudaError_t e = fqkv::launch_gemv(model_dtype == 1, x_dtype == 0, x, W, bias, y, int(B), int(N), int(K),
                                     reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+  return FQKV_OK;
+}
+
+size_t fqkv_argmax_scratch_bytes(int64_t rows) { return rows > 0 ? fqkv::argmax_scratch_bytes(rows) : 0; }
+
+int fqkv_argmax(int32_t model_dtype, const void* logits, int64_t rows, int64_t V, void* scratch, int64_t* idx,
+                fqkv_stream_t stream) {
+  if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (rows < 0 || rows > 65535 || V < 1 || V > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "argmax: bad sizes");
+  if (rows == 0) return FQKV_OK;
+  if (!logits || !scratch || !idx) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(logits, 2) || !aligned(scratch, 4) || !aligned(idx, 8))
+    return fail(FQKV_ERR_MISALIGNED, "argmax: misaligned pointer");
+  cudaError_t e = fqkv::launch_argmax(model_dtype == 1, logits, rows, int(V), scratch, idx,
+                                      reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
   return FQKV_OK;
 }
 

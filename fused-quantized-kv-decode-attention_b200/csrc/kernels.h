@@ -127,8 +127,11 @@ cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void
                                float eps, cudaStream_t stream);
 cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, int I, int64_t row_stride,
                             cudaStream_t stream);
-cudaError_t launch_gemv(bool bf16, const void* x, const void* W, const void* bias, void* y, int B, int N, int K,
-                        cudaStream_t stream);
+cudaError_t launch_gemv(bool bf16, bool x_f16, const void* x, const void* W, const void* bias, void* y, int B, int N,
+                        int K, cudaStream_t stream);
+size_t argmax_scratch_bytes(int64_t rows);
+cudaError_t launch_argmax(bool bf16, const void* logits, int64_t rows, int V, void* scratch, int64_t* out,
+                          cudaStream_t stream);
 // Tensor-parallel arrival wait (tp.cu).
 cudaError_t launch_tp_wait(const unsigned long long* counters, int world, unsigned long long per_call,
                            unsigned long long* sequence, int* status, unsigned long long timeout_ns,

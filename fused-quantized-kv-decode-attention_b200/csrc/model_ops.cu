@@ -15,6 +15,7 @@
 // One CTA per row for add_rmsnorm (hidden sizes up to 8192), a grid-stride
 // loop for silu_mul.  Both are HBM-bound and tiny; the point is the launch
 // count of a decode step.
+#include <type_traits>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -179,9 +180,9 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu,
 // aligned.
 constexpr int kGemvWarps = 8;
 template <typename T, int B, int RPW>
-__global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const T* __restrict__ x, const T* __restrict__ W,
+__global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __restrict__ x, const T* __restrict__ W,
                                                                const T* __restrict__ bias, T* __restrict__ y, int N,
-                                                               int K) {
+                                                               int K, bool x_f16) {
   extern __shared__ uint4 xs[];  // [B][K/8] chunks
   const int kc = K / 8;
   const int lane = threadIdx.x & 31;
@@ -202,7 +203,21 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const T* __restri
       }
   };
   load_w(lane);
-  for (int i = threadIdx.x; i < B * kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
+  if (std::is_same<T, __half>::value || !x_f16) {
+    for (int i = threadIdx.x; i < B * kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
+  } else {
+    // fp16 activations for bf16 weights (the attention output): rounded to
+    // bf16 here, as a separate cast would
+    for (int i = threadIdx.x; i < B * kc; i += blockDim.x) {
+      const uint4 hv = reinterpret_cast<const uint4*>(x)[i];
+      const __half* hp = reinterpret_cast<const __half*>(&hv);
+      uint4 bv;
+      T* bp = reinterpret_cast<T*>(&bv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) bp[e] = cvt<T>(__half2float(hp[e]));
+      xs[i] = bv;
+    }
+  }
   __syncthreads();
   if (n0 >= N) return;
   float acc[RPW][B];
@@ -250,43 +265,136 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const T* __restri
 }
 
 template <typename T, int B>
-cudaError_t launch_gemv_t(const void* x, const void* W, const void* bias, void* y, int N, int K, cudaStream_t stream) {
+cudaError_t launch_gemv_t(const void* x, const void* W, const void* bias, void* y, int N, int K, bool x_f16,
+                          cudaStream_t stream) {
   const size_t smem = size_t(B) * K * sizeof(T);
   if (K <= 2048) {
     constexpr int RPW = 2;
     const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
     auto fn = gemv_kernel<T, B, RPW>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(static_cast<const T*>(x), static_cast<const T*>(W),
-                                                 static_cast<const T*>(bias), static_cast<T*>(y), N, K);
+    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(x, static_cast<const T*>(W), static_cast<const T*>(bias),
+                                                 static_cast<T*>(y), N, K, x_f16);
   } else {
     constexpr int RPW = 1;
     const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
     auto fn = gemv_kernel<T, B, RPW>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(static_cast<const T*>(x), static_cast<const T*>(W),
-                                                 static_cast<const T*>(bias), static_cast<T*>(y), N, K);
+    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(x, static_cast<const T*>(W), static_cast<const T*>(bias),
+                                                 static_cast<T*>(y), N, K, x_f16);
   }
   return cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t launch_gemv_b(const void* x, const void* W, const void* bias, void* y, int B, int N, int K,
+cudaError_t launch_gemv_b(const void* x, const void* W, const void* bias, void* y, int B, int N, int K, bool x_f16,
                           cudaStream_t stream) {
   switch (B) {
-    case 1: return launch_gemv_t<T, 1>(x, W, bias, y, N, K, stream);
-    case 2: return launch_gemv_t<T, 2>(x, W, bias, y, N, K, stream);
-    case 3: return launch_gemv_t<T, 3>(x, W, bias, y, N, K, stream);
-    default: return launch_gemv_t<T, 4>(x, W, bias, y, N, K, stream);
+    case 1: return launch_gemv_t<T, 1>(x, W, bias, y, N, K, x_f16, stream);
+    case 2: return launch_gemv_t<T, 2>(x, W, bias, y, N, K, x_f16, stream);
+    case 3: return launch_gemv_t<T, 3>(x, W, bias, y, N, K, x_f16, stream);
+    default: return launch_gemv_t<T, 4>(x, W, bias, y, N, K, x_f16, stream);
+  }
+}
+
+// Row-wise argmax of logits [rows, V] (model dtype) -> idx [rows] int64, as
+// torch.argmax (first index of the maximum; NaN counts as the maximum).  A
+// single-output torch reduction over a 128K vocabulary runs on one CTA; here
+// kArgBlocks CTAs share a row, each writes its (value, index) partial, and the
+// last CTA to arrive (counter per row, reset by that CTA, so the scratch stays
+// reusable across calls and CUDA-graph replays) reduces the partials.
+constexpr int kArgThreads = 256;
+constexpr int kArgBlocks = 64;
+
+__device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
+  // NaN is the largest value (torch.argmax); ties keep the lower index
+  if (isnan(v)) return !isnan(bv) || i < bi;
+  if (isnan(bv)) return false;
+  return v > bv || (v == bv && i < bi);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict__ logits, int V,
+                                                             float* __restrict__ part_v, int* __restrict__ part_i,
+                                                             unsigned* __restrict__ counters,
+                                                             int64_t* __restrict__ out) {
+  const int row = blockIdx.y, blk = blockIdx.x;
+  const T* lr = logits + int64_t(row) * V;
+  const int per = (V + kArgBlocks - 1) / kArgBlocks;
+  const int lo = blk * per, hi = min(V, lo + per);
+  float bv = -INFINITY;
+  int bi = INT32_MAX;
+  for (int i = lo + threadIdx.x; i < hi; i += kArgThreads) {
+    const float v = ld<T>(lr, i);
+    if (arg_better(v, i, bv, bi)) { bv = v; bi = i; }
+  }
+  __shared__ float sv[kArgThreads / 32];
+  __shared__ int si[kArgThreads / 32];
+  __shared__ bool last;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (arg_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kArgThreads / 32; ++w)
+      if (arg_better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
+    part_v[row * kArgBlocks + blk] = bv;
+    part_i[row * kArgBlocks + blk] = bi;
+    __threadfence();
+    last = atomicAdd(&counters[row], 1u) == kArgBlocks - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (threadIdx.x < 32) {
+    float v = -INFINITY;
+    int i = INT32_MAX;
+    for (int b = threadIdx.x; b < kArgBlocks; b += 32) {
+      const float pv = *reinterpret_cast<volatile float*>(&part_v[row * kArgBlocks + b]);
+      const int pi = *reinterpret_cast<volatile int*>(&part_i[row * kArgBlocks + b]);
+      if (arg_better(pv, pi, v, i)) { v = pv; i = pi; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, off);
+      if (arg_better(ov, oi, v, i)) { v = ov; i = oi; }
+    }
+    if (threadIdx.x == 0) {
+      out[row] = int64_t(i);
+      counters[row] = 0u;  // ready for the next call
+    }
   }
 }
 
 }  // namespace
 
-cudaError_t launch_gemv(bool bf16, const void* x, const void* W, const void* bias, void* y, int B, int N, int K,
-                        cudaStream_t stream) {
-  return bf16 ? launch_gemv_b<__nv_bfloat16>(x, W, bias, y, B, N, K, stream)
-              : launch_gemv_b<__half>(x, W, bias, y, B, N, K, stream);
+size_t argmax_scratch_bytes(int64_t rows) {
+  return size_t(rows) * kArgBlocks * (sizeof(float) + sizeof(int)) + size_t(rows) * sizeof(unsigned);
+}
+
+cudaError_t launch_argmax(bool bf16, const void* logits, int64_t rows, int V, void* scratch, int64_t* out,
+                          cudaStream_t stream) {
+  float* pv = static_cast<float*>(scratch);
+  int* pi = reinterpret_cast<int*>(pv + rows * kArgBlocks);
+  unsigned* cnt = reinterpret_cast<unsigned*>(pi + rows * kArgBlocks);
+  const dim3 grid(kArgBlocks, unsigned(rows));
+  if (bf16)
+    argmax_kernel<__nv_bfloat16><<<grid, kArgThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), V, pv,
+                                                                   pi, cnt, out);
+  else
+    argmax_kernel<__half><<<grid, kArgThreads, 0, stream>>>(static_cast<const __half*>(logits), V, pv, pi, cnt, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(bool bf16, bool x_f16, const void* x, const void* W, const void* bias, void* y, int B, int N,
+                        int K, cudaStream_t stream) {
+  return bf16 ? launch_gemv_b<__nv_bfloat16>(x, W, bias, y, B, N, K, x_f16, stream)
+              : launch_gemv_b<__half>(x, W, bias, y, B, N, K, true, stream);
 }
 
 cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void* w, void* y, int64_t rows, int H,

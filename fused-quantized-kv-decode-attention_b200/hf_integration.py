@@ -193,6 +193,9 @@ class GraphDecoder:
             # 1.5-2x faster than cuBLAS's batch-1..4 kernels on B200); gate/up and the LM head stay
             # on cuBLAS, which streams those large matrices near HBM speed.
             self.small_b = batch <= 4 and H % 256 == 0 and I % 256 == 0 and (self.Hq * self.D) % 256 == 0
+            self.arg_scratch = torch.zeros(int(_native.lib().fqkv_argmax_scratch_bytes(batch)), dtype=torch.uint8,
+                                           device=dev)
+            self.nxt = torch.empty(batch, dtype=torch.long, device=dev)
         self.graph = None
         self.prompt_len = 0
 
@@ -342,12 +345,12 @@ class GraphDecoder:
                 o = self.xchg.gathered(li).permute(1, 0, 2, 3).reshape(B, self.Hq * self.D)
             else:
                 o = self._heads(self.attn_out.view(B, 1, self.Hq_l, self.D), self.gather_buf).view(B, -1)
-            o = o.to(h.dtype)
             if self.small_b:
+                # the GEMV reads the fp16 attention output and rounds it to the model dtype
                 ob = attn.o_proj.bias.detach() if attn.o_proj.bias is not None else None
                 a = ops.gemv(o.contiguous(), attn.o_proj.weight.detach(), ob)
             else:
-                a = attn.o_proj(o)
+                a = attn.o_proj(o.to(h.dtype))
             ops.add_rmsnorm(h, a, layer.post_attention_layernorm.weight, x,
                             layer.post_attention_layernorm.variance_epsilon)
             gu = F.linear(x, self.wgu[li], self.bgu[li])
@@ -359,8 +362,8 @@ class GraphDecoder:
                 d = layer.mlp.down_proj(self.act)
             nrm = layers[li + 1].input_layernorm if li + 1 < len(layers) else m.norm
             ops.add_rmsnorm(h, d, nrm.weight, x, nrm.variance_epsilon)
-        logits = self.model.lm_head(x).float()
-        nxt = logits.argmax(-1)
+        logits = self.model.lm_head(x)
+        nxt = ops.argmax_rows(logits, self.arg_scratch, self.nxt)   # as logits.argmax(-1), multi-CTA
         if self.keep_logits:
             self.logits.copy_(logits)
         self.pos.add_(1)

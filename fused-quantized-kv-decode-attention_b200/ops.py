@@ -572,24 +572,56 @@ def silu_mul(gu: torch.Tensor, y: torch.Tensor) -> None:
 
 def gemv(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = None,
          out: torch.Tensor | None = None) -> torch.Tensor:
-    """Small-batch projection y = x W^T (+ bias): x [B, K] (B <= 4), W [N, K], model dtype, fp32 accumulation."""
+    """Small-batch projection y = x W^T (+ bias): x [B, K] (B <= 4), W [N, K], model dtype, fp32 accumulation.
+
+    With bf16 weights x may be fp16 (rounded to bf16 as it is read, the same
+    as ``x.to(torch.bfloat16)`` first); the output is in the weights' dtype.
+    """
     op = "gemv"
-    ts = dict(x=x, W=W) if bias is None else dict(x=x, W=W, bias=bias)
-    dev = _require_cuda(op, *ts.values())
-    if x.dtype not in (torch.float16, torch.bfloat16):
-        _fail(op, "dtype", "x must be fp16 or bf16")
-    _require_dtype(op, "model dtype", x.dtype, **ts)
+    ts = dict(W=W) if bias is None else dict(W=W, bias=bias)
+    dev = _require_cuda(op, x, *ts.values())
+    if W.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", "W must be fp16 or bf16")
+    _require_dtype(op, "model dtype", W.dtype, **ts)
+    if x.dtype != W.dtype and x.dtype != torch.float16:
+        _fail(op, "dtype", "x must be in the weights' dtype or fp16")
+    _require_contig(op, x=x)
     _require_contig(op, **ts)
     if x.dim() != 2 or W.dim() != 2 or x.shape[1] != W.shape[1] or (bias is not None and bias.shape != (W.shape[0],)):
         _fail(op, "shape", "x [B, K], W [N, K], bias [N]")
     B, K = x.shape
     N = W.shape[0]
     if out is None:
-        out = torch.empty(B, N, dtype=x.dtype, device=dev)
+        out = torch.empty(B, N, dtype=W.dtype, device=dev)
+    code = {torch.float16: 0, torch.bfloat16: 1}
     with _DeviceGuard(dev):
-        rc = _native.lib().fqkv_gemv(1 if x.dtype == torch.bfloat16 else 0, x.data_ptr(), W.data_ptr(),
+        rc = _native.lib().fqkv_gemv(code[W.dtype], code[x.dtype], x.data_ptr(), W.data_ptr(),
                                      bias.data_ptr() if bias is not None else None, out.data_ptr(), B, N, K,
                                      _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return out
+
+
+def argmax_rows(logits: torch.Tensor, scratch: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy choice per row: logits [rows, V] (fp16 / bf16) -> int64 [rows], as torch.argmax(-1).
+
+    ``scratch``: a zero-filled uint8 tensor of ``fqkv_argmax_scratch_bytes(rows)``
+    bytes, reusable across calls (and CUDA-graph replays).
+    """
+    op = "argmax_rows"
+    dev = _require_cuda(op, logits, scratch)
+    if logits.dtype not in (torch.float16, torch.bfloat16) or logits.dim() != 2 or logits.stride(1) != 1 \
+            or logits.stride(0) != logits.shape[1]:
+        _fail(op, "logits", "logits must be a contiguous fp16 / bf16 [rows, V] tensor")
+    rows, V = logits.shape
+    need = int(_native.lib().fqkv_argmax_scratch_bytes(rows))
+    if scratch.dtype != torch.uint8 or scratch.numel() < need:
+        _fail(op, "scratch", f"scratch must be a uint8 tensor of >= {need} bytes")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=dev)
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_argmax(1 if logits.dtype == torch.bfloat16 else 0, logits.data_ptr(), rows, V,
+                                       scratch.data_ptr(), out.data_ptr(), _stream(dev))
     _native.check(rc, f"launch: {op}")
     return out
 

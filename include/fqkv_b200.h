@@ -242,10 +242,21 @@ int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, in
                   fqkv_stream_t stream);
 
 /* Small-batch projection of a decode step: y [B,N] = x [B,K] W^T (+ bias [N])
- * with W [N,K] row-major, all in the model dtype, fp32 accumulation, B in
- * 1..4, K a multiple of 256, x / W / y 16-byte aligned. */
-int fqkv_gemv(int32_t model_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B, int64_t N,
-              int64_t K, fqkv_stream_t stream);
+ * with W [N,K] row-major, W / bias / y in the model dtype, fp32
+ * accumulation, B in 1..4, K a multiple of 256, x / W / y 16-byte aligned.
+ * x_dtype is the model dtype, or 0 (fp16) with bf16 weights: x is then
+ * rounded to bf16 as it is read (the fp16 attention output feeding a bf16
+ * output projection, with no separate cast). */
+int fqkv_gemv(int32_t model_dtype, int32_t x_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B,
+              int64_t N, int64_t K, fqkv_stream_t stream);
+
+/* Greedy token choice: idx [rows] int64 = argmax over each row of logits
+ * [rows, V] (model dtype), first index of the maximum, NaN largest (as
+ * torch.argmax).  `scratch` holds fqkv_argmax_scratch_bytes(rows) bytes,
+ * zero-filled before its first use; the call leaves it reusable. */
+size_t fqkv_argmax_scratch_bytes(int64_t rows);
+int fqkv_argmax(int32_t model_dtype, const void* logits, int64_t rows, int64_t V, void* scratch, int64_t* idx,
+                fqkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Tensor-parallel decode: attention fused with the all-gather of its outputs.

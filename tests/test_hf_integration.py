@@ -271,3 +271,42 @@ def test_gemv_matches_fp32_projection(fqkv, dtype, B, N, K):
     got = fqkv.gemv(x, W, b).float()
     tol = torch.finfo(dtype).eps * ref.abs() + 1e-4 * ref.abs().max()
     assert ((got - ref).abs() <= tol).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("rows,V", [(1, 128256), (4, 32000), (64, 128256), (3, 100), (2, 1)])
+def test_argmax_rows_matches_torch(fqkv, dtype, rows, V):
+    """Multi-CTA argmax: the same index as torch.argmax, ties to the first index, reusable scratch."""
+    from importlib import import_module
+    native = import_module(fqkv.__name__ + "._native")
+
+    torch.manual_seed(rows * 7 + V)
+    scratch = torch.zeros(int(native.lib().fqkv_argmax_scratch_bytes(rows)), dtype=torch.uint8, device="cuda")
+    for trial in range(3):
+        x = (torch.randn(rows, V, device="cuda") * 4).to(dtype)
+        if trial == 1 and V > 8:
+            # ties: the maximum repeated in several slices of the row
+            m = x.float().max() + 1
+            x[:, V // 3] = m.to(dtype)
+            x[:, V - 1] = m.to(dtype)
+            x[:, V // 7 + 1] = m.to(dtype)
+        if trial == 2:
+            x[0, V // 2] = float("nan")
+            if V > 4:
+                x[0, V - 1] = float("nan")
+        got = fqkv.ops.argmax_rows(x, scratch)
+        assert torch.equal(got.cpu(), x.argmax(-1).cpu()), trial
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,N,K", [(1, 2048, 2048), (3, 300, 512), (4, 77, 4096)])
+def test_gemv_fp16_activations_bf16_weights_equal_cast_first(fqkv, B, N, K):
+    """fp16 x with bf16 W: bit-identical to casting x to bf16 before the GEMV."""
+    torch.manual_seed(N + K)
+    x = (torch.randn(B, K, device="cuda") * 3).half()
+    W = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    b = torch.randn(N, device="cuda").bfloat16()
+    got = fqkv.gemv(x, W, b)
+    assert got.dtype == torch.bfloat16
+    assert torch.equal(got, fqkv.gemv(x.to(torch.bfloat16), W, b))
