@@ -24,6 +24,7 @@
 #include <cmath>
 #include <cstdint>
 
+#include "device_common.cuh"
 #include "kernels.h"
 
 namespace fqkv {
@@ -55,6 +56,8 @@ template <typename T>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(T* __restrict__ h, const T* __restrict__ delta,
                                                                    const T* __restrict__ w, T* __restrict__ y, int H,
                                                                    float eps) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
   const int64_t row = blockIdx.x;
   T* hr = h + row * H;
   const T* dr = delta ? delta + row * H : nullptr;
@@ -98,6 +101,8 @@ template <typename T>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_vec_kernel(T* __restrict__ h, const T* __restrict__ delta,
                                                                        const T* __restrict__ w, T* __restrict__ y,
                                                                        int H, float eps) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
   const int64_t row = blockIdx.x;
   const int chunks = H / 8;
   uint4 hv[kMaxChunks], dv[kMaxChunks], wv[kMaxChunks];
@@ -159,6 +164,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_vec_kernel(T* __rest
 template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ y, int64_t rows,
                                                        int I, int64_t row_stride) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
   const int64_t n = rows * I;
   for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
        idx += int64_t(gridDim.x) * blockDim.x) {
@@ -203,6 +210,10 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
       }
   };
   load_w(lane);
+  // Weights are not written by the kernels this launch may overlap: only the
+  // activations wait for the previous kernel.
+  pdl_wait_primary();
+  pdl_launch_dependents();
   if (std::is_same<T, __half>::value || !x_f16) {
     for (int i = threadIdx.x; i < B * kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
   } else {
@@ -273,17 +284,16 @@ cudaError_t launch_gemv_t(const void* x, const void* W, const void* bias, void* 
     const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
     auto fn = gemv_kernel<T, B, RPW>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(x, static_cast<const T*>(W), static_cast<const T*>(bias),
-                                                 static_cast<T*>(y), N, K, x_f16);
+    return launch_pdl(fn, dim3(blocks), dim3(32 * kGemvWarps), smem, stream, x, static_cast<const T*>(W),
+                      static_cast<const T*>(bias), static_cast<T*>(y), N, K, x_f16);
   } else {
     constexpr int RPW = 1;
     const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
     auto fn = gemv_kernel<T, B, RPW>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(x, static_cast<const T*>(W), static_cast<const T*>(bias),
-                                                 static_cast<T*>(y), N, K, x_f16);
+    return launch_pdl(fn, dim3(blocks), dim3(32 * kGemvWarps), smem, stream, x, static_cast<const T*>(W),
+                      static_cast<const T*>(bias), static_cast<T*>(y), N, K, x_f16);
   }
-  return cudaGetLastError();
 }
 
 template <typename T>
@@ -318,6 +328,8 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict
                                                              float* __restrict__ part_v, int* __restrict__ part_i,
                                                              unsigned* __restrict__ counters,
                                                              int64_t* __restrict__ out) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
   const int row = blockIdx.y, blk = blockIdx.x;
   const T* lr = logits + int64_t(row) * V;
   const int per = (V + kArgBlocks - 1) / kArgBlocks;
@@ -384,11 +396,10 @@ cudaError_t launch_argmax(bool bf16, const void* logits, int64_t rows, int V, vo
   unsigned* cnt = reinterpret_cast<unsigned*>(pi + rows * kArgBlocks);
   const dim3 grid(kArgBlocks, unsigned(rows));
   if (bf16)
-    argmax_kernel<__nv_bfloat16><<<grid, kArgThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), V, pv,
-                                                                   pi, cnt, out);
-  else
-    argmax_kernel<__half><<<grid, kArgThreads, 0, stream>>>(static_cast<const __half*>(logits), V, pv, pi, cnt, out);
-  return cudaGetLastError();
+    return launch_pdl(argmax_kernel<__nv_bfloat16>, grid, dim3(kArgThreads), 0, stream,
+                      static_cast<const __nv_bfloat16*>(logits), V, pv, pi, cnt, out);
+  return launch_pdl(argmax_kernel<__half>, grid, dim3(kArgThreads), 0, stream, static_cast<const __half*>(logits), V,
+                    pv, pi, cnt, out);
 }
 
 cudaError_t launch_gemv(bool bf16, bool x_f16, const void* x, const void* W, const void* bias, void* y, int B, int N,
@@ -403,24 +414,20 @@ cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void
   const auto al16 = [](const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   if (H % 8 == 0 && al16(h) && al16(delta) && al16(w) && al16(y)) {
     if (bf16)
-      add_rmsnorm_vec_kernel<__nv_bfloat16><<<unsigned(rows), kNormThreads, 0, stream>>>(
-          static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
-          static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), H, eps);
-    else
-      add_rmsnorm_vec_kernel<__half><<<unsigned(rows), kNormThreads, 0, stream>>>(
-          static_cast<__half*>(h), static_cast<const __half*>(delta), static_cast<const __half*>(w),
-          static_cast<__half*>(y), H, eps);
-    return cudaGetLastError();
+      return launch_pdl(add_rmsnorm_vec_kernel<__nv_bfloat16>, dim3(unsigned(rows)), dim3(kNormThreads), 0, stream,
+                        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
+                        static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), H, eps);
+    return launch_pdl(add_rmsnorm_vec_kernel<__half>, dim3(unsigned(rows)), dim3(kNormThreads), 0, stream,
+                      static_cast<__half*>(h), static_cast<const __half*>(delta), static_cast<const __half*>(w),
+                      static_cast<__half*>(y), H, eps);
   }
   if (bf16)
-    add_rmsnorm_kernel<__nv_bfloat16><<<unsigned(rows), kNormThreads, 0, stream>>>(
-        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
-        static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), H, eps);
-  else
-    add_rmsnorm_kernel<__half><<<unsigned(rows), kNormThreads, 0, stream>>>(
-        static_cast<__half*>(h), static_cast<const __half*>(delta), static_cast<const __half*>(w),
-        static_cast<__half*>(y), H, eps);
-  return cudaGetLastError();
+    return launch_pdl(add_rmsnorm_kernel<__nv_bfloat16>, dim3(unsigned(rows)), dim3(kNormThreads), 0, stream,
+                      static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(delta),
+                      static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), H, eps);
+  return launch_pdl(add_rmsnorm_kernel<__half>, dim3(unsigned(rows)), dim3(kNormThreads), 0, stream,
+                    static_cast<__half*>(h), static_cast<const __half*>(delta), static_cast<const __half*>(w),
+                    static_cast<__half*>(y), H, eps);
 }
 
 cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, int I, int64_t row_stride,
@@ -428,12 +435,10 @@ cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, in
   const int64_t n = rows * I;
   const unsigned blocks = unsigned(std::min<int64_t>((n + 255) / 256, 148 * 16));
   if (bf16)
-    silu_mul_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gu),
-                                                               static_cast<__nv_bfloat16*>(y), rows, I, row_stride);
-  else
-    silu_mul_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(gu), static_cast<__half*>(y), rows,
-                                                        I, row_stride);
-  return cudaGetLastError();
+    return launch_pdl(silu_mul_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream,
+                      static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(y), rows, I, row_stride);
+  return launch_pdl(silu_mul_kernel<__half>, dim3(blocks), dim3(256), 0, stream, static_cast<const __half*>(gu),
+                    static_cast<__half*>(y), rows, I, row_stride);
 }
 
 }  // namespace fqkv

@@ -23,6 +23,7 @@
 #include <cmath>
 #include <cstdint>
 
+#include "device_common.cuh"
 #include "kernels.h"
 
 namespace fqkv {
@@ -205,6 +206,8 @@ struct RopeAppendArgs {
 
 template <typename T, int D, bool kInt8>
 __global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendArgs a) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
   constexpr int M = D / 32;  // elements per lane
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -272,11 +275,11 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendArgs a
 }
 
 template <typename T, int D>
-void launch_rope_append_t(const RopeAppendArgs& a, bool int8, cudaStream_t stream) {
+cudaError_t launch_rope_append_t(const RopeAppendArgs& a, bool int8, cudaStream_t stream) {
   const int64_t rows = int64_t(a.B) * (a.Hq + 2 * a.Hkv);
   const unsigned blocks = unsigned((rows * 32 + 255) / 256);
-  if (int8) rope_append_kernel<T, D, true><<<blocks, 256, 0, stream>>>(a);
-  else rope_append_kernel<T, D, false><<<blocks, 256, 0, stream>>>(a);
+  if (int8) return launch_pdl(rope_append_kernel<T, D, true>, dim3(blocks), dim3(256), 0, stream, a);
+  return launch_pdl(rope_append_kernel<T, D, false>, dim3(blocks), dim3(256), 0, stream, a);
 }
 
 }  // namespace
@@ -288,14 +291,11 @@ cudaError_t launch_rope_append(bool bf16, bool int8_cache, const void* qkv, int6
   const RopeAppendArgs a{qkv,     qkv_stride, cos_t,   sin_t,   table_rows,
                          pos_host, pos_dev,   static_cast<__half*>(q_out), k_cache, v_cache,
                          static_cast<__half*>(k_scales), static_cast<__half*>(v_scales), B, Hq, Hkv, cap};
-  if (bf16) {
-    if (D == 128) launch_rope_append_t<__nv_bfloat16, 128>(a, int8_cache, stream);
-    else launch_rope_append_t<__nv_bfloat16, 64>(a, int8_cache, stream);
-  } else {
-    if (D == 128) launch_rope_append_t<__half, 128>(a, int8_cache, stream);
-    else launch_rope_append_t<__half, 64>(a, int8_cache, stream);
-  }
-  return cudaGetLastError();
+  if (bf16)
+    return D == 128 ? launch_rope_append_t<__nv_bfloat16, 128>(a, int8_cache, stream)
+                    : launch_rope_append_t<__nv_bfloat16, 64>(a, int8_cache, stream);
+  return D == 128 ? launch_rope_append_t<__half, 128>(a, int8_cache, stream)
+                  : launch_rope_append_t<__half, 64>(a, int8_cache, stream);
 }
 
 cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,

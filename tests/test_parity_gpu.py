@@ -181,6 +181,29 @@ def test_cuda_graph_capture_and_side_stream(fqkv):
     torch.testing.assert_close(cap, ref, atol=0, rtol=0)
 
 
+def test_split_launches_on_two_streams_at_once(fqkv):
+    """Split launches (partial kernel + combine) in flight on two streams at once, each with its own workspace."""
+    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 128
+    assert fqkv.workspace_bytes("fp16", B, Hq, Hkv, N, D) > 0
+    inputs = [(_randn(B, Hq, D, seed=100 + i).cuda(), _randn(B, Hkv, N, D, seed=110 + i).cuda(),
+               _randn(B, Hkv, N, D, seed=120 + i).cuda()) for i in range(2)]
+    refs = [fqkv.decode_attn_gqa(*x, 8) for x in inputs]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for st in streams:
+        st.wait_stream(torch.cuda.current_stream())
+    outs = [[], []]
+    for _ in range(20):
+        for i, st in enumerate(streams):
+            with torch.cuda.stream(st):
+                outs[i].append(fqkv.decode_attn_gqa(*inputs[i], 8))
+    for st in streams:
+        torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    for i in range(2):
+        for o in outs[i]:
+            assert torch.equal(o, refs[i])
+
+
 def test_device_status_clean_after_suite(fqkv):
     import ctypes
     st = ctypes.c_int(-1)
