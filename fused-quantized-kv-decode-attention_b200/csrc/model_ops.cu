@@ -181,21 +181,28 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu,
 // Small-batch GEMV: y [B, N] = x [B, K] @ W[N, K]^T (+ bias), B <= 4, fp32
 // accumulation, output rounded to the model dtype.  A batch-1..4 decode step's
 // projections are weight-streaming GEMVs that cuBLAS's batch-1 kernels run far
-// below HBM speed.  One warp per weight row (two rows when K <= 2048); lanes
-// read 16-byte chunks 256 elements apart, x is staged in shared memory, every
-// lane keeps K/256 independent loads in flight.  K % 256 == 0, rows 16-byte
-// aligned.
+// below HBM speed.  A row group of WPR warps owns RPW weight rows (two rows of
+// one warp when K <= 2048; at batch 1 one row split into WPR K-slices of
+// <= 2048 elements), and a lane issues a pass of 8 independent 16-byte loads
+// per row, 256 elements apart (one pass per 2048 elements of its slice).  x is
+// staged in shared memory; the WPR slice sums of a row are added in a fixed
+// order.
+// K % 256 == 0, rows 16-byte aligned.
 constexpr int kGemvWarps = 8;
-template <typename T, int B, int RPW>
+template <typename T, int B, int RPW, int WPR>
 __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __restrict__ x, const T* __restrict__ W,
                                                                const T* __restrict__ bias, T* __restrict__ y, int N,
                                                                int K, bool x_f16) {
   extern __shared__ uint4 xs[];  // [B][K/8] chunks
+  __shared__ float red[kGemvWarps][RPW][B];
+  constexpr int kGroups = kGemvWarps / WPR;  // row groups per CTA
   const int kc = K / 8;
   const int lane = threadIdx.x & 31;
-  const int warp_global = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
-  const int n0 = warp_global * RPW;
-  constexpr int U = 8;  // chunks per lane per pass: K = 2048 is one pass
+  const int warp = threadIdx.x >> 5;
+  const int n0 = (blockIdx.x * kGroups + warp / WPR) * RPW;
+  const int kcw = kc / WPR;                  // chunks of this warp's K slice
+  const int c_lo = (warp % WPR) * kcw, c_hi = c_lo + kcw;
+  constexpr int U = 8;  // chunks per lane per pass: a 2048-element slice is one pass
   uint4 wv[RPW][U];
   // the first pass's weight loads are issued before x is staged, so the two
   // memory round trips overlap
@@ -205,15 +212,15 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int cc = c + 32 * u;
-        if (cc < kc && n0 + r < N) wv[r][u] = reinterpret_cast<const uint4*>(W + int64_t(n0 + r) * K)[cc];
+        if (cc < c_hi && n0 + r < N) wv[r][u] = reinterpret_cast<const uint4*>(W + int64_t(n0 + r) * K)[cc];
         else wv[r][u] = make_uint4(0, 0, 0, 0);
       }
   };
-  load_w(lane);
-  // Weights are not written by the kernels this launch may overlap: only the
-  // activations wait for the previous kernel.
+  load_w(c_lo + lane);
+  // Batch 1 is launched with programmatic dependent launch: the weights are
+  // not written by the kernel this launch may overlap, only the activations
+  // wait for it.  (The next kernel is released when this grid completes.)
   pdl_wait_primary();
-  pdl_launch_dependents();
   if (std::is_same<T, __half>::value || !x_f16) {
     for (int i = threadIdx.x; i < B * kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
   } else {
@@ -230,27 +237,28 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
     }
   }
   __syncthreads();
-  if (n0 >= N) return;
   float acc[RPW][B];
 #pragma unroll
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
-  for (int c = lane; c < kc; c += 32 * U) {
-    if (c != lane) load_w(c);
+  if (n0 < N) {
+    for (int c = c_lo + lane; c < c_hi; c += 32 * U) {
+      if (c != c_lo + lane) load_w(c);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int cc = c + 32 * u;
-      if (cc >= kc) continue;
+      for (int u = 0; u < U; ++u) {
+        const int cc = c + 32 * u;
+        if (cc >= c_hi) continue;
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const uint4 xv = xs[b * kc + cc];
-        const T* xp = reinterpret_cast<const T*>(&xv);
+        for (int b = 0; b < B; ++b) {
+          const uint4 xv = xs[b * kc + cc];
+          const T* xp = reinterpret_cast<const T*>(&xv);
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          const T* wp = reinterpret_cast<const T*>(&wv[r][u]);
+          for (int r = 0; r < RPW; ++r) {
+            const T* wp = reinterpret_cast<const T*>(&wv[r][u]);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[r][b] = fmaf(ld<T>(wp, e), ld<T>(xp, e), acc[r][b]);
+            for (int e = 0; e < 8; ++e) acc[r][b] = fmaf(ld<T>(wp, e), ld<T>(xp, e), acc[r][b]);
+          }
         }
       }
     }
@@ -264,36 +272,76 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
       for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
       acc[r][b] = v;
     }
-  if (lane == 0) {
+  if constexpr (WPR == 1) {
+    if (lane == 0) {
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      if (n0 + r >= N) break;
-      const float bv = bias ? ld<T>(bias, n0 + r) : 0.f;
+      for (int r = 0; r < RPW; ++r) {
+        if (n0 + r >= N) break;
+        const float bv = bias ? ld<T>(bias, n0 + r) : 0.f;
 #pragma unroll
-      for (int b = 0; b < B; ++b) y[int64_t(b) * N + n0 + r] = cvt<T>(acc[r][b] + bv);
+        for (int b = 0; b < B; ++b) y[int64_t(b) * N + n0 + r] = cvt<T>(acc[r][b] + bv);
+      }
+    }
+  } else {
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int b = 0; b < B; ++b) red[warp][r][b] = acc[r][b];
+    }
+    __syncthreads();
+    const int t = threadIdx.x;
+    if (t < kGroups * RPW * B) {
+      const int g = t / (RPW * B), r = (t / B) % RPW, b = t % B;
+      const int n = (blockIdx.x * kGroups + g) * RPW + r;
+      if (n < N) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < WPR; ++w) v += red[g * WPR + w][r][b];
+        const float bv = bias ? ld<T>(bias, n) : 0.f;
+        y[int64_t(b) * N + n] = cvt<T>(v + bv);
+      }
     }
   }
 }
 
+template <typename T, int B, int RPW, int WPR>
+cudaError_t launch_gemv_k(const void* x, const void* W, const void* bias, void* y, int N, int K, bool x_f16,
+                          cudaStream_t stream) {
+  const size_t smem = size_t(B) * K * sizeof(T);
+  constexpr int kRowsPerCta = kGemvWarps / WPR * RPW;
+  const unsigned blocks = unsigned((N + kRowsPerCta - 1) / kRowsPerCta);
+  auto fn = gemv_kernel<T, B, RPW, WPR>;
+  // dynamic + static (the slice sums) shared memory above the 48 KB default needs the opt-in
+  if (smem + sizeof(float) * kGemvWarps * RPW * B > 48 * 1024)
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  // Dependent launch measured faster in the decode step at batch 1 only (Llama-1B
+  // shapes on B200: 802 -> 772 us per step) and slower at batch 2 and 4 (886 ->
+  // 976, 1000 -> 1108 us).
+  if constexpr (B == 1)
+    return launch_pdl(fn, dim3(blocks), dim3(32 * kGemvWarps), smem, stream, x, static_cast<const T*>(W),
+                      static_cast<const T*>(bias), static_cast<T*>(y), N, K, x_f16);
+  fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(x, static_cast<const T*>(W), static_cast<const T*>(bias),
+                                               static_cast<T*>(y), N, K, x_f16);
+  return cudaGetLastError();
+}
+
+// K <= 2048: two rows per warp, one pass.  Longer rows at batch 1: the
+// fewest warps per row (a power of two, <= 8) that cut it into K-slices of at
+// most 2048 elements (down projection K = 8192: 9.35 -> 8.52 us on B200).  At
+// batch 2..4 the x tile (B * K elements per CTA) limits the CTAs per SM and
+// the slices measured slower (B = 4: 14.7 -> 17.7 us): one warp per row,
+// several passes.
 template <typename T, int B>
 cudaError_t launch_gemv_t(const void* x, const void* W, const void* bias, void* y, int N, int K, bool x_f16,
                           cudaStream_t stream) {
-  const size_t smem = size_t(B) * K * sizeof(T);
-  if (K <= 2048) {
-    constexpr int RPW = 2;
-    const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
-    auto fn = gemv_kernel<T, B, RPW>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    return launch_pdl(fn, dim3(blocks), dim3(32 * kGemvWarps), smem, stream, x, static_cast<const T*>(W),
-                      static_cast<const T*>(bias), static_cast<T*>(y), N, K, x_f16);
-  } else {
-    constexpr int RPW = 1;
-    const unsigned blocks = unsigned((N + kGemvWarps * RPW - 1) / (kGemvWarps * RPW));
-    auto fn = gemv_kernel<T, B, RPW>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    return launch_pdl(fn, dim3(blocks), dim3(32 * kGemvWarps), smem, stream, x, static_cast<const T*>(W),
-                      static_cast<const T*>(bias), static_cast<T*>(y), N, K, x_f16);
+  if (K <= 2048) return launch_gemv_k<T, B, 2, 1>(x, W, bias, y, N, K, x_f16, stream);
+  if constexpr (B == 1) {
+    if (K <= 4096) return launch_gemv_k<T, B, 1, 2>(x, W, bias, y, N, K, x_f16, stream);
+    if (K <= 8192) return launch_gemv_k<T, B, 1, 4>(x, W, bias, y, N, K, x_f16, stream);
+    return launch_gemv_k<T, B, 1, 8>(x, W, bias, y, N, K, x_f16, stream);
   }
+  return launch_gemv_k<T, B, 1, 1>(x, W, bias, y, N, K, x_f16, stream);
 }
 
 template <typename T>

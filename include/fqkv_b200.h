@@ -246,11 +246,11 @@ int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, in
  * accumulation, B in 1..4, K a multiple of 256, x / W / y 16-byte aligned.
  * x_dtype is the model dtype, or 0 (fp16) with bf16 weights: x is then
  * rounded to bf16 as it is read (the fp16 attention output feeding a bf16
- * output projection, with no separate cast).  Launched with programmatic
- * dependent launch: the first weight loads are issued before the kernel
- * waits for the previous kernel on the stream, so W and bias must not be
- * written by a kernel that may still be running (model weights never are);
- * x is read after the wait. */
+ * output projection, with no separate cast).  At B = 1 the kernel is
+ * launched with programmatic dependent launch and issues its first weight
+ * loads before it waits for the previous kernel on the stream, so W and bias
+ * must not be written by a kernel that may still be running (model weights
+ * never are); x is read after the wait. */
 int fqkv_gemv(int32_t model_dtype, int32_t x_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B,
               int64_t N, int64_t K, fqkv_stream_t stream);
 
