@@ -178,6 +178,35 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu,
   }
 }
 
+// Same arithmetic, 8 elements per thread with 16-byte loads and stores
+// (I % 8 == 0, row stride % 8 == 0, gu and y 16-byte aligned).
+template <typename T>
+__global__ void __launch_bounds__(256) silu_mul_vec_kernel(const T* __restrict__ gu, T* __restrict__ y,
+                                                           int64_t rows, int I8, int64_t stride8) {
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  const int64_t n = rows * I8;
+  const uint4* g4 = reinterpret_cast<const uint4*>(gu);
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / I8;
+    const int c = int(idx - r * I8);
+    const uint4 gv = g4[r * stride8 + c];
+    const uint4 uv = g4[r * stride8 + I8 + c];
+    const T* gp = reinterpret_cast<const T*>(&gv);
+    const T* up = reinterpret_cast<const T*>(&uv);
+    uint4 ov;
+    T* op = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float g = ld<T>(gp, e);
+      const float s = rnd<T>(g / (1.f + expf(-g)));
+      op[e] = cvt<T>(s * ld<T>(up, e));
+    }
+    reinterpret_cast<uint4*>(y)[idx] = ov;
+  }
+}
+
 // Small-batch GEMV: y [B, N] = x [B, K] @ W[N, K]^T (+ bias), B <= 4, fp32
 // accumulation, output rounded to the model dtype.  A batch-1..4 decode step's
 // projections are weight-streaming GEMVs that cuBLAS's batch-1 kernels run far
@@ -358,11 +387,12 @@ cudaError_t launch_gemv_b(const void* x, const void* W, const void* bias, void* 
 // Row-wise argmax of logits [rows, V] (model dtype) -> idx [rows] int64, as
 // torch.argmax (first index of the maximum; NaN counts as the maximum).  A
 // single-output torch reduction over a 128K vocabulary runs on one CTA; here
-// kArgBlocks CTAs share a row, each writes its (value, index) partial, and the
+// `nblk` CTAs share a row (64 for one row, fewer as rows grow so the grid
+// stays near 8 CTAs per SM), each writes its (value, index) partial, and the
 // last CTA to arrive (counter per row, reset by that CTA, so the scratch stays
 // reusable across calls and CUDA-graph replays) reduces the partials.
 constexpr int kArgThreads = 256;
-constexpr int kArgBlocks = 64;
+constexpr int kArgBlocks = 64;  // partial slots per row in the scratch
 
 __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
   // NaN is the largest value (torch.argmax); ties keep the lower index
@@ -372,21 +402,39 @@ __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict__ logits, int V,
+__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict__ logits, int V, int per, bool vec,
                                                              float* __restrict__ part_v, int* __restrict__ part_i,
                                                              unsigned* __restrict__ counters,
                                                              int64_t* __restrict__ out) {
   pdl_wait_primary();
   pdl_launch_dependents();
-  const int row = blockIdx.y, blk = blockIdx.x;
+  const int row = blockIdx.y, blk = blockIdx.x, nblk = gridDim.x;
   const T* lr = logits + int64_t(row) * V;
-  const int per = (V + kArgBlocks - 1) / kArgBlocks;
   const int lo = blk * per, hi = min(V, lo + per);
   float bv = -INFINITY;
   int bi = INT32_MAX;
-  for (int i = lo + threadIdx.x; i < hi; i += kArgThreads) {
-    const float v = ld<T>(lr, i);
-    if (arg_better(v, i, bv, bi)) { bv = v; bi = i; }
+  if (vec) {
+    // `per` and the row start are multiples of 8 elements: 16-byte chunks,
+    // then the row's ragged end element by element
+    const int hi8 = lo + ((hi - lo) & ~7);
+    for (int i = lo + 8 * threadIdx.x; i < hi8; i += 8 * kArgThreads) {
+      const uint4 c = *reinterpret_cast<const uint4*>(lr + i);
+      const T* cp = reinterpret_cast<const T*>(&c);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float v = ld<T>(cp, e);
+        if (arg_better(v, i + e, bv, bi)) { bv = v; bi = i + e; }
+      }
+    }
+    for (int i = hi8 + threadIdx.x; i < hi; i += kArgThreads) {
+      const float v = ld<T>(lr, i);
+      if (arg_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+  } else {
+    for (int i = lo + threadIdx.x; i < hi; i += kArgThreads) {
+      const float v = ld<T>(lr, i);
+      if (arg_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
   }
   __shared__ float sv[kArgThreads / 32];
   __shared__ int si[kArgThreads / 32];
@@ -405,7 +453,7 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict
     part_v[row * kArgBlocks + blk] = bv;
     part_i[row * kArgBlocks + blk] = bi;
     __threadfence();
-    last = atomicAdd(&counters[row], 1u) == kArgBlocks - 1;
+    last = atomicAdd(&counters[row], 1u) == unsigned(nblk - 1);
   }
   __syncthreads();
   if (!last) return;
@@ -413,7 +461,7 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict
   if (threadIdx.x < 32) {
     float v = -INFINITY;
     int i = INT32_MAX;
-    for (int b = threadIdx.x; b < kArgBlocks; b += 32) {
+    for (int b = threadIdx.x; b < nblk; b += 32) {
       const float pv = *reinterpret_cast<volatile float*>(&part_v[row * kArgBlocks + b]);
       const int pi = *reinterpret_cast<volatile int*>(&part_i[row * kArgBlocks + b]);
       if (arg_better(pv, pi, v, i)) { v = pv; i = pi; }
@@ -442,12 +490,16 @@ cudaError_t launch_argmax(bool bf16, const void* logits, int64_t rows, int V, vo
   float* pv = static_cast<float*>(scratch);
   int* pi = reinterpret_cast<int*>(pv + rows * kArgBlocks);
   unsigned* cnt = reinterpret_cast<unsigned*>(pi + rows * kArgBlocks);
-  const dim3 grid(kArgBlocks, unsigned(rows));
+  const int nblk = int(std::max<int64_t>(1, std::min<int64_t>(kArgBlocks, (148 * 8) / rows)));
+  const bool vec = V % 8 == 0 && reinterpret_cast<uintptr_t>(logits) % 16 == 0;
+  int per = (V + nblk - 1) / nblk;
+  if (vec) per = (per + 7) & ~7;
+  const dim3 grid{unsigned(nblk), unsigned(rows), 1u};
   if (bf16)
     return launch_pdl(argmax_kernel<__nv_bfloat16>, grid, dim3(kArgThreads), 0, stream,
-                      static_cast<const __nv_bfloat16*>(logits), V, pv, pi, cnt, out);
+                      static_cast<const __nv_bfloat16*>(logits), V, per, vec, pv, pi, cnt, out);
   return launch_pdl(argmax_kernel<__half>, grid, dim3(kArgThreads), 0, stream, static_cast<const __half*>(logits), V,
-                    pv, pi, cnt, out);
+                    per, vec, pv, pi, cnt, out);
 }
 
 cudaError_t launch_gemv(bool bf16, bool x_f16, const void* x, const void* W, const void* bias, void* y, int B, int N,
@@ -480,6 +532,17 @@ cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void
 
 cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, int I, int64_t row_stride,
                             cudaStream_t stream) {
+  const auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (I % 8 == 0 && row_stride % 8 == 0 && al16(gu) && al16(y)) {
+    const int64_t n8 = rows * (I / 8);
+    const unsigned vblocks = unsigned(std::min<int64_t>((n8 + 255) / 256, 148 * 16));
+    if (bf16)
+      return launch_pdl(silu_mul_vec_kernel<__nv_bfloat16>, dim3(vblocks), dim3(256), 0, stream,
+                        static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(y), rows, I / 8,
+                        row_stride / 8);
+    return launch_pdl(silu_mul_vec_kernel<__half>, dim3(vblocks), dim3(256), 0, stream,
+                      static_cast<const __half*>(gu), static_cast<__half*>(y), rows, I / 8, row_stride / 8);
+  }
   const int64_t n = rows * I;
   const unsigned blocks = unsigned(std::min<int64_t>((n + 255) / 256, 148 * 16));
   if (bf16)

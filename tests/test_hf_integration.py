@@ -251,11 +251,11 @@ def test_add_rmsnorm_and_silu_mul_kernels(fqkv, dtype, H):
     y2 = torch.empty_like(h)
     fqkv.add_rmsnorm(h, None, norm.weight.detach(), y2, 1e-5)   # plain norm of the updated stream
     assert torch.equal(y2, y)
-    I = 300
-    gu = (torch.randn(rows, 2 * I, device="cuda") * 3).to(dtype)
-    out = torch.empty(rows, I, device="cuda", dtype=dtype)
-    fqkv.silu_mul(gu, out)
-    assert torch.equal(out, torch.nn.functional.silu(gu[:, :I]) * gu[:, I:])
+    for I in (300, 2048):   # scalar path, 16-byte path
+        gu = (torch.randn(rows, 2 * I, device="cuda") * 3).to(dtype)
+        out = torch.empty(rows, I, device="cuda", dtype=dtype)
+        fqkv.silu_mul(gu, out)
+        assert torch.equal(out, torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]), I
 
 
 @pytest.mark.gpu
@@ -275,7 +275,7 @@ def test_gemv_matches_fp32_projection(fqkv, dtype, B, N, K):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("rows,V", [(1, 128256), (4, 32000), (64, 128256), (3, 100), (2, 1)])
+@pytest.mark.parametrize("rows,V", [(1, 128256), (4, 32000), (64, 128256), (3, 100), (2, 1), (2, 16), (300, 1000)])
 def test_argmax_rows_matches_torch(fqkv, dtype, rows, V):
     """Multi-CTA argmax: the same index as torch.argmax, ties to the first index, reusable scratch."""
     from importlib import import_module
