@@ -109,3 +109,27 @@ def test_workspace_query_without_gpu_is_zero(fqkv):
     if torch.cuda.is_available():
         pytest.skip("GPU present: the query returns a real size")
     assert fqkv.native.lib().fqkv_decode_workspace_bytes(0, 64, 32, 8, 16384, 128) == 0
+
+
+def test_decode_step_kernels_reject_bad_arguments(fqkv):
+    """The decode-step entries (GEMV, argmax, SwiGLU, add+RMSNorm) validate before launching."""
+    bad, mis, ok = fqkv.native.ERR_INVALID_ARGUMENT, fqkv.native.ERR_MISALIGNED, fqkv.native.OK
+    # GEMV: batch above 4, K not a multiple of 256, bf16 activations with fp16 weights, misaligned weights
+    assert _call(fqkv, "fqkv_gemv", 1, 1, P, P, None, P, 5, 16, 256, None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv", 1, 1, P, P, None, P, 1, 16, 300, None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv", 0, 1, P, P, None, P, 1, 16, 256, None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv", 1, 1, P, P3, None, P, 1, 16, 256, None)[0] == mis
+    # argmax: unknown dtype, more rows than the grid takes, empty rows, misaligned index output; no rows is a no-op
+    assert _call(fqkv, "fqkv_argmax", 2, P, 1, 10, P, P, None)[0] == bad
+    assert _call(fqkv, "fqkv_argmax", 1, P, 70000, 10, P, P, None)[0] == bad
+    assert _call(fqkv, "fqkv_argmax", 1, P, 1, 0, P, P, None)[0] == bad
+    assert _call(fqkv, "fqkv_argmax", 1, P, 1, 10, P, P3, None)[0] == mis
+    assert _call(fqkv, "fqkv_argmax", 1, None, 0, 10, None, None, None)[0] == ok
+    lib = fqkv.native.lib()
+    assert lib.fqkv_argmax_scratch_bytes(0) == 0
+    assert 0 < lib.fqkv_argmax_scratch_bytes(1) < lib.fqkv_argmax_scratch_bytes(64)
+    # SwiGLU: a row stride shorter than the gate and up halves
+    assert _call(fqkv, "fqkv_silu_mul", 1, P, P, 2, 100, 150, None)[0] == bad
+    # add + RMSNorm: hidden size above 8192, odd address
+    assert _call(fqkv, "fqkv_add_rmsnorm", 1, P, None, P, P, 2, 9000, 1e-5, None)[0] == bad
+    assert _call(fqkv, "fqkv_add_rmsnorm", 1, ctypes.c_void_p(17), None, P, P, 2, 64, 1e-5, None)[0] == mis
