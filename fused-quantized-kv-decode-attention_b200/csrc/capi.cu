@@ -205,12 +205,17 @@ void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_byt
     *S_eff = (tiles + *chunk_tiles - 1) / *chunk_tiles;
   };
   // Modelled time: every round of the persistent grid costs
-  // max(active CTAs, 3/4 of the grid) x tiles per unit -- with fewer CTAs than
+  // max(active CTAs, 3/5 of the grid) x tiles per unit -- with fewer CTAs than
   // that the machine stops being HBM-bound -- and splitting adds about one
-  // tile of epilogue / combine work per unit.  S_fixed > 0 (gqa_sk_fast) caps
-  // the split count at the caller's scratch capacity; otherwise the caller's
-  // workspace bytes cap it when `limit_ws`.
-  const int64_t floor_ctas = (3 * C) / 4;
+  // tile of epilogue work per unit.  S_fixed > 0 (gqa_sk_fast) caps the split
+  // count at the caller's scratch capacity; otherwise the caller's workspace
+  // bytes cap it when `limit_ws`.  The floor and the combine terms below were
+  // fitted on B200 to forced-split sweeps of the fp16 GQA kernel (Hq=32,
+  // Hkv=8, D in {64, 128}, B in {1, 2, 4, 8}, N from 2K to 64K): mean loss
+  // against the best measured split 3.7 % -> 1.4 %; planned calls over
+  // B <= 64, N >= 640 1.6 % faster in sum (B=1, N=2048, D=128: 8.9 -> 7.8 us;
+  // N=16K: 18.4 -> 17.7 us).
+  const int64_t floor_ctas = (3 * C) / 5;
   const int64_t maxS = S_fixed > 0 ? std::min<int64_t>(tiles, S_fixed) : std::min<int64_t>(tiles, 256);
   double best = 1e300;
   int64_t best_S = 1;
@@ -226,10 +231,11 @@ void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_byt
       cost += double(std::max<int64_t>(active, floor_ctas)) * double(ct + (se > 1 ? 1 : 0));
     }
     // The combine kernel (its wait for the partial grid, the partials' round
-    // trip through L2) costs about three tile-rounds of the whole grid,
-    // measured on B200: e.g. B=64, Hkv=8, N=640, D=64 runs 20.4 us unsplit
-    // against 25.7 us in two splits.
-    if (se > 1) cost += 3.0 * double(C);
+    // trip through L2) costs about three tile-rounds of the whole grid (B=64,
+    // Hkv=8, N=640, D=64 runs 20.4 us unsplit against 25.7 us in two splits),
+    // plus 0.07 of a round per split (its loop over the partials: config 4
+    // at 16K measured 3.1 us of combine at 24 splits, 5.6 us at 37).
+    if (se > 1) cost += (3.0 + 0.07 * double(se)) * double(C);
     if (cost < best * 0.999) {
       best = cost;
       best_S = se;
