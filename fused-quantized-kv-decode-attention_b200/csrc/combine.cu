@@ -20,9 +20,10 @@ namespace {
 constexpr int kCombineThreads = 512;
 
 // One CTA per row.  The split range is divided among kCombineThreads / D
-// thread groups (thread = one dim of one group), so the loads of different
-// splits are independent and in flight together; groups are reduced in
-// shared memory.
+// thread groups (thread = one dim of one group); every group merges its
+// splits online -- (M, L, O) rescaled when M grows, branch-free, so the loads
+// of consecutive splits are independent and in flight together -- and the
+// groups' results are merged once through shared memory.
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ pm,
                                                                   const float* __restrict__ pl,
                                                                   const float* __restrict__ po,
@@ -30,42 +31,43 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
                                                                   const TpOut tp) {
   pdl_launch_dependents();  // the next decode kernel may be scheduled now; it waits for this grid
   pdl_wait_primary();
-  __shared__ float red[kCombineThreads / 32];
   __shared__ float sm_o[kCombineThreads];
+  __shared__ float sm_m[kCombineThreads / 64];
   __shared__ float sm_l[kCombineThreads / 64];
   const size_t row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const float* m = pm + row * S;
   const float* l = pl + row * S;
 
-  float M = -INFINITY;
-  for (int s = tid; s < S_eff; s += kCombineThreads) M = fmaxf(M, m[s]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  if (lane == 0) red[warp] = M;
-  __syncthreads();
-  M = red[0];
-#pragma unroll
-  for (int w = 1; w < kCombineThreads / 32; ++w) M = fmaxf(M, red[w]);
-
   const int groups = kCombineThreads / D;
   const int gi = tid / D, d = tid - gi * D;
-  float L = 0.f, O = 0.f;
-#pragma unroll 4
+  float M = -INFINITY, L = 0.f, O = 0.f;
+#pragma unroll 8
   for (int s = gi; s < S_eff; s += groups) {
     const float ms = m[s];
-    const float w = (ms == -INFINITY) ? 0.f : ex2(ms - M);
-    L = fmaf(w, l[s], L);
-    O = fmaf(w, po[(row * S + s) * D + d], O);
+    const float ls = l[s];
+    const float os = po[(row * S + s) * D + d];
+    const float Mn = fmaxf(M, ms);
+    const float a = (Mn == -INFINITY) ? 1.f : ex2(M - Mn);   // M = -inf: ex2 gives 0
+    const float b = (ms == -INFINITY) ? 0.f : ex2(ms - Mn);  // an empty split weighs 0
+    L = fmaf(L, a, b * ls);
+    O = fmaf(O, a, b * os);
+    M = Mn;
   }
   sm_o[tid] = O;
-  if (d == 0) sm_l[gi] = L;
+  if (d == 0) {
+    sm_m[gi] = M;
+    sm_l[gi] = L;
+  }
   __syncthreads();
   if (gi == 0) {
+    float Mt = -INFINITY;
+    for (int g = 0; g < groups; ++g) Mt = fmaxf(Mt, sm_m[g]);
     float Ls = 0.f, Os = 0.f;
     for (int g = 0; g < groups; ++g) {
-      Ls += sm_l[g];
-      Os += sm_o[g * D + d];
+      const float w = (sm_m[g] == -INFINITY) ? 0.f : ex2(sm_m[g] - Mt);
+      Ls = fmaf(w, sm_l[g], Ls);
+      Os = fmaf(w, sm_o[g * D + d], Os);
     }
     const __half_raw h = __half_raw(__float2half_rn(Os / Ls));
     if (tp.world == 0) {
