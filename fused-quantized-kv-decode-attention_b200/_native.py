@@ -66,6 +66,8 @@ SIGNATURES = {
     "fqkv_gemv": (_INT, [ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "fqkv_argmax_scratch_bytes": (_SZ, [_I64]),
     "fqkv_argmax": (_INT, [ctypes.c_int32, _P, _I64, _I64, _P, _P, _P]),
+    "fqkv_decode_attn_kvcache_out": (_INT, [ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
+                                            _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "fqkv_decode_attn_kvcache_tp": (_INT, [ctypes.c_int32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P,
                                            _P, _SZ, ctypes.POINTER(TpOut), _P]),
     "fqkv_tp_arrivals": (_I64, [ctypes.c_int32, _I64, _I64, _I64, _I64, _I64, _SZ]),

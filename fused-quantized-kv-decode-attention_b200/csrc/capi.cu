@@ -284,7 +284,7 @@ int launch(DecodeLaunch& a, cudaStream_t stream) {
 int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const void* Ks, const void* Vs, void* o,
                int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, void* ws, size_t ws_bytes,
                fqkv_stream_t stream, int64_t kv_stride = -1, const int* n_dev = nullptr,
-               const fqkv_tp_out_t* tp = nullptr) {
+               const fqkv_tp_out_t* tp = nullptr, bool out_bf16 = false) {
   if (kv_stride < 0) kv_stride = N;
   if (int rc = check_D(D)) return rc;
   if (B < 0 || Hq < 1 || Hkv < 1 || N < 0) return fail(FQKV_ERR_INVALID_ARGUMENT, "negative or zero size");
@@ -309,6 +309,7 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
   a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
   a.kv_stride = int(kv_stride);
   a.n_dev = n_dev;
+  a.out_bf16 = out_bf16;
   if (tp) {
     a.tp.world = tp->world;
     a.tp.rank = tp->rank;
@@ -637,6 +638,25 @@ int fqkv_argmax(int32_t model_dtype, const void* logits, int64_t rows, int64_t V
 }
 
 // ------------------------------------------------------------------ tensor-parallel decode
+int fqkv_decode_attn_kvcache_out(int32_t kv_format, int32_t out_dtype, const void* q, const void* K, const void* V,
+                                 const void* Ks, const void* Vs, void* o, int64_t B, int64_t Hq, int64_t Hkv,
+                                 int64_t max_len, int64_t D, int64_t n_host, const int32_t* seq_len_dev,
+                                 void* workspace, size_t workspace_bytes, fqkv_stream_t stream) {
+  if (kv_format != FQKV_KV_F16 && kv_format != FQKV_KV_INT8)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "kv_format: FQKV_KV_F16 or FQKV_KV_INT8");
+  if (out_dtype != 0 && out_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "out_dtype: 0 (f16) or 1 (bf16)");
+  if (max_len < 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "max_len must be >= 1");
+  if (!seq_len_dev && (n_host < 1 || n_host > max_len))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "n: valid length %lld outside [1, max_len=%lld]", (long long)n_host,
+                (long long)max_len);
+  if (max_len > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "sizes exceed the 32-bit index range");
+  if (seq_len_dev && !aligned(seq_len_dev, 4)) return fail(FQKV_ERR_MISALIGNED, "seq_len must be 4-byte aligned");
+  const int64_t N = seq_len_dev ? max_len : n_host;
+  return run_decode(kv_format == FQKV_KV_INT8 ? KvFormat::I8 : KvFormat::F16, q, K, V, Ks, Vs, o, B, Hq, Hkv, N, D,
+                    workspace, workspace_bytes, stream, max_len, reinterpret_cast<const int*>(seq_len_dev), nullptr,
+                    out_dtype == 1);
+}
+
 int fqkv_decode_attn_kvcache_tp(int32_t kv_format, const void* q, const void* K, const void* V, const void* Ks,
                                 const void* Vs, int64_t B, int64_t Hq, int64_t Hkv, int64_t max_len, int64_t D,
                                 int64_t n_host, const int32_t* seq_len_dev, void* workspace, size_t workspace_bytes,

@@ -6,6 +6,7 @@
 // dependent launch: the CTAs are scheduled while the partial grid is still
 // streaming and block in griddepcontrol.wait until it has completed, which
 // hides the second launch's latency (the reference pays two full launches).
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -27,8 +28,8 @@ constexpr int kCombineThreads = 512;
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ pm,
                                                                   const float* __restrict__ pl,
                                                                   const float* __restrict__ po,
-                                                                  __half* __restrict__ out, int D, int S, int S_eff,
-                                                                  const TpOut tp) {
+                                                                  void* __restrict__ out, bool out_bf16, int D, int S,
+                                                                  int S_eff, const TpOut tp) {
   pdl_launch_dependents();  // the next decode kernel may be scheduled now; it waits for this grid
   pdl_wait_primary();
   __shared__ float sm_o[kCombineThreads];
@@ -70,8 +71,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
       Os = fmaf(w, sm_o[g * D + d], Os);
     }
     const __half_raw h = __half_raw(__float2half_rn(Os / Ls));
-    if (tp.world == 0) {
-      reinterpret_cast<__half_raw*>(out)[row * D + d] = h;
+    if (out_bf16) {
+      static_cast<__nv_bfloat16*>(out)[row * D + d] = __float2bfloat16_rn(Os / Ls);
+    } else if (tp.world == 0) {
+      static_cast<__half_raw*>(out)[row * D + d] = h;
     } else {
       for (int p = 0; p < tp.world; ++p) tp.dst[p][tp.dst_off + row * D + d] = h;
     }
@@ -100,7 +103,7 @@ cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream) {
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, combine_kernel, static_cast<const float*>(a.part_m),
                             static_cast<const float*>(a.part_l), static_cast<const float*>(a.part_o),
-                            static_cast<__half*>(a.out), a.D, a.S, a.S_eff, a.tp);
+                            a.out, a.out_bf16, a.D, a.S, a.S_eff, a.tp);
 }
 
 }  // namespace fqkv

@@ -5,6 +5,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -76,11 +77,17 @@ struct DecodeLaunch {
   int debug_skip_loads;                // test hook: producer issues nothing
   CUtensorMap tmK, tmV;                // tiled K/V maps (fp16, and int8 GQA)
   TpOut tp;                            // tensor-parallel output (tp.world == 0: write `out`)
+  bool out_bf16;                       // `out` is bf16 (local output only; the default is fp16)
 };
 
 #ifdef __CUDACC__
-// Final fp16 output element `idx` (row * D + d) of a launch.
+// Final output element `idx` (row * D + d) of a launch: fp16, or bf16 when
+// the caller asked for it (rounded once from fp32 either way).
 __device__ __forceinline__ void store_out(const DecodeLaunch& a, size_t idx, float v) {
+  if (a.out_bf16) {
+    static_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(v);
+    return;
+  }
   const __half_raw h = __half_raw(__float2half_rn(v));
   if (a.tp.world == 0) {
     static_cast<__half_raw*>(a.out)[idx] = h;

@@ -193,6 +193,10 @@ class GraphDecoder:
             # 1.5-2x faster than cuBLAS's batch-1..4 kernels on B200); gate/up and the LM head stay
             # on cuBLAS, which streams those large matrices near HBM speed.
             self.small_b = batch <= 4 and H % 256 == 0 and I % 256 == 0 and (self.Hq * self.D) % 256 == 0
+            if not self.small_b and self.world == 1 and self.dtype == torch.bfloat16:
+                # one GPU, batch > 4: attention writes bf16, so cuBLAS's output projection reads it
+                # without a cast kernel (each element rounded once from fp32)
+                self.attn_out = torch.empty(batch, self.Hq_l, self.D, dtype=torch.bfloat16, device=dev)
             self.arg_scratch = torch.zeros(int(_native.lib().fqkv_argmax_scratch_bytes(batch)), dtype=torch.uint8,
                                            device=dev)
             self.nxt = torch.empty(batch, dtype=torch.long, device=dev)

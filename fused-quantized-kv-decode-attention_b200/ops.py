@@ -217,6 +217,18 @@ def decode_attn_gqa(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, W: int) -
     return o
 
 
+def _kv_out(op: str, q: torch.Tensor, out, shape, dev) -> torch.Tensor:
+    """Output of a KV-cache decode call: a new fp16 tensor, or the caller's fp16 / bf16 one."""
+    if out is None:
+        return torch.empty(shape, dtype=torch.float16, device=dev)
+    _require_cuda(op, q, out)
+    if out.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", f"out must be fp16 or bf16 (got {out.dtype})")
+    _require_contig(op, out=out)
+    _require_shape(op, "out", out, shape)
+    return out
+
+
 def decode_attn_gqa_kvcache(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, seq_len,
                             out: torch.Tensor | None = None,
                             workspace: torch.Tensor | None = None) -> torch.Tensor:
@@ -228,7 +240,8 @@ def decode_attn_gqa_kvcache(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, s
     nothing and can be captured in a CUDA graph that is replayed as the cache
     grows.  ``workspace`` needs ``workspace_bytes("fp16", B, Hq, Hkv, max_len, D)``
     bytes (device length) or the same with N = n (host length); too small
-    only reduces the split count.
+    only reduces the split count.  ``out`` may be bf16 (a bf16 model's output
+    projection reads it without a cast; each element is rounded once).
     """
     op = "decode_attn_gqa_kvcache"
     dev = _require_cuda(op, q, K, V)
@@ -249,18 +262,18 @@ def decode_attn_gqa_kvcache(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, s
         n_host, n_ptr, n_plan = 0, seq_len.data_ptr(), max_len
     else:
         n_host, n_ptr, n_plan = int(seq_len), None, int(seq_len)
-    if out is None:
-        out = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
-    else:
-        _require_cuda(op, q, out)
-        _require_dtype(op, "fp16", torch.float16, out=out)
-        _require_contig(op, out=out)
-        _require_shape(op, "out", out, (B, Hq, D))
+    out = _kv_out(op, q, out, (B, Hq, D), dev)
     with _DeviceGuard(dev):
         if workspace is None:
             ws, nb = _workspace(_native.KV_F16, dev, B, Hq, Hkv, max(n_plan, 1), D) if B else (None, 0)
         else:
             ws, nb = workspace, workspace.numel() * workspace.element_size()
+        if out.dtype == torch.bfloat16:
+            rc = _native.lib().fqkv_decode_attn_kvcache_out(
+                _native.KV_F16, 1, q.data_ptr(), K.data_ptr(), V.data_ptr(), None, None, out.data_ptr(), B, Hq, Hkv,
+                max_len, D, n_host, n_ptr, ws.data_ptr() if ws is not None and nb else None, nb, _stream(dev))
+            _native.check(rc, f"launch: {op}")
+            return out
         rc = _native.lib().fqkv_decode_attn_gqa_kvcache(
             q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), B, Hq, Hkv, max_len, D, n_host, n_ptr,
             ws.data_ptr() if ws is not None and nb else None, nb, _stream(dev))
@@ -320,16 +333,19 @@ def decode_attn_gqa_int8_kvcache(q, Kq, Vq, Ks, Vs, seq_len, out=None, workspace
     op = "decode_attn_gqa_int8_kvcache"
     dev, B, Hq, Hkv, max_len, D = _check_int8_gqa(op, q, Kq, Vq, Ks, Vs)
     n_host, n_ptr, n_plan = _seq_len_args(op, seq_len, dev, max_len)
-    if out is None:
-        out = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
-    else:
-        _require_shape(op, "out", out, (B, Hq, D))
-        _require_dtype(op, "fp16", torch.float16, out=out)
+    out = _kv_out(op, q, out, (B, Hq, D), dev)
     with _DeviceGuard(dev):
         if workspace is None:
             ws, nb = _workspace(_native.KV_INT8, dev, B, Hq, Hkv, max(n_plan, 1), D) if B else (None, 0)
         else:
             ws, nb = workspace, workspace.numel() * workspace.element_size()
+        if out.dtype == torch.bfloat16:
+            rc = _native.lib().fqkv_decode_attn_kvcache_out(
+                _native.KV_INT8, 1, q.data_ptr(), Kq.data_ptr(), Vq.data_ptr(), Ks.data_ptr(), Vs.data_ptr(),
+                out.data_ptr(), B, Hq, Hkv, max_len, D, n_host, n_ptr,
+                ws.data_ptr() if ws is not None and nb else None, nb, _stream(dev))
+            _native.check(rc, f"launch: {op}")
+            return out
         rc = _native.lib().fqkv_decode_attn_gqa_int8_kvcache(
             q.data_ptr(), Kq.data_ptr(), Vq.data_ptr(), Ks.data_ptr(), Vs.data_ptr(), out.data_ptr(),
             B, Hq, Hkv, max_len, D, n_host, n_ptr, ws.data_ptr() if ws is not None and nb else None, nb,

@@ -286,6 +286,16 @@ typedef struct fqkv_tp_out {
 } fqkv_tp_out_t;
 
 /* fqkv_decode_attn_gqa_kvcache (kv_format FQKV_KV_F16: Ks = Vs = NULL) or
+ * fqkv_decode_attn_gqa_int8_kvcache (FQKV_KV_INT8) with the output o [B, Hq,
+ * D] in out_dtype 0 (fp16, as those entries) or 1 (bf16, for a bf16 model's
+ * output projection; each element is rounded once from the fp32 result).
+ * No counterpart in the reference. */
+int fqkv_decode_attn_kvcache_out(int32_t kv_format, int32_t out_dtype, const void* q, const void* K, const void* V,
+                                 const void* Ks, const void* Vs, void* o, int64_t B, int64_t Hq, int64_t Hkv,
+                                 int64_t max_len, int64_t D, int64_t n_host, const int32_t* seq_len_dev,
+                                 void* workspace, size_t workspace_bytes, fqkv_stream_t stream);
+
+/* fqkv_decode_attn_gqa_kvcache (kv_format FQKV_KV_F16: Ks = Vs = NULL) or
  * fqkv_decode_attn_gqa_int8_kvcache (FQKV_KV_INT8) for this rank's heads, with
  * the output sent to every rank as described above instead of to an `o`
  * tensor.  Each receive buffer must hold dst_offset + B*Hq*D f16 (16-byte

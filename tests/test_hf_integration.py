@@ -196,21 +196,25 @@ def test_graph_decoder_fused_prologue_equals_hf_ops(fqkv, kv):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_graph_decoder_fused_model_ops_track_hf_modules(fqkv, dtype):
+@pytest.mark.parametrize("B", [2, 8])
+def test_graph_decoder_fused_model_ops_track_hf_modules(fqkv, dtype, B):
     """The fused residual/RMSNorm + SwiGLU step against transformers' modules on
     the same decoder: same tokens, logits within rounding (the RMSNorm sum of
-    squares and the concatenated gate/up GEMM reduce in a different order)."""
+    squares and the concatenated gate/up GEMM reduce in a different order; a
+    bf16 model at batch > 4 also takes the attention output in bf16)."""
     from transformers import LlamaForCausalLM
     torch.manual_seed(8)
     with torch.device("cuda"):
         model = LlamaForCausalLM(_tiny_config()).to(dtype).eval()
-    B, P, T = 2, 31, 12
+    P, T = 31, 12
     ids = torch.randint(0, 1000, (B, P), device="cuda")
     res = {}
     for fused in (False, True):
         dec = fqkv.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, keep_logits=True,
                                                fused_model_ops=fused)
         assert dec.model_fused == fused
+        if fused and dtype == torch.bfloat16 and B > 4:
+            assert dec.attn_out.dtype == torch.bfloat16
         dec.prefill(ids)
         dec.capture()
         lg = [dec.logits.clone()]

@@ -314,6 +314,44 @@ def test_gqa_int8_kvcache_append_and_device_length(fqkv, B, Hq, Hkv, max_len, n,
     _close(fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, n_dev), ref)
 
 
+@pytest.mark.parametrize("kv", ["fp16", "int8"])
+@pytest.mark.parametrize("B,n,D", [(8, 513, 64), (2, 4097, 128), (16, 40, 64)])
+def test_kvcache_bf16_output(fqkv, kv, B, n, D):
+    """bf16 output (for a bf16 model's output projection): the oracle within the fp16 tolerance plus one
+    bf16 rounding, and the fp16 output's value within one bf16 rounding of each other (split and unsplit)."""
+    Hq, Hkv, max_len = 32, 8, n + 100
+    q = _randn(B, Hq, D, seed=130)
+    Kf, Vf = _randn(B, Hkv, n, D, seed=131), _randn(B, Hkv, n, D, seed=132)
+    n_dev = torch.tensor([n], dtype=torch.int32, device="cuda")
+    if kv == "fp16":
+        K = torch.zeros(B, Hkv, max_len, D, dtype=torch.float16, device="cuda")
+        V = torch.zeros_like(K)
+        K[:, :, :n], V[:, :, :n] = Kf.cuda(), Vf.cuda()
+        ref = oatt.decode_attention_gqa(q.numpy(), Kf.numpy(), Vf.numpy())
+        call = lambda out, ws: fqkv.decode_attn_gqa_kvcache(q.cuda(), K, V, n_dev, out=out, workspace=ws)
+    else:
+        Kq = torch.zeros(B, Hkv, max_len, D, dtype=torch.int8, device="cuda")
+        Vq = torch.zeros_like(Kq)
+        Ks = torch.zeros(B, Hkv, max_len, dtype=torch.float16, device="cuda")
+        Vs = torch.zeros_like(Ks)
+        fqkv.quantize_into_cache(Kf.cuda(), Kq, Ks, 0)
+        fqkv.quantize_into_cache(Vf.cuda(), Vq, Vs, 0)
+        ref = _int8_gqa_ref(q.numpy(), Kf.numpy(), Vf.numpy())
+        call = lambda out, ws: fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, n_dev, out=out,
+                                                                  workspace=ws)
+    nb = fqkv.workspace_bytes(kv, B, Hq, Hkv, max_len, D)
+    for ws in (torch.empty(max(nb, 16), dtype=torch.uint8, device="cuda"), torch.empty(0, dtype=torch.uint8,
+                                                                                          device="cuda")):
+        o16 = call(torch.empty(B, Hq, D, dtype=torch.float16, device="cuda"), ws)
+        ob = call(torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda"), ws)
+        assert ob.dtype == torch.bfloat16
+        got = ob.float().cpu().numpy().astype(np.float64)
+        bf_ulp = 2.0 ** -8 * np.abs(ref)
+        np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL + 2.0 ** -8)
+        diff = (ob.float() - o16.float()).abs()
+        assert (diff <= 2.0 ** -8 * o16.float().abs() + 2.0 ** -11 * o16.float().abs() + 1e-6).all()
+
+
 def test_gqa_int8_extreme_q_and_scales(fqkv):
     """q with one huge element per head (fixed-point q planes lose the small ones
     only below the tolerance), all-zero tokens (scale 0), a zero q head."""
