@@ -172,9 +172,78 @@ __device__ __forceinline__ constexpr int qk_dim(int kk, int h, int i) {
   }
 }
 
+// ---- one-head int4 variant (G1): P.V on the integer tensor cores
+//
+// Key (0..31 within a warp's share of a tile) that lane group g holds as
+// score i (0..3; i = 2 * m-tile + row half of S^T).  The P.V k-slot 4a + i
+// carries key g1_key(a, i), so that the B operand of a thread's k-slots
+// 4t..4t+3 (16+4t..) is the four scores of lane group t (t + 4), and the
+// eight keys of every ldmatrix 8x8 matrix differ mod 8 (conflict-free with
+// the 64-byte row swizzle).
+__device__ __forceinline__ constexpr int g1_key(int g, int i) { return 8 * i + (g ^ (4 * (i & 1))); }
+
+// P is fixed point in a frame (reference maximum m_run, scale Ps):
+// v = rint(p * vs * Ps) with p = 2^(s - m_run) <= 2^kG1Headroom.  A frame
+// starts when a tile's largest p * vs would exceed kG1VLim / Ps (Ps is then
+// set to kG1VLim / (1.25 * that product)), so v <= kG1VLim < 2^23 - 32896
+// and the largest products keep about 22 significant bits.  The float
+// 2^23 + v + 32896 (one FMA with kG1Magic, rounding to nearest) holds
+// u = v + 32896 = h * 65536 + (m + 128) * 256 + (l + 128) in its low 23
+// bits: v = h * 65536 + m * 256 + l with the signed bytes m, l and h in
+// [0, 127], the three planes of the B operand (columns 0, 1, 2).
+constexpr float kG1Magic = 8421504.f;
+constexpr float kG1Headroom = 3.f;
+constexpr float kG1VLim = 8.0e6f;
+// s32 accumulator bound: |code term| <= 128 and |plane| <= 128 per key, so a
+// frame ends after at most 2048 tiles (65536 keys per warp, < 2^31 / 16384)
+constexpr int kG1FrameTiles = 2048;
+
+// Ends a frame: adds the integer accumulators times 1/Ps to the warp's fp32 O
+// in shared memory and scales the sum by `rescale` (both are relative to the
+// frame's maximum; rescale moves them to the next frame's), lane (g, 0)
+// owning head dimensions 32s + 4g + 0..3 (s = 0..3); clears the accumulators.
+// oi[s] (s < 4) holds the low nibbles (code + 8, rows g / g + 8 = dimensions
+// 32s + 4g / + 2), oi[4 + s] the high nibbles (16 * code, dimensions + 1);
+// columns 0 / 1 are the h / m planes in lanes t = 0, column 2 the l plane in
+// lanes t = 1.  bsum: the plane sums of this lane's keys (plane t), for the
+// + 8 of the low nibbles.
+__device__ __forceinline__ void g1_flush(int (&oi)[8][4], int& bsum, float* so, float rescale, float inv_ps, int g,
+                                         int t) {
+  int bs = bsum;
+  bs += __shfl_xor_sync(0xffffffffu, bs, 4);
+  bs += __shfl_xor_sync(0xffffffffu, bs, 8);
+  bs += __shfl_xor_sync(0xffffffffu, bs, 16);  // lane (g, c): sum of plane c over the frame
+  const int b1 = __shfl_down_sync(0xffffffffu, bs, 1);
+  const int b2 = __shfl_down_sync(0xffffffffu, bs, 2);
+#pragma unroll
+  for (int sg = 0; sg < 4; ++sg) {
+    const int l0 = __shfl_down_sync(0xffffffffu, oi[sg][0], 1);
+    const int l2 = __shfl_down_sync(0xffffffffu, oi[sg][2], 1);
+    const int h0 = __shfl_down_sync(0xffffffffu, oi[4 + sg][0], 1);
+    const int h2 = __shfl_down_sync(0xffffffffu, oi[4 + sg][2], 1);
+    if (t == 0) {
+      float4* dst = reinterpret_cast<float4*>(so + 32 * sg + 4 * g);
+      float4 c = *dst;
+      const float lg = float(oi[sg][0] - 8 * bs) * 65536.f + float(oi[sg][1] - 8 * b1) * 256.f + float(l0 - 8 * b2);
+      const float hg = (float(oi[4 + sg][0]) * 65536.f + float(oi[4 + sg][1]) * 256.f + float(h0)) * 0.0625f;
+      const float lg8 = float(oi[sg][2] - 8 * bs) * 65536.f + float(oi[sg][3] - 8 * b1) * 256.f + float(l2 - 8 * b2);
+      const float hg8 = (float(oi[4 + sg][2]) * 65536.f + float(oi[4 + sg][3]) * 256.f + float(h2)) * 0.0625f;
+      c.x = fmaf(lg, inv_ps, c.x) * rescale;
+      c.y = fmaf(hg, inv_ps, c.y) * rescale;
+      c.z = fmaf(lg8, inv_ps, c.z) * rescale;
+      c.w = fmaf(hg8, inv_ps, c.w) * rescale;
+      *dst = c;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) oi[i][0] = oi[i][1] = oi[i][2] = oi[i][3] = 0;
+  bsum = 0;
+}
+
 template <int D, bool I4, bool G1>
 __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = QtcCfg<D, I4, G1>;
+  static_assert(I4 == G1 && (!G1 || D == 128), "int4 runs the one-head variant at D = 128, int8 the GQA one");
   constexpr int MH = C::MH;
   constexpr int RB = C::RB;
   constexpr int KPW = C::KPW;
@@ -272,6 +341,19 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
   constexpr bool kSwap = RB <= 64;
   const int vsw = kSwap ? (t & 1) : 0;
   const uint32_t sel_base = vsw ? 0x0044u : 0x4400u;
+  // one head: this lane's ldmatrix row (matrix L/8 = k-slots {4t, 4t+1}, {4t+2, 4t+3} of groups
+  // t < 4, then of groups t + 4; row L%8 = slot of group (L%8)/2) as a swizzled byte offset, and
+  // the P plane this lane packs (t = 0 / 1 / 2: byte 2 / 1 / 0 of the magic float, 3: none)
+  uint32_t v_row_off = 0, psel = 0, pxor = 0, pmask = 0;
+  if constexpr (G1) {
+    const int mi = lane >> 3, rr = lane & 7;
+    const int row = r0 + g1_key((rr >> 1) + 4 * (mi >> 1), 2 * (mi & 1) + (rr & 1));
+    v_row_off = uint32_t(row * RB) | (uint32_t((row >> 1) & 3) << 4);
+    const uint32_t pb_ = t == 0 ? 2u : (t == 1 ? 1u : 0u);
+    psel = pb_ | ((4u + pb_) << 4);
+    pxor = (t == 1 || t == 2) ? 0x80808080u : 0u;
+    pmask = t < 3 ? 0xFFFFFFFFu : 0u;
+  }
   bool alive = true;
   int it = 0;
 
@@ -333,18 +415,30 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
         qa[kk][2] = pack_s8x4(hv[4], hv[5], hv[6], hv[7]);
         qa[kk][3] = pack_s8x4(lv[4], lv[5], lv[6], lv[7]);
         if constexpr (G1) {
-          // one head: q is the B operand of S^T = K Q^T, column 0 = hi plane, column 1 = lo plane
-          const uint32_t b0 = g == 0 ? qa[kk][0] : (g == 1 ? qa[kk][1] : 0u);
-          const uint32_t b1 = g == 0 ? qa[kk][2] : (g == 1 ? qa[kk][3] : 0u);
+          // one head: q is the B operand of S^T = K Q^T; columns 2c / 2c + 1 = hi / lo plane for
+          // c = 0, 1, 2, so the lanes t = 0, 1, 2 of a group all hold the same scores (columns 6, 7 zero)
+          const uint32_t b0 = g < 6 ? ((g & 1) ? qa[kk][1] : qa[kk][0]) : 0u;
+          const uint32_t b1 = g < 6 ? ((g & 1) ? qa[kk][3] : qa[kk][2]) : 0u;
           qa[kk][0] = b0;
           qa[kk][1] = b1;
         }
       }
     }
 
-    float o[MT][4];
+    float o[MT][4];   // several heads: O^T in fp32
+    int oi[8][4];     // one head: the frame's integer O^T (see g1_flush)
+    int bsum = 0, ftiles = 0;
+    float ps = 0.f, inv_ps = 0.f;  // one head: the frame's fixed-point scale of P * vs and 1 / it
+    float* so = sm_o + warp * D;  // one head: the warp's fp32 O
+    if constexpr (G1) {
 #pragma unroll
-    for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      for (int i = 0; i < 8; ++i) oi[i][0] = oi[i][1] = oi[i][2] = oi[i][3] = 0;
+      reinterpret_cast<float4*>(so)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+      __syncwarp();
+    } else {
+#pragma unroll
+      for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    }
     float m_run = -INFINITY, l_run = 0.f;
 
     for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
@@ -373,12 +467,12 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
       if constexpr (G1) {
 #pragma unroll
         for (int mt = 0; mt < KP; ++mt) {
-          uint32_t kw[2][KB / 4];  // keys r0 + 16mt + g and + 8
+          uint32_t kw[2][KB / 4];  // keys r0 + g1_key(g, 2mt) and r0 + g1_key(g, 2mt + 1)
 #pragma unroll
           for (int e = 0; e < 2; ++e)
 #pragma unroll
             for (int c = 0; c < KB; c += 16)
-              lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + 16 * mt + 8 * e + g, t * KB + c), kw[e] + c / 4);
+              lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + g1_key(g, 2 * mt + e), t * KB + c), kw[e] + c / 4);
           int acc[4] = {0, 0, 0, 0};
           if constexpr (!I4) {
 #pragma unroll
@@ -403,8 +497,8 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           }
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int key = r0 + 16 * mt + 8 * e + g;
-            valid[2 * mt][e] = t == 0 && (k0 + key) < hi;
+            const int key = r0 + g1_key(g, 2 * mt + e);
+            valid[2 * mt][e] = t < 3 && (k0 + key) < hi;
             const int si = acc[2 * e] * 256 + acc[2 * e + 1] - (I4 ? qbias : 0);
             const float s = float(si) * (__half2float(kst[key]) * hf);
             sc[2 * mt][e] = valid[2 * mt][e] ? s : -INFINITY;
@@ -445,79 +539,134 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
         }
       }
       }
-      // ---- V fragments and scales, then release the stage
-      uint32_t vw[KP][4][VB / 4];  // per P.V k-step: keys {2t, 2t+1, 2t+8, 2t+9} (t-parity order)
+      if constexpr (G1) {
+        // ---- V fragments: segment sg = bytes 16sg .. 16sg+15 of the 32 keys' rows; thread (g, t)
+        // receives bytes 2g, 2g+1 of k-slots 4t+{0,1} (matrix 0), 4t+{2,3} (1), 16+4t+{0,1} (2), 16+4t+{2,3} (3)
+        uint32_t vr[4][4];
+        const uint32_t vt_s = smem_u32(vt);
 #pragma unroll
-      for (int kp = 0; kp < KP; ++kp)
+        for (int sg = 0; sg < 4; ++sg)
+          ldmatrix_x4_trans(vt_s + (v_row_off ^ uint32_t(sg << 4)), vr[sg][0], vr[sg][1], vr[sg][2], vr[sg][3]);
+        float vs4[4];
 #pragma unroll
-        for (int kq = 0; kq < 4; ++kq) {
-          const int row = r0 + 16 * kp + 2 * t + ((kq & 1) ^ vsw) + 8 * (kq >> 1);
-          lds_words<VB>(vt + tile_off<RB>(row, g * VB), vw[kp][kq]);
-        }
-      float vs[NJ][2];
-#pragma unroll
-      for (int j = 0; j < NJ; ++j)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          if constexpr (G1) {
-            if (j % 2 == 0) vs[j][e] = __half2float(vst[r0 + 8 * j + 8 * e + g]);
-          } else {
-            vs[j][e] = __half2float(vst[r0 + 8 * j + 2 * t + e]);
-          }
-        }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
+        for (int i = 0; i < 4; ++i) vs4[i] = __half2float(vst[r0 + g1_key(g, i)]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
 
-      // ---- online softmax per head g over the KPW keys
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      if constexpr (G1) {  // one head: the maximum over every lane
+        // ---- frames: a key above m_run + headroom moves the reference maximum, a product
+        // p * vs above the fixed-point range (or a full frame) the scale; either ends the frame
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // lanes t < 3 hold the same scores
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      }
-      const float m_new = fmaxf(m_run, mx);
-      if (__any_sync(0xffffffffu, m_new > m_run)) {
-        const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
-        l_run *= alpha;
-        m_run = m_new;
-        // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
-        const float a_lo = G1 ? alpha : __shfl_sync(0xffffffffu, alpha, (2 * t) * 4);
-        const float a_hi = G1 ? alpha : __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4);
-#pragma unroll
-        for (int i = 0; i < MT; ++i) {
-          o[i][0] *= a_lo;
-          o[i][1] *= a_hi;
-          o[i][2] *= a_lo;
-          o[i][3] *= a_hi;
+        if (mx > m_run + kG1Headroom) {
+          const float rescale = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
+          g1_flush(oi, bsum, so, rescale, inv_ps, g, t);
+          l_run *= rescale;
+          m_run = mx;
+          ftiles = 0;
         }
-      }
-      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
-      uint32_t pb[NJ];
+        float pv[4];
+        float pvm = 0.f;
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        if (G1 && (j % 2) == 1) continue;
-        const float p0 = valid[j][0] ? ex2(sc[j][0] - mu) : 0.f;
-        const float p1 = valid[j][1] ? ex2(sc[j][1] - mu) : 0.f;
-        l_run += p0 + p1;
-        pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] : 0.f, valid[j][1] ? p1 * vs[j][1] : 0.f);
-      }
-      if constexpr (G1) {
-        // P^T fragments of each 16-key block: lane (g, t) needs keys 2t, 2t+1 (b0) and
-        // 2t+8, 2t+9 (b1); key k (k' = k + 8) sits in lane 4k, packed {k, k'}.
-#pragma unroll
-        for (int mt = 0; mt < KP; ++mt) {
-          const uint32_t s1 = __shfl_sync(0xffffffffu, pb[2 * mt], 8 * t);
-          const uint32_t s2 = __shfl_sync(0xffffffffu, pb[2 * mt], 8 * t + 4);
-          pb[2 * mt] = __byte_perm(s1, s2, 0x5410u);
-          pb[2 * mt + 1] = __byte_perm(s1, s2, 0x7632u);
+        for (int i = 0; i < 4; ++i) {
+          const bool v_ok = valid[2 * (i >> 1)][i & 1];
+          const float pr = v_ok ? ex2(sc[2 * (i >> 1)][i & 1] - m_run) : 0.f;
+          l_run += pr;
+          pv[i] = v_ok ? pr * vs4[i] : 0.f;
+          pvm = fmaxf(pvm, pv[i]);
         }
-      }
+        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 1));
+        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 4));
+        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 8));
+        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 16));
+        if (pvm * ps > kG1VLim || ftiles >= kG1FrameTiles || (ps == 0.f && pvm > 0.f)) {
+          g1_flush(oi, bsum, so, 1.f, inv_ps, g, t);
+          if (pvm > 0.f) {
+            const float pb_ = 1.25f * fmaxf(pvm, 1e-30f);
+            ps = kG1VLim / pb_;
+            inv_ps = pb_ / kG1VLim;
+          }
+          ftiles = 0;
+        }
+        ++ftiles;
 
-      // ---- O^T += V^T P^T
+        // ---- P in three planes; lane t < 3 packs plane t of its four keys (k-slots 4g + i)
+        // and spreads them as the B operand (column c = plane c, c < 3)
+        uint32_t fw[4];
 #pragma unroll
-      for (int kp = 0; kp < KP; ++kp) {
-        if constexpr (!I4) {
+        for (int i = 0; i < 4; ++i) fw[i] = __float_as_uint(fmaf(pv[i], ps, kG1Magic));
+        const uint32_t px = __byte_perm(fw[0], fw[1], psel);
+        const uint32_t py = __byte_perm(fw[2], fw[3], psel);
+        const uint32_t pw = (__byte_perm(px, py, 0x5410u) ^ pxor) & pmask;
+        bsum = __dp4a(int(pw), 0x01010101, bsum);
+        const uint32_t pb0 = __shfl_sync(0xffffffffu, pw, 4 * t + (g & 3));
+        const uint32_t pb1 = __shfl_sync(0xffffffffu, pw, 16 + 4 * t + (g & 3));
+
+        // ---- O^T += V^T P^T on the integer tensor cores: A rows g / g + 8 = bytes 2g / 2g + 1 of
+        // the segment, four k-slots per register (byte transposes of the ldmatrix pairs)
+#pragma unroll
+        for (int sg = 0; sg < 4; ++sg) {
+          const uint32_t w0 = __byte_perm(vr[sg][0], vr[sg][1], 0x6420u);
+          const uint32_t w1 = __byte_perm(vr[sg][0], vr[sg][1], 0x7531u);
+          const uint32_t w2 = __byte_perm(vr[sg][2], vr[sg][3], 0x6420u);
+          const uint32_t w3 = __byte_perm(vr[sg][2], vr[sg][3], 0x7531u);
+          const uint32_t al[4] = {(w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu,
+                                  (w2 ^ 0x08080808u) & 0x0F0F0F0Fu, (w3 ^ 0x08080808u) & 0x0F0F0F0Fu};
+          const uint32_t ah[4] = {w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u, w2 & 0xF0F0F0F0u, w3 & 0xF0F0F0F0u};
+          mma_i8_16832<true, false>(oi[sg], al, pb0, pb1);
+          mma_i8_16832<false, false>(oi[4 + sg], ah, pb0, pb1);
+        }
+      } else {
+        // ---- V fragments and scales, then release the stage
+        uint32_t vw[KP][4][VB / 4];  // per P.V k-step: keys {2t, 2t+1, 2t+8, 2t+9} (t-parity order)
+#pragma unroll
+        for (int kp = 0; kp < KP; ++kp)
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {
+            const int row = r0 + 16 * kp + 2 * t + ((kq & 1) ^ vsw) + 8 * (kq >> 1);
+            lds_words<VB>(vt + tile_off<RB>(row, g * VB), vw[kp][kq]);
+          }
+        float vs[NJ][2];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) vs[j][e] = __half2float(vst[r0 + 8 * j + 2 * t + e]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
+
+        // ---- online softmax per head g over the KPW keys
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        if (__any_sync(0xffffffffu, m_new > m_run)) {
+          const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
+          l_run *= alpha;
+          m_run = m_new;
+          // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
+          const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * t) * 4);
+          const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4);
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            o[i][0] *= a_lo;
+            o[i][1] *= a_hi;
+            o[i][2] *= a_lo;
+            o[i][3] *= a_hi;
+          }
+        }
+        const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+        uint32_t pb[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const float p0 = valid[j][0] ? ex2(sc[j][0] - mu) : 0.f;
+          const float p1 = valid[j][1] ? ex2(sc[j][1] - mu) : 0.f;
+          l_run += p0 + p1;
+          pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] : 0.f, valid[j][1] ? p1 * vs[j][1] : 0.f);
+        }
+
+        // ---- O^T += V^T P^T
+#pragma unroll
+        for (int kp = 0; kp < KP; ++kp) {
           // m-tile i rows g / g+8: dimensions g*D/8 + i / g*D/8 + MT + i (bytes i / MT + i)
 #pragma unroll
           for (int i = 0; i < MT; ++i) {
@@ -530,34 +679,21 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
             const uint32_t a3 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1));
             mma_16816(o[i], a0, a1, a2, a3, pb[2 * kp], pb[2 * kp + 1]);
           }
-        } else {
-          // m-tile i < MT/2 rows g / g+8: dimensions g*D/8 + 2i / g*D/8 + MT + 2i (low nibbles of
-          // bytes i / MT/2 + i); m-tile MT/2 + i: the high nibbles (+1), accumulating 16 * V.
-#pragma unroll
-          for (int i = 0; i < MT / 2; ++i) {
-            const int w0 = i >> 2, w1 = (MT / 2 + i) >> 2;
-            const uint32_t s0 = uint32_t(i & 3) * 0x1111u + sel_base;
-            const uint32_t s1 = uint32_t((MT / 2 + i) & 3) * 0x1111u + sel_base;
-            const uint32_t p0 = __byte_perm(vw[kp][0][w0], vw[kp][1][w0], s0);
-            const uint32_t p1 = __byte_perm(vw[kp][0][w1], vw[kp][1][w1], s1);
-            const uint32_t p2 = __byte_perm(vw[kp][2][w0], vw[kp][3][w0], s0);
-            const uint32_t p3 = __byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1);
-            mma_16816(o[i], code_pair<kLoA, kLoB>(p0), code_pair<kLoA, kLoB>(p1), code_pair<kLoA, kLoB>(p2),
-                      code_pair<kLoA, kLoB>(p3), pb[2 * kp], pb[2 * kp + 1]);
-            mma_16816(o[MT / 2 + i], code_pair<kHiA, kHiB>(p0), code_pair<kHiA, kHiB>(p1),
-                      code_pair<kHiA, kHiB>(p2), code_pair<kHiA, kHiB>(p3), pb[2 * kp], pb[2 * kp + 1]);
-          }
         }
       }
     }
 
     // ---- unit epilogue: merge the 4 warps' (m, l, O) per head
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-    if constexpr (G1) {  // one head: the keys were spread over every lane
+    if constexpr (G1) {
+      // one head: the last frame joins the fp32 O; the lanes t < 3 of a group summed the
+      // same keys, so l is the sum over the groups
+      g1_flush(oi, bsum, so, 1.f, inv_ps, g, t);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 4);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
+    } else {
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     }
     if (t == 0) {
       sm_m[warp * 8 + g] = m_run;
@@ -566,29 +702,24 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
     const int ct = threadIdx.x;
     const size_t row_base = size_t(uc.b) * a.Hq + h0;
     for (int hp = 0; hp < gvalid; hp += MH) {
+      if constexpr (!G1) {  // one head: the warp's O is in shared memory already
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int head = 2 * t + e;
-        const int gl = head - hp;
-        if (gl >= 0 && gl < MH && head < gvalid) {
-          // this thread's dimensions g*D/8 .. g*D/8 + D/8 - 1 of the head
-          float val[D / 8];
+        for (int e = 0; e < 2; ++e) {
+          const int head = 2 * t + e;
+          const int gl = head - hp;
+          if (gl >= 0 && gl < MH && head < gvalid) {
+            // this thread's dimensions g*D/8 .. g*D/8 + D/8 - 1 of the head
+            float val[D / 8];
 #pragma unroll
-          for (int i = 0; i < MT; ++i) {
-            if constexpr (!I4) {
+            for (int i = 0; i < MT; ++i) {
               val[i] = o[i][e];
               val[MT + i] = o[i][2 + e];
-            } else {
-              const int ii = i % (MT / 2), hb = i / (MT / 2);
-              const float f = hb ? 0.0625f : 1.f;
-              val[2 * ii + hb] = o[i][e] * f;
-              val[MT + 2 * ii + hb] = o[i][2 + e] * f;
             }
-          }
-          float* dst = &sm_o[(warp * MH + gl) * D + g * (D / 8)];
+            float* dst = &sm_o[(warp * MH + gl) * D + g * (D / 8)];
 #pragma unroll
-          for (int i = 0; i < D / 8; i += 4)
-            *reinterpret_cast<float4*>(dst + i) = make_float4(val[i], val[i + 1], val[i + 2], val[i + 3]);
+            for (int i = 0; i < D / 8; i += 4)
+              *reinterpret_cast<float4*>(dst + i) = make_float4(val[i], val[i + 1], val[i + 2], val[i + 3]);
+          }
         }
       }
       named_bar_sync(1, 32 * kConsumerWarps);

@@ -25,7 +25,7 @@ def _status(fqkv, clear=0):
     return st.value
 
 
-@pytest.mark.parametrize("kind", ["gqa", "int8"])
+@pytest.mark.parametrize("kind", ["gqa", "int8", "int4", "gqa_int8"])
 def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
     lib = fqkv.native.lib()
     g = torch.Generator().manual_seed(5)
@@ -39,10 +39,18 @@ def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
     try:
         if kind == "gqa":
             fqkv.decode_attn_gqa(q, K, V, 8)
-        else:
+        elif kind == "int8":
             Kq, Ks = fqkv.qpt(K.view(B * Hkv, N, D))
             Vq, Vs = fqkv.qpt(V.view(B * Hkv, N, D))
             fqkv.decode_attn_int8_mw(q[:, :Hkv].reshape(B * Hkv, D).contiguous(), Kq, Vq, Ks, Vs, 8)
+        elif kind == "int4":  # tensor-core quantized kernel, one head per KV row
+            Kp, Ks = fqkv.quant_int4_per_token(K.view(B * Hkv, N, D))
+            Vp, Vs = fqkv.quant_int4_per_token(V.view(B * Hkv, N, D))
+            fqkv.decode_attn_int4(q[:, :Hkv].reshape(B * Hkv, D).contiguous(), Kp, Vp, Ks, Vs, 8)
+        else:  # tensor-core quantized kernel, several heads per KV row
+            Kq, Ks = fqkv.qpt(K)
+            Vq, Vs = fqkv.qpt(V)
+            fqkv.decode_attn_gqa_int8(q, Kq, Vq, Ks, Vs)
         torch.cuda.synchronize()
     finally:
         lib.fqkv_debug_skip_loads(0)
