@@ -84,7 +84,9 @@ template <int D>
 __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = F16Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // aligned by an offset from the shared array, so that every access through `smem` stays a
+  // shared-memory access (an integer round trip of the pointer would make them generic)
+  uint8_t* smem = smem_raw + ((uint32_t(1024) - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kRingBytes);
   uint64_t* empty = full + C::kStages;
   float* sm_m = reinterpret_cast<float*>(empty + C::kStages);  // [warps][8]

@@ -254,7 +254,9 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
   constexpr int KB = RB / 4;           // bytes of a K row this thread reads
   constexpr int VB = RB / 8;           // bytes of a V row this thread reads
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // aligned by an offset from the shared array, so that every access through `smem` stays a
+  // shared-memory access (an integer round trip of the pointer would make them generic)
+  uint8_t* smem = smem_raw + ((uint32_t(1024) - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::kRingBytes);
   uint64_t* empty = full + C::kStages;

@@ -101,7 +101,9 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
   using C = QCfg<kInt4, D>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  // aligned by an offset from the shared array, so that every access through `smem` stays a
+  // shared-memory access (an integer round trip of the pointer would make them generic)
+  uint8_t* smem = smem_raw + ((uint32_t(128) - (smem_u32(smem_raw) & 127u)) & 127u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * C::kStageBytes);
   uint64_t* empty = full + kStages;
   float* sm_ml = reinterpret_cast<float*>(empty + kStages);  // [warps][2]
