@@ -27,14 +27,18 @@
 //    16 * code they already are in place (one mask).  The head dimension is
 //    permuted identically for q and K so that each thread reads one
 //    contiguous D/4-dimension span of a key row.
-//  * O^T += V^T (P * Vscale)^T on the fp16 tensor cores (m16n8k16): the A
-//    operand pairs one dimension of two consecutive keys, built in registers
-//    from the codes (a byte permute of the two keys' words, one three-input
-//    logic op forming an fp16 with the code in its mantissa, one exact fp16
-//    subtraction: int8 code, int4 code or 16 * code); the B operand is the
-//    fp16 probabilities times the key's V scale, taken directly from the score
-//    accumulators.  Rows of O^T are head dimensions, columns the group's
-//    heads.  The softmax denominator sums the unscaled probabilities.
+//  * Several heads (int8): O^T += V^T (P * Vscale)^T on the fp16 tensor cores
+//    (m16n8k16): the A operand pairs one dimension of two consecutive keys,
+//    built in registers from the codes (a byte permute of the two keys' words,
+//    one three-input logic op forming an fp16 with the code in its mantissa,
+//    one exact fp16 subtraction); the B operand is the fp16 probabilities
+//    times the key's V scale, taken directly from the score accumulators.
+//    Rows of O^T are head dimensions, columns the group's heads.
+//  * One head (int4): the same product on the integer tensor cores
+//    (m16n8k32): V bytes arrive transposed by ldmatrix.trans plus two byte
+//    permutes per register pair, P * Vscale is a three-plane 8-bit fixed-point
+//    number in frames of one reference maximum and scale (see g1_key and
+//    g1_flush below).  The softmax denominator sums the unscaled probabilities.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -115,24 +119,25 @@ __device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t* w) {
   }
 }
 
-// D(16x8, s32) += A(16x32, s8 or u8, row) * B(32x8, s8 or u8, col).
+// D(16x8, s32) += A(16x32, s8 or u8, row) * B(32x8, s8 or u8, col).  A pure
+// register operation (not volatile), so shared-memory loads may be scheduled around it.
 template <bool kAUnsigned, bool kBUnsigned>
 __device__ __forceinline__ void mma_i8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   static_assert(!(kAUnsigned && kBUnsigned), "unused combination");
   if constexpr (kBUnsigned) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
         "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else if constexpr (kAUnsigned) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
         "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
         "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
@@ -557,11 +562,12 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
 
         // ---- frames: a key above m_run + headroom moves the reference maximum, a product
         // p * vs above the fixed-point range (or a full frame) the scale; either ends the frame
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // lanes t < 3 hold the same scores
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        if (mx > m_run + kG1Headroom) {
+        // (lane-local tests and a vote; the warp-wide maxima only when a frame ends)
+        if (__any_sync(0xffffffffu, mx > m_run + kG1Headroom)) {
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // lanes t < 3 hold the same scores
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
           const float rescale = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
           g1_flush(oi, bsum, so, rescale, inv_ps, g, t);
           l_run *= rescale;
@@ -578,11 +584,11 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           pv[i] = v_ok ? pr * vs4[i] : 0.f;
           pvm = fmaxf(pvm, pv[i]);
         }
-        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 1));
-        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 4));
-        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 8));
-        pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 16));
-        if (pvm * ps > kG1VLim || ftiles >= kG1FrameTiles || (ps == 0.f && pvm > 0.f)) {
+        if (__any_sync(0xffffffffu, pvm * ps > kG1VLim || (ps == 0.f && pvm > 0.f)) || ftiles >= kG1FrameTiles) {
+          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 1));
+          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 4));
+          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 8));
+          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 16));
           g1_flush(oi, bsum, so, 1.f, inv_ps, g, t);
           if (pvm > 0.f) {
             const float pb_ = 1.25f * fmaxf(pvm, 1e-30f);
