@@ -390,3 +390,29 @@ def test_int4_extreme_q_and_scales(fqkv, D):
     Kd = oq.dequantize_int4(Kp.cpu().numpy(), Ks.cpu().numpy())
     Vd = oq.dequantize_int4(Vp.cpu().numpy(), Vs.cpu().numpy())
     _close(out, oatt.decode_attention(q.numpy(), Kd, Vd))
+
+
+def test_int4_frames_under_moving_maximum_and_scales(fqkv):
+    """int4 at D=128 with units long enough to span many tiles (R=288 runs
+    unsplit, 32 tiles per unit): scores with a dominant q element move the
+    running maximum by more than 2^3 many times per unit, and V scales spread
+    over five decades (plus zero tokens) move the fixed-point range of P*V, so
+    the kernel's integer accumulators are flushed and rescaled mid-unit over
+    and over.  Sampled rows against the oracle."""
+    R, N, D = 288, 4096, 128
+    g = torch.Generator().manual_seed(140)
+    q = torch.randn(R, D, generator=g)
+    q[:, 0] = 20.0
+    K = torch.randn(R, N, D, generator=g) * 0.3
+    K[:, :, 0] = torch.randn(R, N, generator=g) * 3.0
+    V = torch.randn(R, N, D, generator=g) * torch.pow(10.0, torch.rand(R, N, 1, generator=g) * 5.0 - 3.0)
+    K[:, 200] = 0.0
+    V[:, 100] = 0.0
+    q, K, V = q.half(), K.half(), V.half()
+    Kp, Ks = fqkv.quant_int4_per_token(K.cuda())
+    Vp, Vs = fqkv.quant_int4_per_token(V.cuda())
+    out = fqkv.decode_attn_int4(q.cuda(), Kp, Vp, Ks, Vs, 8)
+    rows = [0, 1, 2, 77, 143, 200, 255, 287]
+    Kd = oq.dequantize_int4(Kp[rows].cpu().numpy(), Ks[rows].cpu().numpy())
+    Vd = oq.dequantize_int4(Vp[rows].cpu().numpy(), Vs[rows].cpu().numpy())
+    _close(out[rows], oatt.decode_attention(q[rows].numpy(), Kd, Vd))
