@@ -181,10 +181,11 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, u
                : "r"(addr));
 }
 
-// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col).
+// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col).  A pure register
+// operation (not volatile), so shared-memory loads may be scheduled around it.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
