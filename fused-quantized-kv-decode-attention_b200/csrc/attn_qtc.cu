@@ -465,9 +465,9 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
 
       // ---- scores of this warp's KPW keys (rows r0 ..) in integers.
       // Several heads: S = Q K^T, n-tile j holds keys 8j + 2t + e of head g.
-      // One head (G1): S^T = K Q^T, m-tile j/2 holds keys 16(j/2) + g (+ 8) in
-      // lanes t == 0 (columns 0 / 1: hi / lo plane); sc[j][e] is key
-      // 16(j/2) + 8e + g for even j (odd j unused).
+      // One head (G1): S^T = K Q^T, m-tile j/2 holds (rows g / g + 8) keys
+      // g1_key(g, j + 0 / 1) in lanes t < 3 (columns 2t / 2t + 1: hi / lo
+      // plane); sc[j][e] is key g1_key(g, j + e) for even j (odd j unused).
       float sc[NJ][2];
       bool valid[NJ][2];
       float mx = -INFINITY;
