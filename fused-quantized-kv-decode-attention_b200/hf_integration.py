@@ -417,10 +417,15 @@ class GraphDecoder:
 
     @torch.no_grad()
     def generate(self, steps: int) -> torch.Tensor:
-        """Decode ``steps`` more tokens after :meth:`prefill`; returns them as [B, steps]."""
+        """Decode ``steps`` more tokens after :meth:`prefill`; returns them as [B, steps].
+
+        Raises RuntimeError when a bounded wait inside the step's kernels gave up -- with the
+        fused tensor-parallel gather, a peer rank that stopped or fell behind (status 64) --
+        instead of returning tokens decoded from missing outputs."""
         P = self.prompt_len
         if P + 1 + steps > self.max_len:
             raise ValueError("generation exceeds max_len")
         for _ in range(steps):
             self.step()
+        ops.check_device_status(self.dev, "decode step")
         return self.out_tokens[:, P + 1:P + 1 + steps]

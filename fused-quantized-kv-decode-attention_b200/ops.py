@@ -482,6 +482,35 @@ def decode_attn_kvcache_tp(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, se
     _native.check(rc, f"launch: {op}")
 
 
+# Codes of the in-kernel status word (fqkv_device_status): the first bounded wait that gave up.
+DEVICE_STATUS = {
+    61: "a decode kernel's wait for a KV tile ran out",
+    62: "a decode kernel's producer waited too long for a free pipeline stage",
+    63: "a decode kernel could not drain its in-flight copies",
+    64: "a tensor-parallel peer's attention outputs never arrived (a rank stopped or fell behind)",
+}
+
+
+def device_status(device: torch.device, clear: bool = True) -> int:
+    """Reads (and by default resets) the in-kernel status word of ``device``: 0 when every
+    bounded wait since the last reset completed, else the code of the first that gave up.
+    Synchronizes with the device."""
+    st = ctypes.c_int(-1)
+    with _DeviceGuard(device):
+        rc = _native.lib().fqkv_device_status(ctypes.byref(st), 1 if clear else 0)
+    _native.check(rc, "device_status")
+    return int(st.value)
+
+
+def check_device_status(device: torch.device, what: str) -> None:
+    """Raises RuntimeError when a bounded in-kernel wait on ``device`` gave up since the
+    last check (the kernels then returned without their result instead of hanging); the
+    status word is reset, so the next call on the device starts clean."""
+    st = device_status(device, clear=True)
+    if st != 0:
+        raise RuntimeError(f"{what}: device status {st}: {DEVICE_STATUS.get(st, 'unknown code')}")
+
+
 def tp_wait(counters_ptr: int, world: int, per_call: int, sequence_ptr: int, device: torch.device) -> None:
     """Enqueue the bounded wait for every rank's tensor-parallel outputs of one call (see the C ABI)."""
     with _DeviceGuard(device):

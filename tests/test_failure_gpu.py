@@ -79,7 +79,9 @@ def test_tensor_parallel_wait_times_out_on_missing_peer(fqkv):
         torch.cuda.synchronize()
     finally:
         lib.fqkv_set_wait_timeout_ms(2000)
-    assert _status(fqkv, clear=1) == 64
+    with pytest.raises(RuntimeError, match="tensor-parallel peer"):   # what GraphDecoder.generate raises
+        fqkv.ops.check_device_status(dev, "decode step")
+    assert _status(fqkv) == 0                                          # the check reset the word
     assert int(seq.item()) == 1
     counters.fill_(6)                                                  # calls 1 and 2 complete
     fqkv.ops.tp_wait(counters.data_ptr(), 2, 3, seq.data_ptr(), dev)

@@ -78,6 +78,8 @@ def test_graph_decoder_matches_sdpa_teacher_forced(fqkv, dtype):
     assert agree >= 0.9
     err = (ours - ref).abs().max().item()
     assert err <= 0.02 + 0.03 * ref.abs().max().item()
+    dec.prefill(ids)                                   # the same graph again through generate(), which
+    assert torch.equal(dec.generate(T - 1), toks[:, 1:])  # also checks the device status word
 
 
 @pytest.mark.gpu
