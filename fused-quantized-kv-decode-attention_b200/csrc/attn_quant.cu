@@ -75,6 +75,11 @@ __device__ __forceinline__ void fma_pair(float& lo, float& hi, uint32_t v2, uint
       : "r"(v2), "h"(p));
 }
 
+// acc += h (an fp16 value), one mixed-precision FMA by 1.0
+__device__ __forceinline__ void add_half(float& acc, uint16_t h) {
+  asm("{\n\t.reg .f16 one;\n\tmov.b16 one, 0x3C00;\n\tfma.rn.f32.f16 %0, %1, one, %0;\n\t}" : "+f"(acc) : "h"(h));
+}
+
 // exact fp16 pair subtraction (both operands are small integers in fp16)
 __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -260,6 +265,9 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
 #pragma unroll
     for (int d = 0; d < kDPL; ++d) o[d] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
+    // int4: sums of the fp16 p (low nibbles) and p / 16 (high nibbles) this lane multiplied,
+    // for the + 8 offset of the nibble fields (see the P.V step)
+    float bias_lo = 0.f, bias_hi = 0.f;
 
     // One tile of this warp's keys; kMask adds the per-key bound checks that
     // only the last (partial) tile of a unit needs.
@@ -313,6 +321,8 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
 #pragma unroll
         for (int d = 0; d < kDPL; ++d) o[d] *= alpha;
         l_run *= alpha;
+        bias_lo *= alpha;
+        bias_hi *= alpha;
         m_run = m_new;
       }
       const float mu = (m_run == -INFINITY) ? 0.f : m_run;
@@ -328,18 +338,22 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         const uint4 v1v = *reinterpret_cast<const uint4*>(vt + kl * C::kRowBytes + 32 * c + 16);
         const uint32_t vwd[8] = {v0v.x, v0v.y, v0v.z, v0v.w, v1v.x, v1v.y, v1v.z, v1v.w};
         if (kInt4) {
-          // nibble n of word w is dim 8w + n.  One logic op builds an fp16 pair
-          // 1024 + s*(code+8) for nibbles (n, n+4), s = 1 or 16; an exact fp16
-          // subtraction leaves s*code; p/16 pairs with the s = 16 halves.
+          // nibble n of word w is dim 8w + n.  One logic op leaves the nibble pair
+          // (n, n+4) in offset binary as fp16 subnormals s*(code+8) * 2^-24, s = 1
+          // or 16 (exact; the FMA takes them as they are); p/16 pairs with the
+          // s = 16 halves.  The offset, 8 * 2^-24 * sum(p) per dimension, leaves
+          // once per unit through bias_lo / bias_hi.
           const uint16_t ph16 = __half_as_ushort(__float2half_rn(pv * 0.0625f));
+          add_half(bias_lo, ph);
+          add_half(bias_hi, ph16);
 #pragma unroll
           for (int w = 0; w < 8; ++w) {
             const uint32_t x = vwd[w];
             const uint32_t y = x >> 8;
-            const uint32_t a04 = hsub2_u32((x & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
-            const uint32_t a15 = hsub2_u32((x & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
-            const uint32_t a26 = hsub2_u32((y & 0x000F000Fu) ^ 0x64086408u, 0x64086408u);
-            const uint32_t a37 = hsub2_u32((y & 0x00F000F0u) ^ 0x64806480u, 0x64806480u);
+            const uint32_t a04 = (x & 0x000F000Fu) ^ 0x00080008u;
+            const uint32_t a15 = (x & 0x00F000F0u) ^ 0x00800080u;
+            const uint32_t a26 = (y & 0x000F000Fu) ^ 0x00080008u;
+            const uint32_t a37 = (y & 0x00F000F0u) ^ 0x00800080u;
             float* od = &o[(8 * w) % kDPL];
             fma_pair(od[0], od[4], a04, ph);
             fma_pair(od[1], od[5], a15, ph16);
@@ -375,6 +389,11 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       else tile(base, st, k0, std::true_type{});
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
+    }
+
+    if (kInt4) {  // scale the subnormal fields back and remove their + 8 offset
+#pragma unroll
+      for (int d = 0; d < kDPL; ++d) o[d] = fmaf(o[d], 16777216.f, -8.f * ((d & 1) ? 16.f * bias_hi : bias_lo));
     }
 
     // ---- warp reduction over key slots, then merge the 4 warps
