@@ -80,13 +80,6 @@ __device__ __forceinline__ void add_half(float& acc, uint16_t h) {
   asm("{\n\t.reg .f16 one;\n\tmov.b16 one, 0x3C00;\n\tfma.rn.f32.f16 %0, %1, one, %0;\n\t}" : "+f"(acc) : "h"(h));
 }
 
-// exact fp16 pair subtraction (both operands are small integers in fp16)
-__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
 // dp4a with a signed-byte first operand and unsigned-byte second operand,
 // and with both unsigned.
 __device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
@@ -265,8 +258,8 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
 #pragma unroll
     for (int d = 0; d < kDPL; ++d) o[d] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
-    // int4: sums of the fp16 p (low nibbles) and p / 16 (high nibbles) this lane multiplied,
-    // for the + 8 offset of the nibble fields (see the P.V step)
+    // sums of the fp16 p (int8 codes, int4 low nibbles) and p / 16 (int4 high nibbles) this
+    // lane multiplied, for the offset of the subnormal code fields (see the P.V step)
     float bias_lo = 0.f, bias_hi = 0.f;
 
     // One tile of this warp's keys; kMask adds the per-key bound checks that
@@ -361,13 +354,15 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
             fma_pair(od[3], od[7], a37, ph16);
           }
         } else {
-          // bytes (code + 128) become fp16 pairs 1024 + code + 128 with one
-          // byte-permute per pair; an exact fp16 subtraction leaves the code.
+          // bytes (code + 128) become the fp16 subnormal pairs (code + 128) * 2^-24
+          // with one byte-permute per pair (exact; the FMA takes them as they
+          // are); the offset, 128 * 2^-24 * sum(p), leaves once per unit.
+          add_half(bias_lo, ph);
 #pragma unroll
           for (int w = 0; w < 8; ++w) {
             const uint32_t x = vwd[w] ^ 0x80808080u;
-            const uint32_t a01 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x5140u), 0x64806480u);
-            const uint32_t a23 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x7362u), 0x64806480u);
+            const uint32_t a01 = __byte_perm(x, 0u, 0x4140u);
+            const uint32_t a23 = __byte_perm(x, 0u, 0x4342u);
             fma_pair(o[(4 * w) % kDPL], o[(4 * w + 1) % kDPL], a01, ph);
             fma_pair(o[(4 * w + 2) % kDPL], o[(4 * w + 3) % kDPL], a23, ph);
           }
@@ -391,9 +386,13 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       if (lane == 0) mbar_arrive(&empty[st]);
     }
 
-    if (kInt4) {  // scale the subnormal fields back and remove their + 8 offset
+    // scale the subnormal fields back and remove their offset (int4: + 8; int8: + 128)
+    if (kInt4) {
 #pragma unroll
       for (int d = 0; d < kDPL; ++d) o[d] = fmaf(o[d], 16777216.f, -8.f * ((d & 1) ? 16.f * bias_hi : bias_lo));
+    } else {
+#pragma unroll
+      for (int d = 0; d < kDPL; ++d) o[d] = fmaf(o[d], 16777216.f, -128.f * bias_lo);
     }
 
     // ---- warp reduction over key slots, then merge the 4 warps
