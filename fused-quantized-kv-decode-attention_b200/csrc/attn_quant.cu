@@ -24,10 +24,12 @@
 //    int8 codes enter dp4a directly; int4 nibbles enter as unsigned
 //    (code + 8) bytes after one xor-and, and the +8 is removed once per unit.
 //    The score is (integer dot) * k_scale * (log2(e) / sqrt(D)) / 2^e.
-//  * p . v in fp32: codes become exact fp16 pairs (one byte-permute or one
-//    logic op per pair plus an exact fp16 subtraction) and are accumulated
-//    with the mixed-precision f16 x f16 + f32 FMA; the V scale is folded
-//    into p.
+//  * p . v in fp32: codes become exact fp16 subnormal pairs in offset binary
+//    ((code + 128) * 2^-24 for int8, s * (code + 8) * 2^-24 for int4 nibbles,
+//    s = 1 or 16; one byte-permute or one logic op per pair) and are
+//    accumulated with the mixed-precision f16 x f16 + f32 FMA, which takes
+//    subnormal operands at full speed; the V scale is folded into p, and the
+//    offset leaves once per unit through per-lane sums of the same fp16 p.
 //  * Online softmax in the log2 domain, warp merge through shared memory,
 //    output fp16 or an fp32 split partial like the fp16 kernel.
 #include <cuda_fp16.h>
