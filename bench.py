@@ -268,6 +268,54 @@ class Case:
             raise RuntimeError(f"launch failed: {self.pkg.native.last_error()}")
 
 
+def timing_methods(pkg, case: Case, w: dict, dev: torch.device, ms_call: float) -> dict:
+    """The reference's other timing methods on the same workload and device-resident inputs: an
+    eager loop of back-to-back C-ABI calls (flashinfer_looptimed.py:34-44), the median of single
+    calls each bracketed by CUDA events and a synchronize (notebook lines 525-534), and the launch
+    floor -- the same two on the op's smallest shape (flashinfer_looptimed.py:47-56).  Each part
+    is capped at a few seconds of device time."""
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def loop_us(c: Case, n: int) -> float:
+        for _ in range(3):
+            c.launch()
+        torch.cuda.synchronize(dev)
+        a, b = ev(), ev()
+        a.record()
+        for _ in range(n):
+            c.launch()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) * 1e3 / n
+
+    def single_median_us(c: Case, n: int) -> float:
+        ts = []
+        for _ in range(n):
+            a, b = ev(), ev()
+            a.record()
+            c.launch()
+            b.record()
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b) * 1e3)
+        return statistics.median(ts)
+
+    n_loop = max(20, min(200, int(3000.0 / max(ms_call, 1e-3))))
+    n_single = max(10, min(100, int(2000.0 / max(ms_call, 1e-3))))
+    small = dict(w)
+    if w["kind"] in ("gqa", "gqa_int8"):
+        small.update(B=1, N=64)
+    elif w["kind"] == "sk":
+        small.update(N=64)
+    else:
+        small.update(R=1, N=64)
+    tiny = Case(pkg, small, dev, seed=7)
+    return {"eager_loop_us_per_call": round(loop_us(case, n_loop), 3), "eager_loop_calls": n_loop,
+            "single_call_median_us": round(single_median_us(case, n_single), 3), "single_calls": n_single,
+            "launch_floor_us": round(loop_us(tiny, 200), 3),
+            "launch_floor_single_call_median_us": round(single_median_us(tiny, 100), 3),
+            "launch_floor_shape": {k: small[k] for k in ("B", "R", "Hq", "Hkv", "N", "D") if k in small}}
+
+
 def e2e_run(pkg, case: Case, steps: int, dev: torch.device) -> dict:
     """Same metric through the public torch API with host (pinned) inputs copied in
     and the output read back every step, timed with CUDA events."""
@@ -623,6 +671,8 @@ def main() -> int:
                     help="do not keep the GPU loaded for clock sampling after the timed region (profiling runs)")
     ap.add_argument("--eager", action="store_true",
                     help="time K eager C-ABI calls instead of one CUDA-graph replay of K calls")
+    ap.add_argument("--no-extra-timing", action="store_true",
+                    help="skip the eager-loop, single-call and launch-floor timings (1-GPU runs only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -740,6 +790,9 @@ def main() -> int:
     clocks = sampler.stop()
 
     t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+    methods = None
+    if world == 1 and not args.no_extra_timing:
+        methods = timing_methods(pkg, case, w, dev, ms_total / args.steps)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = float(t.item()) / args.steps
@@ -781,6 +834,8 @@ def main() -> int:
             "us_per_call": round(ms_step * 1e3, 3), "pct_of_8TBps": round(100 * achieved / NOMINAL_HBM_GBS, 2),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps * case.kernels_per_call, "clocks": clocks, "impl": "ours"}
+    if methods is not None:
+        line["timing_methods"] = methods
     print(json.dumps(line), flush=True)
     return 0
 
