@@ -157,8 +157,6 @@ __device__ __forceinline__ uint32_t code_pair(uint32_t p) {
   return r;
 }
 constexpr uint32_t kI8A = 0x64806480u, kI8B = 0xFF00FF00u;    // whole byte: int8 code
-constexpr uint32_t kLoA = 0x64086408u, kLoB = 0xFFF0FFF0u;    // low nibble: int4 code
-constexpr uint32_t kHiA = 0x64806480u, kHiB = 0xFF0FFF0Fu;    // high nibble: 16 * int4 code
 
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
   return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
