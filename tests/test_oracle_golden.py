@@ -63,6 +63,27 @@ def test_int4_pack_round_trip():
     assert np.array_equal(oq.unpack_int4(oq.pack_int4(codes)), codes)
 
 
+# The reference records int4 accuracy against true fp32 attention as
+# max|int4 - fp32| / max|fp32| = 0.145 / 0.227 / 0.180 for (B, N) = (8, 1024),
+# (8, 4096), (64, 2048), D = 64, N(0,1) inputs (notebook lines 447-449, computed
+# at lines 476-485; "about 15 to 23 %").  Its inputs were drawn on a GPU and
+# cannot be reproduced here, so the pin is the band: the oracle's int4 path (the
+# GPU kernels match it within 2e-3) on seeded CPU draws of the same shapes.
+@pytest.mark.parametrize("B,N,recorded", [(8, 1024, 0.14545), (8, 4096, 0.22689), (64, 2048, 0.17994)])
+def test_int4_accuracy_vs_fp32_in_the_recorded_band(B, N, recorded):
+    import torch
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(B, 64, generator=g).half().numpy()
+    K = torch.randn(B, N, 64, generator=g).half().numpy()
+    V = torch.randn(B, N, 64, generator=g).half().numpy()
+    Kp, Ks = oq.quantize_int4_per_token(K)
+    Vp, Vs = oq.quantize_int4_per_token(V)
+    out = oatt.decode_attention(q, oq.dequantize_int4(Kp, Ks), oq.dequantize_int4(Vp, Vs))
+    ref = oatt.decode_attention(q, K, V)
+    rel = np.abs(out - ref).max() / np.abs(ref).max()
+    assert 0.5 * 0.145 < rel < 2.0 * 0.227, (rel, recorded)
+
+
 @pytest.mark.parametrize("qmax", [127.0, 7.0])
 def test_scale_division_rule_exhaustive(qmax):
     """fp32 division and torch-CUDA's multiply-by-reciprocal agree on every fp16."""
