@@ -59,7 +59,30 @@ WORKLOADS = {
                        "prompt 512 + 128 generated tokens (KV cache type in config.kv_cache)"),
     "sk": dict(kind="sk", Hq=32, Hkv=8, N=16384, D=128, S=64,
                desc="cfg4: GQA split-K batch 1, Hq=32, Hkv=8, N=16384, D=128, S=64 (gqa_sk_fast), 8 rotated KV sets"),
+    "qpt": dict(kind="quant8", R=8192, N=4096, D=128,
+                desc="int8 per-token quantizer (qpt) over config 2's K: 8192 x 4096 tokens, D=128"),
+    "quant_int4": dict(kind="quant4", R=8192, N=4096, D=128,
+                       desc="int4 per-token quantizer + packer over config 3's K: 8192 x 4096 tokens, D=128"),
 }
+
+# Extra workloads timed in the default 1-GPU run (the "configs" key): the reference's published
+# rows -- benchmarks/standalone_quant.json:6-33 (fp16 / int8 / int4), benchmarks/flashinfer_looptimed.json
+# (split-K at D=64 and 128), the quantizers of nb:236-238 / nb:292-299 -- at BASELINE's configs.
+CONFIG_SWEEP = [
+    ("cfg1_fp16", "fp16", {}),
+    ("cfg2_int8_b256", "int8", {}),
+    ("cfg3_int4_b256_d128", "int4", {}),
+    ("cfg3_int4_b256_d64", "int4", {"D": 64}),
+    ("gqa_int8_b64_n16k", "gqa_int8", {}),
+    ("sk_d128_n16k", "sk", {}),
+    ("sk_d128_n64k", "sk", {"N": 65536, "S": 128}),
+    ("sk_d64_n16k", "sk", {"D": 64}),
+    ("sk_d64_n64k", "sk", {"D": 64, "N": 65536, "S": 128}),
+    ("qpt_int8", "qpt", {}),
+    ("quant_int4", "quant_int4", {}),
+    ("cfg3_int4_b2048", "int4_b2048", {}),
+    ("cfg2_int8_b2048", "int8_b2048", {}),
+]
 
 
 # ---------------------------------------------------------------------------- helpers
@@ -72,6 +95,8 @@ def algorithmic_bytes(w: dict) -> int:
     if k == "sk":
         return 2 * w["Hkv"] * w["N"] * w["D"] * 2 + 2 * w["Hq"] * w["D"] * 2
     R, N, D = w["R"], w["N"], w["D"]
+    if k in ("quant8", "quant4"):   # per token: 2D read, D + 2 (int8) or D/2 + 2 (int4) written
+        return R * N * (2 * D + (D if k == "quant8" else D // 2) + 2)
     qo = 2 * R * D * 2
     if k == "fp16":
         return 2 * R * N * D * 2 + qo
@@ -82,7 +107,24 @@ def algorithmic_bytes(w: dict) -> int:
 def path_dtype(kind: str) -> str:
     """Arithmetic types of the path: KV storage type and the accumulation type."""
     return {"int8": "i8 KV, f32 accumulate", "gqa_int8": "i8 KV, f32 accumulate",
-            "int4": "i4 KV, f32 accumulate"}.get(kind, "f16 KV, f32 accumulate")
+            "int4": "i4 KV, f32 accumulate", "quant8": "f16 -> i8 codes + f16 scales",
+            "quant4": "f16 -> packed i4 codes + f16 scales"}.get(kind, "f16 KV, f32 accumulate")
+
+
+def dominant_kernel(w: dict) -> str:
+    """The library kernel that takes (nearly) all of a call's device time for workload `w`."""
+    k, D = w["kind"], w["D"]
+    if k in ("gqa", "fp16"):
+        return f"decode_f16_kernel<{D}>"
+    if k == "sk":
+        return f"decode_f16_kernel<{D}> + combine_kernel (PDL-chained)"
+    if k == "gqa_int8":
+        return f"decode_qtc_kernel<{D},false,false>"
+    if k == "int8":
+        return f"decode_quant_kernel<false,{D}>"
+    if k == "int4":
+        return "decode_qtc_kernel<128,true,true>" if D == 128 else f"decode_quant_kernel<true,{D}>"
+    return "quantize_vec_kernel<int4>" if k == "quant4" else "quantize_vec_kernel<int8>"
 
 
 def measured_peak() -> tuple[float, str]:
@@ -95,12 +137,19 @@ def measured_peak() -> tuple[float, str]:
 
 
 def committed_traffic(workload: str):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (or None)."""
+    """(DRAM bytes per launch of the dominant kernel, how they were measured) from the committed
+    ncu summary ``profiles/dram_traffic.json``, or (None, reason)."""
     p = ROOT / "profiles" / "dram_traffic.json"
     try:
-        return json.loads(p.read_text()).get(workload)
+        d = json.loads(p.read_text())
     except Exception:
-        return None
+        return None, "no committed ncu traffic summary"
+    e = d.get(workload)
+    if e is None:
+        return None, "no committed ncu capture for this workload"
+    if isinstance(e, dict):
+        return e.get("bytes"), e.get("source", d.get("_note", ""))
+    return e, d.get("_note", "")
 
 
 class ClockSampler:
@@ -155,6 +204,32 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------- workload setup
+POOL_BYTES = 1 << 30
+
+
+def quantized_rows(quant, R: int, N: int, D: int, int4: bool, gen, dev):
+    """codes [R, N, D or D/2] and fp16 scales [R, N]: the library's quantizer applied to N(0, 1) fp16 rows
+    for the first 1 GiB of codes (the pool); rows past the pool repeat it (the B=2048 sweeps would
+    otherwise spend minutes drawing 70-140 GB of fp16; every call still streams all R rows from HBM)."""
+    H = D // 2 if int4 else D
+    codes = torch.empty(R, N, H, device=dev, dtype=torch.uint8 if int4 else torch.int8)
+    scales = torch.empty(R, N, device=dev, dtype=torch.float16)
+    pool = max(1, min(R, POOL_BYTES // (N * H)))
+    step = max(1, (1 << 29) // (N * D))  # quantize 1 GiB of fp16 at a time
+    for r0 in range(0, pool, step):
+        r1 = min(pool, r0 + step)
+        x = torch.randn(r1 - r0, N, D, device=dev, generator=gen, dtype=torch.float16)
+        c, sc = quant(x)
+        codes[r0:r1].copy_(c)
+        scales[r0:r1].copy_(sc)
+        del x, c, sc
+    for r0 in range(pool, R, pool):
+        r1 = min(R, r0 + pool)
+        codes[r0:r1].copy_(codes[:r1 - r0])
+        scales[r0:r1].copy_(scales[:r1 - r0])
+    return codes, scales
+
+
 class Case:
     """Device-resident inputs and a zero-allocation launcher for one workload."""
 
@@ -206,6 +281,16 @@ class Case:
             self.o = torch.empty(Hq, D, device=dev, dtype=torch.float16)
             self.i = 0
             self.kernels_per_call = 2
+        elif k in ("quant8", "quant4"):
+            R, N, D = w["R"], w["N"], w["D"]
+            self.X = torch.empty(R * N, D, device=dev, dtype=torch.float16)
+            step = (1 << 29) // D
+            for t0 in range(0, R * N, step):
+                self.X[t0:t0 + step].normal_(generator=gen)
+            self.codes = torch.empty(R * N, D if k == "quant8" else D // 2, device=dev,
+                                     dtype=torch.int8 if k == "quant8" else torch.uint8)
+            self.scales = torch.empty(R * N, device=dev, dtype=torch.float16)
+            self.kernels_per_call = 1
         else:
             R, N, D = w["R"], w["N"], w["D"]
             self.q = torch.randn(R, D, device=dev, generator=gen, dtype=torch.float16)
@@ -214,22 +299,9 @@ class Case:
                 self.K = torch.randn(R, N, D, device=dev, generator=gen, dtype=torch.float16)
                 self.V = torch.randn(R, N, D, device=dev, generator=gen, dtype=torch.float16)
             else:
-                cd = torch.int8 if k == "int8" else torch.uint8
-                H = D if k == "int8" else D // 2
                 quant = pkg.qpt if k == "int8" else pkg.quant_int4_per_token
-                self.K = torch.empty(R, N, H, device=dev, dtype=cd)
-                self.V = torch.empty(R, N, H, device=dev, dtype=cd)
-                self.Ks = torch.empty(R, N, device=dev, dtype=torch.float16)
-                self.Vs = torch.empty(R, N, device=dev, dtype=torch.float16)
-                step = max(1, (1 << 29) // (N * D))  # quantize 1 GiB of fp16 at a time
-                for r0 in range(0, R, step):
-                    r1 = min(R, r0 + step)
-                    for dst, sdst in ((self.K, self.Ks), (self.V, self.Vs)):
-                        x = torch.randn(r1 - r0, N, D, device=dev, generator=gen, dtype=torch.float16)
-                        c, s = quant(x)
-                        dst[r0:r1].copy_(c)
-                        sdst[r0:r1].copy_(s)
-                        del x, c, s
+                self.K, self.Ks = quantized_rows(quant, R, N, D, k == "int4", gen, dev)
+                self.V, self.Vs = quantized_rows(quant, R, N, D, k == "int4", gen, dev)
             fmt = {"fp16": "fp16", "int8": "int8", "int4": "int4"}[k]
             nb = pkg.workspace_bytes(fmt, R, 1, 1, N, D)
             self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
@@ -256,6 +328,9 @@ class Case:
             rc = lib.fqkv_gqa_sk_fast(q.data_ptr(), K.data_ptr(), V.data_ptr(), self.mp.data_ptr(),
                                       self.lp.data_ptr(), self.op.data_ptr(), self.o.data_ptr(),
                                       w["Hq"], w["Hkv"], w["N"], w["D"], w["S"], 8, 8, s)
+        elif k in ("quant8", "quant4"):
+            fn = lib.fqkv_quantize_int8_per_token if k == "quant8" else lib.fqkv_quantize_int4_per_token
+            rc = fn(self.X.data_ptr(), self.codes.data_ptr(), self.scales.data_ptr(), self.X.shape[0], w["D"], s)
         elif k == "fp16":
             rc = lib.fqkv_decode_attn_fp16_mw(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(),
                                               self.o.data_ptr(), w["R"], w["N"], w["D"], 8,
@@ -336,6 +411,11 @@ def e2e_run(pkg, case: Case, steps: int, dev: torch.device) -> dict:
         dev_in = [torch.empty_like(t) for t in (q, K, V)]
         call = lambda: pkg.gqa_sk_fast(dev_in[0], dev_in[1], dev_in[2], case.mp, case.lp, case.op, case.o,
                                        w["S"], 8, 8) or case.o
+    elif k in ("quant8", "quant4"):
+        host = [case.X.cpu().pin_memory()]
+        dev_in = [torch.empty_like(case.X)]
+        quant = pkg.qpt if k == "quant8" else pkg.quant_int4_per_token
+        call = lambda: quant(dev_in[0])
     elif k == "fp16":
         host = [t.cpu().pin_memory() for t in (case.q, case.K, case.V)]
         dev_in = [torch.empty_like(t) for t in (case.q, case.K, case.V)]
@@ -347,14 +427,19 @@ def e2e_run(pkg, case: Case, steps: int, dev: torch.device) -> dict:
         op = pkg.decode_attn_int8_mw if k == "int8" else pkg.decode_attn_int4
         call = lambda: op(*dev_in, 8)
     h2d = sum(t.numel() * t.element_size() for t in host)
-    out_host = torch.empty(case.o.shape, dtype=torch.float16).pin_memory()
-    d2h = out_host.numel() * 2
+    if k in ("quant8", "quant4"):
+        outs_host = [torch.empty(case.codes.shape, dtype=case.codes.dtype).pin_memory(),
+                     torch.empty(case.scales.shape, dtype=torch.float16).pin_memory()]
+    else:
+        outs_host = [torch.empty(case.o.shape, dtype=torch.float16).pin_memory()]
+    d2h = sum(t.numel() * t.element_size() for t in outs_host)
 
     def step():
         for d, h in zip(dev_in, host):
             d.copy_(h, non_blocking=True)
         o = call()
-        out_host.copy_(o, non_blocking=True)
+        for dst, src in zip(outs_host, o if isinstance(o, tuple) else (o,)):
+            dst.copy_(src, non_blocking=True)
 
     step()
     torch.cuda.synchronize(dev)
@@ -404,6 +489,12 @@ def cpu_reference_setup(w: dict):
         nbytes = 2 * Hkv * N * D * 2 + 2 * Hq * D * 2
         desc = f"1 sequence (Hq={Hq}, Hkv={Hkv}, N={N}, D={D}) per call"
         return call, nbytes, desc
+    if k in ("quant8", "quant4"):
+        N, D = w["N"], w["D"]
+        X = torch.randn(32 * N, D, generator=g).half().numpy()   # one sequence's 32 heads of K
+        quant = oq.quantize_int8_per_token if k == "quant8" else oq.quantize_int4_per_token
+        nbytes = 32 * N * (2 * D + (D if k == "quant8" else D // 2) + 2)
+        return (lambda: quant(X)), nbytes, f"1 sequence x 32 heads of K ({32 * N} tokens, D={D}) per call"
     rows, N, D = 32, w["N"], w["D"]  # one sequence's 32 heads
     q = torch.randn(rows, D, generator=g).half()
     Kf = torch.randn(rows, N, D, generator=g).half()
@@ -649,6 +740,75 @@ def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
     return 0
 
 
+# ---------------------------------------------------------------------------- every config in one run
+def time_case(case: Case, dev: torch.device, gpu_index: int, min_seconds: float = 0.6) -> dict:
+    """CUDA-event time per call of one workload: a CUDA graph of n back-to-back C-ABI calls replayed
+    until the timed region lasts >= min_seconds, clocks sampled during it."""
+    for _ in range(3):
+        case.launch()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        case.launch()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    est_ms = max(e0.elapsed_time(e1) / 5, 1e-3)
+    n = int(min(400, max(8, 50.0 / est_ms)))
+    n -= n % 8                                     # whole rotations of the split-K KV sets
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(dev)):
+        for _ in range(n):
+            case.launch()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = max(1, math.ceil(min_seconds * 1e3 / (n * est_ms)))
+    sampler = ClockSampler(gpu_index)
+    sampler.start()
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    del graph
+    return {"us": e0.elapsed_time(e1) * 1e3 / (reps * n), "calls": reps * n, "clocks": clocks}
+
+
+def run_config_sweep(pkg, dev: torch.device, gpu_index: int, peak: float) -> dict:
+    """Every BASELINE config (and the quantizers) timed on this GPU: one entry per workload."""
+    out, t_start = [], time.time()
+    for name, key, over in CONFIG_SWEEP:
+        w = dict(WORKLOADS[key])
+        w.update(over)
+        t0 = time.time()
+        case = None
+        try:
+            case = Case(pkg, w, dev, seed=4321)
+            r = time_case(case, dev, gpu_index)
+        except torch.cuda.OutOfMemoryError as exc:
+            out.append({"name": name, "skipped": f"out of device memory: {str(exc).splitlines()[0]}"})
+            continue
+        finally:
+            del case
+            torch.cuda.empty_cache()
+        nbytes = algorithmic_bytes(w)
+        gbs = nbytes / (r["us"] * 1e-6) / 1e9
+        c = r["clocks"]
+        out.append({"name": name, "workload": w["desc"] + "".join(f" [{k}={v}]" for k, v in over.items()),
+                    "kernel": dominant_kernel(w), "bytes_per_call": nbytes, "us_per_call": round(r["us"], 3),
+                    "GB_s": round(gbs, 1), "pct_of_8TBps": round(100 * gbs / NOMINAL_HBM_GBS, 2),
+                    "frac_of_measured_peak": round(gbs / peak, 4), "calls_timed": r["calls"],
+                    "l2": "8 rotated KV sets > 4x L2" if w["kind"] == "sk" else "inputs > L2",
+                    "clocks": {"sm_mhz": c.get("sm_mhz"), "sm_max_mhz": c.get("sm_max_mhz"),
+                               "reasons": c.get("reasons"), "samples": c.get("samples")},
+                    "setup_plus_timing_s": round(time.time() - t0, 1)})
+    return {"entries": out, "wall_s": round(time.time() - t_start, 1),
+            "timing": "CUDA-graph replays of back-to-back C-ABI calls with device-resident inputs, CUDA events",
+            "data": "synthetic N(0,1) fp16; quantized KV: the library's quantizer on the first 1 GiB of codes, "
+                    "repeated over the remaining rows"}
+
+
 # ---------------------------------------------------------------------------- main
 def main() -> int:
     ap = argparse.ArgumentParser()
@@ -673,6 +833,8 @@ def main() -> int:
                     help="time K eager C-ABI calls instead of one CUDA-graph replay of K calls")
     ap.add_argument("--no-extra-timing", action="store_true",
                     help="skip the eager-loop, single-call and launch-floor timings (1-GPU runs only)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-config sweep (the 'configs' key) of the default 1-GPU run")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -747,6 +909,7 @@ def main() -> int:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     case = Case(pkg, w, dev, seed=1234 + rank)
+    kernels_per_call = case.kernels_per_call
 
     def barrier():
         if dist is not None:
@@ -791,7 +954,7 @@ def main() -> int:
 
     t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
     methods = None
-    if world == 1 and not args.no_extra_timing:
+    if world == 1 and not args.no_extra_timing and w["kind"] not in ("quant8", "quant4"):
         methods = timing_methods(pkg, case, w, dev, ms_total / args.steps)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -810,6 +973,13 @@ def main() -> int:
         e2e = {"value": round(per_rank_bytes * world / (e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]}
 
+    sweep = None
+    if world == 1 and not args.no_configs and args.workload == "gqa" and not (args.batch or args.seq_len
+                                                                               or args.head_dim):
+        del case
+        torch.cuda.empty_cache()
+        sweep = run_config_sweep(pkg, dev, gpu_index, measured_peak()[0])
+
     if dist is not None:
         barrier()
         dist.destroy_process_group()
@@ -818,12 +988,14 @@ def main() -> int:
 
     peak, peak_src = measured_peak()
     achieved = per_rank_bytes / (ms_step / 1e3) / 1e9
+    traffic, traffic_src = committed_traffic(args.workload) if not (args.batch or args.seq_len or args.head_dim) \
+        else (None, "workload overridden: no committed capture")
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_src,
-            "traffic": committed_traffic(args.workload),
+            "traffic": traffic, "traffic_source": traffic_src,
             "algorithmic_bytes_per_launch": per_rank_bytes,
             "note": "achieved = algorithmic bytes per call / CUDA-event time per call on the launch stream"
-                    + (" (partial kernel + PDL-chained combine)" if case.kernels_per_call > 1 else "")}
+                    + (" (partial kernel + PDL-chained combine)" if kernels_per_call > 1 else "")}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         c = cpu_reference_sample(w, args.cpu_seconds)
@@ -833,9 +1005,11 @@ def main() -> int:
             "vs_baseline": None, "dtype": path_dtype(w["kind"]), "data": "synthetic", "config": config,
             "us_per_call": round(ms_step * 1e3, 3), "pct_of_8TBps": round(100 * achieved / NOMINAL_HBM_GBS, 2),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps * case.kernels_per_call, "clocks": clocks, "impl": "ours"}
+            "gpu_launches": args.steps * kernels_per_call, "clocks": clocks, "impl": "ours"}
     if methods is not None:
         line["timing_methods"] = methods
+    if sweep is not None:
+        line["configs"] = sweep
     print(json.dumps(line), flush=True)
     return 0
 

@@ -251,15 +251,23 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
       const uint32_t pa0 = pack_half2(p00, p01);
       const uint32_t pa2 = pack_half2(p10, p11);
 
-      // ---- O += P V  (V^T fragments via ldmatrix.trans)
+      // ---- O += P V  (V^T fragments via ldmatrix.trans).  This lane's B registers
+      // b0/b2 hold keys r0 + 2t, +1 and b1/b3 keys r0 + 8 + 2t, +9 (the columns of
+      // its P registers).  Past the valid length a KV cache may hold anything
+      // (a torch.empty tail): p = 0 there, but 0 * inf / NaN is NaN, so the V
+      // halves of keys past `hi` are masked to zero (all-ones masks on full
+      // tiles; one AND per B register, no extra registers or spills).
+      const int kb = k0 + r0 + 2 * t;
+      const uint32_t vm0 = (kb < hi ? 0x0000ffffu : 0u) | (kb + 1 < hi ? 0xffff0000u : 0u);
+      const uint32_t vm1 = (kb + 8 < hi ? 0x0000ffffu : 0u) | (kb + 9 < hi ? 0xffff0000u : 0u);
 #pragma unroll
       for (int pp = 0; pp < D / 16; ++pp) {
         const int row = r0 + ((mi & 1) << 3) + rr;
         const int chunk = 2 * pp + (mi >> 1);
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4_trans(sv + swz(row, chunk), b0, b1, b2, b3);
-        mma_16816(o[2 * pp], pa0, 0u, pa2, 0u, b0, b1);
-        mma_16816(o[2 * pp + 1], pa0, 0u, pa2, 0u, b2, b3);
+        mma_16816(o[2 * pp], pa0, 0u, pa2, 0u, b0 & vm0, b1 & vm1);
+        mma_16816(o[2 * pp + 1], pa0, 0u, pa2, 0u, b2 & vm0, b3 & vm1);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);

@@ -23,9 +23,13 @@
 //
 // Set-up: host code cannot use the array's name as a device address (in host
 // code it is only a stand-in symbol).  The first call on each device, with
-// that device current, resolves the real address once with
-// cudaGetSymbolAddress and caches it; make that first call before any stream
-// capture begins on the device.  No cudaMalloc, cudaFree or allocating library
+// that device current, resolves the real address with cudaGetSymbolAddress
+// and caches it; make that first call before any stream capture begins on the
+// device.  Only a successful lookup is cached: if it fails (e.g. the first
+// call came during a capture, or the context was not ready), the call
+// returns FQKV_ERR_CUDA and the next call on that device tries again.  A
+// device reset (cudaDeviceReset) is not supported: the cached address would
+// belong to the destroyed context.  No cudaMalloc, cudaFree or allocating library
 // routine is called here or in the launch path it reuses (fqkv_gqa_sk_fast).
 #include <cuda_runtime.h>
 
@@ -46,12 +50,23 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_sk_static_scratch[kStaticScratchBytes];
 
-struct ScratchAddr {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
-  void* ptr = nullptr;
-};
-ScratchAddr g_addr[kMaxDevices];
+// Device address of g_sk_static_scratch per device, set once a lookup succeeds.
+std::mutex g_addr_mu;
+void* g_addr[kMaxDevices] = {};
+
+// Cached address of the array on device `dev` (current), looked up on first use;
+// a failed lookup is not cached, so a later call retries it.
+cudaError_t scratch_address(int dev, void** out) {
+  std::lock_guard<std::mutex> lock(g_addr_mu);
+  if (g_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_sk_static_scratch);
+    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+    g_addr[dev] = p;
+  }
+  *out = g_addr[dev];
+  return cudaSuccess;
+}
 
 size_t pad256(size_t n) { return (n + 255) & ~size_t(255); }
 
@@ -84,14 +99,14 @@ extern "C" int fqkv_gqa_sk_fast_static_scratch(const void* q, const void* K, con
     snprintf(msg, sizeof(msg), "static-scratch split-K: cudaGetDevice: %s", cudaGetErrorString(e));
     return fqkv::record_error(FQKV_ERR_CUDA, msg);
   }
-  ScratchAddr& sa = g_addr[dev];
-  std::call_once(sa.once, [&sa]() { sa.err = cudaGetSymbolAddress(&sa.ptr, g_sk_static_scratch); });
-  if (sa.err != cudaSuccess || sa.ptr == nullptr) {
-    snprintf(msg, sizeof(msg), "static-scratch split-K: cudaGetSymbolAddress failed: %s",
-             cudaGetErrorString(sa.err));
+  void* addr = nullptr;
+  e = scratch_address(dev, &addr);
+  if (e != cudaSuccess) {
+    snprintf(msg, sizeof(msg), "static-scratch split-K: cudaGetSymbolAddress failed: %s (retried on the next call)",
+             cudaGetErrorString(e));
     return fqkv::record_error(FQKV_ERR_CUDA, msg);
   }
-  unsigned char* base = static_cast<unsigned char*>(sa.ptr);
+  unsigned char* base = static_cast<unsigned char*>(addr);
   float* m_part = reinterpret_cast<float*>(base);
   float* l_part = reinterpret_cast<float*>(base + ml);
   float* o_part = reinterpret_cast<float*>(base + 2 * ml);

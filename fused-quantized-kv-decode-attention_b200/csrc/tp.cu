@@ -8,7 +8,11 @@
 // (sequence + 1) * per_call, then advances the rank-local sequence number.
 // Counters only grow, so no reset is ever needed and the whole decode step
 // replays from one CUDA graph.  The wait is bounded: after the limit it
-// records status 64 and lets the step complete.
+// records status 64 and lets the step complete.  Once any bounded wait on the
+// device has given up (the status word is non-zero), later waits return at
+// once: a peer that stopped never catches up, and waiting out the limit again
+// in every layer of every remaining step would stall the host for minutes
+// before it can read the status and raise.
 //
 // Kernels on different GPUs wait on one another here, never two kernels on one
 // GPU: the producers are the other ranks' decode kernels.
@@ -34,7 +38,9 @@ __global__ void tp_wait_kernel(const unsigned long long* __restrict__ counters, 
                                unsigned long long* __restrict__ sequence, int* status, unsigned long long timeout_ns) {
   const unsigned long long target = (*sequence + 1ull) * per_call;
   bool ok = true;
-  if (int(threadIdx.x) < world) {
+  // a wait on this device already gave up: the outputs of this step are void anyway
+  const bool failed = *reinterpret_cast<volatile int*>(status) != kDevOk;
+  if (!failed && int(threadIdx.x) < world) {
     const unsigned long long* c = counters + threadIdx.x;
     if (ld_acquire_sys(c) < target) {
       const unsigned long long t0 = globaltimer_ns();

@@ -114,9 +114,10 @@ int fqkv_decode_attn_gqa(const void* q, const void* K, const void* V, void* o, i
  * valid; out [B,Hq,D] f16.  n = *seq_len_dev when seq_len_dev != NULL (int32,
  * read on the device, clamped to max_len -- so one launch, e.g. replayed from
  * a CUDA graph, follows a growing cache), otherwise n = n_host.  Positions
- * [n, max_len) must hold finite values (they are read and weighted by zero).
- * Workspace: fqkv_decode_workspace_bytes(FQKV_KV_F16, B, Hq, Hkv, N, D) with
- * N = max_len when seq_len_dev is used, else n_host.
+ * [n, max_len) may hold anything (e.g. an unwritten torch.empty tail, NaN or
+ * inf): they never reach the output.  Workspace:
+ * fqkv_decode_workspace_bytes(FQKV_KV_F16, B, Hq, Hkv, N, D) with N = max_len
+ * when seq_len_dev is used, else n_host.
  * Extends decode_attn_gqa (reference: kernels/decode_attn_gqa.cu:56) to the
  * static-cache layout used by the reference's live-model hook (nb:1043-1061). */
 int fqkv_decode_attn_gqa_kvcache(const void* q, const void* K, const void* V, void* o, int64_t B, int64_t Hq,
@@ -136,7 +137,8 @@ int fqkv_decode_attn_gqa_int8(const void* q, const void* Kq, const void* Vq, con
 
 /* GQA int8 decode over a preallocated int8 KV cache: codes [B,Hkv,max_len,D]
  * i8, scales [B,Hkv,max_len] f16, positions [0, n) valid with n as in
- * fqkv_decode_attn_gqa_kvcache (device-side or host length).  Workspace:
+ * fqkv_decode_attn_gqa_kvcache (device-side or host length); codes and
+ * scales past n may hold anything (NaN / inf scales included).  Workspace:
  * fqkv_decode_workspace_bytes(FQKV_KV_INT8, B, Hq, Hkv, N, D) with the same N. */
 int fqkv_decode_attn_gqa_int8_kvcache(const void* q, const void* Kq, const void* Vq, const void* Ks,
                                       const void* Vs, void* o, int64_t B, int64_t Hq, int64_t Hkv,
@@ -163,8 +165,9 @@ int fqkv_gqa_sk_fast(const void* q, const void* K, const void* V, float* m_part,
  * allocator).  Limit: 2*pad256(4*Hq*S) + 4*Hq*S*D bytes must fit in 4 MiB
  * (e.g. Hq=32, D=128 allows S <= 252), else FQKV_ERR_INVALID_ARGUMENT and
  * nothing is launched.  The first call on a device (with it current) looks up
- * the array's device address once; make it before any stream capture.  All
- * calls share the array: calls that overlap on the GPU race on it.
+ * the array's device address and caches it; make it before any stream
+ * capture.  A failed lookup returns FQKV_ERR_CUDA and is retried on the next
+ * call.  All calls share the array: calls that overlap on the GPU race on it.
  * No counterpart in the reference. */
 int fqkv_gqa_sk_fast_static_scratch(const void* q, const void* K, const void* V, void* out, int64_t Hq,
                                     int64_t Hkv, int64_t N, int64_t D, int64_t S, int64_t W, int64_t CW,
@@ -314,7 +317,9 @@ int64_t fqkv_tp_arrivals(int32_t kv_format, int64_t B, int64_t Hq, int64_t Hkv, 
 /* Waits on `stream` until counters[r] >= (*sequence + 1) * per_call for every
  * rank r < world (counters and sequence: this rank's own device memory), then
  * increments *sequence.  Bounded: after the wait limit it records status 64 in
- * the device status word and returns (the call still completes). */
+ * the device status word and returns (the call still completes).  While the
+ * device status word is non-zero (a bounded wait gave up and nobody has read
+ * and cleared it with fqkv_device_status) the wait returns at once. */
 int fqkv_tp_wait(const unsigned long long* counters, int32_t world, uint64_t per_call,
                  unsigned long long* sequence, fqkv_stream_t stream);
 

@@ -1,9 +1,10 @@
 """Generate the golden fixtures in this folder by running the reference itself.
 
 Run from the repository root, in a container where the reference tree is
-mounted (default ``/root/reference``, override with ``FQKV_REFERENCE``)::
+mounted, naming its root with ``--reference`` or the ``FQKV_REFERENCE``
+environment variable (one of them is required)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <path-to-reference-root>
 
 The reference's Python functions live inside notebook cells and a test
 function, so this script extracts their definitions from the reference files
@@ -28,7 +29,7 @@ import torch
 import torch.nn.functional as F
 
 HERE = pathlib.Path(__file__).resolve().parent
-REF = pathlib.Path(os.environ.get("FQKV_REFERENCE", "/root/reference"))
+REF = pathlib.Path(".")  # set by main() from --reference / FQKV_REFERENCE
 
 
 def _notebook_defs() -> dict:
@@ -149,6 +150,15 @@ def make_attention(nb: dict, tf: dict) -> None:
 
 
 def main() -> int:
+    global REF
+    import argparse
+    ap = argparse.ArgumentParser(description="regenerate the golden fixtures from the reference's own code")
+    ap.add_argument("--reference", default=os.environ.get("FQKV_REFERENCE"),
+                    help="root of the reference tree (default: $FQKV_REFERENCE)")
+    args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference tree with --reference or FQKV_REFERENCE")
+    REF = pathlib.Path(args.reference)
     if not REF.exists():
         print(f"reference tree not found at {REF}; fixtures unchanged", file=sys.stderr)
         return 1

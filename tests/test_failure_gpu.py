@@ -66,8 +66,9 @@ def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
 def test_tensor_parallel_wait_times_out_on_missing_peer(fqkv):
     """The arrival wait of the fused tensor-parallel gather is bounded: counters
     that nothing advances (a peer that never sends) end the wait after the limit
-    with status 64; the sequence still advances and a later wait whose counts are
-    in returns clean."""
+    with status 64; the sequence still advances, later waits return at once while
+    the status is set, and once the status is read and cleared a wait whose
+    counts are in returns clean."""
     lib = fqkv.native.lib()
     counters = torch.zeros(2, dtype=torch.int64, device="cuda")     # this rank's slots for 2 ranks
     seq = torch.zeros(1, dtype=torch.int64, device="cuda")
@@ -79,11 +80,25 @@ def test_tensor_parallel_wait_times_out_on_missing_peer(fqkv):
         torch.cuda.synchronize()
     finally:
         lib.fqkv_set_wait_timeout_ms(2000)
+    # a later wait while the status word still records the first timeout returns at once instead of
+    # waiting out its own limit (a dead peer never catches up: every layer of every remaining step
+    # would otherwise stall for the full limit before the host can read the status)
+    lib.fqkv_set_wait_timeout_ms(3000)
+    try:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(4):
+            fqkv.ops.tp_wait(counters.data_ptr(), 2, 3, seq.data_ptr(), dev)
+        e1.record()
+        torch.cuda.synchronize()
+    finally:
+        lib.fqkv_set_wait_timeout_ms(2000)
+    assert e0.elapsed_time(e1) < 500.0                                 # not 4 x 3 s
+    assert int(seq.item()) == 5
     with pytest.raises(RuntimeError, match="tensor-parallel peer"):   # what GraphDecoder.generate raises
         fqkv.ops.check_device_status(dev, "decode step")
     assert _status(fqkv) == 0                                          # the check reset the word
-    assert int(seq.item()) == 1
-    counters.fill_(6)                                                  # calls 1 and 2 complete
+    counters.fill_(18)                                                 # calls 1 .. 6 complete
     fqkv.ops.tp_wait(counters.data_ptr(), 2, 3, seq.data_ptr(), dev)
     torch.cuda.synchronize()
-    assert _status(fqkv) == 0 and int(seq.item()) == 2
+    assert _status(fqkv) == 0 and int(seq.item()) == 6

@@ -416,3 +416,43 @@ def test_int4_frames_under_moving_maximum_and_scales(fqkv):
     Kd = oq.dequantize_int4(Kp[rows].cpu().numpy(), Ks[rows].cpu().numpy())
     Vd = oq.dequantize_int4(Vp[rows].cpu().numpy(), Vs[rows].cpu().numpy())
     _close(out[rows], oatt.decode_attention(q[rows].numpy(), Kd, Vd))
+
+
+# ------------------------------------------------------------------ unwritten KV-cache tails
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("B,Hq,Hkv,max_len,n", [(2, 32, 8, 200, 100), (1, 32, 8, 4096, 3001), (3, 8, 8, 300, 129),
+                                                (64, 32, 8, 640, 513)])
+def test_kvcache_tail_of_nan_and_inf_is_ignored(fqkv, B, Hq, Hkv, max_len, n, D):
+    """A cache allocated with torch.empty and written only up to n: positions [n, max_len) hold NaN
+    and inf (fp16 K/V; int8 scales), and are read by the last tile of each unit.  The outputs must
+    equal the oracle on the first n positions (host and device length, split and unsplit plans)."""
+    q = _randn(B, Hq, D, seed=150)
+    Kf, Vf = _randn(B, Hkv, n, D, seed=151), _randn(B, Hkv, n, D, seed=152)
+    K = torch.empty(B, Hkv, max_len, D, dtype=torch.float16, device="cuda")
+    V = torch.empty_like(K)
+    K[:, :, n:] = float("nan")
+    V[:, :, n:] = float("inf")
+    V[:, :, n + 1::3] = float("nan")
+    V[:, :, n + 2::3] = float("-inf")
+    K[:, :, :n], V[:, :, :n] = Kf.cuda(), Vf.cuda()
+    n_dev = torch.tensor([n], dtype=torch.int32, device="cuda")
+    ref = oatt.decode_attention_gqa(q.numpy(), Kf.numpy(), Vf.numpy())
+    for seq_len in (n, n_dev):
+        for ws in (None, torch.empty(0, dtype=torch.uint8, device="cuda")):   # preferred plan, unsplit
+            out = fqkv.decode_attn_gqa_kvcache(q.cuda(), K, V, seq_len, workspace=ws)
+            assert torch.isfinite(out).all()
+            _close(out, ref)
+    # int8 cache: garbage codes past n and NaN / inf scales
+    Kq = torch.randint(-128, 128, (B, Hkv, max_len, D), dtype=torch.int8, device="cuda")
+    Vq = torch.randint(-128, 128, (B, Hkv, max_len, D), dtype=torch.int8, device="cuda")
+    Ks = torch.full((B, Hkv, max_len), float("nan"), dtype=torch.float16, device="cuda")
+    Vs = torch.full((B, Hkv, max_len), float("inf"), dtype=torch.float16, device="cuda")
+    Vs[:, :, n + 1::2] = float("nan")
+    fqkv.quantize_into_cache(Kf.cuda(), Kq, Ks, 0)
+    fqkv.quantize_into_cache(Vf.cuda(), Vq, Vs, 0)
+    ref8 = _int8_gqa_ref(q.numpy(), Kf.numpy(), Vf.numpy())
+    for seq_len in (n, n_dev):
+        for ws in (None, torch.empty(0, dtype=torch.uint8, device="cuda")):
+            out = fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, seq_len, workspace=ws)
+            assert torch.isfinite(out).all()
+            _close(out, ref8)

@@ -7,17 +7,21 @@ must not stall on an allocation, a C host without an allocator.  For them
 4 MiB array inside the library instead of caller scratch.  This test calls it
 through the C ABI twice in a row (different shapes, so stale contents of the
 shared array from the first call must not leak into the second) and compares
-each result with the existing ``fqkv_gqa_sk_fast`` given torch-allocated
-scratch, at the tolerance the other parity tests use.  It also checks that an
-oversized request is refused with a clear error.  The file name makes pytest
-collect it last; it passes alone in a fresh process as well.
+each result with the float64 oracle and with the existing ``fqkv_gqa_sk_fast``
+given torch-allocated scratch, at the tolerance the other parity tests use.
+It also checks that an oversized request is refused with a clear error.  The
+file name makes pytest collect it last; it passes alone in a fresh process as
+well.
 """
 from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import pytest
 import torch
+
+from oracle import attention as oatt
 
 pytestmark = pytest.mark.gpu
 
@@ -63,6 +67,8 @@ def test_static_scratch_matches_caller_scratch_twice(fqkv):
         ref = _with_caller_scratch(fqkv, q, K, V, S)
         torch.cuda.synchronize()
         torch.testing.assert_close(got.float(), ref.float(), atol=ATOL, rtol=RTOL)
+        oracle = oatt.decode_attention_gqa(q.cpu().numpy()[None], K.cpu().numpy()[None], V.cpu().numpy()[None])[0]
+        np.testing.assert_allclose(got.float().cpu().numpy().astype(np.float64), oracle, atol=ATOL, rtol=RTOL)
 
 
 def test_static_scratch_rejects_oversized_request(fqkv):
