@@ -23,6 +23,9 @@ ERR_PEER = 6
 
 KV_F16, KV_INT8, KV_INT4 = 0, 1, 2
 
+# fqkv_set_split_mode
+SPLIT_AUTO, SPLIT_COMBINE, SPLIT_CLUSTER = 0, 1, 2
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _SZ = ctypes.c_size_t
@@ -44,7 +47,9 @@ SIGNATURES = {
     "fqkv_device_status": (_INT, [ctypes.POINTER(_INT), _INT]),
     "fqkv_set_wait_timeout_ms": (None, [ctypes.c_uint32]),
     "fqkv_debug_skip_loads": (None, [_INT]),
+    "fqkv_set_split_mode": (_INT, [_INT]),
     "fqkv_decode_workspace_bytes": (_SZ, [_INT, _I64, _I64, _I64, _I64, _I64]),
+    "fqkv_decode_plan": (_INT, [_INT, _I64, _I64, _I64, _I64, _I64, _SZ, ctypes.POINTER(ctypes.c_int32)]),
     "fqkv_decode_attn_fp16_mw": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "fqkv_decode_attn_int8_mw": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "fqkv_decode_attn_int4": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),

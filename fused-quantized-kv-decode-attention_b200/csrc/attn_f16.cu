@@ -25,6 +25,16 @@
 //  * Unit epilogue: the 4 warps' (m, l, o) are merged through shared memory
 //    and written either as the fp16 output (one split) or as an fp32 partial
 //    (m in log2 units, l, unnormalised o) for the combine kernel.
+//  * Cluster mode (split plans whose whole grid fits on the GPU at once, e.g.
+//    batch 1): the S split CTAs of a unit form one thread-block cluster, one
+//    CTA per SM with a deep ring.  Each CTA keeps its merged (m, l, o) in its
+//    own shared memory; after a cluster barrier the CTAs merge them through
+//    distributed shared memory (mapa + ld.shared::cluster), each CTA a slice
+//    of the unit's outputs, and write fp16 -- one launch, no partials in
+//    global memory, no combine kernel.
+//  * Before waiting for the previous kernel on the stream (programmatic
+//    dependent launch), the producer warms L2 with the CTA's first tiles, so
+//    the first loads of a call overlap the tail of the previous kernel.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -43,7 +53,7 @@ constexpr int kTK = 64;            // keys per tile
 constexpr int kHalfBytes = kTK * 128;
 constexpr int kMergeHeads = 4;     // heads merged per epilogue pass
 
-template <int D>
+template <int D, bool kCl = false>
 struct F16Cfg {
   static constexpr int kHalves = D / 64;                 // 128-byte column blocks per row
   static constexpr int kTileBytes = kHalves * kHalfBytes;  // K (or V) tile
@@ -51,24 +61,39 @@ struct F16Cfg {
   // D = 64: 3 stages keep shared memory at 55 KB so 4 CTAs fit per SM (one
   // wave for B*Hkv = 512 units; measured 20.5 -> 16.6 us at B=64, N=640 and
   // 329.6 -> 323.3 us at N=16K).  D = 128: 3 stages, 2 CTAs (registers).
-  static constexpr int kStages = 3;
+  // Cluster mode: one CTA per SM streams alone, so it gets a 192 KB ring
+  // (6 stages at D = 128, 12 at D = 64) to keep enough bytes in flight.
+  static constexpr int kStages = kCl ? (192 * 1024) / kStageBytes : 3;
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
   static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
   static constexpr size_t kMergeBytes =
       size_t(kConsumerWarps) * (2 * 8 + kMergeHeads * D) * sizeof(float);
-  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kRingBytes + kBarBytes + kMergeBytes;
+  // cluster mode: this CTA's merged (m, l) of up to 8 heads and o [8][D], read by the cluster
+  static constexpr size_t kClusterBytes = kCl ? (2 * 8 + 8 * D) * sizeof(float) : 0;
+  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kRingBytes + kBarBytes + kMergeBytes + kClusterBytes;
 };
+constexpr int kMaxCluster = 16;
 
 struct UnitCoord {
   int b, kh, grp, s;
 };
 
+// Persistent mode: units ordered (b, kh, s, grp).  Cluster mode: (b, kh, grp, s),
+// so the S_eff split CTAs of one unit are consecutive blocks -- one cluster.
+template <bool kCl>
 __device__ __forceinline__ UnitCoord decode_unit(const DecodeLaunch& a, int u) {
   UnitCoord c;
-  c.grp = u % a.groups;
-  u /= a.groups;
-  c.s = u % a.S_eff;
-  u /= a.S_eff;
+  if constexpr (kCl) {
+    c.s = u % a.S_eff;
+    u /= a.S_eff;
+    c.grp = u % a.groups;
+    u /= a.groups;
+  } else {
+    c.grp = u % a.groups;
+    u /= a.groups;
+    c.s = u % a.S_eff;
+    u /= a.S_eff;
+  }
   c.kh = u % a.Hkv;
   c.b = u / a.Hkv;
   return c;
@@ -80,9 +105,9 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return uint32_t((chunk >> 3) * kHalfBytes + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
-template <int D>
+template <int D, bool kCl>
 __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_constant__ DecodeLaunch a) {
-  using C = F16Cfg<D>;
+  using C = F16Cfg<D, kCl>;
   extern __shared__ uint8_t smem_raw[];
   // aligned by an offset from the shared array, so that every access through `smem` stays a
   // shared-memory access (an integer round trip of the pointer would make them generic)
@@ -92,6 +117,9 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   float* sm_m = reinterpret_cast<float*>(empty + C::kStages);  // [warps][8]
   float* sm_l = sm_m + kConsumerWarps * 8;                     // [warps][8]
   float* sm_o = sm_l + kConsumerWarps * 8;                     // [warps][kMergeHeads][D]
+  float* cl_m = sm_o + kConsumerWarps * kMergeHeads * D;       // cluster mode: [8]
+  float* cl_l = cl_m + 8;                                      // [8]
+  float* cl_o = cl_l + 8;                                      // [8][D]
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -109,6 +137,20 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   if (warp == kConsumerWarps && lane == 0) {
     prefetch_tensormap(&a.tmK);
     prefetch_tensormap(&a.tmV);
+    // warm L2 with this CTA's first tiles while the previous kernel finishes
+    if (blockIdx.x < a.units && !a.debug_skip_loads) {
+      const UnitCoord uc = decode_unit<kCl>(a, blockIdx.x);
+      const int lo = uc.s * a.chunk;
+      const int hi = min(a.N, lo + a.chunk);
+      const int z = uc.b * a.Hkv + uc.kh;
+      for (int k0 = lo, i = 0; k0 < hi && i < C::kStages; k0 += kTK, ++i) {
+#pragma unroll
+        for (int h = 0; h < C::kHalves; ++h) {
+          tma_prefetch_l2_3d(&a.tmK, 64 * h, k0, z);
+          tma_prefetch_l2_3d(&a.tmV, 64 * h, k0, z);
+        }
+      }
+    }
   }
   __syncthreads();
   // Let the combine kernel (if any) get scheduled while this grid streams.
@@ -121,37 +163,44 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
 
   // ------------------------------------------------------------ producer
   if (warp == kConsumerWarps) {
-    if (lane != 0 || a.debug_skip_loads) return;
-    int it = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
-      const UnitCoord uc = decode_unit(a, u);
-      const int lo = uc.s * a.chunk;
-      const int hi = min(n_valid, lo + a.chunk);
-      const int z = uc.b * a.Hkv + uc.kh;
-      for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
-        const int st = it % C::kStages;
-        if (it >= C::kStages) {
-          if (*reinterpret_cast<volatile int*>(&abort_flag) ||
-              !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
-            ok = false;
-            break;
+    if (lane == 0 && !a.debug_skip_loads) {
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+        const UnitCoord uc = decode_unit<kCl>(a, u);
+        const int lo = uc.s * a.chunk;
+        const int hi = min(n_valid, lo + a.chunk);
+        const int z = uc.b * a.Hkv + uc.kh;
+        for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
+          const int st = it % C::kStages;
+          if (it >= C::kStages) {
+            if (*reinterpret_cast<volatile int*>(&abort_flag) ||
+                !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
           }
+          mbar_arrive_expect_tx(&full[st], C::kStageBytes);
+          uint8_t* sk = smem + size_t(st) * C::kStageBytes;
+          uint8_t* sv = sk + C::kTileBytes;
+#pragma unroll
+          for (int h = 0; h < C::kHalves; ++h) tma_load_3d(sk + h * kHalfBytes, &a.tmK, 64 * h, k0, z, &full[st]);
+#pragma unroll
+          for (int h = 0; h < C::kHalves; ++h) tma_load_3d(sv + h * kHalfBytes, &a.tmV, 64 * h, k0, z, &full[st]);
         }
-        mbar_arrive_expect_tx(&full[st], C::kStageBytes);
-        uint8_t* sk = smem + size_t(st) * C::kStageBytes;
-        uint8_t* sv = sk + C::kTileBytes;
-#pragma unroll
-        for (int h = 0; h < C::kHalves; ++h) tma_load_3d(sk + h * kHalfBytes, &a.tmK, 64 * h, k0, z, &full[st]);
-#pragma unroll
-        for (int h = 0; h < C::kHalves; ++h) tma_load_3d(sv + h * kHalfBytes, &a.tmV, 64 * h, k0, z, &full[st]);
+      }
+      if (!ok) {
+        // The consumers gave up: wait (bounded) for our own copies in flight so
+        // no TMA write lands in shared memory after the CTA has exited.
+        for (int j = (it > C::kStages ? it - C::kStages : 0); j < it; ++j)
+          mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, wc, kDevTimeoutDrain);
       }
     }
-    if (!ok) {
-      // The consumers gave up: wait (bounded) for our own copies in flight so
-      // no TMA write lands in shared memory after the CTA has exited.
-      for (int j = (it > C::kStages ? it - C::kStages : 0); j < it; ++j)
-        mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, wc, kDevTimeoutDrain);
+    if constexpr (kCl) {
+      // the whole warp takes part in the consumers' two cluster barriers (see the epilogue)
+      __syncwarp();
+      cluster_sync_all();
+      cluster_sync_all();
     }
     return;
   }
@@ -168,7 +217,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   int it = 0;
 
   for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
-    const UnitCoord uc = decode_unit(a, u);
+    const UnitCoord uc = decode_unit<kCl>(a, u);
     const int lo = uc.s * a.chunk;
     const int hi = min(n_valid, lo + a.chunk);
     const int h0 = uc.kh * a.G + uc.grp * a.GP;
@@ -308,7 +357,13 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
           O += wt * sm_o[(w * kMergeHeads + gl2) * D + d];
         }
         const size_t row = row_base + gg;
-        if (a.S_eff == 1) {
+        if constexpr (kCl) {
+          if (d == 0) {
+            cl_m[gg] = M;
+            cl_l[gg] = L;
+          }
+          cl_o[gg * D + d] = O;
+        } else if (a.S_eff == 1) {
           store_out(a, row * D + d, O / L);
         } else {
           const size_t slot = row * a.S + uc.s;
@@ -321,7 +376,40 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
       }
       named_bar_sync(1, 32 * kConsumerWarps);
     }
-    if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
+    if constexpr (kCl) {
+      // ---- cluster merge: every CTA's (m, l, o) is in its shared memory; CTA r
+      // merges outputs r*128 + ct, r*128 + ct + S*128, ... of the unit's gvalid x D
+      // (log-sum-exp weights, an empty split weighs 0) and writes them as fp16.
+      // Every thread of every CTA (the producer warp too) passes both barriers.
+      cluster_sync_all();
+      const int S = a.S_eff;
+      const uint32_t r = cluster_ctarank();
+      for (int idx = int(r) * (32 * kConsumerWarps) + ct; idx < gvalid * D; idx += S * 32 * kConsumerWarps) {
+        const int gg = idx / D, d = idx - gg * D;
+        const uint32_t am = smem_u32(cl_m + gg), al = smem_u32(cl_l + gg), ao = smem_u32(cl_o + gg * D + d);
+        float mj[kMaxCluster];
+        float M = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kMaxCluster; ++j) {
+          mj[j] = j < S ? ld_dsmem_f32(dsmem_addr(am, j)) : -INFINITY;
+          M = fmaxf(M, mj[j]);
+        }
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMaxCluster; ++j) {
+          if (j < S && mj[j] != -INFINITY) {
+            const float wt = ex2(mj[j] - M);
+            L = fmaf(wt, ld_dsmem_f32(dsmem_addr(al, j)), L);
+            O = fmaf(wt, ld_dsmem_f32(dsmem_addr(ao, j)), O);
+          }
+        }
+        store_out(a, (row_base + gg) * D + d, O / L);
+      }
+      // no CTA may exit (and release its shared memory) while others still read it
+      cluster_sync_all();
+    } else {
+      if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
+    }
   }
 }
 
@@ -329,8 +417,25 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
 
 template <int D>
 static cudaError_t launch_f16(const DecodeLaunch& a, cudaStream_t stream) {
-  launch_pdl(decode_f16_kernel<D>, dim3(a.grid), dim3(kThreads), F16Cfg<D>::kSmemBytes, stream, a);
-  return cudaGetLastError();
+  if (a.cluster == 0) {
+    launch_pdl(decode_f16_kernel<D, false>, dim3(a.grid), dim3(kThreads), F16Cfg<D>::kSmemBytes, stream, a);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = F16Cfg<D, true>::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(a.cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, decode_f16_kernel<D, true>, a);
 }
 
 KernelShape decode_kernel_shape_f16(int D) {
@@ -338,12 +443,46 @@ KernelShape decode_kernel_shape_f16(int D) {
 }
 
 cudaError_t decode_kernel_prepare_f16(int D, int* ctas_per_sm) {
-  const void* fn = D == 128 ? reinterpret_cast<const void*>(&decode_f16_kernel<128>)
-                            : reinterpret_cast<const void*>(&decode_f16_kernel<64>);
+  const void* fn = D == 128 ? reinterpret_cast<const void*>(&decode_f16_kernel<128, false>)
+                            : reinterpret_cast<const void*>(&decode_f16_kernel<64, false>);
   const size_t smem = decode_kernel_shape_f16(D).smem_bytes;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, kThreads, smem);
+}
+
+template <int D>
+static cudaError_t prepare_cluster(int (&max_clusters)[17]) {
+  const void* fn = reinterpret_cast<const void*>(&decode_f16_kernel<D, true>);
+  const size_t smem = F16Cfg<D, true>::kSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  max_clusters[0] = max_clusters[1] = 0;
+  for (int c = 2; c <= kMaxCluster; ++c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(c);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+      cudaGetLastError();  // an unsupported size is not an error of the library
+      n = 0;
+    }
+    max_clusters[c] = n;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t decode_kernel_prepare_f16_cluster(int D, int (&max_clusters)[17]) {
+  return D == 128 ? prepare_cluster<128>(max_clusters) : prepare_cluster<64>(max_clusters);
 }
 
 cudaError_t launch_decode_f16(const DecodeLaunch& a, cudaStream_t stream) {

@@ -68,8 +68,10 @@ struct QtcCfg {
   // issue-bound (consumers almost never wait for a tile), so the GQA variant
   // runs 4 CTAs (20 warps) with a 2-stage ring (332.6 -> 323.7 us at B=64,
   // N=16K, D=128); the one-head int4 variant keeps 3 CTAs and 4 stages.
+  // The one-head int4 variant at D = 64 moves 4 KB tiles; 8 stages keep as many bytes in flight.
   static constexpr int kCtas = G1 ? 3 : 4;
-  static constexpr int kStages = G1 ? 4 : 2;
+  static constexpr int kStages = G1 ? (D == 64 ? 8 : 4) : 2;
+  static constexpr int NSEG = RB / 16;                         // one head: 16-byte V row segments
   static constexpr int MH = G1 ? 1 : 4;                        // heads merged per epilogue pass
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
   static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
@@ -204,12 +206,13 @@ constexpr int kG1FrameTiles = 2048;
 // Ends a frame: adds the integer accumulators times 1/Ps to the warp's fp32 O
 // in shared memory and scales the sum by `rescale` (both are relative to the
 // frame's maximum; rescale moves them to the next frame's), lane (g, 0)
-// owning head dimensions 32s + 4g + 0..3 (s = 0..3); clears the accumulators.
-// oi[s] (s < 4) holds the low nibbles (code + 8, rows g / g + 8 = dimensions
-// 32s + 4g / + 2), oi[4 + s] the high nibbles (16 * code, dimensions + 1);
-// columns 0 / 1 are the h / m planes in lanes t = 0, column 2 the l plane in
-// lanes t = 1.  bsum: the plane sums of this lane's keys (plane t), for the
-// + 8 of the low nibbles.
+// owning head dimensions 32s + 4g + 0..3 (s < NSEG = D/32); clears the
+// accumulators.  oi[s] (s < NSEG) holds the low nibbles (code + 8, rows g /
+// g + 8 = dimensions 32s + 4g / + 2), oi[NSEG + s] the high nibbles (16 *
+// code, dimensions + 1); columns 0 / 1 are the h / m planes in lanes t = 0,
+// column 2 the l plane in lanes t = 1.  bsum: the plane sums of this lane's
+// keys (plane t), for the + 8 of the low nibbles.
+template <int NSEG>
 __device__ __forceinline__ void g1_flush(int (&oi)[8][4], int& bsum, float* so, float rescale, float inv_ps, int g,
                                          int t) {
   int bs = bsum;
@@ -219,18 +222,19 @@ __device__ __forceinline__ void g1_flush(int (&oi)[8][4], int& bsum, float* so, 
   const int b1 = __shfl_down_sync(0xffffffffu, bs, 1);
   const int b2 = __shfl_down_sync(0xffffffffu, bs, 2);
 #pragma unroll
-  for (int sg = 0; sg < 4; ++sg) {
+  for (int sg = 0; sg < NSEG; ++sg) {
     const int l0 = __shfl_down_sync(0xffffffffu, oi[sg][0], 1);
     const int l2 = __shfl_down_sync(0xffffffffu, oi[sg][2], 1);
-    const int h0 = __shfl_down_sync(0xffffffffu, oi[4 + sg][0], 1);
-    const int h2 = __shfl_down_sync(0xffffffffu, oi[4 + sg][2], 1);
+    const int h0 = __shfl_down_sync(0xffffffffu, oi[NSEG + sg][0], 1);
+    const int h2 = __shfl_down_sync(0xffffffffu, oi[NSEG + sg][2], 1);
     if (t == 0) {
       float4* dst = reinterpret_cast<float4*>(so + 32 * sg + 4 * g);
       float4 c = *dst;
       const float lg = float(oi[sg][0] - 8 * bs) * 65536.f + float(oi[sg][1] - 8 * b1) * 256.f + float(l0 - 8 * b2);
-      const float hg = (float(oi[4 + sg][0]) * 65536.f + float(oi[4 + sg][1]) * 256.f + float(h0)) * 0.0625f;
+      const float hg = (float(oi[NSEG + sg][0]) * 65536.f + float(oi[NSEG + sg][1]) * 256.f + float(h0)) * 0.0625f;
       const float lg8 = float(oi[sg][2] - 8 * bs) * 65536.f + float(oi[sg][3] - 8 * b1) * 256.f + float(l2 - 8 * b2);
-      const float hg8 = (float(oi[4 + sg][2]) * 65536.f + float(oi[4 + sg][3]) * 256.f + float(h2)) * 0.0625f;
+      const float hg8 =
+          (float(oi[NSEG + sg][2]) * 65536.f + float(oi[NSEG + sg][3]) * 256.f + float(h2)) * 0.0625f;
       c.x = fmaf(lg, inv_ps, c.x) * rescale;
       c.y = fmaf(hg, inv_ps, c.y) * rescale;
       c.z = fmaf(lg8, inv_ps, c.z) * rescale;
@@ -246,7 +250,8 @@ __device__ __forceinline__ void g1_flush(int (&oi)[8][4], int& bsum, float* so, 
 template <int D, bool I4, bool G1>
 __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = QtcCfg<D, I4, G1>;
-  static_assert(I4 == G1 && (!G1 || D == 128), "int4 runs the one-head variant at D = 128, int8 the GQA one");
+  static_assert(I4 == G1, "int4 runs the one-head variant, int8 the GQA one");
+  constexpr int NSEG = C::NSEG;
   constexpr int MH = C::MH;
   constexpr int RB = C::RB;
   constexpr int KPW = C::KPW;
@@ -353,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
   if constexpr (G1) {
     const int mi = lane >> 3, rr = lane & 7;
     const int row = r0 + g1_key((rr >> 1) + 4 * (mi >> 1), 2 * (mi & 1) + (rr & 1));
-    v_row_off = uint32_t(row * RB) | (uint32_t((row >> 1) & 3) << 4);
+    v_row_off = tile_off<RB>(row, 0);  // chunk 0 of the swizzled row; segment sg: ^ (sg << 4)
     const uint32_t pb_ = t == 0 ? 2u : (t == 1 ? 1u : 0u);
     psel = pb_ | ((4u + pb_) << 4);
     pxor = (t == 1 || t == 2) ? 0x80808080u : 0u;
@@ -438,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
     if constexpr (G1) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) oi[i][0] = oi[i][1] = oi[i][2] = oi[i][3] = 0;
-      reinterpret_cast<float4*>(so)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (lane < D / 4) reinterpret_cast<float4*>(so)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
       __syncwarp();
     } else {
 #pragma unroll
@@ -547,10 +552,10 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
       if constexpr (G1) {
         // ---- V fragments: segment sg = bytes 16sg .. 16sg+15 of the 32 keys' rows; thread (g, t)
         // receives bytes 2g, 2g+1 of k-slots 4t+{0,1} (matrix 0), 4t+{2,3} (1), 16+4t+{0,1} (2), 16+4t+{2,3} (3)
-        uint32_t vr[4][4];
+        uint32_t vr[NSEG][4];
         const uint32_t vt_s = smem_u32(vt);
 #pragma unroll
-        for (int sg = 0; sg < 4; ++sg)
+        for (int sg = 0; sg < NSEG; ++sg)
           ldmatrix_x4_trans(vt_s + (v_row_off ^ uint32_t(sg << 4)), vr[sg][0], vr[sg][1], vr[sg][2], vr[sg][3]);
         float vs4[4];
 #pragma unroll
@@ -567,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
           const float rescale = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
-          g1_flush(oi, bsum, so, rescale, inv_ps, g, t);
+          g1_flush<NSEG>(oi, bsum, so, rescale, inv_ps, g, t);
           l_run *= rescale;
           m_run = mx;
           ftiles = 0;
@@ -587,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 4));
           pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 8));
           pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 16));
-          g1_flush(oi, bsum, so, 1.f, inv_ps, g, t);
+          g1_flush<NSEG>(oi, bsum, so, 1.f, inv_ps, g, t);
           if (pvm > 0.f) {
             const float pb_ = 1.25f * fmaxf(pvm, 1e-30f);
             ps = kG1VLim / pb_;
@@ -612,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
         // ---- O^T += V^T P^T on the integer tensor cores: A rows g / g + 8 = bytes 2g / 2g + 1 of
         // the segment, four k-slots per register (byte transposes of the ldmatrix pairs)
 #pragma unroll
-        for (int sg = 0; sg < 4; ++sg) {
+        for (int sg = 0; sg < NSEG; ++sg) {
           const uint32_t w0 = __byte_perm(vr[sg][0], vr[sg][1], 0x6420u);
           const uint32_t w1 = __byte_perm(vr[sg][0], vr[sg][1], 0x7531u);
           const uint32_t w2 = __byte_perm(vr[sg][2], vr[sg][3], 0x6420u);
@@ -621,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
                                   (w2 ^ 0x08080808u) & 0x0F0F0F0Fu, (w3 ^ 0x08080808u) & 0x0F0F0F0Fu};
           const uint32_t ah[4] = {w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u, w2 & 0xF0F0F0F0u, w3 & 0xF0F0F0F0u};
           mma_i8_16832<true, false>(oi[sg], al, pb0, pb1);
-          mma_i8_16832<false, false>(oi[4 + sg], ah, pb0, pb1);
+          mma_i8_16832<false, false>(oi[NSEG + sg], ah, pb0, pb1);
         }
       } else {
         // ---- V fragments and scales, then release the stage
@@ -693,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
     if constexpr (G1) {
       // one head: the last frame joins the fp32 O; the lanes t < 3 of a group summed the
       // same keys, so l is the sum over the groups
-      g1_flush(oi, bsum, so, 1.f, inv_ps, g, t);
+      g1_flush<NSEG>(oi, bsum, so, 1.f, inv_ps, g, t);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 4);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
@@ -780,20 +785,18 @@ void launch_one(const DecodeLaunch& a, cudaStream_t stream) {
 
 // int8 codes reach this kernel only with several query heads per KV head
 // (the planner's I8Gqa); int4 codes only with one (the C ABI requires
-// Hq == Hkv for int4) and D = 128, which runs the one-head (S^T) variant.
+// Hq == Hkv for int4), which runs the one-head (S^T) variant.
 cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm) {
-  if (int4) {
-    if (D != 128) return cudaErrorInvalidValue;
-    return prepare_one<128, true, true>(ctas_per_sm);
-  }
+  if (int4) return D == 128 ? prepare_one<128, true, true>(ctas_per_sm) : prepare_one<64, true, true>(ctas_per_sm);
   return D == 128 ? prepare_one<128, false, false>(ctas_per_sm) : prepare_one<64, false, false>(ctas_per_sm);
 }
 
 cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream) {
   const bool i4 = a.fmt == KvFormat::I4Tc;
-  if (i4 != (a.GP == 1) || (i4 && a.D != 128)) return cudaErrorInvalidValue;
+  if (i4 != (a.GP == 1)) return cudaErrorInvalidValue;
   if (i4) {
-    launch_one<128, true, true>(a, stream);
+    if (a.D == 128) launch_one<128, true, true>(a, stream);
+    else launch_one<64, true, true>(a, stream);
   } else {
     if (a.D == 128) launch_one<128, false, false>(a, stream);
     else launch_one<64, false, false>(a, stream);

@@ -47,6 +47,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 std::atomic<unsigned long long> g_timeout_ns{2000ull * 1000ull * 1000ull};
 std::atomic<int> g_debug_skip_loads{0};
+std::atomic<int> g_split_mode{FQKV_SPLIT_AUTO};
 
 // ------------------------------------------------------------------ device state
 constexpr int kMaxDevices = 64;
@@ -60,6 +61,7 @@ struct DeviceState {
   int occ_f16[2] = {0, 0};      // D = 64, 128
   int occ_q[2][2] = {{0, 0}, {0, 0}};  // [int4][D==128]
   int occ_qtc[2][2] = {{0, 0}, {0, 0}};  // tensor-core quantized kernel [int4][D==128]
+  int max_clusters_f16[2][17] = {};      // fp16 cluster mode: resident clusters per cluster size [D==128][size]
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -81,11 +83,13 @@ void init_device(DeviceState& ds, int dev) {
   e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status), g_fqkv_device_status);
   if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
   for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_f16(i ? 128 : 64, &ds.occ_f16[i]);
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i)
+    e = fqkv::decode_kernel_prepare_f16_cluster(i ? 128 : 64, ds.max_clusters_f16[i]);
   for (int q = 0; q < 2 && e == cudaSuccess; ++q)
     for (int i = 0; i < 2 && e == cudaSuccess; ++i)
       e = fqkv::decode_kernel_prepare_quant(q == 1, i ? 128 : 64, &ds.occ_q[q][i]);
   for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_qtc(false, i ? 128 : 64, &ds.occ_qtc[0][i]);
-  if (e == cudaSuccess) e = fqkv::decode_kernel_prepare_qtc(true, 128, &ds.occ_qtc[1][1]);
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_qtc(true, i ? 128 : 64, &ds.occ_qtc[1][i]);
   if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -217,38 +221,66 @@ void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_byt
   // N=16K: 18.4 -> 17.7 us).
   const int64_t floor_ctas = (3 * C) / 5;
   const int64_t maxS = S_fixed > 0 ? std::min<int64_t>(tiles, S_fixed) : std::min<int64_t>(tiles, 256);
-  double best = 1e300;
-  int64_t best_S = 1;
-  for (int64_t S = 1; S <= maxS; ++S) {
-    int64_t ct, se;
-    geometry(S, &ct, &se);
-    if (se != S) continue;
-    if (S_fixed <= 0 && limit_ws && se > 1 && partial_bytes(rows, se, a.D) > ws_bytes) continue;
-    const int64_t U = units0 * se;
-    double cost = 0;
-    for (int64_t done = 0; done < U; done += C) {
-      const int64_t active = std::min(C, U - done);
-      cost += double(std::max<int64_t>(active, floor_ctas)) * double(ct + (se > 1 ? 1 : 0));
+  auto best_split = [&](bool respect_ws) {
+    double best = 1e300;
+    int64_t best_S = 1;
+    for (int64_t S = 1; S <= maxS; ++S) {
+      int64_t ct, se;
+      geometry(S, &ct, &se);
+      if (se != S) continue;
+      if (respect_ws && se > 1 && partial_bytes(rows, se, a.D) > ws_bytes) continue;
+      const int64_t U = units0 * se;
+      double cost = 0;
+      for (int64_t done = 0; done < U; done += C) {
+        const int64_t active = std::min(C, U - done);
+        cost += double(std::max<int64_t>(active, floor_ctas)) * double(ct + (se > 1 ? 1 : 0));
+      }
+      // The combine kernel (its wait for the partial grid, the partials' round
+      // trip through L2) costs about three tile-rounds of the whole grid (B=64,
+      // Hkv=8, N=640, D=64 runs 20.4 us unsplit against 25.7 us in two splits),
+      // plus 0.07 of a round per split (its loop over the partials: config 4
+      // at 16K measured 3.1 us of combine at 24 splits, 5.6 us at 37).
+      if (se > 1) cost += (3.0 + 0.07 * double(se)) * double(C);
+      if (cost < best * 0.999) {
+        best = cost;
+        best_S = se;
+      }
     }
-    // The combine kernel (its wait for the partial grid, the partials' round
-    // trip through L2) costs about three tile-rounds of the whole grid (B=64,
-    // Hkv=8, N=640, D=64 runs 20.4 us unsplit against 25.7 us in two splits),
-    // plus 0.07 of a round per split (its loop over the partials: config 4
-    // at 16K measured 3.1 us of combine at 24 splits, 5.6 us at 37).
-    if (se > 1) cost += (3.0 + 0.07 * double(se)) * double(C);
-    if (cost < best * 0.999) {
-      best = cost;
-      best_S = se;
+    return best_S;
+  };
+  // The cluster merge below needs no workspace, so whether to split is decided
+  // first without the workspace limit; the limit applies to the combine plan.
+  const bool ws_limited = S_fixed <= 0 && limit_ws;
+  int64_t ct, se;
+  geometry(best_split(false), &ct, &se);
+  a.cluster = 0;
+  // Cluster mode (fp16, local output): when the grid is too small to fill the GPU without
+  // splitting, the S split CTAs of each unit form one thread-block cluster (S <= 16), one CTA
+  // per SM, and merge through distributed shared memory -- one launch, no partials, no combine.
+  // Used when the whole grid is resident at once and keeps at least half the SMs streaming
+  // (batch-1 decode: Hkv = 8 KV heads x 16 splits = 128 CTAs).
+  const int mode = g_split_mode.load();
+  if (a.fmt == KvFormat::F16 && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
+      (se > 1 || mode == FQKV_SPLIT_CLUSTER) && units0 < ds.sm_count) {
+    int64_t sc = std::min<int64_t>({16, tiles, std::max<int64_t>(1, ds.sm_count / units0)});
+    if (S_fixed > 0) sc = std::min<int64_t>(sc, S_fixed);
+    int64_t cct = 0, cse = 0;
+    if (sc >= 2) geometry(sc, &cct, &cse);
+    const int di = a.D == 128 ? 1 : 0;
+    if (sc >= 2 && cse >= 2 && units0 <= ds.max_clusters_f16[di][cse] &&
+        (mode == FQKV_SPLIT_CLUSTER || 2 * units0 * cse >= ds.sm_count)) {
+      ct = cct;
+      se = cse;
+      a.cluster = int(cse);
     }
   }
-  int64_t ct, se;
-  geometry(best_S, &ct, &se);
+  if (!a.cluster && ws_limited && se > 1 && partial_bytes(rows, se, a.D) > ws_bytes) geometry(best_split(true), &ct, &se);
   a.S = S_fixed > 0 ? int(S_fixed) : int(se);   // partial-slot stride per row
   a.S_eff = int(se);
   a.chunk = int(ct * TK);
   const int64_t units = units0 * a.S_eff;
   a.units = int(units);
-  a.grid = int(std::min<int64_t>(units, C));
+  a.grid = a.cluster ? int(units) : int(std::min<int64_t>(units, C));
   a.sm_scale_log2 = float(1.4426950408889634 / std::sqrt(double(a.D)));
   a.status = ds.status;
   a.timeout_ns = g_timeout_ns.load();
@@ -271,7 +303,7 @@ int launch(DecodeLaunch& a, cudaStream_t stream) {
                   : (a.fmt == KvFormat::I8Gqa || a.fmt == KvFormat::I4Tc) ? fqkv::launch_decode_qtc(a, stream)
                                              : fqkv::launch_decode_quant(a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "launch");
-  if (a.S_eff > 1) {
+  if (a.S_eff > 1 && !a.cluster) {
     e = fqkv::launch_combine(a, stream);
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }
@@ -321,7 +353,7 @@ int run_decode(KvFormat fmt, const void* q, const void* K, const void* V, const 
   }
   plan(a, *ds, 0, ws ? ws_bytes : 0, true);
   if (int64_t(a.B) * a.Hkv * a.groups * a.S_eff > INT32_MAX) return fail(FQKV_ERR_INVALID_ARGUMENT, "too many work units");
-  if (a.S_eff > 1) {
+  if (a.S_eff > 1 && !a.cluster) {
     if (!aligned(ws, 16)) return fail(FQKV_ERR_MISALIGNED, "workspace must be 16-byte aligned");
     carve_partials(a, ws, int64_t(a.B) * a.Hq);
   }
@@ -354,6 +386,13 @@ void fqkv_set_wait_timeout_ms(uint32_t ms) { g_timeout_ns.store(uint64_t(ms) * 1
 
 void fqkv_debug_skip_loads(int enable) { g_debug_skip_loads.store(enable ? 1 : 0); }
 
+int fqkv_set_split_mode(int mode) {
+  if (mode != FQKV_SPLIT_AUTO && mode != FQKV_SPLIT_COMBINE && mode != FQKV_SPLIT_CLUSTER)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "split mode: FQKV_SPLIT_AUTO, _COMBINE or _CLUSTER (got %d)", mode);
+  g_split_mode.store(mode);
+  return FQKV_OK;
+}
+
 int fqkv_device_status(int* status_out, int clear) {
   if (!status_out) return fail(FQKV_ERR_INVALID_ARGUMENT, "status_out is null");
   DeviceState* ds = nullptr;
@@ -380,7 +419,27 @@ size_t fqkv_decode_workspace_bytes(int kv_format, int64_t B, int64_t Hq, int64_t
   a.fmt = static_cast<KvFormat>(kv_format);
   a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
   plan(a, *ds, 0, 0, false);
-  return a.S_eff > 1 ? partial_bytes(B * Hq, a.S_eff, D) : 0;
+  return (a.S_eff > 1 && !a.cluster) ? partial_bytes(B * Hq, a.S_eff, D) : 0;
+}
+
+int fqkv_decode_plan(int kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, size_t workspace_bytes,
+                     int32_t* plan_out) {
+  if (!plan_out) return fail(FQKV_ERR_INVALID_ARGUMENT, "plan_out is null");
+  if (kv_format < 0 || kv_format > 2 || B <= 0 || Hq < 1 || Hkv < 1 || N < 1 || (D != 64 && D != 128) ||
+      Hq % Hkv != 0 || (kv_format == FQKV_KV_INT4 && Hq != Hkv) || B * Hkv > INT32_MAX || N > INT32_MAX)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "decode_plan: bad kv_format or sizes");
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  DecodeLaunch a{};
+  a.fmt = static_cast<KvFormat>(kv_format);
+  a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
+  plan(a, *ds, 0, workspace_bytes, true);
+  plan_out[0] = a.S_eff;
+  plan_out[1] = a.cluster;
+  plan_out[2] = a.grid;
+  plan_out[3] = a.chunk;
+  plan_out[4] = static_cast<int32_t>(a.fmt);
+  return FQKV_OK;
 }
 
 int fqkv_decode_attn_fp16_mw(const void* q, const void* K, const void* V, void* o, int64_t R, int64_t N,
@@ -465,7 +524,7 @@ static int run_quantize_into(bool int4, const void* X, void* codes, void* scales
   DeviceState* ds = nullptr;
   if (int rc = device_state(&ds)) return rc;
   cudaError_t e = fqkv::launch_quantize_into(int4, X, codes, scales, groups, T, int(D), cap, pos_host,
-                                             reinterpret_cast<const int*>(pos_dev),
+                                             reinterpret_cast<const int*>(pos_dev), ds->sm_count,
                                              reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
   return FQKV_OK;
@@ -523,7 +582,8 @@ static int run_quantize(bool int4, const void* X, void* codes, void* scales, int
   if (rows > (int64_t(1) << 40)) return fail(FQKV_ERR_INVALID_ARGUMENT, "too many rows");
   DeviceState* ds = nullptr;
   if (int rc = device_state(&ds)) return rc;
-  cudaError_t e = fqkv::launch_quantize(int4, X, codes, scales, rows, int(D), reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t e =
+      fqkv::launch_quantize(int4, X, codes, scales, rows, int(D), ds->sm_count, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
   return FQKV_OK;
 }
@@ -697,6 +757,7 @@ int64_t fqkv_tp_arrivals(int32_t kv_format, int64_t B, int64_t Hq, int64_t Hkv, 
   DecodeLaunch a{};
   a.fmt = kv_format == FQKV_KV_F16 ? KvFormat::F16 : KvFormat::I8;
   a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(max_len); a.D = int(D);
+  a.tp.world = 2;  // tensor-parallel output: planned as fqkv_decode_attn_kvcache_tp plans it (no cluster mode)
   plan(a, *ds, 0, workspace_bytes, true);
   // unsplit: one arrival per unit (decode kernel epilogue); split: one per row (combine)
   return a.S_eff == 1 ? int64_t(a.units) : B * Hq;

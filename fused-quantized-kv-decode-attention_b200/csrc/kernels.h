@@ -70,7 +70,9 @@ struct DecodeLaunch {
   int S_eff;          // non-empty splits actually launched (<= S)
   int chunk;          // keys per split, a multiple of the tile
   int units;          // B * Hkv * groups * S_eff
-  int grid;           // persistent CTAs
+  int grid;           // persistent CTAs (cluster mode: one CTA per unit)
+  int cluster;        // fp16 only: 0, or S_eff when the S_eff split CTAs of a unit form a thread-block
+                      // cluster and merge through distributed shared memory (no partials, no combine)
   float sm_scale_log2;                 // (1/sqrt(D)) * log2(e)
   int* status;                         // device status word
   unsigned long long timeout_ns;
@@ -118,6 +120,9 @@ struct KernelShape {
 };
 KernelShape decode_kernel_shape_f16(int D);
 cudaError_t decode_kernel_prepare_f16(int D, int* ctas_per_sm);
+// Cluster variant of the fp16 kernel: sets its attributes on the current device and
+// returns, for cluster sizes 0..16, how many such clusters can be resident at once.
+cudaError_t decode_kernel_prepare_f16_cluster(int D, int (&max_clusters)[17]);
 cudaError_t launch_decode_f16(const DecodeLaunch& a, cudaStream_t stream);
 KernelShape decode_kernel_shape_quant(bool int4, int D);
 cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm);
@@ -148,12 +153,13 @@ cudaError_t launch_tp_wait(const unsigned long long* counters, int world, unsign
 // chained to the preceding launch by programmatic dependent launch.
 cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream);
 
-cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,
+cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D, int sm_count,
                             cudaStream_t stream);
 // Quantize groups x T tokens [groups, T, D] into a cache [groups, cap, D]
 // (int4: [groups, cap, D/2]) at positions pos .. pos+T-1 of every group, pos =
 // *pos_dev if given else pos_host; D in {64, 128}; X 16-byte aligned.
 cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
-                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, cudaStream_t stream);
+                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, int sm_count,
+                                 cudaStream_t stream);
 
 }  // namespace fqkv

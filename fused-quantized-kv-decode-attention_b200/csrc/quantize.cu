@@ -12,14 +12,30 @@
 //   r    = fp16( fp32(x) / fp32(s) )         (second rounding to fp16)
 //   code = rint(r) clamped to [-Q, Q];  NaN -> 0
 // clamp(min=1e-8) never changes an fp16 value (1e-8 rounds to fp16 zero), and
-// amax propagates NaN like torch.amax.  Divisions use __fdiv_rn so the result
-// does not depend on fast-math flags.
+// amax propagates NaN like torch.amax.
 //
-// HBM-bound: one 16-byte load per lane (8 elements), D/8 lanes per token.
+// The quotient x / s: for a scale s that is a normal fp16 number (the common
+// case) it is computed with Markstein's FMA-corrected division (P. Markstein,
+// "IA-64 and Elementary Functions", 2000): y ~ 1/s from the hardware
+// reciprocal approximation (relative error < 2^-22), q0 = x*y, r = x - s*q0
+// (one FMA), q1 = q0 + r*y (one FMA).  q1 - x/s = (q0 - x/s)(1 - s*y), about
+// 2^-21 of an fp32 ulp.  With fp16 operands, x/s = (A/B) 2^k with integers
+// A, B < 2^11; such a quotient is never an fp32 rounding midpoint and, when it
+// is not one, lies at least 2^-12 ulp away from every midpoint (the distance
+// is a nonzero integer over B 2^(24-e)).  So q1 rounds exactly as the IEEE
+// quotient -- for every fp16 pair, checked on the GPU over all (amax, x)
+// pairs by the quantizer tests.  With s normal, |x/s| <= Q (1 + 2^-10), so the
+// rounded code needs no clamp.  Scales that are 0, subnormal, inf or NaN
+// (all-zero / tiny tokens, non-finite inputs) take the IEEE __fdiv_rn path
+// with the clamp and the NaN rule.
+//
+// HBM-bound: a persistent grid; each lane keeps 16-byte loads of kUnroll
+// tokens in flight (streaming, evict-first), D/8 lanes per token.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 
@@ -37,13 +53,28 @@ __device__ __forceinline__ int quant_code(float x, float s) {
   return static_cast<int>(fminf(fmaxf(rr, -float(Q)), float(Q)));
 }
 
+// Code of x for a normal fp16 scale s (y = approximate 1/s): round(fp16(x / s)).
+__device__ __forceinline__ int quant_code_fast(float x, float s, float y) {
+  const float q0 = x * y;
+  const float q1 = fmaf(fmaf(-s, q0, x), y, q0);
+  return __half2int_rn(__float2half_rn(q1));
+}
+
+__device__ __forceinline__ float rcp_approx(float s) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s));
+  return y;
+}
+
+// s is a normal fp16 number: the fast division applies (see the file comment)
+__device__ __forceinline__ bool normal_fp16_scale(float s) { return s >= 6.103515625e-05f && s <= 65504.f; }
+
 template <int Q>
 __device__ __forceinline__ __half quant_scale(float amax, bool any_nan) {
   const float a = any_nan ? __int_as_float(0x7fc00000) : amax;
   return __float2half_rn(__fdiv_rn(a, float(Q)));
 }
 
-// Vectorised path: D in {64, 128, 256}; LPR = D/8 lanes per token.
 // Output placement: token `row` of the input (rows = groups x T tokens) goes
 // to output row (row / T) * cap + pos + row % T, where pos is *pos_dev when
 // given (a growing KV cache) else pos_host; tokens landing at or past `cap`
@@ -53,55 +84,85 @@ struct QuantPlace {
   const int* pos_dev;
 };
 
+// Four codes (low bytes of c0..c3) as one word, c0 in the low byte.
+__device__ __forceinline__ uint32_t pack4(int c0, int c1, int c2, int c3) {
+  return __byte_perm(__byte_perm(c0, c1, 0x0040u), __byte_perm(c2, c3, 0x0040u), 0x5410u);
+}
+
+// Vectorised path: D in {64, 128, 256}; LPR = D/8 lanes per token, each with 8
+// consecutive elements.  Persistent: warp w handles tokens w*RPW + j + i*stride.
 template <bool kInt4, int D>
-__global__ void __launch_bounds__(256) quantize_vec_kernel(const __half* __restrict__ X, void* __restrict__ codes,
+__global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __restrict__ X, void* __restrict__ codes,
                                                            __half* __restrict__ scales, int64_t rows,
                                                            QuantPlace pl) {
   constexpr int LPR = D / 8;
   constexpr int RPW = 32 / LPR;
   constexpr int Q = kInt4 ? 7 : 127;
+  constexpr int kUnroll = 4;
   const int lane = threadIdx.x & 31;
-  const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t row = warp_global * RPW + lane / LPR;
   const int c = lane % LPR;
-  const bool active = row < rows;
-  uint4 raw = make_uint4(0, 0, 0, 0);
-  if (active) raw = *reinterpret_cast<const uint4*>(X + row * D + 8 * c);
-  const __half* hx = reinterpret_cast<const __half*>(&raw);
-  float xf[8];
-  float amax = 0.f;
-  bool nan = false;
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int64_t stride = warps * RPW;  // tokens covered by one pass of all warps
+  const int64_t pos0 = pl.pos_dev ? int64_t(*pl.pos_dev) : pl.pos_host;
+  for (int64_t wbase = ((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * RPW; wbase < rows;
+       wbase += kUnroll * stride) {  // warp-uniform: every lane takes part in the shuffles below
+    uint4 raw[kUnroll];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    xf[i] = __half2float(hx[i]);
-    nan |= isnan(xf[i]);
-    amax = fmaxf(amax, fabsf(xf[i]));
-  }
-#pragma unroll
-  for (int off = 1; off < LPR; off <<= 1) {
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    nan |= __shfl_xor_sync(0xffffffffu, int(nan), off) != 0;
-  }
-  const __half sh = quant_scale<Q>(amax, nan);
-  const float s = __half2float(sh);
-  if (!active) return;
-  const int64_t pos = (pl.pos_dev ? int64_t(*pl.pos_dev) : pl.pos_host) + row % pl.T;
-  if (pos < 0 || pos >= pl.cap) return;
-  const int64_t orow = (row / pl.T) * pl.cap + pos;
-  if (c == 0) scales[orow] = sh;
-  if (kInt4) {
-    uint32_t packed = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) packed |= (uint32_t(quant_code<Q>(xf[i], s)) & 0xFu) << (4 * i);
-    reinterpret_cast<uint32_t*>(codes)[(orow * D) / 8 + c] = packed;
-  } else {
-    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      w0 |= (uint32_t(quant_code<Q>(xf[i], s)) & 0xFFu) << (8 * i);
-      w1 |= (uint32_t(quant_code<Q>(xf[4 + i], s)) & 0xFFu) << (8 * i);
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t row = wbase + lane / LPR + u * stride;
+      raw[u] = row < rows ? __ldcs(reinterpret_cast<const uint4*>(X + row * D + 8 * c)) : make_uint4(0, 0, 0, 0);
     }
-    reinterpret_cast<uint2*>(codes)[(orow * D) / 8 + c] = make_uint2(w0, w1);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t row = wbase + lane / LPR + u * stride;
+      if (wbase + u * stride >= rows) break;  // warp-uniform
+      const __half2* h2 = reinterpret_cast<const __half2*>(&raw[u]);
+      // amax in fp16 (exact), NaN-propagating like torch.amax
+      __half2 m2 = __habs2(h2[0]);
+#pragma unroll
+      for (int i = 1; i < 4; ++i) m2 = __hmax2_nan(m2, __habs2(h2[i]));
+      float amax = fmaxf(__low2float(m2), __high2float(m2));
+      bool nan = __hisnan(m2.x) || __hisnan(m2.y);
+#pragma unroll
+      for (int off = 1; off < LPR; off <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        nan |= __shfl_xor_sync(0xffffffffu, int(nan), off) != 0;
+      }
+      const __half sh = quant_scale<Q>(amax, nan);
+      const float sc = __half2float(sh);
+      if (row >= rows) continue;
+      const int64_t pos = pos0 + row % pl.T;
+      if (pos < 0 || pos >= pl.cap) continue;
+      const int64_t orow = (row / pl.T) * pl.cap + pos;
+      if (c == 0) scales[orow] = sh;
+      int q[8];
+      if (normal_fp16_scale(sc)) {
+        const float y = rcp_approx(sc);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h2[i]);
+          q[2 * i] = quant_code_fast(f.x, sc, y);
+          q[2 * i + 1] = quant_code_fast(f.y, sc, y);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h2[i]);
+          q[2 * i] = quant_code<Q>(f.x, sc);
+          q[2 * i + 1] = quant_code<Q>(f.y, sc);
+        }
+      }
+      if (kInt4) {
+        // nibble pairs: byte t = (q[2t] & 0xF) | (q[2t+1] << 4)
+        const uint32_t lo = pack4(q[0], q[2], q[4], q[6]) & 0x0F0F0F0Fu;
+        const uint32_t hi = (pack4(q[1], q[3], q[5], q[7]) << 4) & 0xF0F0F0F0u;
+        const uint32_t w = lo | hi;  // byte t holds elements 2t, 2t+1: bytes 0..3 = elements 0..7
+        __stcs(reinterpret_cast<unsigned int*>(codes) + (orow * D) / 8 + c, w);
+      } else {
+        const uint2 w = make_uint2(pack4(q[0], q[1], q[2], q[3]), pack4(q[4], q[5], q[6], q[7]));
+        __stcs(reinterpret_cast<uint2*>(codes) + (orow * D) / 8 + c, w);
+      }
+    }
   }
 }
 
@@ -142,20 +203,26 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const __half* __r
   }
 }
 
+// Persistent grid of the vectorised quantizer: enough 256-thread CTAs for every
+// token once (4 tokens per lane), at most 4 per SM (64 registers per thread).
+int64_t quant_blocks(int64_t rows, int D, int sm_count) {
+  const int64_t warps_needed = (rows * (D / 8) + 31) / 32;
+  const int64_t blocks = (warps_needed + 4 * 8 - 1) / (4 * 8);
+  return std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count) * 4));
+}
+
 template <bool kInt4>
-cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int D, cudaStream_t stream) {
+cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int D, int sm_count, cudaStream_t stream) {
   const __half* x = static_cast<const __half*>(X);
   __half* sc = static_cast<__half*>(scales);
   const bool aligned = (reinterpret_cast<uintptr_t>(X) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(codes) % (kInt4 ? 4 : 8) == 0);
   if (aligned && (D == 64 || D == 128 || D == 256)) {
-    const int lpr = D / 8;
-    const int64_t threads_needed = rows * lpr;
-    const int64_t blocks = (threads_needed + 255) / 256;
+    const unsigned blocks = unsigned(quant_blocks(rows, D, sm_count));
     const QuantPlace pl{rows, rows, 0, nullptr};
-    if (D == 64) quantize_vec_kernel<kInt4, 64><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else if (D == 128) quantize_vec_kernel<kInt4, 128><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<kInt4, 256><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+    if (D == 64) quantize_vec_kernel<kInt4, 64><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else if (D == 128) quantize_vec_kernel<kInt4, 128><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<kInt4, 256><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
   } else {
     const int64_t blocks = (rows * 32 + 255) / 256;
     quantize_generic_kernel<kInt4><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, D);
@@ -299,25 +366,27 @@ cudaError_t launch_rope_append(bool bf16, bool int8_cache, const void* qkv, int6
 }
 
 cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
-                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, cudaStream_t stream) {
+                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, int sm_count,
+                                 cudaStream_t stream) {
   const __half* x = static_cast<const __half*>(X);
   __half* sc = static_cast<__half*>(scales);
   const int64_t rows = groups * T;
   const QuantPlace pl{T, cap, pos_host, pos_dev};
-  const int64_t blocks = (rows * (D / 8) + 255) / 256;
+  const unsigned blocks = unsigned(quant_blocks(rows, D, sm_count));
   if (D == 64) {
-    if (int4) quantize_vec_kernel<true, 64><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<false, 64><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+    if (int4) quantize_vec_kernel<true, 64><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<false, 64><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
   } else {
-    if (int4) quantize_vec_kernel<true, 128><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<false, 128><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, pl);
+    if (int4) quantize_vec_kernel<true, 128><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<false, 128><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,
+cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D, int sm_count,
                             cudaStream_t stream) {
-  return int4 ? launch_q<true>(X, codes, scales, rows, D, stream) : launch_q<false>(X, codes, scales, rows, D, stream);
+  return int4 ? launch_q<true>(X, codes, scales, rows, D, sm_count, stream)
+              : launch_q<false>(X, codes, scales, rows, D, sm_count, stream);
 }
 
 }  // namespace fqkv

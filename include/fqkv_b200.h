@@ -74,12 +74,36 @@ void fqkv_set_wait_timeout_ms(uint32_t ms);
  * such launches are undefined.  Never enable it outside tests. */
 void fqkv_debug_skip_loads(int enable);
 
+/* How split plans of the fp16 kernel merge their splits (process-wide).
+ * FQKV_SPLIT_AUTO (default): the library decides per call.  When a grid is
+ * too small to fill the GPU unsplit (e.g. batch-1 decode), the split CTAs of
+ * each unit form a thread-block cluster that merges through distributed
+ * shared memory in the same launch (no workspace used); otherwise splits
+ * write fp32 partials to the workspace and a second, PDL-chained kernel
+ * merges them.  FQKV_SPLIT_COMBINE: always the partials + combine kernel.
+ * FQKV_SPLIT_CLUSTER: the cluster merge whenever the grid fits on the GPU.
+ * Results agree to fp32 rounding.  For tuning and tests; no counterpart in
+ * the reference (which always launches its partial + combine kernel pair). */
+enum { FQKV_SPLIT_AUTO = 0, FQKV_SPLIT_COMBINE = 1, FQKV_SPLIT_CLUSTER = 2 };
+int fqkv_set_split_mode(int mode);
+
 /* Bytes of optional workspace (split-K partials) that makes the single-block
  * entry points below run with their preferred split count on the current
  * device.  Passing less (or NULL) is valid: the split count is reduced to what
  * fits, down to 1 (no workspace).  Rows are B*Hq (Hq = Hkv = 1 for the
  * non-GQA entry points with B = R). */
 size_t fqkv_decode_workspace_bytes(int kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D);
+
+/* The launch plan a decode call with these sizes and this much workspace gets
+ * on the current device (for tuning, tests and benchmark records):
+ * plan_out[0] = splits per (sequence, KV head) work unit (1 = unsplit),
+ * plan_out[1] = cluster size when the splits merge through a thread-block
+ * cluster (0 = they do not), plan_out[2] = CTAs launched, plan_out[3] = keys
+ * per split, plan_out[4] = kernel family (0 fp16, 1 int8 CUDA-core, 2 int4
+ * CUDA-core, 3 int8 tensor-core GQA, 4 int4 tensor-core).  Rows as in
+ * fqkv_decode_workspace_bytes.  No counterpart in the reference. */
+int fqkv_decode_plan(int kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, size_t workspace_bytes,
+                     int32_t* plan_out);
 
 /* fp16 KV.  q [R,D] f16, K/V [R,N,D] f16 -> o [R,D] f16.  D in {64,128};
  * W in {2,4,8} is accepted for compatibility (the kernel picks its own

@@ -456,3 +456,86 @@ def test_kvcache_tail_of_nan_and_inf_is_ignored(fqkv, B, Hq, Hkv, max_len, n, D)
             out = fqkv.decode_attn_gqa_int8_kvcache(q.cuda(), Kq, Vq, Ks, Vs, seq_len, workspace=ws)
             assert torch.isfinite(out).all()
             _close(out, ref8)
+
+
+# ------------------------------------------------------------------ split merge: cluster (DSMEM) vs combine kernel
+@pytest.fixture
+def split_mode(fqkv):
+    lib = fqkv.native.lib()
+
+    def set_mode(m):
+        fqkv.native.check(lib.fqkv_set_split_mode(m), "set_split_mode")
+    yield set_mode
+    set_mode(fqkv.native.SPLIT_AUTO)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("B,Hq,Hkv,N", [(1, 32, 8, 16384), (1, 32, 8, 65536), (1, 32, 8, 1000), (1, 32, 8, 65),
+                                        (2, 32, 8, 4097), (1, 8, 1, 3000), (1, 64, 4, 2048), (3, 12, 4, 777),
+                                        (1, 32, 2, 9000)])
+def test_split_merge_modes_agree_with_oracle(fqkv, split_mode, B, Hq, Hkv, N, D):
+    """The same split plan merged in one launch through a thread-block cluster's distributed shared
+    memory, and by the partials + combine kernel pair: both against the oracle, and each other."""
+    q, K, V = (_randn(B, Hq, D, seed=160).cuda(), _randn(B, Hkv, N, D, seed=161).cuda(),
+               _randn(B, Hkv, N, D, seed=162).cuda())
+    ref = oatt.decode_attention_gqa(q.cpu().numpy(), K.cpu().numpy(), V.cpu().numpy())
+    outs = {}
+    for mode in (fqkv.native.SPLIT_CLUSTER, fqkv.native.SPLIT_COMBINE, fqkv.native.SPLIT_AUTO):
+        split_mode(mode)
+        outs[mode] = fqkv.decode_attn_gqa(q, K, V, 8)
+        _close(outs[mode], ref)
+    torch.testing.assert_close(outs[fqkv.native.SPLIT_CLUSTER].float(), outs[fqkv.native.SPLIT_COMBINE].float(),
+                               atol=1e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_cluster_merge_sk_fast_and_kvcache(fqkv, split_mode, D):
+    """gqa_sk_fast (batch 1) and a device-length KV cache with a NaN tail, in cluster mode, inside a
+    CUDA graph replayed as the cache grows."""
+    split_mode(fqkv.native.SPLIT_CLUSTER)
+    Hq, Hkv, N = 32, 8, 16384
+    q, K, V = _randn(Hq, D, seed=170), _randn(Hkv, N, D, seed=171), _randn(Hkv, N, D, seed=172)
+    S = 64
+    mp = torch.empty(Hq, S, device="cuda")
+    lp = torch.empty(Hq, S, device="cuda")
+    op = torch.empty(Hq, S, D, device="cuda")
+    out = torch.empty(Hq, D, dtype=torch.float16, device="cuda")
+    fqkv.gqa_sk_fast(q.cuda(), K.cuda(), V.cuda(), mp, lp, op, out, S, 8, 8)
+    _close(out, oatt.decode_attention_gqa(q.numpy()[None], K.numpy()[None], V.numpy()[None])[0])
+
+    B, max_len = 1, 8192
+    qc = _randn(B, Hq, D, seed=173).cuda()
+    Kc = torch.full((B, Hkv, max_len, D), float("nan"), dtype=torch.float16, device="cuda")
+    Vc = torch.full_like(Kc, float("inf"))
+    Kc[:, :, :6000] = _randn(B, Hkv, 6000, D, seed=174).cuda()
+    Vc[:, :, :6000] = _randn(B, Hkv, 6000, D, seed=175).cuda()
+    n_dev = torch.tensor([100], dtype=torch.int32, device="cuda")
+    o = torch.empty(B, Hq, D, dtype=torch.float16, device="cuda")
+    ws = torch.empty(max(fqkv.workspace_bytes("fp16", B, Hq, Hkv, max_len, D), 16), dtype=torch.uint8, device="cuda")
+    fqkv.decode_attn_gqa_kvcache(qc, Kc, Vc, n_dev, out=o, workspace=ws)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fqkv.decode_attn_gqa_kvcache(qc, Kc, Vc, n_dev, out=o, workspace=ws)
+    for n in (100, 64, 1, 4097, 6000, 5999):
+        n_dev.fill_(n)
+        g.replay()
+        torch.cuda.synchronize()
+        ref = oatt.decode_attention_gqa(qc.cpu().numpy(), Kc[:, :, :n].cpu().numpy(), Vc[:, :, :n].cpu().numpy())
+        assert torch.isfinite(o).all()
+        _close(o, ref)
+
+
+def test_batch1_decode_plans_a_cluster_merge(fqkv):
+    """Batch-1 GQA decode (the reference's gqa_sk_fast case) splits and merges inside one launch:
+    the plan reports more than one split and a thread-block cluster of that size, no workspace."""
+    lib = fqkv.native.lib()
+    import ctypes
+    out = (ctypes.c_int32 * 5)()
+    for D in (64, 128):
+        fqkv.native.check(lib.fqkv_decode_plan(0, 1, 32, 8, 16384, D, 0, out), "plan")
+        splits, cluster, grid, chunk, kernel = list(out)
+        assert splits > 1 and cluster == splits and grid == 8 * splits and kernel == 0, list(out)
+        assert fqkv.workspace_bytes("fp16", 1, 32, 8, 16384, D) == 0
+    # the batch-64 bench shape stays unsplit and persistent
+    fqkv.native.check(lib.fqkv_decode_plan(0, 64, 32, 8, 16384, 128, 0, out), "plan")
+    assert out[0] == 1 and out[1] == 0

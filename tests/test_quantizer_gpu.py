@@ -99,3 +99,56 @@ def test_empty_and_large_row_counts(fqkv):
     rc, rs = oq.quantize_int8_per_token(Xs)
     assert np.array_equal(c.view(-1, 128)[i].cpu().numpy(), rc)
     assert _fp16_equal(s.view(-1)[i].cpu().numpy(), rs)
+
+
+def _every_fp16_pair_tokens(dev):
+    """Tokens of D=128 covering every pair (a, x) of fp16 values with a > 0 finite and |x| <= a:
+    element 0 of a token is a (its largest magnitude, so the token's scale is fp16(a / Q)), the
+    other 127 are consecutive fp16 bit patterns 0 .. a of x (the last token of each a padded with a).
+    About 4M tokens (1 GiB); the same tokens negated cover x < 0."""
+    per = 127
+    a_bits = torch.arange(1, 0x7C00, device=dev, dtype=torch.int64)          # positive finite fp16
+    ntok = (a_bits + per) // per                                             # ceil((a_bits + 1) / 127)
+    tok_a = torch.repeat_interleave(a_bits, ntok)
+    first = torch.cumsum(ntok, 0) - ntok
+    tok_j = torch.arange(tok_a.numel(), device=dev) - torch.repeat_interleave(first, ntok)
+    xp = torch.minimum(tok_j[:, None] * per + torch.arange(per, device=dev)[None, :], tok_a[:, None])
+    return torch.cat([tok_a[:, None], xp], 1).to(torch.int16).view(torch.float16).contiguous()
+
+
+def _reference_expression(X: torch.Tensor, Q: int):
+    """The reference quantizer (notebook lines 236-238 / 292-299) as torch evaluates it on CUDA tensors;
+    NaN codes (0 / 0 in a token whose scale underflowed) -> 0 as .to(int8) gives on the CPU."""
+    a = X.abs().amax(-1, keepdim=True)
+    s = (a / Q).clamp(min=1e-8)
+    r = torch.clamp(torch.round(X / s), -Q, Q)
+    return torch.where(torch.isnan(r), torch.zeros_like(r), r).to(torch.int8), s.squeeze(-1)
+
+
+def test_every_fp16_pair_bit_exact(fqkv):
+    """Codes and scales bit-exact with the reference expression for every (amax, x) fp16 pair, both
+    signs, int8 and int4: the kernel's division (FMA-corrected reciprocal for normal scales, IEEE
+    division otherwise) must round exactly as the IEEE quotient everywhere."""
+    dev = "cuda"
+    Xp = _every_fp16_pair_tokens(dev)
+    for X in (Xp, -Xp):
+        c8, s8 = fqkv.qpt(X)
+        r8, rs = _reference_expression(X, 127)
+        assert torch.equal(s8.view(torch.int16), rs.view(torch.int16))
+        bad = (c8 != r8).sum().item()
+        assert bad == 0, f"{bad} int8 codes differ"
+        p4, s4 = fqkv.quant_int4_per_token(X)
+        r4, rs4 = _reference_expression(X, 7)
+        assert torch.equal(s4.view(torch.int16), rs4.view(torch.int16))
+        lo = (p4 & 0xF).to(torch.int8)
+        hi = (p4 >> 4).to(torch.int8)
+        unpacked = torch.stack([torch.where(lo >= 8, lo - 16, lo), torch.where(hi >= 8, hi - 16, hi)], -1).flatten(-2)
+        bad = (unpacked != r4).sum().item()
+        assert bad == 0, f"{bad} int4 codes differ"
+        del c8, r8, p4, r4, lo, hi, unpacked
+    # and a slice against the numpy restatement (IEEE fp32 division on the CPU)
+    idx = torch.randint(0, Xp.shape[0], (20000,), device=dev, generator=torch.Generator(device=dev).manual_seed(9))
+    Xs = Xp[idx]
+    c8, s8 = fqkv.qpt(Xs)
+    rc, rsc = oq.quantize_int8_per_token(Xs.cpu().numpy())
+    assert np.array_equal(c8.cpu().numpy(), rc) and _fp16_equal(s8.cpu().numpy(), rsc)
