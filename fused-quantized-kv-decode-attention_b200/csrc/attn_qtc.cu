@@ -68,9 +68,9 @@ struct QtcCfg {
   // issue-bound (consumers almost never wait for a tile), so the GQA variant
   // runs 4 CTAs (20 warps) with a 2-stage ring (332.6 -> 323.7 us at B=64,
   // N=16K, D=128); the one-head int4 variant keeps 3 CTAs and 4 stages.
-  // The one-head int4 variant at D = 64 moves 4 KB tiles; 8 stages keep as many bytes in flight.
+  // The one-head int4 variant at D = 64 moves 4 KB tiles: 7 stages (3 CTAs still fit in 228 KB).
   static constexpr int kCtas = G1 ? 3 : 4;
-  static constexpr int kStages = G1 ? (D == 64 ? 8 : 4) : 2;
+  static constexpr int kStages = G1 ? (D == 64 ? 7 : 4) : 2;
   static constexpr int NSEG = RB / 16;                         // one head: 16-byte V row segments
   static constexpr int MH = G1 ? 1 : 4;                        // heads merged per epilogue pass
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
