@@ -111,20 +111,28 @@ def path_dtype(kind: str) -> str:
             "quant4": "f16 -> packed i4 codes + f16 scales"}.get(kind, "f16 KV, f32 accumulate")
 
 
-def dominant_kernel(w: dict) -> str:
-    """The library kernel that takes (nearly) all of a call's device time for workload `w`."""
+def plan_record(plan):
+    """The library's launch plan (fqkv_decode_plan) as a JSON object."""
+    if plan is None:
+        return None
+    kernels = ["fp16 (decode_f16_kernel)", "int8 CUDA-core (decode_quant_kernel)", "int4 CUDA-core (decode_quant_kernel)",
+               "int8 tensor-core GQA (decode_qtc_kernel)", "int4 tensor-core (decode_qtc_kernel)"]
+    merge = ("none" if plan[0] == 1 else "thread-block cluster / DSMEM, same launch" if plan[1]
+             else "fp32 partials + PDL-chained combine kernel")
+    return {"splits": plan[0], "cluster": plan[1], "ctas": plan[2], "keys_per_split": plan[3],
+            "kernel": kernels[plan[4]], "split_merge": merge}
+
+
+def dominant_kernel(w: dict, plan) -> str:
+    """The library kernel(s) that take (nearly) all of a call's device time for workload `w` under `plan`."""
     k, D = w["kind"], w["D"]
-    if k in ("gqa", "fp16"):
-        return f"decode_f16_kernel<{D}>"
-    if k == "sk":
-        return f"decode_f16_kernel<{D}> + combine_kernel (PDL-chained)"
-    if k == "gqa_int8":
-        return f"decode_qtc_kernel<{D},false,false>"
-    if k == "int8":
-        return f"decode_quant_kernel<false,{D}>"
-    if k == "int4":
-        return "decode_qtc_kernel<128,true,true>" if D == 128 else f"decode_quant_kernel<true,{D}>"
-    return "quantize_vec_kernel<int4>" if k == "quant4" else "quantize_vec_kernel<int8>"
+    if k in ("quant8", "quant4"):
+        return "quantize_vec_kernel<int4>" if k == "quant4" else "quantize_vec_kernel<int8>"
+    names = {0: f"decode_f16_kernel<{D},{'1' if plan[1] else '0'}>", 1: f"decode_quant_kernel<false,{D}>",
+             2: f"decode_quant_kernel<true,{D}>", 3: f"decode_qtc_kernel<{D},false,false>",
+             4: f"decode_qtc_kernel<{D},true,true>"}
+    name = names[plan[4]]
+    return name + (" + combine_kernel (PDL-chained)" if plan[0] > 1 and not plan[1] else "")
 
 
 def measured_peak() -> tuple[float, str]:
@@ -308,37 +316,71 @@ class Case:
             self.nb = nb
             self.kernels_per_call = 1 + (1 if nb > 0 else 0)
         torch.cuda.synchronize(dev)
+        self.plan = self._plan()
+        if self.plan is not None:   # one kernel, plus the combine when splits merge through global partials
+            self.kernels_per_call = 1 + (1 if self.plan[0] > 1 and self.plan[1] == 0 else 0)
+        self._bind()
 
-    def launch(self) -> None:
-        """One decode call through the C ABI, no allocation, on the current stream."""
-        w, lib, s = self.w, self.lib, torch.cuda.current_stream(self.dev).cuda_stream
-        k = w["kind"]
+    def _plan(self):
+        """The library's launch plan for this workload ([splits, cluster, CTAs, keys per split, kernel])."""
+        import ctypes
+        w, k = self.w, self.w["kind"]
+        if k in ("quant8", "quant4"):
+            return None
+        out = (ctypes.c_int32 * 5)()
+        if k in ("gqa", "gqa_int8", "sk"):
+            fmt = 1 if k == "gqa_int8" else 0
+            args = (1 if k == "sk" else w["B"], w["Hq"], w["Hkv"], w["N"], w["D"])
+        else:
+            fmt = {"fp16": 0, "int8": 1, "int4": 2}[k]
+            args = (w["R"], 1, 1, w["N"], w["D"])
+        rc = self.lib.fqkv_decode_plan(fmt, *args, getattr(self, "nb", 0) if k != "sk" else 1 << 40, out)
+        if rc != 0:
+            raise RuntimeError(f"plan failed: {self.pkg.native.last_error()}")
+        return list(out)
+
+    def _bind(self) -> None:
+        """The C-ABI function and its argument list (all but the stream) for each call of the rotation,
+        converted to ctypes values once, so a launch costs one foreign call."""
+        import ctypes
+        w, lib, k = self.w, self.lib, self.w["kind"]
+        P, I = ctypes.c_void_p, ctypes.c_int64
+        ws = (P(self.ws.data_ptr()) if self.nb else P(None), ctypes.c_size_t(self.nb)) if hasattr(self, "nb") else ()
         if k == "gqa":
-            rc = lib.fqkv_decode_attn_gqa(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(), self.o.data_ptr(),
-                                          w["B"], w["Hq"], w["Hkv"], w["N"], w["D"], 8,
-                                          self.ws.data_ptr() if self.nb else None, self.nb, s)
+            calls = [(lib.fqkv_decode_attn_gqa, (P(self.q.data_ptr()), P(self.K.data_ptr()), P(self.V.data_ptr()),
+                                                 P(self.o.data_ptr()), I(w["B"]), I(w["Hq"]), I(w["Hkv"]), I(w["N"]),
+                                                 I(w["D"]), I(8)) + ws)]
         elif k == "gqa_int8":
-            rc = lib.fqkv_decode_attn_gqa_int8(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(),
-                                               self.Ks.data_ptr(), self.Vs.data_ptr(), self.o.data_ptr(),
-                                               w["B"], w["Hq"], w["Hkv"], w["N"], w["D"],
-                                               self.ws.data_ptr() if self.nb else None, self.nb, s)
+            calls = [(lib.fqkv_decode_attn_gqa_int8, (P(self.q.data_ptr()), P(self.K.data_ptr()), P(self.V.data_ptr()),
+                                                      P(self.Ks.data_ptr()), P(self.Vs.data_ptr()), P(self.o.data_ptr()),
+                                                      I(w["B"]), I(w["Hq"]), I(w["Hkv"]), I(w["N"]), I(w["D"])) + ws)]
         elif k == "sk":
-            q, K, V = self.sets[self.i % len(self.sets)]
-            self.i += 1
-            rc = lib.fqkv_gqa_sk_fast(q.data_ptr(), K.data_ptr(), V.data_ptr(), self.mp.data_ptr(),
-                                      self.lp.data_ptr(), self.op.data_ptr(), self.o.data_ptr(),
-                                      w["Hq"], w["Hkv"], w["N"], w["D"], w["S"], 8, 8, s)
+            calls = [(lib.fqkv_gqa_sk_fast, (P(q.data_ptr()), P(K.data_ptr()), P(V.data_ptr()), P(self.mp.data_ptr()),
+                                             P(self.lp.data_ptr()), P(self.op.data_ptr()), P(self.o.data_ptr()),
+                                             I(w["Hq"]), I(w["Hkv"]), I(w["N"]), I(w["D"]), I(w["S"]), I(8), I(8)))
+                     for q, K, V in self.sets]
         elif k in ("quant8", "quant4"):
             fn = lib.fqkv_quantize_int8_per_token if k == "quant8" else lib.fqkv_quantize_int4_per_token
-            rc = fn(self.X.data_ptr(), self.codes.data_ptr(), self.scales.data_ptr(), self.X.shape[0], w["D"], s)
+            calls = [(fn, (P(self.X.data_ptr()), P(self.codes.data_ptr()), P(self.scales.data_ptr()),
+                           I(self.X.shape[0]), I(w["D"])))]
         elif k == "fp16":
-            rc = lib.fqkv_decode_attn_fp16_mw(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(),
-                                              self.o.data_ptr(), w["R"], w["N"], w["D"], 8,
-                                              self.ws.data_ptr() if self.nb else None, self.nb, s)
+            calls = [(lib.fqkv_decode_attn_fp16_mw, (P(self.q.data_ptr()), P(self.K.data_ptr()), P(self.V.data_ptr()),
+                                                     P(self.o.data_ptr()), I(w["R"]), I(w["N"]), I(w["D"]), I(8)) + ws)]
         else:
             fn = lib.fqkv_decode_attn_int8_mw if k == "int8" else lib.fqkv_decode_attn_int4
-            rc = fn(self.q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(), self.Ks.data_ptr(), self.Vs.data_ptr(),
-                    self.o.data_ptr(), w["R"], w["N"], w["D"], 8, self.ws.data_ptr() if self.nb else None, self.nb, s)
+            calls = [(fn, (P(self.q.data_ptr()), P(self.K.data_ptr()), P(self.V.data_ptr()), P(self.Ks.data_ptr()),
+                           P(self.Vs.data_ptr()), P(self.o.data_ptr()), I(w["R"]), I(w["N"]), I(w["D"]), I(8)) + ws)]
+        self._calls = calls
+        self.i = 0
+
+    def launch(self, stream: int | None = None) -> None:
+        """One decode call through the C ABI, no allocation, on `stream` (a cudaStream_t handle; default:
+        torch's current stream).  The arguments are bound once (see _bind)."""
+        if stream is None:
+            stream = torch.cuda.current_stream(self.dev).cuda_stream
+        fn, args = self._calls[self.i % len(self._calls)]
+        self.i += 1
+        rc = fn(*args, stream)
         if rc != 0:
             raise RuntimeError(f"launch failed: {self.pkg.native.last_error()}")
 
@@ -352,13 +394,14 @@ def timing_methods(pkg, case: Case, w: dict, dev: torch.device, ms_call: float) 
     ev = lambda: torch.cuda.Event(enable_timing=True)
 
     def loop_us(c: Case, n: int) -> float:
+        s = torch.cuda.current_stream(dev).cuda_stream   # the caller's stream, resolved once
         for _ in range(3):
-            c.launch()
+            c.launch(s)
         torch.cuda.synchronize(dev)
         a, b = ev(), ev()
         a.record()
         for _ in range(n):
-            c.launch()
+            c.launch(s)
         b.record()
         torch.cuda.synchronize(dev)
         return a.elapsed_time(b) * 1e3 / n
@@ -655,32 +698,21 @@ def run_llama_reference(args, w, rank: int) -> int:
     return 0
 
 
-def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
-    """Config 5 tensor-parallel over `world` GPUs by KV head (NCCL all-gather of the attention
-    outputs every layer, inside the captured decode step); same model and workload as run_llama.
-    Total work is fixed as the GPU count grows ("scaling": "strong")."""
-    import torch.distributed as dist
-    from transformers import LlamaForCausalLM
-
-    pkg = importlib.import_module(PKG)
+def tp_decode_measure(pkg, dist, model, ids, B: int, P: int, T: int, kv: str, world: int, rank: int,
+                      local_rank: int, reps: int, fused: bool = False) -> dict | None:
+    """One tensor-parallel decode configuration on every rank (collective): decode tok/s (CUDA events,
+    max over ranks), tokens identical on all ranks, and -- on rank 0 -- agreement with the 1-GPU decoder
+    on the same replicated weights and with teacher-forced SDPA logits (greedy agreement, max logit
+    difference of the TP decoder's own logits).  Returns the record on rank 0, None elsewhere."""
     dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    B, P, T = w["B"], w["prompt"], w["gen"]
-    torch.manual_seed(0)
-    with torch.device(dev):
-        model = LlamaForCausalLM(llama_1b_config()).to(torch.bfloat16).eval()
-    for prm in model.parameters():          # identical replicated weights on every rank
-        dist.broadcast(prm.data, src=0)
-    ids = torch.randint(0, model.config.vocab_size, (B, P), device=dev)
-    dist.broadcast(ids, src=0)
+    GD = pkg.hf_integration.GraphDecoder
     ev = lambda: torch.cuda.Event(enable_timing=True)
-    dec = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, kv_dtype=args.kv,
-                                          tp_group=dist.group.WORLD, tp_fused=args.tp_gather == "fused")
+    ids = ids[:B].contiguous()
+    dec = GD(model, batch=B, max_len=P + T, kv_dtype=kv, tp_group=dist.group.WORLD, tp_fused=fused)
     dec.prefill(ids)
     dec.capture()
     best_pre, best_dec = 1e30, 1e30
-    for _ in range(max(1, args.warmup // 3) + 2):
+    for _ in range(reps):
         dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(dev)
         e0, e1, e2 = ev(), ev(), ev()
@@ -694,17 +726,24 @@ def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         best_pre, best_dec = min(best_pre, float(t[0])), min(best_dec, float(t[1]))
     ours = dec.out_tokens[:, P:P + T].clone()
-    same = torch.tensor([1.0], device=dev)
     ref_tok = ours.clone()
     dist.broadcast(ref_tok, src=0)
-    same.fill_(float(torch.equal(ref_tok, ours)))
+    same = torch.tensor([float(torch.equal(ref_tok, ours))], device=dev)
     dist.all_reduce(same, op=dist.ReduceOp.MIN)
     dec.release()
-    line = None
+    # the TP decoder's own logits for the first sequences (eager steps, collective on every rank)
+    nb = min(B, 4)
+    chk = GD(model, batch=B, max_len=P + T, kv_dtype=kv, tp_group=dist.group.WORLD, keep_logits=True)
+    chk.prefill(ids)
+    tp_logits = [chk.logits[:nb].clone()]
+    for _ in range(T - 1):
+        chk.step()
+        tp_logits.append(chk.logits[:nb].clone())
+    tp_logits = torch.stack(tp_logits, dim=1)
+    chk.release()
+    rec = None
     if rank == 0:
-        nb = min(B, 4)
-        # the 1-GPU decoder on the same replicated weights, and SDPA teacher-forced logits
-        one = pkg.hf_integration.GraphDecoder(model, batch=B, max_len=P + T, kv_dtype=args.kv)
+        one = GD(model, batch=B, max_len=P + T, kv_dtype=kv)
         one.prefill(ids)
         one.capture()
         one.generate(T - 1)
@@ -713,31 +752,114 @@ def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
         seq = torch.cat([ids[:nb], ours[:nb]], dim=1)
         with torch.no_grad():
             ref_logits = model(seq).logits[:, P - 1:P - 1 + T].float()
-        agree = (ref_logits.argmax(-1) == ours[:nb]).float().mean().item()
-        decode_tps = B * (T - 1) / (best_dec / 1e3)
-        e2e_tps = B * T / ((best_pre + best_dec) / 1e3)
-        line = {"metric": METRIC, "workload": "llama", "value": round(decode_tps, 2), "unit": "tok/s",
+        rec = {"batch": B, "kv_cache": kv, "gather": "fused NVLink stores + bounded wait" if fused
+               else "NCCL all_gather_into_tensor",
+               "decode_tok_s": round(B * (T - 1) / (best_dec / 1e3), 2),
+               "e2e_generate_tok_s": round(B * T / ((best_pre + best_dec) / 1e3), 2),
+               "decode_ms_per_step": round(best_dec / (T - 1), 4), "prefill_ms": round(best_pre, 3),
+               "tokens_identical_on_all_ranks": bool(same.item() == 1.0),
+               "token_match_vs_1gpu_decoder": round((one_tok == ours).float().mean().item(), 4),
+               "greedy_agreement_vs_sdpa_teacher_forced": round(
+                   (ref_logits.argmax(-1) == ours[:nb]).float().mean().item(), 4),
+               "max_logit_diff_vs_sdpa": round((tp_logits - ref_logits).abs().max().item(), 5)}
+    dist.barrier(device_ids=[local_rank])
+    return rec
+
+
+def tp_model(dist, dev, P: int):
+    """The config-5 model (random N(0, 0.02) bf16 weights, seed 0) and prompt ids, identical on every rank."""
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(llama_1b_config()).to(torch.bfloat16).eval()
+    for prm in model.parameters():          # identical replicated weights on every rank
+        dist.broadcast(prm.data, src=0)
+    ids = torch.randint(0, model.config.vocab_size, (64, P), device=dev)
+    dist.broadcast(ids, src=0)
+    return model, ids
+
+
+def run_llama_tp(args, w, world: int, rank: int, local_rank: int) -> int:
+    """Config 5 tensor-parallel over `world` GPUs by KV head (NCCL all-gather of the attention
+    outputs every layer, inside the captured decode step); same model and workload as run_llama.
+    Total work is fixed as the GPU count grows ("scaling": "strong")."""
+    import torch.distributed as dist
+
+    pkg = importlib.import_module(PKG)
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B, P, T = w["B"], w["prompt"], w["gen"]
+    model, ids = tp_model(dist, dev, P)
+    rec = tp_decode_measure(pkg, dist, model, ids, B, P, T, args.kv, world, rank, local_rank,
+                            max(1, args.warmup // 3) + 2, fused=args.tp_gather == "fused")
+    dist.destroy_process_group()
+    if rank == 0:
+        line = {"metric": METRIC, "workload": "llama", "value": rec["decode_tok_s"], "unit": "tok/s",
                 "n_gpus": world, "higher_is_better": True, "scaling": "strong",
                 "dtype": f"bf16 weights, {args.kv} KV", "data": "synthetic",
                 "config": {"workload": w["desc"], "global_batch": B, "prompt": P, "gen": T, "head_dim": 64,
                            "parallelism": f"tp{world} by KV head (q/k/v rows, KV cache, attention sharded; "
-                                          + ("NCCL all_gather_into_tensor" if args.tp_gather == "nccl" else
-                                             "attention kernel stores its output to every rank over NVLink + "
-                                             "bounded arrival wait")
-                                          + " per layer; o_proj, MLP, LM head replicated)",
+                                          + rec["gather"] + " per layer; o_proj, MLP, LM head replicated)",
                            "kv_cache": f"{args.kv}, static, graph-captured decode step (collectives in the graph)"},
-                "decode_tok_s": round(decode_tps, 2), "e2e_generate_tok_s": round(e2e_tps, 2),
-                "prefill_ms": round(best_pre, 3), "decode_ms_per_step": round(best_dec / (T - 1), 4),
-                "timing": "CUDA events, max over ranks",
-                "tokens_identical_on_all_ranks": bool(same.item() == 1.0),
-                "token_match_vs_1gpu_decoder": round((one_tok == ours).float().mean().item(), 4),
-                "greedy_agreement_vs_sdpa_teacher_forced": round(agree, 4),
-                "gpu_launches_note": "per step: one CUDA graph replay", "impl": "ours"}
-    dist.barrier(device_ids=[local_rank])
-    dist.destroy_process_group()
-    if line is not None:
+                "timing": "CUDA events, max over ranks", "gpu_launches_note": "per step: one CUDA graph replay",
+                "impl": "ours", **{k: v for k, v in rec.items() if k not in ("batch", "kv_cache", "gather")}}
         print(json.dumps(line), flush=True)
     return 0
+
+
+def run_multi_gpu_extras(pkg, dist, world: int, rank: int, local_rank: int, dev: torch.device,
+                         gpu_index: int) -> dict | None:
+    """Extra records of a multi-GPU run (every rank calls this; rank 0 gets the result):
+
+    * ``cfg4_strong_kv_heads``: ONE batch-64 config-4 problem (Hq=32, Hkv=8, N=16384, D=128) with its KV
+      heads sharded over the GPUs -- 8/world KV heads and their 32/world query heads per GPU, no
+      collective on the data path; aggregate GB/s = the whole problem's bytes / the slowest GPU's time.
+      Each rank checks one sequence of its shard against the float64 oracle.
+    * ``cfg5_tensor_parallel``: the config-5 Llama-1B-architecture greedy decode tensor-parallel over
+      all GPUs by KV head, batch 1 and 64, fp16 and int8 KV caches (tp_decode_measure)."""
+    from oracle import attention as oatt
+
+    out = {}
+    full = dict(WORKLOADS["gqa"])
+    if full["Hkv"] % world == 0:
+        w = dict(full, Hq=full["Hq"] // world, Hkv=full["Hkv"] // world)
+        case = Case(pkg, w, dev, seed=77 + rank)
+        dist.barrier(device_ids=[local_rank])
+        r = time_case(case, dev, gpu_index, min_seconds=0.3)
+        ref = oatt.decode_attention_gqa(case.q[:1].cpu().numpy(), case.K[:1].cpu().numpy(), case.V[:1].cpu().numpy())
+        case.launch()
+        torch.cuda.synchronize(dev)
+        err = float(abs(case.o[:1].float().cpu().numpy() - ref).max())
+        t = torch.tensor([r["us"], err], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del case
+        torch.cuda.empty_cache()
+        us, err = float(t[0]), float(t[1])
+        total = algorithmic_bytes(full)
+        out["cfg4_strong_kv_heads"] = {
+            "workload": full["desc"] + f", KV heads sharded {world} ways ({full['Hkv'] // world} KV / "
+                                       f"{full['Hq'] // world} query heads per GPU)",
+            "bytes_per_call": total, "us_per_call_max_over_ranks": round(us, 3),
+            "aggregate_GB_s": round(total / (us * 1e-6) / 1e9, 1),
+            "per_gpu_GB_s": round(total / world / (us * 1e-6) / 1e9, 1),
+            "max_abs_err_vs_float64_oracle": err, "scaling": "strong",
+            "timing": "CUDA-graph replays per rank, CUDA events, max over ranks"}
+    if 8 % world == 0:
+        P, T = 512, 128
+        model, ids = tp_model(dist, dev, P)
+        recs = []
+        for B, kv in ((1, "fp16"), (64, "fp16"), (1, "int8"), (64, "int8")):
+            rec = tp_decode_measure(pkg, dist, model, ids, B, P, T, kv, world, rank, local_rank, reps=3)
+            if rank == 0:
+                recs.append(rec)
+        del model
+        torch.cuda.empty_cache()
+        out["cfg5_tensor_parallel"] = {
+            "workload": WORKLOADS["llama"]["desc"] + f", tensor-parallel over {world} GPUs by KV head "
+                                                     "(o_proj, MLP, LM head replicated)",
+            "configs": recs, "scaling": "strong", "timing": "CUDA events, max over ranks"}
+    return out if rank == 0 else None
 
 
 # ---------------------------------------------------------------------------- every config in one run
@@ -772,7 +894,7 @@ def time_case(case: Case, dev: torch.device, gpu_index: int, min_seconds: float 
     torch.cuda.synchronize(dev)
     clocks = sampler.stop()
     del graph
-    return {"us": e0.elapsed_time(e1) * 1e3 / (reps * n), "calls": reps * n, "clocks": clocks}
+    return {"us": e0.elapsed_time(e1) * 1e3 / (reps * n), "calls": reps * n, "clocks": clocks, "plan": case.plan}
 
 
 def run_config_sweep(pkg, dev: torch.device, gpu_index: int, peak: float) -> dict:
@@ -794,15 +916,16 @@ def run_config_sweep(pkg, dev: torch.device, gpu_index: int, peak: float) -> dic
             torch.cuda.empty_cache()
         nbytes = algorithmic_bytes(w)
         gbs = nbytes / (r["us"] * 1e-6) / 1e9
+        plan = r["plan"]
         c = r["clocks"]
         out.append({"name": name, "workload": w["desc"] + "".join(f" [{k}={v}]" for k, v in over.items()),
-                    "kernel": dominant_kernel(w), "bytes_per_call": nbytes, "us_per_call": round(r["us"], 3),
+                    "kernel": dominant_kernel(w, plan), "bytes_per_call": nbytes, "us_per_call": round(r["us"], 3),
                     "GB_s": round(gbs, 1), "pct_of_8TBps": round(100 * gbs / NOMINAL_HBM_GBS, 2),
                     "frac_of_measured_peak": round(gbs / peak, 4), "calls_timed": r["calls"],
                     "l2": "8 rotated KV sets > 4x L2" if w["kind"] == "sk" else "inputs > L2",
                     "clocks": {"sm_mhz": c.get("sm_mhz"), "sm_max_mhz": c.get("sm_max_mhz"),
                                "reasons": c.get("reasons"), "samples": c.get("samples")},
-                    "setup_plus_timing_s": round(time.time() - t0, 1)})
+                    "plan": plan_record(plan), "setup_plus_timing_s": round(time.time() - t0, 1)})
     return {"entries": out, "wall_s": round(time.time() - t_start, 1),
             "timing": "CUDA-graph replays of back-to-back C-ABI calls with device-resident inputs, CUDA events",
             "data": "synthetic N(0,1) fp16; quantized KV: the library's quantizer on the first 1 GiB of codes, "
@@ -834,7 +957,8 @@ def main() -> int:
     ap.add_argument("--no-extra-timing", action="store_true",
                     help="skip the eager-loop, single-call and launch-floor timings (1-GPU runs only)")
     ap.add_argument("--no-configs", action="store_true",
-                    help="skip the per-config sweep (the 'configs' key) of the default 1-GPU run")
+                    help="skip the per-config sweep of the default run (1 GPU: the 'configs' key; several "
+                         "GPUs: the 'multi_gpu' key -- KV-head-sharded config 4 and tensor-parallel config 5)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -910,6 +1034,7 @@ def main() -> int:
     torch.cuda.set_device(dev)
     case = Case(pkg, w, dev, seed=1234 + rank)
     kernels_per_call = case.kernels_per_call
+    main_plan = case.plan
 
     def barrier():
         if dist is not None:
@@ -973,12 +1098,14 @@ def main() -> int:
         e2e = {"value": round(per_rank_bytes * world / (e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                "ms_per_step": round(e_ms, 3), "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]}
 
-    sweep = None
-    if world == 1 and not args.no_configs and args.workload == "gqa" and not (args.batch or args.seq_len
-                                                                               or args.head_dim):
+    sweep = multi = None
+    if not args.no_configs and args.workload == "gqa" and not (args.batch or args.seq_len or args.head_dim):
         del case
         torch.cuda.empty_cache()
-        sweep = run_config_sweep(pkg, dev, gpu_index, measured_peak()[0])
+        if world == 1:
+            sweep = run_config_sweep(pkg, dev, gpu_index, measured_peak()[0])
+        else:
+            multi = run_multi_gpu_extras(pkg, dist, world, rank, local_rank, dev, gpu_index)
 
     if dist is not None:
         barrier()
@@ -1005,11 +1132,14 @@ def main() -> int:
             "vs_baseline": None, "dtype": path_dtype(w["kind"]), "data": "synthetic", "config": config,
             "us_per_call": round(ms_step * 1e3, 3), "pct_of_8TBps": round(100 * achieved / NOMINAL_HBM_GBS, 2),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps * kernels_per_call, "clocks": clocks, "impl": "ours"}
+            "gpu_launches": args.steps * kernels_per_call, "clocks": clocks, "impl": "ours",
+            "plan": plan_record(main_plan)}
     if methods is not None:
         line["timing_methods"] = methods
     if sweep is not None:
         line["configs"] = sweep
+    if multi is not None:
+        line["multi_gpu"] = multi
     print(json.dumps(line), flush=True)
     return 0
 

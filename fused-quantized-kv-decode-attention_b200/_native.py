@@ -49,6 +49,7 @@ SIGNATURES = {
     "fqkv_debug_skip_loads": (None, [_INT]),
     "fqkv_set_split_mode": (_INT, [_INT]),
     "fqkv_decode_workspace_bytes": (_SZ, [_INT, _I64, _I64, _I64, _I64, _I64]),
+    "fqkv_device_info": (_INT, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
     "fqkv_decode_plan": (_INT, [_INT, _I64, _I64, _I64, _I64, _I64, _SZ, ctypes.POINTER(ctypes.c_int32)]),
     "fqkv_decode_attn_fp16_mw": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
     "fqkv_decode_attn_int8_mw": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P]),

@@ -47,8 +47,7 @@
 namespace fqkv {
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kGroupWarps = 4;     // consumer warps of one group: 16 keys of every tile each
 constexpr int kTK = 64;            // keys per tile
 constexpr int kHalfBytes = kTK * 128;
 constexpr int kMergeHeads = 4;     // heads merged per epilogue pass
@@ -66,8 +65,13 @@ struct F16Cfg {
   static constexpr int kStages = kCl ? (192 * 1024) / kStageBytes : 3;
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
   static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
-  static constexpr size_t kMergeBytes =
-      size_t(kConsumerWarps) * (2 * 8 + kMergeHeads * D) * sizeof(float);
+  // Cluster mode runs one CTA per SM, so it gets two consumer groups taking
+  // alternate tiles (two warps per scheduler to hide the MMA / ldmatrix /
+  // exp latency chains); persistent mode has 2-4 CTAs per SM instead.
+  static constexpr int kGroups = kCl ? 2 : 1;
+  static constexpr int kCW = kGroupWarps * kGroups;  // consumer warps
+  static constexpr int kThr = 32 * (kCW + 1);        // + the producer warp
+  static constexpr size_t kMergeBytes = size_t(kCW) * (2 * 8 + kMergeHeads * D) * sizeof(float);
   // cluster mode: this CTA's merged (m, l) of up to 8 heads and o [8][D], read by the cluster
   static constexpr size_t kClusterBytes = kCl ? (2 * 8 + 8 * D) * sizeof(float) : 0;
   static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kRingBytes + kBarBytes + kMergeBytes + kClusterBytes;
@@ -106,7 +110,7 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
 }
 
 template <int D, bool kCl>
-__global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_constant__ DecodeLaunch a) {
+__global__ void __launch_bounds__(F16Cfg<D, kCl>::kThr) decode_f16_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = F16Cfg<D, kCl>;
   extern __shared__ uint8_t smem_raw[];
   // aligned by an offset from the shared array, so that every access through `smem` stays a
@@ -115,9 +119,9 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kRingBytes);
   uint64_t* empty = full + C::kStages;
   float* sm_m = reinterpret_cast<float*>(empty + C::kStages);  // [warps][8]
-  float* sm_l = sm_m + kConsumerWarps * 8;                     // [warps][8]
-  float* sm_o = sm_l + kConsumerWarps * 8;                     // [warps][kMergeHeads][D]
-  float* cl_m = sm_o + kConsumerWarps * kMergeHeads * D;       // cluster mode: [8]
+  float* sm_l = sm_m + C::kCW * 8;                             // [warps][8]
+  float* sm_o = sm_l + C::kCW * 8;                             // [warps][kMergeHeads][D]
+  float* cl_m = sm_o + C::kCW * kMergeHeads * D;               // cluster mode: [8]
   float* cl_l = cl_m + 8;                                      // [8]
   float* cl_o = cl_l + 8;                                      // [8][D]
   __shared__ int abort_flag;
@@ -129,12 +133,12 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], kGroupWarps);  // the 4 warps of the group that consumes the stage
     }
     abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kConsumerWarps && lane == 0) {
+  if (warp == C::kCW && lane == 0) {
     prefetch_tensormap(&a.tmK);
     prefetch_tensormap(&a.tmV);
     // warm L2 with this CTA's first tiles while the previous kernel finishes
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
 
   // ------------------------------------------------------------ producer
-  if (warp == kConsumerWarps) {
+  if (warp == C::kCW) {
     if (lane == 0 && !a.debug_skip_loads) {
       int it = 0;
       bool ok = true;
@@ -210,7 +214,8 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
   const int t = lane & 3;
   const int mi = lane >> 3;  // ldmatrix matrix index supplied by this lane
   const int rr = lane & 7;   // ldmatrix row within that matrix
-  const int r0 = warp * 16;  // this warp's 16 keys within a tile
+  const int grp = warp / kGroupWarps;         // consumer group: takes tiles it with it % kGroups == grp
+  const int r0 = (warp % kGroupWarps) * 16;   // this warp's 16 keys within a tile
   const uint32_t ring = smem_u32(smem);
   const float csc = a.sm_scale_log2;
   bool alive = true;
@@ -244,6 +249,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
     float m_run = -INFINITY, l_run = 0.f;
 
     for (int k0 = lo; k0 < hi; k0 += kTK, ++it) {
+      if (C::kGroups > 1 && it % C::kGroups != grp) continue;
       const int st = it % C::kStages;
       if (alive) {
         // warp-uniform decision: every lane waits, the warp proceeds only if all did
@@ -340,17 +346,17 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
           *reinterpret_cast<float2*>(&sm_o[(warp * kMergeHeads + gl) * D + 8 * j + 2 * t]) = v2;
         }
       }
-      named_bar_sync(1, 32 * kConsumerWarps);
+      named_bar_sync(1, 32 * C::kCW);
       const int nh = min(kMergeHeads, gvalid - hp);
-      for (int idx = ct; idx < nh * D; idx += 32 * kConsumerWarps) {
+      for (int idx = ct; idx < nh * D; idx += 32 * C::kCW) {
         const int gl2 = idx / D, d = idx - gl2 * D;
         const int gg = hp + gl2;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_m[w * 8 + gg]);
+        for (int w = 0; w < C::kCW; ++w) M = fmaxf(M, sm_m[w * 8 + gg]);
         float L = 0.f, O = 0.f;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
+        for (int w = 0; w < C::kCW; ++w) {
           const float mw = sm_m[w * 8 + gg];
           const float wt = (mw == -INFINITY) ? 0.f : ex2(mw - M);
           L += wt * sm_l[w * 8 + gg];
@@ -374,7 +380,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
           a.part_o[slot * D + d] = O;
         }
       }
-      named_bar_sync(1, 32 * kConsumerWarps);
+      named_bar_sync(1, 32 * C::kCW);
     }
     if constexpr (kCl) {
       // ---- cluster merge: every CTA's (m, l, o) is in its shared memory; CTA r
@@ -384,7 +390,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
       cluster_sync_all();
       const int S = a.S_eff;
       const uint32_t r = cluster_ctarank();
-      for (int idx = int(r) * (32 * kConsumerWarps) + ct; idx < gvalid * D; idx += S * 32 * kConsumerWarps) {
+      for (int idx = int(r) * (32 * C::kCW) + ct; idx < gvalid * D; idx += S * 32 * C::kCW) {
         const int gg = idx / D, d = idx - gg * D;
         const uint32_t am = smem_u32(cl_m + gg), al = smem_u32(cl_l + gg), ao = smem_u32(cl_o + gg * D + d);
         float mj[kMaxCluster];
@@ -408,7 +414,7 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
       // no CTA may exit (and release its shared memory) while others still read it
       cluster_sync_all();
     } else {
-      if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
+      if (a.S_eff == 1) signal_out(a, ct, 1, 32 * C::kCW);
     }
   }
 }
@@ -418,12 +424,12 @@ __global__ void __launch_bounds__(kThreads) decode_f16_kernel(const __grid_const
 template <int D>
 static cudaError_t launch_f16(const DecodeLaunch& a, cudaStream_t stream) {
   if (a.cluster == 0) {
-    launch_pdl(decode_f16_kernel<D, false>, dim3(a.grid), dim3(kThreads), F16Cfg<D>::kSmemBytes, stream, a);
+    launch_pdl(decode_f16_kernel<D, false>, dim3(a.grid), dim3(F16Cfg<D>::kThr), F16Cfg<D>::kSmemBytes, stream, a);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(F16Cfg<D, true>::kThr);
   cfg.dynamicSmemBytes = F16Cfg<D, true>::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -439,7 +445,7 @@ static cudaError_t launch_f16(const DecodeLaunch& a, cudaStream_t stream) {
 }
 
 KernelShape decode_kernel_shape_f16(int D) {
-  return KernelShape{kThreads, D == 128 ? F16Cfg<128>::kSmemBytes : F16Cfg<64>::kSmemBytes};
+  return KernelShape{F16Cfg<64>::kThr, D == 128 ? F16Cfg<128>::kSmemBytes : F16Cfg<64>::kSmemBytes};
 }
 
 cudaError_t decode_kernel_prepare_f16(int D, int* ctas_per_sm) {
@@ -448,7 +454,7 @@ cudaError_t decode_kernel_prepare_f16(int D, int* ctas_per_sm) {
   const size_t smem = decode_kernel_shape_f16(D).smem_bytes;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, kThreads, smem);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, F16Cfg<64>::kThr, smem);
 }
 
 template <int D>
@@ -462,7 +468,7 @@ static cudaError_t prepare_cluster(int (&max_clusters)[17]) {
   for (int c = 2; c <= kMaxCluster; ++c) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(F16Cfg<D, true>::kThr);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;

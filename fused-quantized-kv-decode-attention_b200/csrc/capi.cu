@@ -105,6 +105,37 @@ int device_state(DeviceState** out) {
   return FQKV_OK;
 }
 
+// ------------------------------------------------------------------ per-thread caches
+// A decode call's host work is dominated by the split plan (a search over split
+// counts) and two TMA descriptor encodings; both are pure functions of their
+// inputs, so the last few results are kept per thread and reused when the same
+// sizes (and, for descriptors, the same pointers) come again -- the usual case
+// in a decode loop.
+template <typename Key, typename Val, int kN>
+struct SmallCache {
+  Key keys[kN];
+  Val vals[kN];
+  bool used[kN] = {};
+  int next = 0;
+  const Val* find(const Key& k) const {
+    for (int i = 0; i < kN; ++i)
+      if (used[i] && std::memcmp(&keys[i], &k, sizeof(Key)) == 0) return &vals[i];
+    return nullptr;
+  }
+  void put(const Key& k, const Val& v) {
+    keys[next] = k;
+    vals[next] = v;
+    used[next] = true;
+    next = (next + 1) % kN;
+  }
+};
+
+struct MapKey {
+  const void* base;
+  int64_t BH, N, inner, stride;
+  int tile, kind;  // kind 0: fp16 rows of `inner` dims; 1: code rows of `inner` bytes
+};
+
 // ------------------------------------------------------------------ tensor maps
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -125,6 +156,14 @@ EncodeTiledFn encode_fn() {
 // K or V viewed as [B*Hkv][N][D] fp16 with `stride` keys between consecutive
 // (b, kv head) rows, box = 64 dims x 64 keys x 1, 128B swizzle.
 int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t D, int64_t stride) {
+  thread_local SmallCache<MapKey, CUtensorMap, 8> cache;
+  MapKey key;
+  std::memset(&key, 0, sizeof(key));
+  key.base = base; key.BH = BH; key.N = N; key.inner = D; key.stride = stride; key.tile = 64; key.kind = 0;
+  if (const CUtensorMap* hit = cache.find(key)) {
+    *map = *hit;
+    return FQKV_OK;
+  }
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   const cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(BH)};
@@ -135,6 +174,7 @@ int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  cache.put(key, *map);
   return FQKV_OK;
 }
 
@@ -143,6 +183,14 @@ int make_kv_map(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64
 // one tile of `tile` whole rows, swizzled at the row width.
 int make_kv_map_codes(CUtensorMap* map, const void* base, int64_t BH, int64_t N, int64_t rb, int64_t stride,
                       int tile) {
+  thread_local SmallCache<MapKey, CUtensorMap, 8> cache;
+  MapKey key;
+  std::memset(&key, 0, sizeof(key));
+  key.base = base; key.BH = BH; key.N = N; key.inner = rb; key.stride = stride; key.tile = tile; key.kind = 1;
+  if (const CUtensorMap* hit = cache.find(key)) {
+    *map = *hit;
+    return FQKV_OK;
+  }
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   const cuuint64_t dims[3] = {cuuint64_t(rb), cuuint64_t(N), cuuint64_t(BH)};
@@ -156,6 +204,7 @@ int make_kv_map_codes(CUtensorMap* map, const void* base, int64_t BH, int64_t N,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FQKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+  cache.put(key, *map);
   return FQKV_OK;
 }
 
@@ -186,7 +235,42 @@ int ctas_per_sm(const DeviceState& ds, KvFormat f, int D) {
 // S_fixed > 0: use at most S_fixed splits (gqa_sk_fast).  Otherwise pick the
 // split count that minimises the modelled time, limited to what `ws_bytes`
 // can hold when `limit_ws`.
+struct PlanKey {
+  const DeviceState* ds;
+  int fmt, B, Hq, Hkv, N, D, tp, mode;
+  int64_t S_fixed;
+  size_t ws_bytes;
+  int limit_ws;
+};
+struct PlanVal {
+  int fmt, G, GP, groups, cluster, S, S_eff, chunk, units, grid;
+};
+
+void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_bytes, bool limit_ws);
+
+// Fills the plan of `a` (fmt, B, Hq, Hkv, N, D and tp set by the caller), from the
+// per-thread cache when the same sizes were planned before.
 void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_bytes, bool limit_ws) {
+  thread_local SmallCache<PlanKey, PlanVal, 8> cache;
+  PlanKey key;
+  std::memset(&key, 0, sizeof(key));
+  key.ds = &ds; key.fmt = int(a.fmt); key.B = a.B; key.Hq = a.Hq; key.Hkv = a.Hkv; key.N = a.N; key.D = a.D;
+  key.tp = a.tp.world != 0; key.mode = g_split_mode.load(); key.S_fixed = S_fixed;
+  key.ws_bytes = limit_ws ? ws_bytes : 0; key.limit_ws = limit_ws;
+  if (const PlanVal* v = cache.find(key)) {
+    a.fmt = KvFormat(v->fmt); a.G = v->G; a.GP = v->GP; a.groups = v->groups; a.cluster = v->cluster;
+    a.S = v->S; a.S_eff = v->S_eff; a.chunk = v->chunk; a.units = v->units; a.grid = v->grid;
+  } else {
+    plan_geometry(a, ds, S_fixed, ws_bytes, limit_ws);
+    cache.put(key, PlanVal{int(a.fmt), a.G, a.GP, a.groups, a.cluster, a.S, a.S_eff, a.chunk, a.units, a.grid});
+  }
+  a.sm_scale_log2 = float(1.4426950408889634 / std::sqrt(double(a.D)));
+  a.status = ds.status;
+  a.timeout_ns = g_timeout_ns.load();
+  a.debug_skip_loads = g_debug_skip_loads.load();
+}
+
+void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_bytes, bool limit_ws) {
   // int8 codes shared by several query heads go to the tensor-core GQA kernel.
   // int8 codes shared by several query heads, and int4 codes with D = 128, go
   // to the tensor-core quantized kernel (measured on B200: int4 D = 128 817 vs
@@ -281,10 +365,6 @@ void plan(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size_t ws_byt
   const int64_t units = units0 * a.S_eff;
   a.units = int(units);
   a.grid = a.cluster ? int(units) : int(std::min<int64_t>(units, C));
-  a.sm_scale_log2 = float(1.4426950408889634 / std::sqrt(double(a.D)));
-  a.status = ds.status;
-  a.timeout_ns = g_timeout_ns.load();
-  a.debug_skip_loads = g_debug_skip_loads.load();
 }
 
 bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
@@ -420,6 +500,22 @@ size_t fqkv_decode_workspace_bytes(int kv_format, int64_t B, int64_t Hq, int64_t
   a.B = int(B); a.Hq = int(Hq); a.Hkv = int(Hkv); a.N = int(N); a.D = int(D);
   plan(a, *ds, 0, 0, false);
   return (a.S_eff > 1 && !a.cluster) ? partial_bytes(B * Hq, a.S_eff, D) : 0;
+}
+
+int fqkv_device_info(int32_t* info, int32_t n) {
+  if (!info || n < 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "device_info: need an output array");
+  DeviceState* ds = nullptr;
+  if (int rc = device_state(&ds)) return rc;
+  int32_t v[FQKV_DEVICE_INFO_LEN];
+  v[0] = ds->sm_count;
+  v[1] = ds->occ_f16[1];
+  v[2] = ds->occ_f16[0];
+  for (int c = 2; c <= 16; ++c) {
+    v[3 + (c - 2)] = ds->max_clusters_f16[1][c];
+    v[18 + (c - 2)] = ds->max_clusters_f16[0][c];
+  }
+  for (int i = 0; i < n && i < FQKV_DEVICE_INFO_LEN; ++i) info[i] = v[i];
+  return FQKV_OK;
 }
 
 int fqkv_decode_plan(int kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, size_t workspace_bytes,

@@ -75,6 +75,17 @@ __device__ __forceinline__ __half quant_scale(float amax, bool any_nan) {
   return __float2half_rn(__fdiv_rn(a, float(Q)));
 }
 
+// The same scale for a finite amax by the FMA-corrected division (amax and Q are
+// fp16 values, so the argument of the file comment applies); inf / NaN take
+// quant_scale's IEEE path.
+template <int Q>
+__device__ __forceinline__ __half quant_scale_fast(float amax, bool any_nan) {
+  if (any_nan || !(amax <= 65504.f)) return quant_scale<Q>(amax, any_nan);
+  constexpr float kY = 1.0f / float(Q);  // within half an ulp of 1/Q
+  const float q0 = amax * kY;
+  return __float2half_rn(fmaf(fmaf(-float(Q), q0, amax), kY, q0));
+}
+
 // Output placement: token `row` of the input (rows = groups x T tokens) goes
 // to output row (row / T) * cap + pos + row % T, where pos is *pos_dev when
 // given (a growing KV cache) else pos_host; tokens landing at or past `cap`
@@ -91,7 +102,7 @@ __device__ __forceinline__ uint32_t pack4(int c0, int c1, int c2, int c3) {
 
 // Vectorised path: D in {64, 128, 256}; LPR = D/8 lanes per token, each with 8
 // consecutive elements.  Persistent: warp w handles tokens w*RPW + j + i*stride.
-template <bool kInt4, int D>
+template <bool kInt4, int D, bool kPlace>
 __global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __restrict__ X, void* __restrict__ codes,
                                                            __half* __restrict__ scales, int64_t rows,
                                                            QuantPlace pl) {
@@ -103,7 +114,7 @@ __global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __re
   const int c = lane % LPR;
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int64_t stride = warps * RPW;  // tokens covered by one pass of all warps
-  const int64_t pos0 = pl.pos_dev ? int64_t(*pl.pos_dev) : pl.pos_host;
+  const int64_t pos0 = kPlace ? (pl.pos_dev ? int64_t(*pl.pos_dev) : pl.pos_host) : 0;
   for (int64_t wbase = ((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * RPW; wbase < rows;
        wbase += kUnroll * stride) {  // warp-uniform: every lane takes part in the shuffles below
     uint4 raw[kUnroll];
@@ -128,12 +139,15 @@ __global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __re
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
         nan |= __shfl_xor_sync(0xffffffffu, int(nan), off) != 0;
       }
-      const __half sh = quant_scale<Q>(amax, nan);
+      const __half sh = quant_scale_fast<Q>(amax, nan);
       const float sc = __half2float(sh);
       if (row >= rows) continue;
-      const int64_t pos = pos0 + row % pl.T;
-      if (pos < 0 || pos >= pl.cap) continue;
-      const int64_t orow = (row / pl.T) * pl.cap + pos;
+      int64_t orow = row;
+      if constexpr (kPlace) {  // append into a cache: group row / T, position pos0 + row % T
+        const int64_t pos = pos0 + row % pl.T;
+        if (pos < 0 || pos >= pl.cap) continue;
+        orow = (row / pl.T) * pl.cap + pos;
+      }
       if (c == 0) scales[orow] = sh;
       int q[8];
       if (normal_fp16_scale(sc)) {
@@ -220,9 +234,9 @@ cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int
   if (aligned && (D == 64 || D == 128 || D == 256)) {
     const unsigned blocks = unsigned(quant_blocks(rows, D, sm_count));
     const QuantPlace pl{rows, rows, 0, nullptr};
-    if (D == 64) quantize_vec_kernel<kInt4, 64><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else if (D == 128) quantize_vec_kernel<kInt4, 128><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<kInt4, 256><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    if (D == 64) quantize_vec_kernel<kInt4, 64, false><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else if (D == 128) quantize_vec_kernel<kInt4, 128, false><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<kInt4, 256, false><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
   } else {
     const int64_t blocks = (rows * 32 + 255) / 256;
     quantize_generic_kernel<kInt4><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, D);
@@ -374,11 +388,11 @@ cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* sc
   const QuantPlace pl{T, cap, pos_host, pos_dev};
   const unsigned blocks = unsigned(quant_blocks(rows, D, sm_count));
   if (D == 64) {
-    if (int4) quantize_vec_kernel<true, 64><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<false, 64><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    if (int4) quantize_vec_kernel<true, 64, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<false, 64, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
   } else {
-    if (int4) quantize_vec_kernel<true, 128><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<false, 128><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    if (int4) quantize_vec_kernel<true, 128, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
+    else quantize_vec_kernel<false, 128, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
   }
   return cudaGetLastError();
 }

@@ -94,6 +94,15 @@ int fqkv_set_split_mode(int mode);
  * non-GQA entry points with B = R). */
 size_t fqkv_decode_workspace_bytes(int kv_format, int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D);
 
+/* What the library found on the current device (for tuning records): info[0]
+ * = SMs, info[1] / info[2] = resident CTAs per SM of the fp16 decode kernel at
+ * D = 128 / 64, info[3 + c - 2] (c = 2..16) = thread-block clusters of size c
+ * of the fp16 cluster-merge kernel that can be resident at once at D = 128,
+ * info[18 + c - 2] the same at D = 64.  Writes min(n, FQKV_DEVICE_INFO_LEN)
+ * values.  No counterpart in the reference. */
+#define FQKV_DEVICE_INFO_LEN 33
+int fqkv_device_info(int32_t* info, int32_t n);
+
 /* The launch plan a decode call with these sizes and this much workspace gets
  * on the current device (for tuning, tests and benchmark records):
  * plan_out[0] = splits per (sequence, KV head) work unit (1 = unsplit),
