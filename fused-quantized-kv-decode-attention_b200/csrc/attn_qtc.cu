@@ -450,6 +450,11 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
       for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     }
     float m_run = -INFINITY, l_run = 0.f;
+    // several heads: the fp16 B operand p * vscale carries a warp-uniform power-of-two factor vsc,
+    // lowered (O rescaled exactly) whenever a key's V scale times vsc would pass 2^14, so the operand
+    // stays in fp16's normal range for any V magnitude (small V no longer rounds to subnormals,
+    // which the fp16 MMA also runs slower on); O leaves the frame (/ vsc) in the epilogue.
+    float vsc = 1099511627776.f;  // 2^40
 
     for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
       const int st = it % C::kStages;
@@ -666,13 +671,33 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           }
         }
         const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+        float vmax = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          if (valid[j][0]) vmax = fmaxf(vmax, vs[j][0]);
+          if (valid[j][1]) vmax = fmaxf(vmax, vs[j][1]);
+        }
+        if (__any_sync(0xffffffffu, vmax * vsc > 16384.f)) {  // rare: the frame moves down
+          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // keys depend on t only
+          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+          const float nsc = ldexpf(1.f, 13 - ilogbf(vmax));
+          const float ratio = nsc / vsc;  // a power of two: exact
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            o[i][0] *= ratio;
+            o[i][1] *= ratio;
+            o[i][2] *= ratio;
+            o[i][3] *= ratio;
+          }
+          vsc = nsc;
+        }
         uint32_t pb[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
           const float p0 = valid[j][0] ? ex2(sc[j][0] - mu) : 0.f;
           const float p1 = valid[j][1] ? ex2(sc[j][1] - mu) : 0.f;
           l_run += p0 + p1;
-          pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] : 0.f, valid[j][1] ? p1 * vs[j][1] : 0.f);
+          pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] * vsc : 0.f, valid[j][1] ? p1 * vs[j][1] * vsc : 0.f);
         }
 
         // ---- O^T += V^T P^T
@@ -721,10 +746,11 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           if (gl >= 0 && gl < MH && head < gvalid) {
             // this thread's dimensions g*D/8 .. g*D/8 + D/8 - 1 of the head
             float val[D / 8];
+            const float inv_vsc = 1.f / vsc;  // leave the V-scale frame (a power of two: exact)
 #pragma unroll
             for (int i = 0; i < MT; ++i) {
-              val[i] = o[i][e];
-              val[MT + i] = o[i][2 + e];
+              val[i] = o[i][e] * inv_vsc;
+              val[MT + i] = o[i][2 + e] * inv_vsc;
             }
             float* dst = &sm_o[(warp * MH + gl) * D + g * (D / 8)];
 #pragma unroll

@@ -263,6 +263,12 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
     // sums of the fp16 p (int8 codes, int4 low nibbles) and p / 16 (int4 high nibbles) this
     // lane multiplied, for the offset of the subnormal code fields (see the P.V step)
     float bias_lo = 0.f, bias_hi = 0.f;
+    // p * vscale enters the fp16 FMA operand multiplied by vsc, a power of two that keeps it in
+    // fp16's normal range: vsc is lowered (o and the bias sums rescaled exactly) whenever a key's
+    // V scale times vsc would pass 2^14, so p * vscale * vsc <= 2^14 (p <= 1), and otherwise stays
+    // as large as the largest V scale so far allows -- a small V (|V| ~ 1e-4) no longer rounds to
+    // fp16 subnormals.  The lane's o leaves the frame (/ vsc) before the cross-lane reduction.
+    float vsc = 1099511627776.f;  // 2^40: any nonzero fp16 V scale lowers it on its first tile
 
     // One tile of this warp's keys; kMask adds the per-key bound checks that
     // only the last (partial) tile of a unit needs.
@@ -321,13 +327,28 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         m_run = m_new;
       }
       const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+      float vs4[4];
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        const int kl = kw + j + C::kKPS * sp;
+        vs4[sp] = (!kMask || (k0 + kl) < hi) ? __half2float(vst[kl]) : 0.f;
+      }
+      const float vmax = fmaxf(fmaxf(vs4[0], vs4[1]), fmaxf(vs4[2], vs4[3]));
+      if (vmax * vsc > 16384.f) {  // lane-local and rare: the frame moves down to fit this V scale
+        const float nsc = ldexpf(1.f, 13 - ilogbf(vmax));
+        const float ratio = nsc / vsc;  // a power of two: exact
+#pragma unroll
+        for (int d = 0; d < kDPL; ++d) o[d] *= ratio;
+        bias_lo *= ratio;
+        bias_hi *= ratio;
+        vsc = nsc;
+      }
 #pragma unroll
       for (int sp = 0; sp < 4; ++sp) {
         const int kl = kw + j + C::kKPS * sp;
         const float p = ex2(sco[sp] - mu);
         l_run += p;
-        float pv = p * __half2float(vst[kl]);
-        if (kMask) pv = ((k0 + kl) < hi) ? pv : 0.f;
+        const float pv = p * vs4[sp] * vsc;
         const uint16_t ph = __half_as_ushort(__float2half_rn(pv));
         const uint4 v0v = *reinterpret_cast<const uint4*>(vt + kl * C::kRowBytes + 32 * c);
         const uint4 v1v = *reinterpret_cast<const uint4*>(vt + kl * C::kRowBytes + 32 * c + 16);
@@ -388,13 +409,16 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       if (lane == 0) mbar_arrive(&empty[st]);
     }
 
-    // scale the subnormal fields back and remove their offset (int4: + 8; int8: + 128)
+    // scale the subnormal fields back, remove their offset (int4: + 8; int8: + 128) and leave
+    // the lane's V-scale frame
+    const float inv_vsc = 1.f / vsc;  // a power of two: exact
     if (kInt4) {
 #pragma unroll
-      for (int d = 0; d < kDPL; ++d) o[d] = fmaf(o[d], 16777216.f, -8.f * ((d & 1) ? 16.f * bias_hi : bias_lo));
+      for (int d = 0; d < kDPL; ++d)
+        o[d] = fmaf(o[d], 16777216.f, -8.f * ((d & 1) ? 16.f * bias_hi : bias_lo)) * inv_vsc;
     } else {
 #pragma unroll
-      for (int d = 0; d < kDPL; ++d) o[d] = fmaf(o[d], 16777216.f, -128.f * bias_lo);
+      for (int d = 0; d < kDPL; ++d) o[d] = fmaf(o[d], 16777216.f, -128.f * bias_lo) * inv_vsc;
     }
 
     // ---- warp reduction over key slots, then merge the 4 warps

@@ -539,3 +539,32 @@ def test_batch1_decode_plans_a_cluster_merge(fqkv):
     # the batch-64 bench shape stays unsplit and persistent
     fqkv.native.check(lib.fqkv_decode_plan(0, 64, 32, 8, 16384, 128, 0, out), "plan")
     assert out[0] == 1 and out[1] == 0
+
+
+@pytest.mark.parametrize("scale", [1e-4, 1e-3, 1e2])
+@pytest.mark.parametrize("D", [64, 128])
+def test_quantized_kernels_relative_accuracy_at_any_v_scale(fqkv, scale, D):
+    """V scaled by 1e-4 .. 1e2 (p * vscale would fall into fp16 subnormals for small V): every
+    quantized kernel -- int8 and int4 with one head per row, int8 GQA on the tensor cores -- within a
+    tolerance relative to the output's scale (atol = 2e-3 * scale, rtol = 1e-2) of the oracle."""
+    R, N = 6, 1500
+    q, K = _randn(R, D, seed=180), _randn(R, N, D, seed=181)
+    V = (_randn(R, N, D, seed=182).float() * scale).half()
+    for quant, dq, op in ((fqkv.qpt, oq.dequantize_int8, fqkv.decode_attn_int8_mw),
+                          (fqkv.quant_int4_per_token, oq.dequantize_int4, fqkv.decode_attn_int4)):
+        Kc, Ks = quant(K.cuda())
+        Vc, Vs = quant(V.cuda())
+        out = op(q.cuda(), Kc, Vc, Ks, Vs, 8)
+        ref = oatt.decode_attention(q.numpy(), dq(Kc.cpu().numpy(), Ks.cpu().numpy()),
+                                    dq(Vc.cpu().numpy(), Vs.cpu().numpy()))
+        np.testing.assert_allclose(out.float().cpu().numpy().astype(np.float64), ref, atol=2e-3 * scale, rtol=1e-2)
+    B, Hq, Hkv = 2, 16, 4
+    qg = _randn(B, Hq, D, seed=183)
+    Kg = _randn(B, Hkv, N, D, seed=184)
+    Vg = (_randn(B, Hkv, N, D, seed=185).float() * scale).half()
+    Kq, Ks = fqkv.qpt(Kg.cuda())
+    Vq, Vs = fqkv.qpt(Vg.cuda())
+    out = fqkv.decode_attn_gqa_int8(qg.cuda(), Kq, Vq, Ks, Vs)
+    ref = oatt.decode_attention_gqa(qg.numpy(), oq.dequantize_int8(Kq.cpu().numpy(), Ks.cpu().numpy()),
+                                    oq.dequantize_int8(Vq.cpu().numpy(), Vs.cpu().numpy()))
+    np.testing.assert_allclose(out.float().cpu().numpy().astype(np.float64), ref, atol=2e-3 * scale, rtol=1e-2)
