@@ -651,17 +651,29 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
 
-        // ---- online softmax per head g over the KPW keys
+        // ---- online softmax per head g over the KPW keys, and the V-scale frame: one rescale
+        // block for both (a head's maximum grew; a key's V scale would push p * vs * vsc past 2^14)
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const float m_new = fmaxf(m_run, mx);
-        if (__any_sync(0xffffffffu, m_new > m_run)) {
+        float vmax = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          if (valid[j][0]) vmax = fmaxf(vmax, vs[j][0]);
+          if (valid[j][1]) vmax = fmaxf(vmax, vs[j][1]);
+        }
+        if (__any_sync(0xffffffffu, m_new > m_run || vmax * vsc > 16384.f)) {
+          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // keys depend on t only
+          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+          const float nsc = vmax * vsc > 16384.f ? ldexpf(1.f, 13 - ilogbf(vmax)) : vsc;  // warp-uniform
+          const float ratio = nsc / vsc;  // a power of two: exact
+          vsc = nsc;
           const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
           l_run *= alpha;
           m_run = m_new;
           // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
-          const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * t) * 4);
-          const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4);
+          const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * t) * 4) * ratio;
+          const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4) * ratio;
 #pragma unroll
           for (int i = 0; i < MT; ++i) {
             o[i][0] *= a_lo;
@@ -671,26 +683,6 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           }
         }
         const float mu = (m_run == -INFINITY) ? 0.f : m_run;
-        float vmax = 0.f;
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          if (valid[j][0]) vmax = fmaxf(vmax, vs[j][0]);
-          if (valid[j][1]) vmax = fmaxf(vmax, vs[j][1]);
-        }
-        if (__any_sync(0xffffffffu, vmax * vsc > 16384.f)) {  // rare: the frame moves down
-          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // keys depend on t only
-          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-          const float nsc = ldexpf(1.f, 13 - ilogbf(vmax));
-          const float ratio = nsc / vsc;  // a power of two: exact
-#pragma unroll
-          for (int i = 0; i < MT; ++i) {
-            o[i][0] *= ratio;
-            o[i][1] *= ratio;
-            o[i][2] *= ratio;
-            o[i][3] *= ratio;
-          }
-          vsc = nsc;
-        }
         uint32_t pb[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {

@@ -317,16 +317,6 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
 #pragma unroll
       for (int off = C::kL; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       const float m_new = fmaxf(m_run, mx);
-      if (m_new > m_run) {  // warp-uniform
-        const float alpha = ex2(m_run - m_new);
-#pragma unroll
-        for (int d = 0; d < kDPL; ++d) o[d] *= alpha;
-        l_run *= alpha;
-        bias_lo *= alpha;
-        bias_hi *= alpha;
-        m_run = m_new;
-      }
-      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
       float vs4[4];
 #pragma unroll
       for (int sp = 0; sp < 4; ++sp) {
@@ -334,15 +324,22 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         vs4[sp] = (!kMask || (k0 + kl) < hi) ? __half2float(vst[kl]) : 0.f;
       }
       const float vmax = fmaxf(fmaxf(vs4[0], vs4[1]), fmaxf(vs4[2], vs4[3]));
-      if (vmax * vsc > 16384.f) {  // lane-local and rare: the frame moves down to fit this V scale
-        const float nsc = ldexpf(1.f, 13 - ilogbf(vmax));
-        const float ratio = nsc / vsc;  // a power of two: exact
+      const bool grow_v = vmax * vsc > 16384.f;  // lane-local, rare: the V frame must move down
+      // one rescale block for both causes (a larger running maximum: warp-uniform; a lower V
+      // frame: lane-local), so the loop carries one copy of the per-dimension multiply
+      if (m_new > m_run || grow_v) {
+        const float alpha = m_new > m_run ? ex2(m_run - m_new) : 1.f;
+        const float nsc = grow_v ? ldexpf(1.f, 13 - ilogbf(vmax)) : vsc;
+        const float f = alpha * (nsc / vsc);  // the frame ratio is a power of two: exact
 #pragma unroll
-        for (int d = 0; d < kDPL; ++d) o[d] *= ratio;
-        bias_lo *= ratio;
-        bias_hi *= ratio;
+        for (int d = 0; d < kDPL; ++d) o[d] *= f;
+        l_run *= alpha;
+        bias_lo *= f;
+        bias_hi *= f;
+        m_run = m_new;
         vsc = nsc;
       }
+      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
 #pragma unroll
       for (int sp = 0; sp < 4; ++sp) {
         const int kl = kw + j + C::kKPS * sp;

@@ -341,11 +341,15 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   // Cluster mode (fp16, local output): when the grid is too small to fill the GPU without
   // splitting, the S split CTAs of each unit form one thread-block cluster (S <= 16), one CTA
   // per SM, and merge through distributed shared memory -- one launch, no partials, no combine.
-  // Used when the whole grid is resident at once and keeps at least half the SMs streaming
-  // (batch-1 decode: Hkv = 8 KV heads x 16 splits = 128 CTAs).
+  // Used when the whole grid is resident at once and keeps at least half the SMs streaming.
+  // Automatic only at D = 128, where it measured faster than partials + combine on B200 (B=4,
+  // Hkv=8: N=4K 16.5 -> 14.0 us, 16K 43.8 -> 43.1, 64K 159.9 -> 156.8; B=8: 26.1 -> 23.8,
+  // 84.0 -> 82.0, 325.6 -> 323.3); at D = 64 one CTA per SM streams too slowly for long
+  // contexts (B=4, N=64K: 83 -> 97 us).  Batch 1 with 8 KV heads would need 8 resident clusters
+  // of 16, and B200 holds 7 (one GPC has fewer than 16 SMs free), so it keeps the combine.
   const int mode = g_split_mode.load();
   if (a.fmt == KvFormat::F16 && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
-      (se > 1 || mode == FQKV_SPLIT_CLUSTER) && units0 < ds.sm_count) {
+      (mode == FQKV_SPLIT_CLUSTER || (se > 1 && a.D == 128)) && units0 < ds.sm_count) {
     int64_t sc = std::min<int64_t>({16, tiles, std::max<int64_t>(1, ds.sm_count / units0)});
     if (S_fixed > 0) sc = std::min<int64_t>(sc, S_fixed);
     int64_t cct = 0, cse = 0;

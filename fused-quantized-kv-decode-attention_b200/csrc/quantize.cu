@@ -95,6 +95,9 @@ struct QuantPlace {
   const int* pos_dev;
 };
 
+// Tokens whose 16-byte loads each lane of the quantizer keeps in flight.
+constexpr int kUnroll = 3;
+
 // Four codes (low bytes of c0..c3) as one word, c0 in the low byte.
 __device__ __forceinline__ uint32_t pack4(int c0, int c1, int c2, int c3) {
   return __byte_perm(__byte_perm(c0, c1, 0x0040u), __byte_perm(c2, c3, 0x0040u), 0x5410u);
@@ -109,7 +112,6 @@ __global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __re
   constexpr int LPR = D / 8;
   constexpr int RPW = 32 / LPR;
   constexpr int Q = kInt4 ? 7 : 127;
-  constexpr int kUnroll = 4;
   const int lane = threadIdx.x & 31;
   const int c = lane % LPR;
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -128,17 +130,16 @@ __global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __re
       const int64_t row = wbase + lane / LPR + u * stride;
       if (wbase + u * stride >= rows) break;  // warp-uniform
       const __half2* h2 = reinterpret_cast<const __half2*>(&raw[u]);
-      // amax in fp16 (exact), NaN-propagating like torch.amax
+      // amax in fp16 (exact), NaN-propagating like torch.amax, reduced over the token's lanes
+      // as packed fp16 pairs: one shuffle per step carries both the maximum and any NaN
       __half2 m2 = __habs2(h2[0]);
 #pragma unroll
       for (int i = 1; i < 4; ++i) m2 = __hmax2_nan(m2, __habs2(h2[i]));
-      float amax = fmaxf(__low2float(m2), __high2float(m2));
-      bool nan = __hisnan(m2.x) || __hisnan(m2.y);
 #pragma unroll
-      for (int off = 1; off < LPR; off <<= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        nan |= __shfl_xor_sync(0xffffffffu, int(nan), off) != 0;
-      }
+      for (int off = 1; off < LPR; off <<= 1) m2 = __hmax2_nan(m2, __shfl_xor_sync(0xffffffffu, m2, off));
+      m2 = __hmax2_nan(m2, __lowhigh2highlow(m2));
+      const bool nan = __hisnan(__low2half(m2));
+      const float amax = __low2float(m2);
       const __half sh = quant_scale_fast<Q>(amax, nan);
       const float sc = __half2float(sh);
       if (row >= rows) continue;
@@ -218,10 +219,10 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const __half* __r
 }
 
 // Persistent grid of the vectorised quantizer: enough 256-thread CTAs for every
-// token once (4 tokens per lane), at most 4 per SM (64 registers per thread).
+// token once (kUnroll tokens per lane), at most 4 per SM (64 registers per thread).
 int64_t quant_blocks(int64_t rows, int D, int sm_count) {
   const int64_t warps_needed = (rows * (D / 8) + 31) / 32;
-  const int64_t blocks = (warps_needed + 4 * 8 - 1) / (4 * 8);
+  const int64_t blocks = (warps_needed + kUnroll * 8 - 1) / (kUnroll * 8);
   return std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count) * 4));
 }
 
