@@ -213,6 +213,7 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------- workload setup
 POOL_BYTES = 1 << 30
+L2_ROTATE_BYTES = 537_000_000   # > 4 x the 126 MB L2: rotated input sets per call stream from HBM
 
 
 def quantized_rows(quant, R: int, N: int, D: int, int4: bool, gen, dev):
@@ -249,9 +250,13 @@ class Case:
         self.stream = torch.cuda.current_stream(dev)
         if k == "gqa":
             B, Hq, Hkv, N, D = w["B"], w["Hq"], w["Hkv"], w["N"], w["D"]
-            self.q = torch.randn(B, Hq, D, device=dev, generator=gen, dtype=torch.float16)
-            self.K = torch.randn(B, Hkv, N, D, device=dev, generator=gen, dtype=torch.float16)
-            self.V = torch.randn(B, Hkv, N, D, device=dev, generator=gen, dtype=torch.float16)
+            # KV sets smaller than 4x L2 are rotated so every call streams from HBM
+            self.n_sets = min(8, max(1, -(-L2_ROTATE_BYTES // (2 * B * Hkv * N * D * 2))))
+            self.sets = [(torch.randn(B, Hq, D, device=dev, generator=gen, dtype=torch.float16),
+                          torch.randn(B, Hkv, N, D, device=dev, generator=gen, dtype=torch.float16),
+                          torch.randn(B, Hkv, N, D, device=dev, generator=gen, dtype=torch.float16))
+                         for _ in range(self.n_sets)]
+            self.q, self.K, self.V = self.sets[0]
             self.o = torch.empty(B, Hq, D, device=dev, dtype=torch.float16)
             nb = pkg.workspace_bytes("fp16", B, Hq, Hkv, N, D)
             self.ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
@@ -347,9 +352,9 @@ class Case:
         P, I = ctypes.c_void_p, ctypes.c_int64
         ws = (P(self.ws.data_ptr()) if self.nb else P(None), ctypes.c_size_t(self.nb)) if hasattr(self, "nb") else ()
         if k == "gqa":
-            calls = [(lib.fqkv_decode_attn_gqa, (P(self.q.data_ptr()), P(self.K.data_ptr()), P(self.V.data_ptr()),
+            calls = [(lib.fqkv_decode_attn_gqa, (P(q.data_ptr()), P(K.data_ptr()), P(V.data_ptr()),
                                                  P(self.o.data_ptr()), I(w["B"]), I(w["Hq"]), I(w["Hkv"]), I(w["N"]),
-                                                 I(w["D"]), I(8)) + ws)]
+                                                 I(w["D"]), I(8)) + ws) for q, K, V in self.sets]
         elif k == "gqa_int8":
             calls = [(lib.fqkv_decode_attn_gqa_int8, (P(self.q.data_ptr()), P(self.K.data_ptr()), P(self.V.data_ptr()),
                                                       P(self.Ks.data_ptr()), P(self.Vs.data_ptr()), P(self.o.data_ptr()),
@@ -956,6 +961,9 @@ def main() -> int:
                     help="time K eager C-ABI calls instead of one CUDA-graph replay of K calls")
     ap.add_argument("--no-extra-timing", action="store_true",
                     help="skip the eager-loop, single-call and launch-floor timings (1-GPU runs only)")
+    ap.add_argument("--split-mode", default="auto", choices=["auto", "combine", "cluster"],
+                    help="how split plans merge (fqkv_set_split_mode): the library's choice, partials + combine "
+                         "kernel, or thread-block cluster")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-config sweep of the default run (1 GPU: the 'configs' key; several "
                          "GPUs: the 'multi_gpu' key -- KV-head-sharded config 4 and tensor-parallel config 5)")
@@ -987,8 +995,8 @@ def main() -> int:
         return run_llama_tp(args, w, world, rank, local_rank) if world > 1 else run_llama(args, w)
     config = {"workload": w["desc"], "global_batch": None, "seq_len": w["N"], "head_dim": w["D"],
               "parallelism": f"{world} GPU(s), sequences sharded, no data-path collective",
-              "l2": "inputs larger than L2 per step (no flush needed)" if w["kind"] != "sk"
-              else "8 rotated KV sets (537 MB) > 4x L2",
+              "l2": "8 rotated KV sets (537 MB) > 4x L2" if w["kind"] == "sk"
+              else "inputs larger than L2 per step (no flush needed)",
               "timing": "CUDA events around K eager C-ABI calls" if args.eager
               else "CUDA events around one CUDA-graph replay of K C-ABI calls"}
     if w["kind"] in ("gqa", "gqa_int8"):
@@ -1024,6 +1032,11 @@ def main() -> int:
 
     # ---------------- our arm
     pkg = importlib.import_module(PKG)
+    mode = {"auto": 0, "combine": 1, "cluster": 2}[args.split_mode]
+    if pkg.native.lib().fqkv_set_split_mode(mode) != 0:
+        raise RuntimeError(pkg.native.last_error())
+    if args.split_mode != "auto":
+        config["split_mode"] = args.split_mode
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -1033,6 +1046,8 @@ def main() -> int:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     case = Case(pkg, w, dev, seed=1234 + rank)
+    if getattr(case, "n_sets", 1) > 1:
+        config["l2"] = f"{case.n_sets} rotated input sets > 4x L2"
     kernels_per_call = case.kernels_per_call
     main_plan = case.plan
 

@@ -7,16 +7,18 @@
 // Layout in HBM (exactly the reference's): codes [R, N, D] int8 or packed
 // [R, N, D/2] uint8 (element 2t in the low nibble), scales [R, N] fp16.
 //
-//  * Persistent, warp-specialised: warp 4 streams 16 KiB tiles of K and V
-//    codes plus the matching scale windows into a 3-stage ring with 1-D bulk
-//    copies (cp.async.bulk) completing on mbarriers.  A scale window starts at
+//  * Persistent, warp-specialised: warp 4 streams 16 KiB (int4 at D = 64:
+//    8 KiB) tiles of K and V codes plus the matching scale windows into a
+//    3-stage (4-stage) ring with 1-D bulk copies (cp.async.bulk) completing
+//    on mbarriers.  A scale window starts at
 //    the 16-byte boundary at or below the tile's first scale, so it may read up
 //    to 15 bytes on either side of the scale array -- always inside the
 //    16-byte blocks that hold the first / last scale, never used.
 //  * Each consumer warp owns a quarter of every tile.  A key row is split into
 //    32-byte chunks, one per lane (L = row_bytes/32 lanes per key: 64 int4 or
 //    32 int8 dims per lane, so the per-key work -- score reduction, softmax,
-//    scale loads -- is shared by many elements), and every lane handles 4 keys
+//    scale loads -- is shared by many elements; int4 at D = 64 uses 16-byte
+//    chunks, two lanes per key, for occupancy), and every lane handles 4 keys
 //    per tile.  Full tiles skip the per-key bounds masks.
 //  * q . k on integer dot-product units: q is held as a 2-plane fixed-point
 //    number (q * 2^e = hi * 256 + lo, hi signed byte, lo unsigned byte, 14
@@ -47,26 +49,41 @@ namespace {
 
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
-constexpr int kTileBytes = 16384;
 
 template <bool kInt4, int D>
 struct QCfg {
-  // 3-stage ring of 16 KiB K + V tiles, 2 CTAs per SM (shared memory and
-  // the int4 register budget both allow two).
-  static constexpr int kStages = 3;
-  static constexpr int kMinBlocks = 2;
   static constexpr int kRowBytes = kInt4 ? D / 2 : D;
-  static constexpr int kTK = kTileBytes / kRowBytes;       // keys per tile
-  static constexpr int kL = kRowBytes / 32;                // lanes per key row
+  // Bytes of a key row per lane: 32 (int8: 32 dims, int4 at D = 128: 64 dims).  int4 at
+  // D = 64 splits its 32-byte rows over two lanes of 16 bytes (32 dims): half the
+  // accumulators and q planes per lane, so three CTAs fit per SM instead of two (the
+  // one-lane-per-key form was latency-bound: 0.84 eligible warps per scheduler).
+  static constexpr int kLaneBytes = (kInt4 && D == 64) ? 16 : 32;
+  static constexpr int kL = kRowBytes / kLaneBytes;        // lanes per key row
   static constexpr int kKPS = 32 / kL;                     // keys per warp step
-  static constexpr int kDimsPerLane = kInt4 ? 64 : 32;
-  static constexpr int kWords = 8;                         // 32-bit words per lane chunk
+  static constexpr int kTK = 4 * kConsumerWarps * kKPS;    // keys per tile: 4 per lane
+  static constexpr int kTileBytes = kTK * kRowBytes;       // K (or V) codes of one tile (16 or 8 KiB)
+  static constexpr int kDimsPerLane = kInt4 ? 2 * kLaneBytes : kLaneBytes;
+  static constexpr int kWords = kLaneBytes / 4;            // 32-bit words per lane chunk
+  // 16 KiB tiles: a 3-stage ring, 2 CTAs per SM; 8 KiB tiles (int4, D = 64): 4 stages, 3 CTAs
+  static constexpr int kStages = kTileBytes == 16384 ? 3 : 4;
+  static constexpr int kMinBlocks = kTileBytes == 16384 ? 2 : 3;
   static constexpr int kScaleBytes = 2 * kTK + 32;         // scale window capacity
   static constexpr int kStageBytes = 2 * kTileBytes + 2 * kScaleBytes;
   static constexpr size_t kSmemBytes = 128 + size_t(kStages) * kStageBytes + 2 * kStages * sizeof(uint64_t) +
                                        size_t(kConsumerWarps) * (2 + D) * sizeof(float);
-  static_assert(kTK == 4 * kConsumerWarps * kKPS, "each lane owns 4 keys per tile");
+  static_assert(kTileBytes == 16384 || kTileBytes == 8192, "tile size");
 };
+
+// The kLaneBytes (16 or 32) bytes of a key row this lane handles, from shared memory.
+template <int kLaneBytes>
+__device__ __forceinline__ void lane_words(const uint8_t* p, uint32_t* w) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  if constexpr (kLaneBytes == 32) {
+    const uint4 b = *reinterpret_cast<const uint4*>(p + 16);
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+  }
+}
 
 // fp32 accumulate of p (fp16) times both halves of an fp16 pair:
 // lo += p * v.lo, hi += p * v.hi, with the sm_100 mixed-precision FMA.
@@ -169,9 +186,9 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         // visible to consumers that acquire the completed phase.
         mbar_arrive_expect_tx(&full[st], 2 * kv_bytes + kwin + vwin);
         bulk_g2s(base, Kr + size_t(k0) * C::kRowBytes, kv_bytes, &full[st]);
-        bulk_g2s(base + kTileBytes, Vr + size_t(k0) * C::kRowBytes, kv_bytes, &full[st]);
-        bulk_g2s(base + 2 * kTileBytes, reinterpret_cast<const void*>(ka0), kwin, &full[st]);
-        bulk_g2s(base + 2 * kTileBytes + C::kScaleBytes, reinterpret_cast<const void*>(va0), vwin, &full[st]);
+        bulk_g2s(base + C::kTileBytes, Vr + size_t(k0) * C::kRowBytes, kv_bytes, &full[st]);
+        bulk_g2s(base + 2 * C::kTileBytes, reinterpret_cast<const void*>(ka0), kwin, &full[st]);
+        bulk_g2s(base + 2 * C::kTileBytes + C::kScaleBytes, reinterpret_cast<const void*>(va0), vwin, &full[st]);
       }
     }
     if (!ok) {
@@ -183,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
 
   // ------------------------------------------------------------ consumers
   constexpr int kDPL = C::kDimsPerLane;
-  constexpr int kPW = kInt4 ? 16 : 8;  // q plane words per lane
+  constexpr int kPW = kInt4 ? 2 * C::kWords : C::kWords;  // q plane words per lane
   const int c = lane % C::kL;          // 32-byte chunk of the key row
   const int j = lane / C::kL;          // key slot
   const int kw = warp * (C::kTK / kConsumerWarps);
@@ -275,21 +292,20 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
     auto tile = [&](const uint8_t* base, int st, int k0, auto mask_tag) {
       constexpr bool kMask = decltype(mask_tag)::value;
       const uint8_t* kt = base;
-      const uint8_t* vt = base + kTileBytes;
-      const __half* kst = reinterpret_cast<const __half*>(base + 2 * kTileBytes) + stage_off[st][0];
-      const __half* vst = reinterpret_cast<const __half*>(base + 2 * kTileBytes + C::kScaleBytes) + stage_off[st][1];
+      const uint8_t* vt = base + C::kTileBytes;
+      const __half* kst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes) + stage_off[st][0];
+      const __half* vst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes + C::kScaleBytes) + stage_off[st][1];
       float sco[4];
 #pragma unroll
       for (int sp = 0; sp < 4; ++sp) {
         const int kl = kw + j + C::kKPS * sp;
-        const uint4 k0v = *reinterpret_cast<const uint4*>(kt + kl * C::kRowBytes + 32 * c);
-        const uint4 k1v = *reinterpret_cast<const uint4*>(kt + kl * C::kRowBytes + 32 * c + 16);
-        const uint32_t kwd[8] = {k0v.x, k0v.y, k0v.z, k0v.w, k1v.x, k1v.y, k1v.z, k1v.w};
+        uint32_t kwd[C::kWords];
+        lane_words<C::kLaneBytes>(kt + kl * C::kRowBytes + C::kLaneBytes * c, kwd);
         int acc;
         if (kInt4) {
           int ahe = 0, aho = 0, ale = 0, alo = 0;
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
+          for (int w = 0; w < C::kWords; ++w) {
             const uint32_t x = kwd[w] ^ 0x88888888u;
             const uint32_t ev = x & 0x0F0F0F0Fu;  // (code + 8) of even dims
             const uint32_t od = x & 0xF0F0F0F0u;  // 16 * (code + 8) of odd dims
@@ -302,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         } else {
           int ah = 0, al = 0;
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
+          for (int w = 0; w < C::kWords; ++w) {
             ah = dp4a_ss(qh[w % kPW], kwd[w], ah);
             al = dp4a_us(ql[w % kPW], kwd[w], al);
           }
@@ -347,9 +363,8 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         l_run += p;
         const float pv = p * vs4[sp] * vsc;
         const uint16_t ph = __half_as_ushort(__float2half_rn(pv));
-        const uint4 v0v = *reinterpret_cast<const uint4*>(vt + kl * C::kRowBytes + 32 * c);
-        const uint4 v1v = *reinterpret_cast<const uint4*>(vt + kl * C::kRowBytes + 32 * c + 16);
-        const uint32_t vwd[8] = {v0v.x, v0v.y, v0v.z, v0v.w, v1v.x, v1v.y, v1v.z, v1v.w};
+        uint32_t vwd[C::kWords];
+        lane_words<C::kLaneBytes>(vt + kl * C::kRowBytes + C::kLaneBytes * c, vwd);
         if (kInt4) {
           // nibble n of word w is dim 8w + n.  One logic op leaves the nibble pair
           // (n, n+4) in offset binary as fp16 subnormals s*(code+8) * 2^-24, s = 1
@@ -360,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
           add_half(bias_lo, ph);
           add_half(bias_hi, ph16);
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
+          for (int w = 0; w < C::kWords; ++w) {
             const uint32_t x = vwd[w];
             const uint32_t y = x >> 8;
             const uint32_t a04 = (x & 0x000F000Fu) ^ 0x00080008u;
@@ -379,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
           // are); the offset, 128 * 2^-24 * sum(p), leaves once per unit.
           add_half(bias_lo, ph);
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
+          for (int w = 0; w < C::kWords; ++w) {
             const uint32_t x = vwd[w] ^ 0x80808080u;
             const uint32_t a01 = __byte_perm(x, 0u, 0x4140u);
             const uint32_t a23 = __byte_perm(x, 0u, 0x4342u);
