@@ -53,11 +53,20 @@ __device__ __forceinline__ int quant_code(float x, float s) {
   return static_cast<int>(fminf(fmaxf(rr, -float(Q)), float(Q)));
 }
 
-// Code of x for a normal fp16 scale s (y = approximate 1/s): round(fp16(x / s)).
-__device__ __forceinline__ int quant_code_fast(float x, float s, float y) {
+// fp32 quotient x / s for a normal fp16 scale s (y = approximate 1/s), rounded as IEEE division.
+__device__ __forceinline__ float quot_fast(float x, float s, float y) {
   const float q0 = x * y;
-  const float q1 = fmaf(fmaf(-s, q0, x), y, q0);
-  return __half2int_rn(__float2half_rn(q1));
+  return fmaf(fmaf(-s, q0, x), y, q0);
+}
+
+// Codes of two fp32 quotients with |q| <= 128: fp16(q) (the reference's rounding of X / s),
+// then round half to even to an integer by one fp16 addition of 1536 = 1.5 * 2^10 (the sums
+// lie in [1408, 1664], where fp16 spacing is 1 and 1536 is even); each code is then the low
+// byte of its half's bit pattern (1536 + k has mantissa 512 + k: low byte = k mod 256).
+__device__ __forceinline__ uint32_t code_pair_bits(float q_lo, float q_hi) {
+  const __half2 r = __floats2half2_rn(q_lo, q_hi);
+  const __half2 m = __hadd2(r, __half2half2(__ushort_as_half(0x6600u)));  // + 1536
+  return *reinterpret_cast<const uint32_t*>(&m);  // byte 0: code(q_lo), byte 2: code(q_hi)
 }
 
 __device__ __forceinline__ float rcp_approx(float s) {
@@ -98,10 +107,6 @@ struct QuantPlace {
 // Tokens whose 16-byte loads each lane of the quantizer keeps in flight.
 constexpr int kUnroll = 3;
 
-// Four codes (low bytes of c0..c3) as one word, c0 in the low byte.
-__device__ __forceinline__ uint32_t pack4(int c0, int c1, int c2, int c3) {
-  return __byte_perm(__byte_perm(c0, c1, 0x0040u), __byte_perm(c2, c3, 0x0040u), 0x5410u);
-}
 
 // Vectorised path: D in {64, 128, 256}; LPR = D/8 lanes per token, each with 8
 // consecutive elements.  Persistent: warp w handles tokens w*RPW + j + i*stride.
@@ -150,32 +155,31 @@ __global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __re
         orow = (row / pl.T) * pl.cap + pos;
       }
       if (c == 0) scales[orow] = sh;
-      int q[8];
+      // cb[i]: codes of elements 2i (byte 0) and 2i + 1 (byte 2)
+      uint32_t cb[4];
       if (normal_fp16_scale(sc)) {
         const float y = rcp_approx(sc);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 f = __half22float2(h2[i]);
-          q[2 * i] = quant_code_fast(f.x, sc, y);
-          q[2 * i + 1] = quant_code_fast(f.y, sc, y);
+          cb[i] = code_pair_bits(quot_fast(f.x, sc, y), quot_fast(f.y, sc, y));
         }
       } else {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 f = __half22float2(h2[i]);
-          q[2 * i] = quant_code<Q>(f.x, sc);
-          q[2 * i + 1] = quant_code<Q>(f.y, sc);
+          cb[i] = (uint32_t(quant_code<Q>(f.x, sc)) & 0xFFu) | ((uint32_t(quant_code<Q>(f.y, sc)) & 0xFFu) << 16);
         }
       }
+      const uint32_t w0 = __byte_perm(cb[0], cb[1], 0x6420u);  // elements 0..3, one byte each
+      const uint32_t w1 = __byte_perm(cb[2], cb[3], 0x6420u);  // elements 4..7
       if (kInt4) {
-        // nibble pairs: byte t = (q[2t] & 0xF) | (q[2t+1] << 4)
-        const uint32_t lo = pack4(q[0], q[2], q[4], q[6]) & 0x0F0F0F0Fu;
-        const uint32_t hi = (pack4(q[1], q[3], q[5], q[7]) << 4) & 0xF0F0F0F0u;
-        const uint32_t w = lo | hi;  // byte t holds elements 2t, 2t+1: bytes 0..3 = elements 0..7
-        __stcs(reinterpret_cast<unsigned int*>(codes) + (orow * D) / 8 + c, w);
+        // byte t = (code[2t] & 0xF) | (code[2t+1] << 4): even elements from bytes 0/2, odd from 1/3
+        const uint32_t ev = __byte_perm(w0, w1, 0x6420u) & 0x0F0F0F0Fu;
+        const uint32_t od = (__byte_perm(w0, w1, 0x7531u) << 4) & 0xF0F0F0F0u;
+        __stcs(reinterpret_cast<unsigned int*>(codes) + (orow * D) / 8 + c, ev | od);
       } else {
-        const uint2 w = make_uint2(pack4(q[0], q[1], q[2], q[3]), pack4(q[4], q[5], q[6], q[7]));
-        __stcs(reinterpret_cast<uint2*>(codes) + (orow * D) / 8 + c, w);
+        __stcs(reinterpret_cast<uint2*>(codes) + (orow * D) / 8 + c, make_uint2(w0, w1));
       }
     }
   }
