@@ -665,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
         if (__any_sync(0xffffffffu, m_new > m_run || vmax * vsc > 16384.f)) {
           vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // keys depend on t only
           vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-          const float nsc = vmax * vsc > 16384.f ? ldexpf(1.f, 13 - ilogbf(vmax)) : vsc;  // warp-uniform
+          const float nsc = vmax * vsc > 16384.f ? frame_for(vmax) : vsc;  // warp-uniform
           const float ratio = nsc / vsc;  // a power of two: exact
           vsc = nsc;
           const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);

@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       // frame: lane-local), so the loop carries one copy of the per-dimension multiply
       if (m_new > m_run || grow_v) {
         const float alpha = m_new > m_run ? ex2(m_run - m_new) : 1.f;
-        const float nsc = grow_v ? ldexpf(1.f, 13 - ilogbf(vmax)) : vsc;
+        const float nsc = grow_v ? frame_for(vmax) : vsc;
         const float f = alpha * (nsc / vsc);  // the frame ratio is a power of two: exact
 #pragma unroll
         for (int d = 0; d < kDPL; ++d) o[d] *= f;

@@ -183,6 +183,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^(13 - floor(log2(v))) for a positive normal float v: the power of two that puts v
+// in [2^13, 2^14) -- exponent-field arithmetic, no library call in the hot loops.
+__device__ __forceinline__ float frame_for(float v) {
+  const int e = (__float_as_int(v) >> 23) & 0xFF;  // biased exponent of v
+  return __int_as_float((127 + 127 + 13 - e) << 23);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
