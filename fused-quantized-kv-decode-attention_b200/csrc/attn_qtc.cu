@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
     // lowered (O rescaled exactly) whenever a key's V scale times vsc would pass 2^14, so the operand
     // stays in fp16's normal range for any V magnitude (small V no longer rounds to subnormals,
     // which the fp16 MMA also runs slower on); O leaves the frame (/ vsc) in the epilogue.
-    float vsc = 1099511627776.f;  // 2^40
+    float vsc = 1099511627776.f, vk = 40.f;  // 2^40 = 2^vk; ex2(s - (m - vk)) = p * vsc, l sums the same
 
     for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
       const int st = it % C::kStages;
@@ -665,11 +665,13 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
         if (__any_sync(0xffffffffu, m_new > m_run || vmax * vsc > 16384.f)) {
           vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // keys depend on t only
           vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-          const float nsc = vmax * vsc > 16384.f ? frame_for(vmax) : vsc;  // warp-uniform
+          float nk = vk;
+          const float nsc = vmax * vsc > 16384.f ? frame_for(vmax, nk) : vsc;  // warp-uniform
           const float ratio = nsc / vsc;  // a power of two: exact
           vsc = nsc;
+          vk = nk;
           const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
-          l_run *= alpha;
+          l_run *= alpha * ratio;
           m_run = m_new;
           // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
           const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * t) * 4) * ratio;
@@ -682,14 +684,14 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
             o[i][3] *= a_hi;
           }
         }
-        const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+        const float mu = ((m_run == -INFINITY) ? 0.f : m_run) - vk;  // ex2(s - mu) = p * vsc
         uint32_t pb[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
           const float p0 = valid[j][0] ? ex2(sc[j][0] - mu) : 0.f;
           const float p1 = valid[j][1] ? ex2(sc[j][1] - mu) : 0.f;
           l_run += p0 + p1;
-          pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] * vsc : 0.f, valid[j][1] ? p1 * vs[j][1] * vsc : 0.f);
+          pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] : 0.f, valid[j][1] ? p1 * vs[j][1] : 0.f);
         }
 
         // ---- O^T += V^T P^T
@@ -720,6 +722,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
     } else {
+      l_run *= 1.f / vsc;  // leave the V-scale frame (a power of two: exact)
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     }

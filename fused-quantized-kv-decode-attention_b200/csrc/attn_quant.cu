@@ -280,12 +280,14 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
     // sums of the fp16 p (int8 codes, int4 low nibbles) and p / 16 (int4 high nibbles) this
     // lane multiplied, for the offset of the subnormal code fields (see the P.V step)
     float bias_lo = 0.f, bias_hi = 0.f;
-    // p * vscale enters the fp16 FMA operand multiplied by vsc, a power of two that keeps it in
-    // fp16's normal range: vsc is lowered (o and the bias sums rescaled exactly) whenever a key's
-    // V scale times vsc would pass 2^14, so p * vscale * vsc <= 2^14 (p <= 1), and otherwise stays
-    // as large as the largest V scale so far allows -- a small V (|V| ~ 1e-4) no longer rounds to
-    // fp16 subnormals.  The lane's o leaves the frame (/ vsc) before the cross-lane reduction.
-    float vsc = 1099511627776.f;  // 2^40: any nonzero fp16 V scale lowers it on its first tile
+    // p * vscale enters the fp16 FMA operand multiplied by vsc = 2^vk, a power of two that keeps
+    // it in fp16's normal range: vsc is lowered (o, l and the bias sums rescaled exactly) whenever
+    // a key's V scale times vsc would pass 2^14, so p * vscale * vsc <= 2^14 (p <= 1), and
+    // otherwise stays as large as the largest V scale so far allows -- a small V (|V| ~ 1e-4) no
+    // longer rounds to fp16 subnormals.  The frame costs nothing per key: it is folded into the
+    // exponent, ex2(s - (m - vk)) = p * vsc, and l sums the same scaled values; the lane's o and l
+    // leave the frame (/ vsc) before the cross-lane reduction.
+    float vsc = 1099511627776.f, vk = 40.f;  // 2^40: any nonzero fp16 V scale lowers it on its first tile
 
     // One tile of this warp's keys; kMask adds the per-key bound checks that
     // only the last (partial) tile of a unit needs.
@@ -345,23 +347,25 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       // frame: lane-local), so the loop carries one copy of the per-dimension multiply
       if (m_new > m_run || grow_v) {
         const float alpha = m_new > m_run ? ex2(m_run - m_new) : 1.f;
-        const float nsc = grow_v ? frame_for(vmax) : vsc;
+        float nk = vk;
+        const float nsc = grow_v ? frame_for(vmax, nk) : vsc;
         const float f = alpha * (nsc / vsc);  // the frame ratio is a power of two: exact
 #pragma unroll
         for (int d = 0; d < kDPL; ++d) o[d] *= f;
-        l_run *= alpha;
+        l_run *= f;
         bias_lo *= f;
         bias_hi *= f;
         m_run = m_new;
         vsc = nsc;
+        vk = nk;
       }
-      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+      const float mu = ((m_run == -INFINITY) ? 0.f : m_run) - vk;  // ex2(s - mu) = p * vsc
 #pragma unroll
       for (int sp = 0; sp < 4; ++sp) {
         const int kl = kw + j + C::kKPS * sp;
         const float p = ex2(sco[sp] - mu);
         l_run += p;
-        const float pv = p * vs4[sp] * vsc;
+        const float pv = p * vs4[sp];
         const uint16_t ph = __half_as_ushort(__float2half_rn(pv));
         uint32_t vwd[C::kWords];
         lane_words<C::kLaneBytes>(vt + kl * C::kRowBytes + C::kLaneBytes * c, vwd);
@@ -424,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
     // scale the subnormal fields back, remove their offset (int4: + 8; int8: + 128) and leave
     // the lane's V-scale frame
     const float inv_vsc = 1.f / vsc;  // a power of two: exact
+    l_run *= inv_vsc;
     if (kInt4) {
 #pragma unroll
       for (int d = 0; d < kDPL; ++d)

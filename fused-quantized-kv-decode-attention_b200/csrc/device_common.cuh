@@ -183,10 +183,11 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^(13 - floor(log2(v))) for a positive normal float v: the power of two that puts v
-// in [2^13, 2^14) -- exponent-field arithmetic, no library call in the hot loops.
-__device__ __forceinline__ float frame_for(float v) {
+// The power of two 2^k, k = 13 - floor(log2(v)), that puts a positive normal float v in
+// [2^13, 2^14), and k itself (as a float) -- exponent-field arithmetic, no library call.
+__device__ __forceinline__ float frame_for(float v, float& k) {
   const int e = (__float_as_int(v) >> 23) & 0xFF;  // biased exponent of v
+  k = float(127 + 13 - e);
   return __int_as_float((127 + 127 + 13 - e) << 23);
 }
 
