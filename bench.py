@@ -623,6 +623,18 @@ def run_llama(args, w) -> int:
     ours_tokens = torch.cat([dec.out_tokens[:, P:P + T]], dim=1).clone()
     decode_tps = B * (T - 1) / (best_dec / 1e3)
     e2e_tps = B * T / ((best_pre + best_dec) / 1e3)
+    if args.profile_steps:
+        # profiling run: a CUDA-profiler range (ncu --profile-from-start off) around K decode steps,
+        # i.e. K replays of the step's graph after a fresh prefill; nothing else runs
+        dec.prefill(ids)
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.start()
+        dec.generate(args.profile_steps)
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        print(json.dumps({"workload": "llama", "batch": B, "kv": args.kv, "profile_steps": args.profile_steps,
+                          "decode_tok_s": round(decode_tps, 2)}), flush=True)
+        return 0
 
     # ---- stock transformers generate (SDPA) and the reference-style hook
     def hf_generate_tps(impl):
@@ -964,6 +976,9 @@ def main() -> int:
     ap.add_argument("--split-mode", default="auto", choices=["auto", "combine", "cluster"],
                     help="how split plans merge (fqkv_set_split_mode): the library's choice, partials + combine "
                          "kernel, or thread-block cluster")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="llama workload: after timing, run this many decode steps inside a CUDA-profiler range "
+                         "(for ncu --profile-from-start off) and exit without the transformers comparison")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-config sweep of the default run (1 GPU: the 'configs' key; several "
                          "GPUs: the 'multi_gpu' key -- KV-head-sharded config 4 and tensor-parallel config 5)")

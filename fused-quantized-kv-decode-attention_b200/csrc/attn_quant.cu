@@ -280,14 +280,15 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
     // sums of the fp16 p (int8 codes, int4 low nibbles) and p / 16 (int4 high nibbles) this
     // lane multiplied, for the offset of the subnormal code fields (see the P.V step)
     float bias_lo = 0.f, bias_hi = 0.f;
-    // p * vscale enters the fp16 FMA operand multiplied by vsc = 2^vk, a power of two that keeps
-    // it in fp16's normal range: vsc is lowered (o, l and the bias sums rescaled exactly) whenever
-    // a key's V scale times vsc would pass 2^14, so p * vscale * vsc <= 2^14 (p <= 1), and
-    // otherwise stays as large as the largest V scale so far allows -- a small V (|V| ~ 1e-4) no
-    // longer rounds to fp16 subnormals.  The frame costs nothing per key: it is folded into the
-    // exponent, ex2(s - (m - vk)) = p * vsc, and l sums the same scaled values; the lane's o and l
-    // leave the frame (/ vsc) before the cross-lane reduction.
+    // p * vscale enters the fp16 FMA operand multiplied by vsc = 2^vk, a warp-uniform power of two
+    // that keeps it in fp16's normal range: vsc is lowered (o, l and the bias sums rescaled
+    // exactly) whenever a key's V scale passes vthr = 2^14 / vsc, so p * vscale * vsc <= 2^14
+    // (p <= 1), and otherwise stays as large as the largest V scale so far allows -- a small V
+    // (|V| ~ 1e-4) no longer rounds to fp16 subnormals.  The frame costs nothing per key: it is
+    // folded into the exponent, ex2(s - (m - vk)) = p * vsc, and l sums the same scaled values;
+    // the lane's o and l leave the frame (/ vsc) before the cross-lane reduction.
     float vsc = 1099511627776.f, vk = 40.f;  // 2^40: any nonzero fp16 V scale lowers it on its first tile
+    float vthr = 1.4901161193847656e-8f;     // 2^14 / vsc = 2^-26
 
     // One tile of this warp's keys; kMask adds the per-key bound checks that
     // only the last (partial) tile of a unit needs.
@@ -297,6 +298,15 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       const uint8_t* vt = base + C::kTileBytes;
       const __half* kst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes) + stage_off[st][0];
       const __half* vst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes + C::kScaleBytes) + stage_off[st][1];
+      // the V scales of this lane's four keys first, so that the frame test below does not wait
+      // for their loads
+      float vs4[4];
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        const int kl = kw + j + C::kKPS * sp;
+        vs4[sp] = (!kMask || (k0 + kl) < hi) ? __half2float(vst[kl]) : 0.f;
+      }
+      float vmax = fmaxf(fmaxf(vs4[0], vs4[1]), fmaxf(vs4[2], vs4[3]));
       float sco[4];
 #pragma unroll
       for (int sp = 0; sp < 4; ++sp) {
@@ -335,17 +345,12 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
 #pragma unroll
       for (int off = C::kL; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       const float m_new = fmaxf(m_run, mx);
-      float vs4[4];
+      // one warp-uniform rescale block for both causes (a larger running maximum; a V scale above
+      // the frame's threshold), so the loop carries one copy of the per-dimension multiply
+      if (__any_sync(0xffffffffu, m_new > m_run || vmax > vthr)) {
 #pragma unroll
-      for (int sp = 0; sp < 4; ++sp) {
-        const int kl = kw + j + C::kKPS * sp;
-        vs4[sp] = (!kMask || (k0 + kl) < hi) ? __half2float(vst[kl]) : 0.f;
-      }
-      const float vmax = fmaxf(fmaxf(vs4[0], vs4[1]), fmaxf(vs4[2], vs4[3]));
-      const bool grow_v = vmax * vsc > 16384.f;  // lane-local, rare: the V frame must move down
-      // one rescale block for both causes (a larger running maximum: warp-uniform; a lower V
-      // frame: lane-local), so the loop carries one copy of the per-dimension multiply
-      if (m_new > m_run || grow_v) {
+        for (int off = 1; off < 32; off <<= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, off));
+        const bool grow_v = vmax > vthr;  // rare: the V frame must move down
         const float alpha = m_new > m_run ? ex2(m_run - m_new) : 1.f;
         float nk = vk;
         const float nsc = grow_v ? frame_for(vmax, nk) : vsc;
@@ -358,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         m_run = m_new;
         vsc = nsc;
         vk = nk;
+        vthr = 16384.f / nsc;  // a power of two: exact
       }
       const float mu = ((m_run == -INFINITY) ? 0.f : m_run) - vk;  // ex2(s - mu) = p * vsc
 #pragma unroll
