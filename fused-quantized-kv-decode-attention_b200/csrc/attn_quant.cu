@@ -55,7 +55,7 @@ struct QCfg {
   static constexpr int kRowBytes = kInt4 ? D / 2 : D;
   // Bytes of a key row per lane: 32 (int8: 32 dims, int4 at D = 128: 64 dims).  int4 at
   // D = 64 splits its 32-byte rows over two lanes of 16 bytes (32 dims): half the
-  // accumulators and q planes per lane, so three CTAs fit per SM instead of two (the
+  // accumulators and q planes per lane, so four CTAs fit per SM instead of two (the
   // one-lane-per-key form was latency-bound: 0.84 eligible warps per scheduler).
   static constexpr int kLaneBytes = (kInt4 && D == 64) ? 16 : 32;
   static constexpr int kL = kRowBytes / kLaneBytes;        // lanes per key row
@@ -64,9 +64,12 @@ struct QCfg {
   static constexpr int kTileBytes = kTK * kRowBytes;       // K (or V) codes of one tile (16 or 8 KiB)
   static constexpr int kDimsPerLane = kInt4 ? 2 * kLaneBytes : kLaneBytes;
   static constexpr int kWords = kLaneBytes / 4;            // 32-bit words per lane chunk
-  // 16 KiB tiles: a 3-stage ring, 2 CTAs per SM; 8 KiB tiles (int4, D = 64): 4 stages, 3 CTAs
-  static constexpr int kStages = kTileBytes == 16384 ? 3 : 4;
-  static constexpr int kMinBlocks = kTileBytes == 16384 ? 2 : 3;
+  // 16 KiB tiles: a 3-stage ring, 2 CTAs per SM.  8 KiB tiles (int4, D = 64): 3 stages and 4 CTAs
+  // per SM (96 registers, no spills): the kernel is issue- and latency-bound, so 16 consumer warps
+  // per SM beat 12 with a deeper ring (481 -> 466 us at R=8192, N=4096 on one box; 5 CTAs with
+  // 2 stages spill 192 bytes and ran 526 us)
+  static constexpr int kStages = 3;
+  static constexpr int kMinBlocks = kTileBytes == 16384 ? 2 : 4;
   static constexpr int kScaleBytes = 2 * kTK + 32;         // scale window capacity
   static constexpr int kStageBytes = 2 * kTileBytes + 2 * kScaleBytes;
   static constexpr size_t kSmemBytes = 128 + size_t(kStages) * kStageBytes + 2 * kStages * sizeof(uint64_t) +
