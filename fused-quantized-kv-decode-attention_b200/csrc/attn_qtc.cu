@@ -44,6 +44,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include "device_common.cuh"
 #include "kernels.h"
@@ -465,252 +466,259 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
         if (!alive && lane == 0) abort_flag = 1;
       }
       if (!alive) continue;
-      const uint8_t* kt = ring + size_t(st) * C::kStageBytes;
-      const uint8_t* vt = kt + C::kTileBytes;
-      const __half* kst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes) + stage_off[st][0];
-      const __half* vst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes + C::kScaleBytes) +
-                          stage_off[st][1];
+      // the tile's body, compiled twice: full tiles (all but the last of a unit) without the
+      // per-key bound checks
+      auto tile = [&](auto mask_tag) {
+        constexpr bool kMask = decltype(mask_tag)::value;
+        const uint8_t* kt = ring + size_t(st) * C::kStageBytes;
+        const uint8_t* vt = kt + C::kTileBytes;
+        const __half* kst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes) + stage_off[st][0];
+        const __half* vst = reinterpret_cast<const __half*>(kt + 2 * C::kTileBytes + C::kScaleBytes) +
+                            stage_off[st][1];
 
-      // ---- scores of this warp's KPW keys (rows r0 ..) in integers.
-      // Several heads: S = Q K^T, n-tile j holds keys 8j + 2t + e of head g.
-      // One head (G1): S^T = K Q^T, m-tile j/2 holds (rows g / g + 8) keys
-      // g1_key(g, j + 0 / 1) in lanes t < 3 (columns 2t / 2t + 1: hi / lo
-      // plane); sc[j][e] is key g1_key(g, j + e) for even j (odd j unused).
-      float sc[NJ][2];
-      bool valid[NJ][2];
-      float mx = -INFINITY;
-      if constexpr (G1) {
+        // ---- scores of this warp's KPW keys (rows r0 ..) in integers.
+        // Several heads: S = Q K^T, n-tile j holds keys 8j + 2t + e of head g.
+        // One head (G1): S^T = K Q^T, m-tile j/2 holds (rows g / g + 8) keys
+        // g1_key(g, j + 0 / 1) in lanes t < 3 (columns 2t / 2t + 1: hi / lo
+        // plane); sc[j][e] is key g1_key(g, j + e) for even j (odd j unused).
+        float sc[NJ][2];
+        bool valid[NJ][2];
+        float mx = -INFINITY;
+        if constexpr (G1) {
 #pragma unroll
-        for (int mt = 0; mt < KP; ++mt) {
-          uint32_t kw[2][KB / 4];  // keys r0 + g1_key(g, 2mt) and r0 + g1_key(g, 2mt + 1)
+          for (int mt = 0; mt < KP; ++mt) {
+            uint32_t kw[2][KB / 4];  // keys r0 + g1_key(g, 2mt) and r0 + g1_key(g, 2mt + 1)
 #pragma unroll
-          for (int e = 0; e < 2; ++e)
+            for (int e = 0; e < 2; ++e)
 #pragma unroll
-            for (int c = 0; c < KB; c += 16)
-              lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + g1_key(g, 2 * mt + e), t * KB + c), kw[e] + c / 4);
+              for (int c = 0; c < KB; c += 16)
+                lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + g1_key(g, 2 * mt + e), t * KB + c), kw[e] + c / 4);
+            int acc[4] = {0, 0, 0, 0};
+            if constexpr (!I4) {
+#pragma unroll
+              for (int kk = 0; kk < KS; ++kk) {
+                const uint32_t af[4] = {kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1]};
+                mma_i8_16832<false, false>(acc, af, qa[kk][0], qa[kk][1]);
+              }
+            } else {
+              int acch[4] = {0, 0, 0, 0};
+#pragma unroll
+              for (int kk = 0; kk < KS / 2; ++kk) {
+                const uint32_t al[4] = {(kw[0][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu, (kw[1][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu,
+                                        (kw[0][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu,
+                                        (kw[1][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu};
+                const uint32_t ah[4] = {kw[0][2 * kk] & 0xF0F0F0F0u, kw[1][2 * kk] & 0xF0F0F0F0u,
+                                        kw[0][2 * kk + 1] & 0xF0F0F0F0u, kw[1][2 * kk + 1] & 0xF0F0F0F0u};
+                mma_i8_16832<true, false>(acc, al, qa[kk][0], qa[kk][1]);
+                mma_i8_16832<false, false>(acch, ah, qa[KS / 2 + kk][0], qa[KS / 2 + kk][1]);
+              }
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[e] = 16 * acc[e] + acch[e];
+            }
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = r0 + g1_key(g, 2 * mt + e);
+              valid[2 * mt][e] = t < 3 && (!kMask || (k0 + key) < hi);
+              const int si = acc[2 * e] * 256 + acc[2 * e + 1] - (I4 ? qbias : 0);
+              const float s = float(si) * (__half2float(kst[key]) * hf);
+              sc[2 * mt][e] = valid[2 * mt][e] ? s : -INFINITY;
+              mx = fmaxf(mx, sc[2 * mt][e]);
+            }
+          }
+        } else {
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          uint32_t kw[KB / 4];  // key r0 + 8j + g, bytes [t*KB, (t+1)*KB)
+#pragma unroll
+          for (int c = 0; c < KB; c += 16)
+            lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + 8 * j + g, t * KB + c), kw + c / 4);
           int acc[4] = {0, 0, 0, 0};
           if constexpr (!I4) {
 #pragma unroll
-            for (int kk = 0; kk < KS; ++kk) {
-              const uint32_t af[4] = {kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1]};
-              mma_i8_16832<false, false>(acc, af, qa[kk][0], qa[kk][1]);
-            }
+            for (int kk = 0; kk < KS; ++kk) mma_i8_16832<false, false>(acc, qa[kk], kw[2 * kk], kw[2 * kk + 1]);
           } else {
             int acch[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int kk = 0; kk < KS / 2; ++kk) {
-              const uint32_t al[4] = {(kw[0][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu, (kw[1][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu,
-                                      (kw[0][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu,
-                                      (kw[1][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu};
-              const uint32_t ah[4] = {kw[0][2 * kk] & 0xF0F0F0F0u, kw[1][2 * kk] & 0xF0F0F0F0u,
-                                      kw[0][2 * kk + 1] & 0xF0F0F0F0u, kw[1][2 * kk + 1] & 0xF0F0F0F0u};
-              mma_i8_16832<true, false>(acc, al, qa[kk][0], qa[kk][1]);
-              mma_i8_16832<false, false>(acch, ah, qa[KS / 2 + kk][0], qa[KS / 2 + kk][1]);
+              const uint32_t w0 = kw[2 * kk], w1 = kw[2 * kk + 1];
+              mma_i8_16832<false, true>(acc, qa[kk], (w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu);
+              mma_i8_16832<false, false>(acch, qa[KS / 2 + kk], w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u);
             }
+            // 16 * (low sum - 8 sum q) + high sum (a multiple of 16); hf carries the 1/16
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[e] = 16 * acc[e] + acch[e];
           }
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int key = r0 + g1_key(g, 2 * mt + e);
-            valid[2 * mt][e] = t < 3 && (k0 + key) < hi;
-            const int si = acc[2 * e] * 256 + acc[2 * e + 1] - (I4 ? qbias : 0);
+            const int key = r0 + 8 * j + 2 * t + e;
+            valid[j][e] = !kMask || (k0 + key) < hi;
+            const int si = I4 ? acc[e] * 256 + acc[2 + e] - qbias : acc[e] * 256 + acc[2 + e];
             const float s = float(si) * (__half2float(kst[key]) * hf);
-            sc[2 * mt][e] = valid[2 * mt][e] ? s : -INFINITY;
-            mx = fmaxf(mx, sc[2 * mt][e]);
+            sc[j][e] = valid[j][e] ? s : -INFINITY;
+            mx = fmaxf(mx, sc[j][e]);
           }
         }
-      } else {
+        }
+        if constexpr (G1) {
+          // ---- V fragments: segment sg = bytes 16sg .. 16sg+15 of the 32 keys' rows; thread (g, t)
+          // receives bytes 2g, 2g+1 of k-slots 4t+{0,1} (matrix 0), 4t+{2,3} (1), 16+4t+{0,1} (2), 16+4t+{2,3} (3)
+          uint32_t vr[NSEG][4];
+          const uint32_t vt_s = smem_u32(vt);
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        uint32_t kw[KB / 4];  // key r0 + 8j + g, bytes [t*KB, (t+1)*KB)
+          for (int sg = 0; sg < NSEG; ++sg)
+            ldmatrix_x4_trans(vt_s + (v_row_off ^ uint32_t(sg << 4)), vr[sg][0], vr[sg][1], vr[sg][2], vr[sg][3]);
+          float vs4[4];
 #pragma unroll
-        for (int c = 0; c < KB; c += 16)
-          lds_words<(KB < 16 ? KB : 16)>(kt + tile_off<RB>(r0 + 8 * j + g, t * KB + c), kw + c / 4);
-        int acc[4] = {0, 0, 0, 0};
-        if constexpr (!I4) {
+          for (int i = 0; i < 4; ++i) vs4[i] = __half2float(vst[r0 + g1_key(g, i)]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
+
+          // ---- frames: a key above m_run + headroom moves the reference maximum, a product
+          // p * vs above the fixed-point range (or a full frame) the scale; either ends the frame
+          // (lane-local tests and a vote; the warp-wide maxima only when a frame ends)
+          if (__any_sync(0xffffffffu, mx > m_run + kG1Headroom)) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // lanes t < 3 hold the same scores
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float rescale = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
+            g1_flush<NSEG>(oi, bsum, so, rescale, inv_ps, g, t);
+            l_run *= rescale;
+            m_run = mx;
+            ftiles = 0;
+          }
+          float pv[4];
+          float pvm = 0.f;
 #pragma unroll
-          for (int kk = 0; kk < KS; ++kk) mma_i8_16832<false, false>(acc, qa[kk], kw[2 * kk], kw[2 * kk + 1]);
+          for (int i = 0; i < 4; ++i) {
+            const bool v_ok = valid[2 * (i >> 1)][i & 1];
+            const float pr = v_ok ? ex2(sc[2 * (i >> 1)][i & 1] - m_run) : 0.f;
+            l_run += pr;
+            pv[i] = v_ok ? pr * vs4[i] : 0.f;
+            pvm = fmaxf(pvm, pv[i]);
+          }
+          if (__any_sync(0xffffffffu, pvm * ps > kG1VLim || (ps == 0.f && pvm > 0.f)) || ftiles >= kG1FrameTiles) {
+            pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 1));
+            pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 4));
+            pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 8));
+            pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 16));
+            g1_flush<NSEG>(oi, bsum, so, 1.f, inv_ps, g, t);
+            if (pvm > 0.f) {
+              const float pb_ = 1.25f * fmaxf(pvm, 1e-30f);
+              ps = kG1VLim / pb_;
+              inv_ps = pb_ / kG1VLim;
+            }
+            ftiles = 0;
+          }
+          ++ftiles;
+
+          // ---- P in three planes; lane t < 3 packs plane t of its four keys (k-slots 4g + i)
+          // and spreads them as the B operand (column c = plane c, c < 3)
+          uint32_t fw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) fw[i] = __float_as_uint(fmaf(pv[i], ps, kG1Magic));
+          const uint32_t px = __byte_perm(fw[0], fw[1], psel);
+          const uint32_t py = __byte_perm(fw[2], fw[3], psel);
+          const uint32_t pw = (__byte_perm(px, py, 0x5410u) ^ pxor) & pmask;
+          bsum = __dp4a(int(pw), 0x01010101, bsum);
+          const uint32_t pb0 = __shfl_sync(0xffffffffu, pw, 4 * t + (g & 3));
+          const uint32_t pb1 = __shfl_sync(0xffffffffu, pw, 16 + 4 * t + (g & 3));
+
+          // ---- O^T += V^T P^T on the integer tensor cores: A rows g / g + 8 = bytes 2g / 2g + 1 of
+          // the segment, four k-slots per register (byte transposes of the ldmatrix pairs)
+#pragma unroll
+          for (int sg = 0; sg < NSEG; ++sg) {
+            const uint32_t w0 = __byte_perm(vr[sg][0], vr[sg][1], 0x6420u);
+            const uint32_t w1 = __byte_perm(vr[sg][0], vr[sg][1], 0x7531u);
+            const uint32_t w2 = __byte_perm(vr[sg][2], vr[sg][3], 0x6420u);
+            const uint32_t w3 = __byte_perm(vr[sg][2], vr[sg][3], 0x7531u);
+            const uint32_t al[4] = {(w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu,
+                                    (w2 ^ 0x08080808u) & 0x0F0F0F0Fu, (w3 ^ 0x08080808u) & 0x0F0F0F0Fu};
+            const uint32_t ah[4] = {w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u, w2 & 0xF0F0F0F0u, w3 & 0xF0F0F0F0u};
+            mma_i8_16832<true, false>(oi[sg], al, pb0, pb1);
+            mma_i8_16832<false, false>(oi[NSEG + sg], ah, pb0, pb1);
+          }
         } else {
-          int acch[4] = {0, 0, 0, 0};
+          // ---- V fragments and scales, then release the stage
+          uint32_t vw[KP][4][VB / 4];  // per P.V k-step: keys {2t, 2t+1, 2t+8, 2t+9} (t-parity order)
 #pragma unroll
-          for (int kk = 0; kk < KS / 2; ++kk) {
-            const uint32_t w0 = kw[2 * kk], w1 = kw[2 * kk + 1];
-            mma_i8_16832<false, true>(acc, qa[kk], (w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu);
-            mma_i8_16832<false, false>(acch, qa[KS / 2 + kk], w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u);
+          for (int kp = 0; kp < KP; ++kp)
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) {
+              const int row = r0 + 16 * kp + 2 * t + ((kq & 1) ^ vsw) + 8 * (kq >> 1);
+              lds_words<VB>(vt + tile_off<RB>(row, g * VB), vw[kp][kq]);
+            }
+          float vs[NJ][2];
+#pragma unroll
+          for (int j = 0; j < NJ; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) vs[j][e] = __half2float(vst[r0 + 8 * j + 2 * t + e]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
+
+          // ---- online softmax per head g over the KPW keys, and the V-scale frame: one rescale
+          // block for both (a head's maximum grew; a key's V scale would push p * vs * vsc past 2^14)
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float m_new = fmaxf(m_run, mx);
+          float vmax = 0.f;
+#pragma unroll
+          for (int j = 0; j < NJ; ++j) {
+            if (valid[j][0]) vmax = fmaxf(vmax, vs[j][0]);
+            if (valid[j][1]) vmax = fmaxf(vmax, vs[j][1]);
           }
-          // 16 * (low sum - 8 sum q) + high sum (a multiple of 16); hf carries the 1/16
+          if (__any_sync(0xffffffffu, m_new > m_run || vmax * vsc > 16384.f)) {
+            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // keys depend on t only
+            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+            float nk = vk;
+            const float nsc = vmax * vsc > 16384.f ? frame_for(vmax, nk) : vsc;  // warp-uniform
+            const float ratio = nsc / vsc;  // a power of two: exact
+            vsc = nsc;
+            vk = nk;
+            const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
+            l_run *= alpha * ratio;
+            m_run = m_new;
+            // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
+            const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * t) * 4) * ratio;
+            const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4) * ratio;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[e] = 16 * acc[e] + acch[e];
-        }
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = r0 + 8 * j + 2 * t + e;
-          valid[j][e] = (k0 + key) < hi;
-          const int si = I4 ? acc[e] * 256 + acc[2 + e] - qbias : acc[e] * 256 + acc[2 + e];
-          const float s = float(si) * (__half2float(kst[key]) * hf);
-          sc[j][e] = valid[j][e] ? s : -INFINITY;
-          mx = fmaxf(mx, sc[j][e]);
-        }
-      }
-      }
-      if constexpr (G1) {
-        // ---- V fragments: segment sg = bytes 16sg .. 16sg+15 of the 32 keys' rows; thread (g, t)
-        // receives bytes 2g, 2g+1 of k-slots 4t+{0,1} (matrix 0), 4t+{2,3} (1), 16+4t+{0,1} (2), 16+4t+{2,3} (3)
-        uint32_t vr[NSEG][4];
-        const uint32_t vt_s = smem_u32(vt);
-#pragma unroll
-        for (int sg = 0; sg < NSEG; ++sg)
-          ldmatrix_x4_trans(vt_s + (v_row_off ^ uint32_t(sg << 4)), vr[sg][0], vr[sg][1], vr[sg][2], vr[sg][3]);
-        float vs4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) vs4[i] = __half2float(vst[r0 + g1_key(g, i)]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
-
-        // ---- frames: a key above m_run + headroom moves the reference maximum, a product
-        // p * vs above the fixed-point range (or a full frame) the scale; either ends the frame
-        // (lane-local tests and a vote; the warp-wide maxima only when a frame ends)
-        if (__any_sync(0xffffffffu, mx > m_run + kG1Headroom)) {
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // lanes t < 3 hold the same scores
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-          const float rescale = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
-          g1_flush<NSEG>(oi, bsum, so, rescale, inv_ps, g, t);
-          l_run *= rescale;
-          m_run = mx;
-          ftiles = 0;
-        }
-        float pv[4];
-        float pvm = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const bool v_ok = valid[2 * (i >> 1)][i & 1];
-          const float pr = v_ok ? ex2(sc[2 * (i >> 1)][i & 1] - m_run) : 0.f;
-          l_run += pr;
-          pv[i] = v_ok ? pr * vs4[i] : 0.f;
-          pvm = fmaxf(pvm, pv[i]);
-        }
-        if (__any_sync(0xffffffffu, pvm * ps > kG1VLim || (ps == 0.f && pvm > 0.f)) || ftiles >= kG1FrameTiles) {
-          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 1));
-          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 4));
-          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 8));
-          pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 16));
-          g1_flush<NSEG>(oi, bsum, so, 1.f, inv_ps, g, t);
-          if (pvm > 0.f) {
-            const float pb_ = 1.25f * fmaxf(pvm, 1e-30f);
-            ps = kG1VLim / pb_;
-            inv_ps = pb_ / kG1VLim;
+            for (int i = 0; i < MT; ++i) {
+              o[i][0] *= a_lo;
+              o[i][1] *= a_hi;
+              o[i][2] *= a_lo;
+              o[i][3] *= a_hi;
+            }
           }
-          ftiles = 0;
-        }
-        ++ftiles;
-
-        // ---- P in three planes; lane t < 3 packs plane t of its four keys (k-slots 4g + i)
-        // and spreads them as the B operand (column c = plane c, c < 3)
-        uint32_t fw[4];
+          const float mu = ((m_run == -INFINITY) ? 0.f : m_run) - vk;  // ex2(s - mu) = p * vsc
+          uint32_t pb[NJ];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) fw[i] = __float_as_uint(fmaf(pv[i], ps, kG1Magic));
-        const uint32_t px = __byte_perm(fw[0], fw[1], psel);
-        const uint32_t py = __byte_perm(fw[2], fw[3], psel);
-        const uint32_t pw = (__byte_perm(px, py, 0x5410u) ^ pxor) & pmask;
-        bsum = __dp4a(int(pw), 0x01010101, bsum);
-        const uint32_t pb0 = __shfl_sync(0xffffffffu, pw, 4 * t + (g & 3));
-        const uint32_t pb1 = __shfl_sync(0xffffffffu, pw, 16 + 4 * t + (g & 3));
-
-        // ---- O^T += V^T P^T on the integer tensor cores: A rows g / g + 8 = bytes 2g / 2g + 1 of
-        // the segment, four k-slots per register (byte transposes of the ldmatrix pairs)
-#pragma unroll
-        for (int sg = 0; sg < NSEG; ++sg) {
-          const uint32_t w0 = __byte_perm(vr[sg][0], vr[sg][1], 0x6420u);
-          const uint32_t w1 = __byte_perm(vr[sg][0], vr[sg][1], 0x7531u);
-          const uint32_t w2 = __byte_perm(vr[sg][2], vr[sg][3], 0x6420u);
-          const uint32_t w3 = __byte_perm(vr[sg][2], vr[sg][3], 0x7531u);
-          const uint32_t al[4] = {(w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu,
-                                  (w2 ^ 0x08080808u) & 0x0F0F0F0Fu, (w3 ^ 0x08080808u) & 0x0F0F0F0Fu};
-          const uint32_t ah[4] = {w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u, w2 & 0xF0F0F0F0u, w3 & 0xF0F0F0F0u};
-          mma_i8_16832<true, false>(oi[sg], al, pb0, pb1);
-          mma_i8_16832<false, false>(oi[NSEG + sg], ah, pb0, pb1);
-        }
-      } else {
-        // ---- V fragments and scales, then release the stage
-        uint32_t vw[KP][4][VB / 4];  // per P.V k-step: keys {2t, 2t+1, 2t+8, 2t+9} (t-parity order)
-#pragma unroll
-        for (int kp = 0; kp < KP; ++kp)
-#pragma unroll
-          for (int kq = 0; kq < 4; ++kq) {
-            const int row = r0 + 16 * kp + 2 * t + ((kq & 1) ^ vsw) + 8 * (kq >> 1);
-            lds_words<VB>(vt + tile_off<RB>(row, g * VB), vw[kp][kq]);
+          for (int j = 0; j < NJ; ++j) {
+            const float p0 = valid[j][0] ? ex2(sc[j][0] - mu) : 0.f;
+            const float p1 = valid[j][1] ? ex2(sc[j][1] - mu) : 0.f;
+            l_run += p0 + p1;
+            pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] : 0.f, valid[j][1] ? p1 * vs[j][1] : 0.f);
           }
-        float vs[NJ][2];
-#pragma unroll
-        for (int j = 0; j < NJ; ++j)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) vs[j][e] = __half2float(vst[r0 + 8 * j + 2 * t + e]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
 
-        // ---- online softmax per head g over the KPW keys, and the V-scale frame: one rescale
-        // block for both (a head's maximum grew; a key's V scale would push p * vs * vsc past 2^14)
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        float vmax = 0.f;
+          // ---- O^T += V^T P^T
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          if (valid[j][0]) vmax = fmaxf(vmax, vs[j][0]);
-          if (valid[j][1]) vmax = fmaxf(vmax, vs[j][1]);
-        }
-        if (__any_sync(0xffffffffu, m_new > m_run || vmax * vsc > 16384.f)) {
-          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));  // keys depend on t only
-          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-          float nk = vk;
-          const float nsc = vmax * vsc > 16384.f ? frame_for(vmax, nk) : vsc;  // warp-uniform
-          const float ratio = nsc / vsc;  // a power of two: exact
-          vsc = nsc;
-          vk = nk;
-          const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
-          l_run *= alpha * ratio;
-          m_run = m_new;
-          // O^T columns are heads 2t, 2t+1; their factors live with g = 2t, 2t+1
-          const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * t) * 4) * ratio;
-          const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * t + 1) * 4) * ratio;
+          for (int kp = 0; kp < KP; ++kp) {
+            // m-tile i rows g / g+8: dimensions g*D/8 + i / g*D/8 + MT + i (bytes i / MT + i)
 #pragma unroll
-          for (int i = 0; i < MT; ++i) {
-            o[i][0] *= a_lo;
-            o[i][1] *= a_hi;
-            o[i][2] *= a_lo;
-            o[i][3] *= a_hi;
+            for (int i = 0; i < MT; ++i) {
+              const int w0 = i >> 2, w1 = (MT + i) >> 2;
+              const uint32_t s0 = uint32_t(i & 3) * 0x1111u + sel_base;
+              const uint32_t s1 = uint32_t((MT + i) & 3) * 0x1111u + sel_base;
+              const uint32_t a0 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w0], vw[kp][1][w0], s0));
+              const uint32_t a1 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w1], vw[kp][1][w1], s1));
+              const uint32_t a2 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w0], vw[kp][3][w0], s0));
+              const uint32_t a3 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1));
+              mma_16816(o[i], a0, a1, a2, a3, pb[2 * kp], pb[2 * kp + 1]);
+            }
           }
         }
-        const float mu = ((m_run == -INFINITY) ? 0.f : m_run) - vk;  // ex2(s - mu) = p * vsc
-        uint32_t pb[NJ];
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          const float p0 = valid[j][0] ? ex2(sc[j][0] - mu) : 0.f;
-          const float p1 = valid[j][1] ? ex2(sc[j][1] - mu) : 0.f;
-          l_run += p0 + p1;
-          pb[j] = pack_half2(valid[j][0] ? p0 * vs[j][0] : 0.f, valid[j][1] ? p1 * vs[j][1] : 0.f);
-        }
-
-        // ---- O^T += V^T P^T
-#pragma unroll
-        for (int kp = 0; kp < KP; ++kp) {
-          // m-tile i rows g / g+8: dimensions g*D/8 + i / g*D/8 + MT + i (bytes i / MT + i)
-#pragma unroll
-          for (int i = 0; i < MT; ++i) {
-            const int w0 = i >> 2, w1 = (MT + i) >> 2;
-            const uint32_t s0 = uint32_t(i & 3) * 0x1111u + sel_base;
-            const uint32_t s1 = uint32_t((MT + i) & 3) * 0x1111u + sel_base;
-            const uint32_t a0 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w0], vw[kp][1][w0], s0));
-            const uint32_t a1 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w1], vw[kp][1][w1], s1));
-            const uint32_t a2 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w0], vw[kp][3][w0], s0));
-            const uint32_t a3 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1));
-            mma_16816(o[i], a0, a1, a2, a3, pb[2 * kp], pb[2 * kp + 1]);
-          }
-        }
-      }
+      };
+      if (k0 + C::TK <= hi) tile(std::false_type{});
+      else tile(std::true_type{});
     }
 
     // ---- unit epilogue: merge the 4 warps' (m, l, O) per head
