@@ -346,17 +346,31 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   // Hkv=8: N=4K 16.5 -> 14.0 us, 16K 43.8 -> 43.1, 64K 159.9 -> 156.8; B=8: 26.1 -> 23.8,
   // 84.0 -> 82.0, 325.6 -> 323.3); at D = 64 one CTA per SM streams too slowly for long
   // contexts (B=4, N=64K: 83 -> 97 us).  Batch 1 with 8 KV heads would need 8 resident clusters
-  // of 16, and B200 holds 7 (one GPC has fewer than 16 SMs free), so it keeps the combine.
+  // of 16, and B200 holds 7 (one GPC has fewer than 16 SMs free): the cluster shrinks to the
+  // largest size whose clusters are all resident (below).
   const int mode = g_split_mode.load();
   if (a.fmt == KvFormat::F16 && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
       (mode == FQKV_SPLIT_CLUSTER || (se > 1 && a.D == 128)) && units0 < ds.sm_count) {
     int64_t sc = std::min<int64_t>({16, tiles, std::max<int64_t>(1, ds.sm_count / units0)});
     if (S_fixed > 0) sc = std::min<int64_t>(sc, S_fixed);
-    int64_t cct = 0, cse = 0;
-    if (sc >= 2) geometry(sc, &cct, &cse);
     const int di = a.D == 128 ? 1 : 0;
+    // the largest cluster size (<= sc) whose clusters are all resident at once
+    int64_t cct = 0, cse = 0;
+    const int64_t sc0 = sc;
+    for (; sc >= 2; --sc) {
+      geometry(sc, &cct, &cse);
+      if (cse >= 2 && units0 <= ds.max_clusters_f16[di][cse]) break;
+    }
+    // A cluster smaller than the grid-filling size (batch 1-3 with 8 KV heads: 16 CTAs per cluster
+    // are not all resident, 10 / 6 / 5 are) streams from fewer SMs but drops the combine's fixed
+    // cost; on B200 it measured faster up to N = 32K and within 3 % either way at 64K (batch 1,
+    // N = 2K / 16K / 32K / 64K: 7.21 -> 5.36, 16.99 -> 15.56, 27.2 -> 26.4, 46.0 -> 47.4 us; batch 2:
+    // 8.75 -> 7.18, 25.8 -> 24.3, 44.8 -> 44.4, 83.0 -> 84.0; batch 3: 9.33 -> 8.77, 34.9 -> 33.0,
+    // 63.4 -> 61.3, 120.4 -> 116.8), so it is taken automatically up to N = 32K.
+    const bool reduced = sc < sc0;
     if (sc >= 2 && cse >= 2 && units0 <= ds.max_clusters_f16[di][cse] &&
-        (mode == FQKV_SPLIT_CLUSTER || 2 * units0 * cse >= ds.sm_count)) {
+        (mode == FQKV_SPLIT_CLUSTER ||
+         (2 * units0 * cse >= ds.sm_count && (!reduced || a.N <= 32768)))) {
       ct = cct;
       se = cse;
       a.cluster = int(cse);

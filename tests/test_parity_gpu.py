@@ -143,8 +143,9 @@ def test_gqa_sk_fast(fqkv, N, D, S, W, CW):
 
 # ------------------------------------------------------------------ properties
 def test_split_count_does_not_change_the_result(fqkv):
-    """Same op with no workspace (one split) and with the preferred split-K plan."""
-    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 128
+    """Same op with no workspace (one split) and with the preferred split-K plan (partials +
+    combine: at D = 64 batch 1 does not use the cluster merge)."""
+    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 64
     q, K, V = (_randn(B, Hq, D, seed=50).cuda(), _randn(B, Hkv, N, D, seed=51).cuda(),
                _randn(B, Hkv, N, D, seed=52).cuda())
     lib = fqkv.native.lib()
@@ -182,8 +183,9 @@ def test_cuda_graph_capture_and_side_stream(fqkv):
 
 
 def test_split_launches_on_two_streams_at_once(fqkv):
-    """Split launches (partial kernel + combine) in flight on two streams at once, each with its own workspace."""
-    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 128
+    """Split launches (partial kernel + combine) in flight on two streams at once, each with its own workspace
+    (D = 64: batch 1 splits into partials + combine there)."""
+    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 64
     assert fqkv.workspace_bytes("fp16", B, Hq, Hkv, N, D) > 0
     inputs = [(_randn(B, Hq, D, seed=100 + i).cuda(), _randn(B, Hkv, N, D, seed=110 + i).cuda(),
                _randn(B, Hkv, N, D, seed=120 + i).cuda()) for i in range(2)]
@@ -528,9 +530,9 @@ def test_cluster_merge_sk_fast_and_kvcache(fqkv, split_mode, D):
 def test_split_plans_pick_the_cluster_merge_where_it_fits(fqkv):
     """Automatic split merging: a D = 128 split plan merges through a thread-block cluster (one
     launch, no workspace) when its whole grid of clusters is resident at once -- e.g. B=4, Hkv=8
-    (32 clusters of 4) -- and otherwise through partials + the combine kernel (batch 1 with 8 KV
-    heads needs 8 resident clusters of 16; the plan checks the device's limit).  The batch-64
-    bench shape stays unsplit."""
+    (32 clusters of 4), or through smaller clusters when the grid-filling size is not all resident
+    (batch 1 with 8 KV heads: 8 clusters of 16 do not fit on B200, 8 of 10 do) up to N = 32K --
+    and otherwise through partials + the combine kernel.  The batch-64 bench shape stays unsplit."""
     import ctypes
     lib = fqkv.native.lib()
     info = (ctypes.c_int32 * 33)()
@@ -541,11 +543,18 @@ def test_split_plans_pick_the_cluster_merge_where_it_fits(fqkv):
     splits, cluster, grid, chunk, kernel = list(out)
     assert splits > 1 and cluster == splits and grid == 32 * splits and kernel == 0, list(out)
     assert fqkv.workspace_bytes("fp16", 4, 32, 8, 16384, 128) == 0
+    # batch 1 (8 units): the largest cluster size whose 8 clusters are all resident (B200: 10 of
+    # 16), taken automatically up to N = 32K; longer contexts keep partials + combine
+    sm = info[0]
+    fits = [c for c in range(2, min(16, sm // 8) + 1) if max_clusters_128[c] >= 8 and 2 * 8 * c >= sm]
     fqkv.native.check(lib.fqkv_decode_plan(0, 1, 32, 8, 16384, 128, 1 << 30, out), "plan")
-    if max_clusters_128[16] >= 8:
-        assert out[1] == out[0] > 1, list(out)
+    if fits:
+        assert out[1] == out[0] == max(fits), (list(out), fits)
+        assert fqkv.workspace_bytes("fp16", 1, 32, 8, 16384, 128) == 0
     else:
         assert out[0] > 1 and out[1] == 0, list(out)
-        assert fqkv.workspace_bytes("fp16", 1, 32, 8, 16384, 128) > 0
+    fqkv.native.check(lib.fqkv_decode_plan(0, 1, 32, 8, 65536, 128, 1 << 30, out), "plan")
+    assert out[0] > 1 and out[1] == 0, list(out)
+    assert fqkv.workspace_bytes("fp16", 1, 32, 8, 65536, 128) > 0
     fqkv.native.check(lib.fqkv_decode_plan(0, 64, 32, 8, 16384, 128, 0, out), "plan")
     assert out[0] == 1 and out[1] == 0
