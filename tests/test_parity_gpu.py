@@ -558,3 +558,46 @@ def test_split_plans_pick_the_cluster_merge_where_it_fits(fqkv):
     assert fqkv.workspace_bytes("fp16", 1, 32, 8, 65536, 128) > 0
     fqkv.native.check(lib.fqkv_decode_plan(0, 64, 32, 8, 16384, 128, 0, out), "plan")
     assert out[0] == 1 and out[1] == 0
+
+
+@pytest.mark.parametrize("scale", [1e-4, 1e-3, 1e2, "ramp"])
+@pytest.mark.parametrize("D", [64, 128])
+def test_quantized_kernels_relative_accuracy_at_any_v_scale(fqkv, scale, D):
+    """V scaled by 1e-4 .. 1e2 (p * vscale would fall into fp16 subnormals for small V), or by a
+    factor rising over the keys from 1e-4 to 1e2 (the V-scale frame moves down inside a unit):
+    every quantized kernel -- int8 and int4 with one head per row (the CUDA-core kernel; int4 at
+    D = 128 on the tensor cores), int8 GQA on the tensor cores -- within a tolerance relative to
+    the output's scale (atol = 2e-3 * scale, or 2e-3 * max|out| for the ramp; rtol = 1e-2) of the
+    float64 oracle."""
+    R, N = 6, 1500
+
+    def scaled(x, n_axis):
+        if scale == "ramp":
+            f = torch.logspace(-4, 2, x.shape[n_axis], dtype=torch.float64)
+            shape = [1] * x.dim()
+            shape[n_axis] = -1
+            return (x.double() * f.view(shape)).half(), None
+        return (x.float() * scale).half(), scale
+
+    q, K = _randn(R, D, seed=180), _randn(R, N, D, seed=181)
+    V, mag = scaled(_randn(R, N, D, seed=182), 1)
+    for quant, dq, op in ((fqkv.qpt, oq.dequantize_int8, fqkv.decode_attn_int8_mw),
+                          (fqkv.quant_int4_per_token, oq.dequantize_int4, fqkv.decode_attn_int4)):
+        Kc, Ks = quant(K.cuda())
+        Vc, Vs = quant(V.cuda())
+        out = op(q.cuda(), Kc, Vc, Ks, Vs, 8)
+        ref = oatt.decode_attention(q.numpy(), dq(Kc.cpu().numpy(), Ks.cpu().numpy()),
+                                    dq(Vc.cpu().numpy(), Vs.cpu().numpy()))
+        atol = 2e-3 * (mag if mag is not None else np.abs(ref).max())  # ramp: relative to the output's size
+        np.testing.assert_allclose(out.float().cpu().numpy().astype(np.float64), ref, atol=atol, rtol=1e-2)
+    B, Hq, Hkv = 2, 16, 4
+    qg = _randn(B, Hq, D, seed=183)
+    Kg = _randn(B, Hkv, N, D, seed=184)
+    Vg, mag = scaled(_randn(B, Hkv, N, D, seed=185), 2)
+    Kq, Ks = fqkv.qpt(Kg.cuda())
+    Vq, Vs = fqkv.qpt(Vg.cuda())
+    out = fqkv.decode_attn_gqa_int8(qg.cuda(), Kq, Vq, Ks, Vs)
+    ref = oatt.decode_attention_gqa(qg.numpy(), oq.dequantize_int8(Kq.cpu().numpy(), Ks.cpu().numpy()),
+                                    oq.dequantize_int8(Vq.cpu().numpy(), Vs.cpu().numpy()))
+    atol = 2e-3 * (mag if mag is not None else np.abs(ref).max())
+    np.testing.assert_allclose(out.float().cpu().numpy().astype(np.float64), ref, atol=atol, rtol=1e-2)
