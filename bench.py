@@ -78,11 +78,20 @@ CONFIG_SWEEP = [
     ("sk_d128_n64k", "sk", {"N": 65536, "S": 128}),
     ("sk_d64_n16k", "sk", {"D": 64}),
     ("sk_d64_n64k", "sk", {"D": 64, "N": 65536, "S": 128}),
+] + [(f"sk_d{D}_n{N}", "sk", {"D": D, "N": N}) for D in (128, 64) for N in (512, 1024, 2048, 4096, 8192)] + [
     ("qpt_int8", "qpt", {}),
     ("quant_int4", "quant_int4", {}),
     ("cfg3_int4_b2048", "int4_b2048", {}),
     ("cfg2_int8_b2048", "int8_b2048", {}),
 ]
+
+
+# The reference's published loop-timed gqa_sk_fast times (A100, us per call, Hq=32, Hkv=8, S=64;
+# benchmarks/flashinfer_looptimed.json:6-149), printed beside the same shapes here.
+REFERENCE_A100_SK_US = {
+    64: {512: 10.48, 1024: 12.57, 2048: 16.93, 4096: 25.05, 8192: 39.23, 16384: 94.30},
+    128: {512: 11.86, 1024: 14.71, 2048: 20.11, 4096: 30.63, 8192: 74.25, 16384: 129.34},
+}
 
 
 # ---------------------------------------------------------------------------- helpers
@@ -914,6 +923,15 @@ def time_case(case: Case, dev: torch.device, gpu_index: int, min_seconds: float 
     return {"us": e0.elapsed_time(e1) * 1e3 / (reps * n), "calls": reps * n, "clocks": clocks, "plan": case.plan}
 
 
+def sk_l2_note(w: dict) -> str:
+    """Where the rotated batch-1 split-K inputs live: 8 KV sets, streamed from HBM when they exceed L2."""
+    tot = 8 * 2 * w["Hkv"] * w["N"] * w["D"] * 2
+    if tot > 126e6:
+        return f"8 rotated KV sets, {tot / 1e6:.0f} MB > L2"
+    return (f"8 rotated KV sets, {tot / 1e6:.0f} MB: L2-resident (a latency-bound row, as the reference notes "
+            "for its own short-N rows)")
+
+
 def run_config_sweep(pkg, dev: torch.device, gpu_index: int, peak: float) -> dict:
     """Every BASELINE config (and the quantizers) timed on this GPU: one entry per workload."""
     out, t_start = [], time.time()
@@ -939,10 +957,13 @@ def run_config_sweep(pkg, dev: torch.device, gpu_index: int, peak: float) -> dic
                     "kernel": dominant_kernel(w, plan), "bytes_per_call": nbytes, "us_per_call": round(r["us"], 3),
                     "GB_s": round(gbs, 1), "pct_of_8TBps": round(100 * gbs / NOMINAL_HBM_GBS, 2),
                     "frac_of_measured_peak": round(gbs / peak, 4), "calls_timed": r["calls"],
-                    "l2": "8 rotated KV sets > 4x L2" if w["kind"] == "sk" else "inputs > L2",
+                    "l2": sk_l2_note(w) if w["kind"] == "sk" else "inputs > L2",
                     "clocks": {"sm_mhz": c.get("sm_mhz"), "sm_max_mhz": c.get("sm_max_mhz"),
                                "reasons": c.get("reasons"), "samples": c.get("samples")},
                     "plan": plan_record(plan), "setup_plus_timing_s": round(time.time() - t0, 1)})
+        ref_us = REFERENCE_A100_SK_US.get(w["D"], {}).get(w["N"]) if w["kind"] == "sk" else None
+        if ref_us is not None:
+            out[-1]["reference_a100_us"] = ref_us
     return {"entries": out, "wall_s": round(time.time() - t_start, 1),
             "timing": "CUDA-graph replays of back-to-back C-ABI calls with device-resident inputs, CUDA events",
             "data": "synthetic N(0,1) fp16; quantized KV: the library's quantizer on the first 1 GiB of codes, "
