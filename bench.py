@@ -690,6 +690,8 @@ def run_llama(args, w) -> int:
             "max_logit_diff_vs_sdpa": round(max_diff, 5),
             "token_match_stock_vs_ours": round((stock_tokens[:nb] == ours_tokens[:nb]).float().mean().item(), 4),
             "impl": "ours"}
+    if args.split_mode != "auto":
+        line["config"]["split_mode"] = args.split_mode
     print(json.dumps(line), flush=True)
     return 0
 
@@ -1028,11 +1030,14 @@ def main() -> int:
             w["B"] = args.batch
         if args.impl == "reference":
             return run_llama_reference(args, w, rank)
+        if args.split_mode != "auto":  # how the attention's split plans merge (A/B of the merge modes)
+            lib = importlib.import_module(PKG).native.lib()
+            if lib.fqkv_set_split_mode({"combine": 1, "cluster": 2}[args.split_mode]) != 0:
+                raise RuntimeError(importlib.import_module(PKG).native.last_error())
         return run_llama_tp(args, w, world, rank, local_rank) if world > 1 else run_llama(args, w)
     config = {"workload": w["desc"], "global_batch": None, "seq_len": w["N"], "head_dim": w["D"],
               "parallelism": f"{world} GPU(s), sequences sharded, no data-path collective",
-              "l2": "8 rotated KV sets (537 MB) > 4x L2" if w["kind"] == "sk"
-              else "inputs larger than L2 per step (no flush needed)",
+              "l2": sk_l2_note(w) if w["kind"] == "sk" else "inputs larger than L2 per step (no flush needed)",
               "timing": "CUDA events around K eager C-ABI calls" if args.eager
               else "CUDA events around one CUDA-graph replay of K C-ABI calls"}
     if w["kind"] in ("gqa", "gqa_int8"):

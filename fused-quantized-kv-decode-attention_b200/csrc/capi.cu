@@ -341,16 +341,28 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   // Cluster mode (fp16, local output): when the grid is too small to fill the GPU without
   // splitting, the S split CTAs of each unit form one thread-block cluster (S <= 16), one CTA
   // per SM, and merge through distributed shared memory -- one launch, no partials, no combine.
-  // Used when the whole grid is resident at once and keeps at least half the SMs streaming.
-  // Automatic only at D = 128, where it measured faster than partials + combine on B200 (B=4,
-  // Hkv=8: N=4K 16.5 -> 14.0 us, 16K 43.8 -> 43.1, 64K 159.9 -> 156.8; B=8: 26.1 -> 23.8,
-  // 84.0 -> 82.0, 325.6 -> 323.3); at D = 64 one CTA per SM streams too slowly for long
-  // contexts (B=4, N=64K: 83 -> 97 us).  Batch 1 with 8 KV heads would need 8 resident clusters
-  // of 16, and B200 holds 7 (one GPC has fewer than 16 SMs free): the cluster shrinks to the
-  // largest size whose clusters are all resident (below).
+  // The cluster is the largest size whose clusters are all resident at once (batch 1 with 8 KV
+  // heads would need 8 resident clusters of 16 and B200 holds 7 -- one GPC has fewer than 16 SMs
+  // free -- so it gets 10).  Automatic choice, from forced-mode sweeps on B200 (us per call,
+  // partials + combine -> cluster merge; Hkv = 8):
+  //  * short contexts, D = 64 and 128: dropping the combine's fixed cost wins even with few SMs
+  //    streaming and even where the split search alone would not split (D = 64, N = 512 / 640 /
+  //    1024 / 2048: batch 1 4.76 -> 3.68, 5.42 -> 3.99, 5.68 -> 3.88, 6.38 -> 4.56; batch 4 5.56
+  //    -> 4.21, 5.65 -> 4.65, 6.34 -> 4.90, 8.08 -> 7.25; batch 8 (unsplit plan) 7.82 -> 4.80,
+  //    6.90 -> 5.39, 8.10 -> 7.07, 10.16 -> 10.26), so it is taken up to N = 4096 at D = 64;
+  //  * D = 128 up to N = 32K (batch 1, N = 2K / 16K / 32K / 64K: 7.21 -> 5.36, 16.99 -> 15.56,
+  //    27.2 -> 26.4, 46.0 -> 47.4; batch 2: 8.75 -> 7.18, 25.8 -> 24.3, 44.8 -> 44.4, 83.0 -> 84.0;
+  //    batch 3: 9.33 -> 8.77, 34.9 -> 33.0, 63.4 -> 61.3, 120.4 -> 116.8), and at any length when
+  //    the grid-filling cluster is resident and keeps at least half the SMs streaming (B=4:
+  //    N=4K 16.5 -> 14.0, 16K 43.8 -> 43.1, 64K 159.9 -> 156.8; B=8: 26.1 -> 23.8, 84.0 -> 82.0,
+  //    325.6 -> 323.3);
+  //  * D = 64 longer contexts keep the combine: one CTA per SM streams too slowly there (batch 1,
+  //    N=16K: 11.8 -> 12.6 us; B=4, N=64K: 83 -> 97 us).
   const int mode = g_split_mode.load();
+  const int64_t short_n = a.D == 128 ? 32768 : 4096;
+  const bool auto_ok = a.N <= short_n ? true : (a.D == 128 && se > 1);
   if (a.fmt == KvFormat::F16 && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
-      (mode == FQKV_SPLIT_CLUSTER || (se > 1 && a.D == 128)) && units0 < ds.sm_count) {
+      (mode == FQKV_SPLIT_CLUSTER || auto_ok) && units0 < ds.sm_count) {
     int64_t sc = std::min<int64_t>({16, tiles, std::max<int64_t>(1, ds.sm_count / units0)});
     if (S_fixed > 0) sc = std::min<int64_t>(sc, S_fixed);
     const int di = a.D == 128 ? 1 : 0;
@@ -361,16 +373,9 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
       geometry(sc, &cct, &cse);
       if (cse >= 2 && units0 <= ds.max_clusters_f16[di][cse]) break;
     }
-    // A cluster smaller than the grid-filling size (batch 1-3 with 8 KV heads: 16 CTAs per cluster
-    // are not all resident, 10 / 6 / 5 are) streams from fewer SMs but drops the combine's fixed
-    // cost; on B200 it measured faster up to N = 32K and within 3 % either way at 64K (batch 1,
-    // N = 2K / 16K / 32K / 64K: 7.21 -> 5.36, 16.99 -> 15.56, 27.2 -> 26.4, 46.0 -> 47.4 us; batch 2:
-    // 8.75 -> 7.18, 25.8 -> 24.3, 44.8 -> 44.4, 83.0 -> 84.0; batch 3: 9.33 -> 8.77, 34.9 -> 33.0,
-    // 63.4 -> 61.3, 120.4 -> 116.8), so it is taken automatically up to N = 32K.
     const bool reduced = sc < sc0;
     if (sc >= 2 && cse >= 2 && units0 <= ds.max_clusters_f16[di][cse] &&
-        (mode == FQKV_SPLIT_CLUSTER ||
-         (2 * units0 * cse >= ds.sm_count && (!reduced || a.N <= 32768)))) {
+        (mode == FQKV_SPLIT_CLUSTER || a.N <= short_n || (!reduced && 2 * units0 * cse >= ds.sm_count))) {
       ct = cct;
       se = cse;
       a.cluster = int(cse);

@@ -558,6 +558,18 @@ def test_split_plans_pick_the_cluster_merge_where_it_fits(fqkv):
     assert fqkv.workspace_bytes("fp16", 1, 32, 8, 65536, 128) > 0
     fqkv.native.check(lib.fqkv_decode_plan(0, 64, 32, 8, 16384, 128, 0, out), "plan")
     assert out[0] == 1 and out[1] == 0
+    # short contexts at D = 64 (the decode step of a Llama-1B-architecture model: N = 640) merge in a
+    # cluster too, even where the split search alone would not split (batch 8, N = 512); long ones
+    # keep partials + combine
+    max_clusters_64 = {c: info[18 + c - 2] for c in range(2, 17)}
+    for B, N in ((1, 640), (4, 640), (8, 512)):
+        units = B * 8
+        fits64 = [c for c in range(2, min(16, N // 64, sm // units) + 1) if max_clusters_64[c] >= units]
+        fqkv.native.check(lib.fqkv_decode_plan(0, B, 32, 8, N, 64, 1 << 30, out), "plan")
+        if fits64:
+            assert out[1] == out[0] >= 2, (B, N, list(out), fits64)
+    fqkv.native.check(lib.fqkv_decode_plan(0, 1, 32, 8, 16384, 64, 1 << 30, out), "plan")
+    assert out[0] > 1 and out[1] == 0, list(out)
 
 
 @pytest.mark.parametrize("scale", [1e-4, 1e-3, 1e2, "ramp"])
