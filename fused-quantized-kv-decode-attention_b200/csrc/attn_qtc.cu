@@ -56,7 +56,7 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
 constexpr int kQMax = 32639;  // |q * Qs| bound: hi = (v + 128) >> 8 stays in [-127, 127]
 
-template <int D, bool I4, bool G1>
+template <int D, bool I4, bool G1, bool kCl = false>
 struct QtcCfg {
   static constexpr int RB = I4 ? D / 2 : D;                   // bytes of one key row
   static constexpr int KPW = (!I4 && D == 128) ? 16 : 32;      // keys per consumer warp per tile
@@ -77,21 +77,35 @@ struct QtcCfg {
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
   static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
   static constexpr size_t kMergeBytes = size_t(kConsumerWarps) * (2 * 8 + MH * D) * sizeof(float);
-  static constexpr size_t kSmemBytes = 1024 + kRingBytes + kBarBytes + kMergeBytes;
+  // cluster mode (int8 GQA): this CTA's merged (m, l) of up to 8 heads and o [8][D], read by the cluster
+  static constexpr size_t kClusterBytes = kCl ? (2 * 8 + 8 * D) * sizeof(float) : 0;
+  static constexpr size_t kSmemBytes = 1024 + kRingBytes + kBarBytes + kMergeBytes + kClusterBytes;
   static_assert(TK == tile_keys(I4 ? KvFormat::I4Tc : KvFormat::I8Gqa, D), "planner tile size");
   static_assert(!G1 || KPW % 16 == 0, "one-head variant works in 16-key blocks");
 };
+
+constexpr int kMaxCluster = 16;
 
 struct UnitCoord {
   int b, kh, grp, s;
 };
 
+// Persistent mode: units ordered (b, kh, s, grp).  Cluster mode: (b, kh, grp, s),
+// so the S_eff split CTAs of one unit are consecutive blocks -- one cluster.
+template <bool kCl>
 __device__ __forceinline__ UnitCoord decode_unit(const DecodeLaunch& a, int u) {
   UnitCoord c;
-  c.grp = u % a.groups;
-  u /= a.groups;
-  c.s = u % a.S_eff;
-  u /= a.S_eff;
+  if constexpr (kCl) {
+    c.s = u % a.S_eff;
+    u /= a.S_eff;
+    c.grp = u % a.groups;
+    u /= a.groups;
+  } else {
+    c.grp = u % a.groups;
+    u /= a.groups;
+    c.s = u % a.S_eff;
+    u /= a.S_eff;
+  }
   c.kh = u % a.Hkv;
   c.b = u / a.Hkv;
   return c;
@@ -248,10 +262,11 @@ __device__ __forceinline__ void g1_flush(int (&oi)[8][4], int& bsum, float* so, 
   bsum = 0;
 }
 
-template <int D, bool I4, bool G1>
+template <int D, bool I4, bool G1, bool kCl = false>
 __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
-  using C = QtcCfg<D, I4, G1>;
+  using C = QtcCfg<D, I4, G1, kCl>;
   static_assert(I4 == G1, "int4 runs the one-head variant, int8 the GQA one");
+  static_assert(!kCl || !G1, "the cluster merge serves the several-heads (int8 GQA) variant");
   constexpr int NSEG = C::NSEG;
   constexpr int MH = C::MH;
   constexpr int RB = C::RB;
@@ -272,6 +287,9 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
   float* sm_m = reinterpret_cast<float*>(empty + C::kStages);
   float* sm_l = sm_m + kConsumerWarps * 8;
   float* sm_o = sm_l + kConsumerWarps * 8;
+  float* cl_m = sm_o + kConsumerWarps * MH * D;  // cluster mode: [8]
+  float* cl_l = cl_m + 8;                        // [8]
+  float* cl_o = cl_l + 8;                        // [8][D]
   __shared__ int abort_flag;
   __shared__ int stage_off[C::kStages][2];
 
@@ -300,44 +318,51 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
 
   // ------------------------------------------------------------ producer
   if (warp == kConsumerWarps) {
-    if (lane != 0 || a.debug_skip_loads) return;
-    int it = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
-      const UnitCoord uc = decode_unit(a, u);
-      const int lo = uc.s * a.chunk;
-      const int hi = min(n_valid, lo + a.chunk);
-      const int z = uc.b * a.Hkv + uc.kh;
-      const __half* Ksr = static_cast<const __half*>(a.Ks) + size_t(z) * a.kv_stride;
-      const __half* Vsr = static_cast<const __half*>(a.Vs) + size_t(z) * a.kv_stride;
-      for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
-        const int st = it % C::kStages;
-        if (it >= C::kStages) {
-          if (*reinterpret_cast<volatile int*>(&abort_flag) ||
-              !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
-            ok = false;
-            break;
+    if (lane == 0 && !a.debug_skip_loads) {
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+        const UnitCoord uc = decode_unit<kCl>(a, u);
+        const int lo = uc.s * a.chunk;
+        const int hi = min(n_valid, lo + a.chunk);
+        const int z = uc.b * a.Hkv + uc.kh;
+        const __half* Ksr = static_cast<const __half*>(a.Ks) + size_t(z) * a.kv_stride;
+        const __half* Vsr = static_cast<const __half*>(a.Vs) + size_t(z) * a.kv_stride;
+        for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
+          const int st = it % C::kStages;
+          if (it >= C::kStages) {
+            if (*reinterpret_cast<volatile int*>(&abort_flag) ||
+                !mbar_wait(&empty[st], ((it / C::kStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
           }
+          const int nk = min(C::TK, hi - k0);
+          const uintptr_t ka = reinterpret_cast<uintptr_t>(Ksr + k0);
+          const uintptr_t va = reinterpret_cast<uintptr_t>(Vsr + k0);
+          const uintptr_t ka0 = ka & ~uintptr_t(15), va0 = va & ~uintptr_t(15);
+          const uint32_t kwin = uint32_t(((ka + 2u * nk + 15u) & ~uintptr_t(15)) - ka0);
+          const uint32_t vwin = uint32_t(((va + 2u * nk + 15u) & ~uintptr_t(15)) - va0);
+          stage_off[st][0] = int(ka - ka0) >> 1;
+          stage_off[st][1] = int(va - va0) >> 1;
+          uint8_t* base = ring + size_t(st) * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[st], 2 * C::kTileBytes + kwin + vwin);
+          tma_load_3d(base, &a.tmK, 0, k0, z, &full[st]);
+          tma_load_3d(base + C::kTileBytes, &a.tmV, 0, k0, z, &full[st]);
+          bulk_g2s(base + 2 * C::kTileBytes, reinterpret_cast<const void*>(ka0), kwin, &full[st]);
+          bulk_g2s(base + 2 * C::kTileBytes + C::kScaleBytes, reinterpret_cast<const void*>(va0), vwin, &full[st]);
         }
-        const int nk = min(C::TK, hi - k0);
-        const uintptr_t ka = reinterpret_cast<uintptr_t>(Ksr + k0);
-        const uintptr_t va = reinterpret_cast<uintptr_t>(Vsr + k0);
-        const uintptr_t ka0 = ka & ~uintptr_t(15), va0 = va & ~uintptr_t(15);
-        const uint32_t kwin = uint32_t(((ka + 2u * nk + 15u) & ~uintptr_t(15)) - ka0);
-        const uint32_t vwin = uint32_t(((va + 2u * nk + 15u) & ~uintptr_t(15)) - va0);
-        stage_off[st][0] = int(ka - ka0) >> 1;
-        stage_off[st][1] = int(va - va0) >> 1;
-        uint8_t* base = ring + size_t(st) * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[st], 2 * C::kTileBytes + kwin + vwin);
-        tma_load_3d(base, &a.tmK, 0, k0, z, &full[st]);
-        tma_load_3d(base + C::kTileBytes, &a.tmV, 0, k0, z, &full[st]);
-        bulk_g2s(base + 2 * C::kTileBytes, reinterpret_cast<const void*>(ka0), kwin, &full[st]);
-        bulk_g2s(base + 2 * C::kTileBytes + C::kScaleBytes, reinterpret_cast<const void*>(va0), vwin, &full[st]);
+      }
+      if (!ok) {
+        for (int j = (it > C::kStages ? it - C::kStages : 0); j < it; ++j)
+          mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, wc, kDevTimeoutDrain);
       }
     }
-    if (!ok) {
-      for (int j = (it > C::kStages ? it - C::kStages : 0); j < it; ++j)
-        mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, wc, kDevTimeoutDrain);
+    if constexpr (kCl) {
+      // the whole warp takes part in the consumers' two cluster barriers (see the epilogue)
+      __syncwarp();
+      cluster_sync_all();
+      cluster_sync_all();
     }
     return;
   }
@@ -369,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
   int it = 0;
 
   for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
-    const UnitCoord uc = decode_unit(a, u);
+    const UnitCoord uc = decode_unit<kCl>(a, u);
     const int lo = uc.s * a.chunk;
     const int hi = min(n_valid, lo + a.chunk);
     const int h0 = uc.kh * a.G + uc.grp * a.GP;
@@ -779,7 +804,13 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
           O += wt * sm_o[(w * MH + gl2) * D + d];
         }
         const size_t row = row_base + gg;
-        if (a.S_eff == 1) {
+        if constexpr (kCl) {  // merged across the cluster below
+          if (d == 0) {
+            cl_m[gg] = M;
+            cl_l[gg] = L;
+          }
+          cl_o[gg * D + d] = O;
+        } else if (a.S_eff == 1) {
           store_out(a, row * D + d, O / L);
         } else {
           const size_t slot = row * a.S + uc.s;
@@ -792,7 +823,40 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1>::kCtas) decode_qtc
       }
       named_bar_sync(1, 32 * kConsumerWarps);
     }
-    if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
+    if constexpr (kCl) {
+      // ---- cluster merge: every CTA's (m, l, o) of the unit's heads is in its shared memory;
+      // CTA r merges outputs r*128 + ct, r*128 + ct + S*128, ... of the unit's gvalid x D
+      // (log-sum-exp weights, an empty split weighs 0) and writes them as fp16.  Every thread
+      // of every CTA (the producer warp too) passes both barriers, on every path.
+      cluster_sync_all();
+      const int S = a.S_eff;
+      const uint32_t r = cluster_ctarank();
+      for (int idx = int(r) * (32 * kConsumerWarps) + ct; idx < gvalid * D; idx += S * 32 * kConsumerWarps) {
+        const int gg = idx / D, d = idx - gg * D;
+        const uint32_t am = smem_u32(cl_m + gg), al = smem_u32(cl_l + gg), ao = smem_u32(cl_o + gg * D + d);
+        float mj[kMaxCluster];
+        float M = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kMaxCluster; ++j) {
+          mj[j] = j < S ? ld_dsmem_f32(dsmem_addr(am, j)) : -INFINITY;
+          M = fmaxf(M, mj[j]);
+        }
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMaxCluster; ++j) {
+          if (j < S && mj[j] != -INFINITY) {
+            const float wt = ex2(mj[j] - M);
+            L = fmaf(wt, ld_dsmem_f32(dsmem_addr(al, j)), L);
+            O = fmaf(wt, ld_dsmem_f32(dsmem_addr(ao, j)), O);
+          }
+        }
+        store_out(a, (row_base + gg) * D + d, O / L);
+      }
+      // no CTA may exit (and release its shared memory) while others still read it
+      cluster_sync_all();
+    } else {
+      if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
+    }
   }
 }
 
@@ -810,6 +874,57 @@ void launch_one(const DecodeLaunch& a, cudaStream_t stream) {
   launch_pdl(decode_qtc_kernel<D, I4, G1>, dim3(a.grid), dim3(kThreads), QtcCfg<D, I4, G1>::kSmemBytes, stream, a);
 }
 
+// int8 GQA with the split CTAs of a unit merged inside one thread-block cluster.
+template <int D>
+cudaError_t launch_cluster(const DecodeLaunch& a, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = QtcCfg<D, false, false, true>::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(a.cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, decode_qtc_kernel<D, false, false, true>, a);
+}
+
+// Resident clusters of the cluster-merge int8 GQA kernel per cluster size (2..16).
+template <int D>
+cudaError_t prepare_cluster(int (&max_clusters)[17]) {
+  const void* fn = reinterpret_cast<const void*>(&decode_qtc_kernel<D, false, false, true>);
+  const size_t smem = QtcCfg<D, false, false, true>::kSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  max_clusters[0] = max_clusters[1] = 0;
+  for (int c = 2; c <= kMaxCluster; ++c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(c);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+      cudaGetLastError();  // an unsupported size is not an error of the library
+      n = 0;
+    }
+    max_clusters[c] = n;
+  }
+  return cudaSuccess;
+}
+
 }  // namespace
 
 // int8 codes reach this kernel only with several query heads per KV head
@@ -820,9 +935,17 @@ cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm) {
   return D == 128 ? prepare_one<128, false, false>(ctas_per_sm) : prepare_one<64, false, false>(ctas_per_sm);
 }
 
+cudaError_t decode_kernel_prepare_qtc_cluster(int D, int (&max_clusters)[17]) {
+  return D == 128 ? prepare_cluster<128>(max_clusters) : prepare_cluster<64>(max_clusters);
+}
+
 cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream) {
   const bool i4 = a.fmt == KvFormat::I4Tc;
   if (i4 != (a.GP == 1)) return cudaErrorInvalidValue;
+  if (a.cluster) {
+    if (i4) return cudaErrorInvalidValue;  // only the several-heads variant merges in a cluster
+    return a.D == 128 ? launch_cluster<128>(a, stream) : launch_cluster<64>(a, stream);
+  }
   if (i4) {
     if (a.D == 128) launch_one<128, true, true>(a, stream);
     else launch_one<64, true, true>(a, stream);

@@ -62,6 +62,7 @@ struct DeviceState {
   int occ_q[2][2] = {{0, 0}, {0, 0}};  // [int4][D==128]
   int occ_qtc[2][2] = {{0, 0}, {0, 0}};  // tensor-core quantized kernel [int4][D==128]
   int max_clusters_f16[2][17] = {};      // fp16 cluster mode: resident clusters per cluster size [D==128][size]
+  int max_clusters_qtc[2][17] = {};      // int8 GQA cluster mode: the same for the tensor-core kernel
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -85,6 +86,8 @@ void init_device(DeviceState& ds, int dev) {
   for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_f16(i ? 128 : 64, &ds.occ_f16[i]);
   for (int i = 0; i < 2 && e == cudaSuccess; ++i)
     e = fqkv::decode_kernel_prepare_f16_cluster(i ? 128 : 64, ds.max_clusters_f16[i]);
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i)
+    e = fqkv::decode_kernel_prepare_qtc_cluster(i ? 128 : 64, ds.max_clusters_qtc[i]);
   for (int q = 0; q < 2 && e == cudaSuccess; ++q)
     for (int i = 0; i < 2 && e == cudaSuccess; ++i)
       e = fqkv::decode_kernel_prepare_quant(q == 1, i ? 128 : 64, &ds.occ_q[q][i]);
@@ -360,22 +363,31 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   //    N=16K: 11.8 -> 12.6 us; B=4, N=64K: 83 -> 97 us).
   const int mode = g_split_mode.load();
   const int64_t short_n = a.D == 128 ? 32768 : 4096;
-  const bool auto_ok = a.N <= short_n ? true : (a.D == 128 && se > 1);
-  if (a.fmt == KvFormat::F16 && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
+  const bool f16 = a.fmt == KvFormat::F16;
+  // int8 GQA (tensor-core kernel, sized for 4 co-resident CTAs per SM with a 2-stage ring, so a
+  // split that streams alone is slow): the cluster merge only for small, short calls, where it
+  // measured faster (us per call, combine -> cluster; Hkv = 8): batch 1, N = 640 / 2048 / 4096:
+  // D = 64 5.77 -> 4.54, 6.59 -> 6.06, 7.86 -> 7.33; D = 128 8.49 -> 5.43, 10.30 -> 8.86, 11.96
+  // -> 11.38; batch 2, N = 640: 5.90 -> 5.15, 9.14 -> 7.45.  Longer or larger calls lost up to
+  // 2.7x (batch 1, N = 16K, D = 128: 17.3 -> 25.1; batch 4, N = 2048: 11.3 -> 16.1).
+  const bool i8_small = !f16 && (units0 * a.N <= 16384 || (units0 <= 8 && a.N <= 4096));
+  const bool auto_ok = f16 ? (a.N <= short_n ? true : (a.D == 128 && se > 1)) : i8_small;
+  if ((f16 || a.fmt == KvFormat::I8Gqa) && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
       (mode == FQKV_SPLIT_CLUSTER || auto_ok) && units0 < ds.sm_count) {
     int64_t sc = std::min<int64_t>({16, tiles, std::max<int64_t>(1, ds.sm_count / units0)});
     if (S_fixed > 0) sc = std::min<int64_t>(sc, S_fixed);
     const int di = a.D == 128 ? 1 : 0;
+    const int(&max_cl)[17] = f16 ? ds.max_clusters_f16[di] : ds.max_clusters_qtc[di];
     // the largest cluster size (<= sc) whose clusters are all resident at once
     int64_t cct = 0, cse = 0;
     const int64_t sc0 = sc;
     for (; sc >= 2; --sc) {
       geometry(sc, &cct, &cse);
-      if (cse >= 2 && units0 <= ds.max_clusters_f16[di][cse]) break;
+      if (cse >= 2 && units0 <= max_cl[cse]) break;
     }
     const bool reduced = sc < sc0;
-    if (sc >= 2 && cse >= 2 && units0 <= ds.max_clusters_f16[di][cse] &&
-        (mode == FQKV_SPLIT_CLUSTER || a.N <= short_n || (!reduced && 2 * units0 * cse >= ds.sm_count))) {
+    const bool f16_ok = f16 && (a.N <= short_n || (!reduced && 2 * units0 * cse >= ds.sm_count));
+    if (sc >= 2 && cse >= 2 && units0 <= max_cl[cse] && (mode == FQKV_SPLIT_CLUSTER || f16_ok || i8_small)) {
       ct = cct;
       se = cse;
       a.cluster = int(cse);

@@ -128,6 +128,8 @@ KernelShape decode_kernel_shape_quant(bool int4, int D);
 cudaError_t decode_kernel_prepare_quant(bool int4, int D, int* ctas_per_sm);
 cudaError_t launch_decode_quant(const DecodeLaunch& a, cudaStream_t stream);
 cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm);
+// Resident thread-block clusters (sizes 2..16) of the int8 GQA tensor-core kernel's cluster-merge form.
+cudaError_t decode_kernel_prepare_qtc_cluster(int D, int (&max_clusters)[17]);
 cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream);
 // Fused RoPE + q cast + KV append (quantize.cu).
 cudaError_t launch_rope_append(bool bf16, bool int8_cache, const void* qkv, int64_t qkv_stride, const void* cos_t,

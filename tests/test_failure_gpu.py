@@ -25,8 +25,11 @@ def _status(fqkv, clear=0):
     return st.value
 
 
-@pytest.mark.parametrize("kind", ["gqa", "int8", "int4", "gqa_int8"])
+@pytest.mark.parametrize("kind", ["gqa", "int8", "int4", "gqa_int8", "gqa_int8_cluster"])
 def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
+    """A pipeline whose tiles never arrive: every bounded wait gives up, the kernel unwinds by itself
+    (in the cluster-merge forms every thread still passes both cluster barriers), status 61 is
+    recorded, and the context stays usable.  The "gqa" shape (N = 300) runs the fp16 cluster merge."""
     lib = fqkv.native.lib()
     g = torch.Generator().manual_seed(5)
     B, Hq, Hkv, N, D = 2, 8, 2, 300, 128
@@ -47,14 +50,17 @@ def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
             Kp, Ks = fqkv.quant_int4_per_token(K.view(B * Hkv, N, D))
             Vp, Vs = fqkv.quant_int4_per_token(V.view(B * Hkv, N, D))
             fqkv.decode_attn_int4(q[:, :Hkv].reshape(B * Hkv, D).contiguous(), Kp, Vp, Ks, Vs, 8)
-        else:  # tensor-core quantized kernel, several heads per KV row
+        else:  # tensor-core quantized kernel, several heads per KV row (forced: its cluster-merge form)
             Kq, Ks = fqkv.qpt(K)
             Vq, Vs = fqkv.qpt(V)
+            if kind == "gqa_int8_cluster":
+                fqkv.native.check(lib.fqkv_set_split_mode(fqkv.native.SPLIT_CLUSTER), "split mode")
             fqkv.decode_attn_gqa_int8(q, Kq, Vq, Ks, Vs)
         torch.cuda.synchronize()
     finally:
         lib.fqkv_debug_skip_loads(0)
         lib.fqkv_set_wait_timeout_ms(2000)
+        lib.fqkv_set_split_mode(fqkv.native.SPLIT_AUTO)
     assert _status(fqkv, clear=1) == 61          # a consumer's wait for a tile ran out
     assert _status(fqkv) == 0
     out = fqkv.decode_attn_gqa(q, K, V, 8)        # the context is still healthy

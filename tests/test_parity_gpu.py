@@ -491,6 +491,58 @@ def test_split_merge_modes_agree_with_oracle(fqkv, split_mode, B, Hq, Hkv, N, D)
 
 
 @pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("B,Hq,Hkv,N", [(1, 32, 8, 16384), (1, 32, 8, 1000), (1, 32, 8, 65), (2, 32, 8, 4097),
+                                        (1, 8, 1, 3000), (1, 64, 4, 2048), (3, 12, 4, 777), (4, 32, 8, 640)])
+def test_int8_gqa_split_merge_modes_agree_with_oracle(fqkv, split_mode, B, Hq, Hkv, N, D):
+    """int8 GQA on the tensor-core kernel: a split plan merged in one launch through a thread-block
+    cluster's distributed shared memory, and by the partials + combine kernel pair -- both against
+    the oracle on the dequantised cache, and each other."""
+    q = _randn(B, Hq, D, seed=190).cuda()
+    Kq, Ks = fqkv.qpt(_randn(B, Hkv, N, D, seed=191).cuda())
+    Vq, Vs = fqkv.qpt(_randn(B, Hkv, N, D, seed=192).cuda())
+    ref = oatt.decode_attention_gqa(q.cpu().numpy(), oq.dequantize_int8(Kq.cpu().numpy(), Ks.cpu().numpy()),
+                                    oq.dequantize_int8(Vq.cpu().numpy(), Vs.cpu().numpy()))
+    outs = {}
+    for mode in (fqkv.native.SPLIT_CLUSTER, fqkv.native.SPLIT_COMBINE, fqkv.native.SPLIT_AUTO):
+        split_mode(mode)
+        outs[mode] = fqkv.decode_attn_gqa_int8(q, Kq, Vq, Ks, Vs)
+        _close(outs[mode], ref)
+    torch.testing.assert_close(outs[fqkv.native.SPLIT_CLUSTER].float(), outs[fqkv.native.SPLIT_COMBINE].float(),
+                               atol=1e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_int8_gqa_cluster_merge_kvcache_in_graph(fqkv, split_mode, D):
+    """The int8 GQA cluster merge over a device-length cache whose tail holds garbage codes and NaN /
+    inf scales, inside a CUDA graph replayed as the cache grows."""
+    split_mode(fqkv.native.SPLIT_CLUSTER)
+    B, Hq, Hkv, max_len = 1, 32, 8, 8192
+    q = _randn(B, Hq, D, seed=193).cuda()
+    Kq = torch.randint(-127, 128, (B, Hkv, max_len, D), dtype=torch.int8, device="cuda")
+    Vq = torch.randint(-127, 128, (B, Hkv, max_len, D), dtype=torch.int8, device="cuda")
+    Ks = torch.full((B, Hkv, max_len), float("nan"), dtype=torch.float16, device="cuda")
+    Vs = torch.full_like(Ks, float("inf"))
+    k8, ks = fqkv.qpt(_randn(B, Hkv, 6000, D, seed=194).cuda())
+    v8, vs = fqkv.qpt(_randn(B, Hkv, 6000, D, seed=195).cuda())
+    Kq[:, :, :6000], Ks[:, :, :6000], Vq[:, :, :6000], Vs[:, :, :6000] = k8, ks, v8, vs
+    n_dev = torch.tensor([100], dtype=torch.int32, device="cuda")
+    o = torch.empty(B, Hq, D, dtype=torch.float16, device="cuda")
+    fqkv.decode_attn_gqa_int8_kvcache(q, Kq, Vq, Ks, Vs, n_dev, out=o)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fqkv.decode_attn_gqa_int8_kvcache(q, Kq, Vq, Ks, Vs, n_dev, out=o)
+    for n in (100, 64, 1, 4097, 6000, 5999):
+        n_dev.fill_(n)
+        g.replay()
+        torch.cuda.synchronize()
+        ref = oatt.decode_attention_gqa(q.cpu().numpy(),
+                                        oq.dequantize_int8(Kq[:, :, :n].cpu().numpy(), Ks[:, :, :n].cpu().numpy()),
+                                        oq.dequantize_int8(Vq[:, :, :n].cpu().numpy(), Vs[:, :, :n].cpu().numpy()))
+        assert torch.isfinite(o).all()
+        _close(o, ref)
+
+
+@pytest.mark.parametrize("D", [64, 128])
 def test_cluster_merge_sk_fast_and_kvcache(fqkv, split_mode, D):
     """gqa_sk_fast (batch 1) and a device-length KV cache with a NaN tail, in cluster mode, inside a
     CUDA graph replayed as the cache grows."""
