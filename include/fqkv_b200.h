@@ -74,13 +74,12 @@ void fqkv_set_wait_timeout_ms(uint32_t ms);
  * such launches are undefined.  Never enable it outside tests. */
 void fqkv_debug_skip_loads(int enable);
 
-/* How split plans of the fp16 kernel merge their splits (process-wide).
- * FQKV_SPLIT_AUTO (default): the library decides per call.  When a grid is
- * too small to fill the GPU unsplit (e.g. batch-1 decode), the split CTAs of
- * each unit form a thread-block cluster that merges through distributed
- * shared memory in the same launch (no workspace used); otherwise splits
- * write fp32 partials to the workspace and a second, PDL-chained kernel
- * merges them.  FQKV_SPLIT_COMBINE: always the partials + combine kernel.
+/* How split plans of the fp16 and the int8 GQA kernels merge their splits
+ * (process-wide).  FQKV_SPLIT_AUTO (default): the library decides per call.
+ * For small grids (batch-1 decode, short contexts) the split CTAs of each
+ * unit form a thread-block cluster that merges through distributed shared
+ * memory in the same launch (no workspace used); otherwise splits write fp32
+ * partials to the workspace and a second, PDL-chained kernel merges them.  FQKV_SPLIT_COMBINE: always the partials + combine kernel.
  * FQKV_SPLIT_CLUSTER: the cluster merge whenever the grid fits on the GPU.
  * Results agree to fp32 rounding.  For tuning and tests; no counterpart in
  * the reference (which always launches its partial + combine kernel pair). */
