@@ -39,6 +39,12 @@
 //    permutes per register pair, P * Vscale is a three-plane 8-bit fixed-point
 //    number in frames of one reference maximum and scale (see g1_key and
 //    g1_flush below).  The softmax denominator sums the unscaled probabilities.
+//  * Split plans of the several-heads variant merge either through fp32
+//    partials and the PDL-chained combine kernel, or (kCl, small short calls)
+//    inside one thread-block cluster: each CTA leaves its merged (m, l, O) of
+//    the group's heads in shared memory and, after a cluster barrier that the
+//    producer warp joins on every path, CTA r merges a slice of the outputs
+//    through distributed shared memory -- one launch, no workspace.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
