@@ -341,9 +341,10 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   int64_t ct, se;
   geometry(best_split(false), &ct, &se);
   a.cluster = 0;
-  // Cluster mode (fp16, local output): when the grid is too small to fill the GPU without
-  // splitting, the S split CTAs of each unit form one thread-block cluster (S <= 16), one CTA
-  // per SM, and merge through distributed shared memory -- one launch, no partials, no combine.
+  // Cluster mode (fp16 and int8 GQA, local output): when the grid is too small to fill the GPU
+  // without splitting, the S split CTAs of each unit form one thread-block cluster (S <= 16) and
+  // merge through distributed shared memory -- one launch, no partials, no combine.  The fp16
+  // kernel's cluster form runs one CTA per SM with a deep ring and two consumer groups.
   // The cluster is the largest size whose clusters are all resident at once (batch 1 with 8 KV
   // heads would need 8 resident clusters of 16 and B200 holds 7 -- one GPC has fewer than 16 SMs
   // free -- so it gets 10).  Automatic choice, from forced-mode sweeps on B200 (us per call,
