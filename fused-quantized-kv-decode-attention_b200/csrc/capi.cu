@@ -365,13 +365,14 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   const int mode = g_split_mode.load();
   const int64_t short_n = a.D == 128 ? 32768 : 4096;
   const bool f16 = a.fmt == KvFormat::F16;
-  // int8 GQA (tensor-core kernel, sized for 4 co-resident CTAs per SM with a 2-stage ring, so a
-  // split that streams alone is slow): the cluster merge only for small, short calls, where it
-  // measured faster (us per call, combine -> cluster; Hkv = 8): batch 1, N = 640 / 2048 / 4096:
-  // D = 64 5.77 -> 4.54, 6.59 -> 6.06, 7.86 -> 7.33; D = 128 8.49 -> 5.43, 10.30 -> 8.86, 11.96
-  // -> 11.38; batch 2, N = 640: 5.90 -> 5.15, 9.14 -> 7.45.  Longer or larger calls lost up to
-  // 2.7x (batch 1, N = 16K, D = 128: 17.3 -> 25.1; batch 4, N = 2048: 11.3 -> 16.1).
-  const bool i8_small = !f16 && (units0 * a.N <= 16384 || (units0 <= 8 && a.N <= 4096));
+  // int8 GQA (tensor-core kernel; its cluster form runs one CTA per SM with an 8-stage ring): the
+  // cluster merge for short calls, where it measured faster than partials + combine (us per call,
+  // combine -> cluster; Hkv = 8): D = 64, N = 640 / 2048 / 4096: batch 1 5.78 -> 4.00, 6.59 -> 4.63,
+  // 7.86 -> 5.86; batch 4 7.28 -> 4.65, 7.88 -> 6.02, 9.30 -> 8.48; batch 8 9.07 -> 5.24; D = 128:
+  // batch 1 8.49 -> 4.68, 10.28 -> 6.35, 11.95 -> 8.25; batch 4 8.70 -> 5.86, 11.30 -> 8.77, 14.99
+  // -> 13.15; batch 8 10.06 -> 7.59.  From N = 16K, and for 64 units beyond N = 640, it lost
+  // (batch 1, N = 16K, D = 128: 17.3 -> 18.8; batch 8, N = 2048, D = 128: 12.8 -> 13.8).
+  const bool i8_small = !f16 && a.N <= 4096 && (units0 < 64 || a.N <= 640);
   const bool auto_ok = f16 ? (a.N <= short_n ? true : (a.D == 128 && se > 1)) : i8_small;
   if ((f16 || a.fmt == KvFormat::I8Gqa) && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
       (mode == FQKV_SPLIT_CLUSTER || auto_ok) && units0 < ds.sm_count) {
