@@ -58,11 +58,12 @@
 namespace fqkv {
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kConsumerWarps = 4;  // consumer warps of one group: KPW keys of every tile each
 constexpr int kQMax = 32639;  // |q * Qs| bound: hi = (v + 128) >> 8 stays in [-127, 127]
 
-template <int D, bool I4, bool G1, bool kCl = false>
+// kCl: 0 = persistent grid; 1 / 2 = the split CTAs of a unit merge inside one thread-block cluster,
+// with one / two consumer groups per CTA.
+template <int D, bool I4, bool G1, int kCl = 0>
 struct QtcCfg {
   static constexpr int RB = I4 ? D / 2 : D;                   // bytes of one key row
   static constexpr int KPW = (!I4 && D == 128) ? 16 : 32;      // keys per consumer warp per tile
@@ -85,7 +86,14 @@ struct QtcCfg {
   static constexpr int MH = G1 ? 1 : 4;                        // heads merged per epilogue pass
   static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
   static constexpr size_t kBarBytes = 2 * kStages * sizeof(uint64_t);
-  static constexpr size_t kMergeBytes = size_t(kConsumerWarps) * (2 * 8 + MH * D) * sizeof(float);
+  // Cluster mode runs one CTA per SM; its two-group form has two consumer groups taking alternate
+  // tiles (twice the warps to issue the per-key work: batch 1, N = 16K, D = 128 18.8 -> 15.5 us),
+  // the one-group form serves splits of one or two tiles, where a second group would sit idle
+  // (N = 640: 5.3 -> 4.7 us); persistent mode has 3-4 CTAs per SM instead.
+  static constexpr int kGroups = kCl == 2 ? 2 : 1;
+  static constexpr int kCW = kConsumerWarps * kGroups;  // consumer warps
+  static constexpr int kThr = 32 * (kCW + 1);           // + the producer warp
+  static constexpr size_t kMergeBytes = size_t(kCW) * (2 * 8 + MH * D) * sizeof(float);
   // cluster mode (int8 GQA): this CTA's merged (m, l) of up to 8 heads and o [8][D], read by the cluster
   static constexpr size_t kClusterBytes = kCl ? (2 * 8 + 8 * D) * sizeof(float) : 0;
   static constexpr size_t kSmemBytes = 1024 + kRingBytes + kBarBytes + kMergeBytes + kClusterBytes;
@@ -101,10 +109,10 @@ struct UnitCoord {
 
 // Persistent mode: units ordered (b, kh, s, grp).  Cluster mode: (b, kh, grp, s),
 // so the S_eff split CTAs of one unit are consecutive blocks -- one cluster.
-template <bool kCl>
+template <int kCl>
 __device__ __forceinline__ UnitCoord decode_unit(const DecodeLaunch& a, int u) {
   UnitCoord c;
-  if constexpr (kCl) {
+  if constexpr (kCl != 0) {
     c.s = u % a.S_eff;
     u /= a.S_eff;
     c.grp = u % a.groups;
@@ -271,11 +279,11 @@ __device__ __forceinline__ void g1_flush(int (&oi)[8][4], int& bsum, float* so, 
   bsum = 0;
 }
 
-template <int D, bool I4, bool G1, bool kCl = false>
-__global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
+template <int D, bool I4, bool G1, int kCl = 0>
+__global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1, kCl>::kCtas) decode_qtc_kernel(const __grid_constant__ DecodeLaunch a) {
   using C = QtcCfg<D, I4, G1, kCl>;
   static_assert(I4 == G1, "int4 runs the one-head variant, int8 the GQA one");
-  static_assert(!kCl || !G1, "the cluster merge serves the several-heads (int8 GQA) variant");
+  static_assert(kCl == 0 || !G1, "the cluster merge serves the several-heads (int8 GQA) variant");
   constexpr int NSEG = C::NSEG;
   constexpr int MH = C::MH;
   constexpr int RB = C::RB;
@@ -294,9 +302,9 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::kRingBytes);
   uint64_t* empty = full + C::kStages;
   float* sm_m = reinterpret_cast<float*>(empty + C::kStages);
-  float* sm_l = sm_m + kConsumerWarps * 8;
-  float* sm_o = sm_l + kConsumerWarps * 8;
-  float* cl_m = sm_o + kConsumerWarps * MH * D;  // cluster mode: [8]
+  float* sm_l = sm_m + C::kCW * 8;
+  float* sm_o = sm_l + C::kCW * 8;
+  float* cl_m = sm_o + C::kCW * MH * D;  // cluster mode: [8]
   float* cl_l = cl_m + 8;                        // [8]
   float* cl_o = cl_l + 8;                        // [8][D]
   __shared__ int abort_flag;
@@ -309,12 +317,12 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], kConsumerWarps);  // the warps of the group that consumes the stage
     }
     abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kConsumerWarps && lane == 0) {
+  if (warp == C::kCW && lane == 0) {
     prefetch_tensormap(&a.tmK);
     prefetch_tensormap(&a.tmV);
   }
@@ -326,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
   const int n_valid = a.n_dev ? min(a.N, *a.n_dev) : a.N;
 
   // ------------------------------------------------------------ producer
-  if (warp == kConsumerWarps) {
+  if (warp == C::kCW) {
     if (lane == 0 && !a.debug_skip_loads) {
       int it = 0;
       bool ok = true;
@@ -367,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
           mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, wc, kDevTimeoutDrain);
       }
     }
-    if constexpr (kCl) {
+    if constexpr (kCl != 0) {
       // the whole warp takes part in the consumers' two cluster barriers (see the epilogue)
       __syncwarp();
       cluster_sync_all();
@@ -379,7 +387,8 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
   // ------------------------------------------------------------ consumers
   const int g = lane >> 2;
   const int t = lane & 3;
-  const int r0 = warp * KPW;
+  const int cgrp = warp / kConsumerWarps;       // consumer group: takes tiles it with it % kGroups == cgrp
+  const int r0 = (warp % kConsumerWarps) * KPW;
   const float csc = a.sm_scale_log2;
   // V rows are read in a t-parity-dependent key order where that avoids bank
   // conflicts (rows of <= 64 bytes); the pair selector undoes the swap.
@@ -492,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
     float vsc = 1099511627776.f, vk = 40.f;  // 2^40 = 2^vk; ex2(s - (m - vk)) = p * vsc, l sums the same
 
     for (int k0 = lo; k0 < hi; k0 += C::TK, ++it) {
+      if (C::kGroups > 1 && it % C::kGroups != cgrp) continue;
       const int st = it % C::kStages;
       if (alive) {
         const bool ok = mbar_wait(&full[st], (it / C::kStages) & 1, wc, kDevTimeoutFull) &&
@@ -796,24 +806,24 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
           }
         }
       }
-      named_bar_sync(1, 32 * kConsumerWarps);
+      named_bar_sync(1, 32 * C::kCW);
       const int nh = min(MH, gvalid - hp);
-      for (int idx = ct; idx < nh * D; idx += 32 * kConsumerWarps) {
+      for (int idx = ct; idx < nh * D; idx += 32 * C::kCW) {
         const int gl2 = idx / D, d = idx - gl2 * D;
         const int gg = hp + gl2;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_m[w * 8 + gg]);
+        for (int w = 0; w < C::kCW; ++w) M = fmaxf(M, sm_m[w * 8 + gg]);
         float L = 0.f, O = 0.f;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
+        for (int w = 0; w < C::kCW; ++w) {
           const float mw = sm_m[w * 8 + gg];
           const float wt = (mw == -INFINITY) ? 0.f : ex2(mw - M);
           L += wt * sm_l[w * 8 + gg];
           O += wt * sm_o[(w * MH + gl2) * D + d];
         }
         const size_t row = row_base + gg;
-        if constexpr (kCl) {  // merged across the cluster below
+        if constexpr (kCl != 0) {  // merged across the cluster below
           if (d == 0) {
             cl_m[gg] = M;
             cl_l[gg] = L;
@@ -830,9 +840,9 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
           a.part_o[slot * D + d] = O;
         }
       }
-      named_bar_sync(1, 32 * kConsumerWarps);
+      named_bar_sync(1, 32 * C::kCW);
     }
-    if constexpr (kCl) {
+    if constexpr (kCl != 0) {
       // ---- cluster merge: every CTA's (m, l, o) of the unit's heads is in its shared memory;
       // CTA r merges outputs r*128 + ct, r*128 + ct + S*128, ... of the unit's gvalid x D
       // (log-sum-exp weights, an empty split weighs 0) and writes them as fp16.  Every thread
@@ -840,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
       cluster_sync_all();
       const int S = a.S_eff;
       const uint32_t r = cluster_ctarank();
-      for (int idx = int(r) * (32 * kConsumerWarps) + ct; idx < gvalid * D; idx += S * 32 * kConsumerWarps) {
+      for (int idx = int(r) * (32 * C::kCW) + ct; idx < gvalid * D; idx += S * 32 * C::kCW) {
         const int gg = idx / D, d = idx - gg * D;
         const uint32_t am = smem_u32(cl_m + gg), al = smem_u32(cl_l + gg), ao = smem_u32(cl_o + gg * D + d);
         float mj[kMaxCluster];
@@ -864,7 +874,7 @@ __global__ void __launch_bounds__(kThreads, QtcCfg<D, I4, G1, kCl>::kCtas) decod
       // no CTA may exit (and release its shared memory) while others still read it
       cluster_sync_all();
     } else {
-      if (a.S_eff == 1) signal_out(a, ct, 1, 32 * kConsumerWarps);
+      if (a.S_eff == 1) signal_out(a, ct, 1, 32 * C::kCW);
     }
   }
 }
@@ -875,21 +885,22 @@ cudaError_t prepare_one(int* ctas_per_sm) {
   const size_t smem = QtcCfg<D, I4, G1>::kSmemBytes;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, kThreads, smem);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, fn, QtcCfg<D, I4, G1>::kThr, smem);
 }
 
 template <int D, bool I4, bool G1>
 void launch_one(const DecodeLaunch& a, cudaStream_t stream) {
-  launch_pdl(decode_qtc_kernel<D, I4, G1>, dim3(a.grid), dim3(kThreads), QtcCfg<D, I4, G1>::kSmemBytes, stream, a);
+  launch_pdl(decode_qtc_kernel<D, I4, G1>, dim3(a.grid), dim3(QtcCfg<D, I4, G1>::kThr), QtcCfg<D, I4, G1>::kSmemBytes,
+             stream, a);
 }
 
 // int8 GQA with the split CTAs of a unit merged inside one thread-block cluster.
-template <int D>
+template <int D, int kCl>
 cudaError_t launch_cluster(const DecodeLaunch& a, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = QtcCfg<D, false, false, true>::kSmemBytes;
+  cfg.blockDim = dim3(QtcCfg<D, false, false, kCl>::kThr);
+  cfg.dynamicSmemBytes = QtcCfg<D, false, false, kCl>::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -900,14 +911,15 @@ cudaError_t launch_cluster(const DecodeLaunch& a, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, decode_qtc_kernel<D, false, false, true>, a);
+  return cudaLaunchKernelEx(&cfg, decode_qtc_kernel<D, false, false, kCl>, a);
 }
 
-// Resident clusters of the cluster-merge int8 GQA kernel per cluster size (2..16).
-template <int D>
+// Resident clusters of the cluster-merge int8 GQA kernel per cluster size (2..16); both forms run one
+// CTA per SM, the two-group one (queried) with more threads and shared memory.
+template <int D, int kCl>
 cudaError_t prepare_cluster(int (&max_clusters)[17]) {
-  const void* fn = reinterpret_cast<const void*>(&decode_qtc_kernel<D, false, false, true>);
-  const size_t smem = QtcCfg<D, false, false, true>::kSmemBytes;
+  const void* fn = reinterpret_cast<const void*>(&decode_qtc_kernel<D, false, false, kCl>);
+  const size_t smem = QtcCfg<D, false, false, kCl>::kSmemBytes;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
@@ -915,7 +927,7 @@ cudaError_t prepare_cluster(int (&max_clusters)[17]) {
   for (int c = 2; c <= kMaxCluster; ++c) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(QtcCfg<D, false, false, kCl>::kThr);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -945,7 +957,9 @@ cudaError_t decode_kernel_prepare_qtc(bool int4, int D, int* ctas_per_sm) {
 }
 
 cudaError_t decode_kernel_prepare_qtc_cluster(int D, int (&max_clusters)[17]) {
-  return D == 128 ? prepare_cluster<128>(max_clusters) : prepare_cluster<64>(max_clusters);
+  cudaError_t e = D == 128 ? prepare_cluster<128, 1>(max_clusters) : prepare_cluster<64, 1>(max_clusters);
+  if (e != cudaSuccess) return e;  // the one-group form: attributes only (same residency per SM)
+  return D == 128 ? prepare_cluster<128, 2>(max_clusters) : prepare_cluster<64, 2>(max_clusters);
 }
 
 cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream) {
@@ -953,7 +967,10 @@ cudaError_t launch_decode_qtc(const DecodeLaunch& a, cudaStream_t stream) {
   if (i4 != (a.GP == 1)) return cudaErrorInvalidValue;
   if (a.cluster) {
     if (i4) return cudaErrorInvalidValue;  // only the several-heads variant merges in a cluster
-    return a.D == 128 ? launch_cluster<128>(a, stream) : launch_cluster<64>(a, stream);
+    // one consumer group when each split is one or two tiles, two otherwise
+    const bool two = a.chunk > 2 * (a.D == 128 ? QtcCfg<128, false, false, 2>::TK : QtcCfg<64, false, false, 2>::TK);
+    if (a.D == 128) return two ? launch_cluster<128, 2>(a, stream) : launch_cluster<128, 1>(a, stream);
+    return two ? launch_cluster<64, 2>(a, stream) : launch_cluster<64, 1>(a, stream);
   }
   if (i4) {
     if (a.D == 128) launch_one<128, true, true>(a, stream);

@@ -365,14 +365,15 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   const int mode = g_split_mode.load();
   const int64_t short_n = a.D == 128 ? 32768 : 4096;
   const bool f16 = a.fmt == KvFormat::F16;
-  // int8 GQA (tensor-core kernel; its cluster form runs one CTA per SM with an 8-stage ring): the
-  // cluster merge for short calls, where it measured faster than partials + combine (us per call,
-  // combine -> cluster; Hkv = 8): D = 64, N = 640 / 2048 / 4096: batch 1 5.78 -> 4.00, 6.59 -> 4.63,
-  // 7.86 -> 5.86; batch 4 7.28 -> 4.65, 7.88 -> 6.02, 9.30 -> 8.48; batch 8 9.07 -> 5.24; D = 128:
-  // batch 1 8.49 -> 4.68, 10.28 -> 6.35, 11.95 -> 8.25; batch 4 8.70 -> 5.86, 11.30 -> 8.77, 14.99
-  // -> 13.15; batch 8 10.06 -> 7.59.  From N = 16K, and for 64 units beyond N = 640, it lost
-  // (batch 1, N = 16K, D = 128: 17.3 -> 18.8; batch 8, N = 2048, D = 128: 12.8 -> 13.8).
-  const bool i8_small = !f16 && a.N <= 4096 && (units0 < 64 || a.N <= 640);
+  // int8 GQA (tensor-core kernel; its cluster form runs one CTA per SM with an 8-stage ring and one
+  // or two consumer groups): the cluster merge up to N = 16K (N = 4096 from 64 units on), where it
+  // measured faster than partials + combine (us per call, combine -> cluster; Hkv = 8): D = 64,
+  // N = 640 / 4096 / 16384: batch 1 5.76 -> 3.99, 7.85 -> 5.52, 11.58 -> 9.89; batch 4 6.79 ->
+  // 4.64, 9.30 -> 7.44, 21.10 -> 17.72; batch 8 9.02 -> 5.24, 10.71 -> 10.89; D = 128: batch 1
+  // 8.47 -> 4.69, 11.93 -> 7.88, 17.28 -> 15.47; batch 4 8.65 -> 5.85, 14.98 -> 11.40, 32.46 ->
+  // 31.00; batch 8 10.04 -> 6.87, 21.10 -> 17.70.  At N = 64K partials + combine stay faster
+  // (batch 1, D = 128: 37.2 against 47.3).
+  const bool i8_small = !f16 && a.N <= 16384 && (units0 < 64 || a.N <= 4096);
   const bool auto_ok = f16 ? (a.N <= short_n ? true : (a.D == 128 && se > 1)) : i8_small;
   if ((f16 || a.fmt == KvFormat::I8Gqa) && a.tp.world == 0 && mode != FQKV_SPLIT_COMBINE &&
       (mode == FQKV_SPLIT_CLUSTER || auto_ok) && units0 < ds.sm_count) {

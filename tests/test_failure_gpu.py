@@ -25,14 +25,15 @@ def _status(fqkv, clear=0):
     return st.value
 
 
-@pytest.mark.parametrize("kind", ["gqa", "int8", "int4", "gqa_int8", "gqa_int8_cluster"])
+@pytest.mark.parametrize("kind", ["gqa", "int8", "int4", "gqa_int8", "gqa_int8_cluster", "gqa_int8_cluster_long"])
 def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
     """A pipeline whose tiles never arrive: every bounded wait gives up, the kernel unwinds by itself
     (in the cluster-merge forms every thread still passes both cluster barriers), status 61 is
-    recorded, and the context stays usable.  The "gqa" shape (N = 300) runs the fp16 cluster merge."""
+    recorded, and the context stays usable.  The "gqa" shape (N = 300) runs the fp16 cluster merge;
+    the int8 cluster cases run its one-group (N = 300) and two-group (N = 4096) forms."""
     lib = fqkv.native.lib()
     g = torch.Generator().manual_seed(5)
-    B, Hq, Hkv, N, D = 2, 8, 2, 300, 128
+    B, Hq, Hkv, N, D = 2, 8, 2, 4096 if kind == "gqa_int8_cluster_long" else 300, 128
     q = torch.randn(B, Hq, D, generator=g).half().cuda()
     K = torch.randn(B, Hkv, N, D, generator=g).half().cuda()
     V = torch.randn(B, Hkv, N, D, generator=g).half().cuda()
@@ -53,7 +54,7 @@ def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
         else:  # tensor-core quantized kernel, several heads per KV row (forced: its cluster-merge form)
             Kq, Ks = fqkv.qpt(K)
             Vq, Vs = fqkv.qpt(V)
-            if kind == "gqa_int8_cluster":
+            if kind.startswith("gqa_int8_cluster"):
                 fqkv.native.check(lib.fqkv_set_split_mode(fqkv.native.SPLIT_CLUSTER), "split mode")
             fqkv.decode_attn_gqa_int8(q, Kq, Vq, Ks, Vs)
         torch.cuda.synchronize()
