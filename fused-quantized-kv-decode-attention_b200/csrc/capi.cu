@@ -63,6 +63,7 @@ struct DeviceState {
   int occ_qtc[2][2] = {{0, 0}, {0, 0}};  // tensor-core quantized kernel [int4][D==128]
   int max_clusters_f16[2][17] = {};      // fp16 cluster mode: resident clusters per cluster size [D==128][size]
   int max_clusters_qtc[2][17] = {};      // int8 GQA cluster mode: the same for the tensor-core kernel
+  int occ_quantize = 0;                  // staged quantizer CTAs per SM
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -93,6 +94,7 @@ void init_device(DeviceState& ds, int dev) {
       e = fqkv::decode_kernel_prepare_quant(q == 1, i ? 128 : 64, &ds.occ_q[q][i]);
   for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_qtc(false, i ? 128 : 64, &ds.occ_qtc[0][i]);
   for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = fqkv::decode_kernel_prepare_qtc(true, i ? 128 : 64, &ds.occ_qtc[1][i]);
+  if (e == cudaSuccess) e = fqkv::quantize_kernel_prepare(&ds.occ_quantize);
   if (e != cudaSuccess) return bad(FQKV_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -641,6 +643,10 @@ int fqkv_decode_attn_gqa_int8_kvcache(const void* q, const void* Kq, const void*
                     max_len, reinterpret_cast<const int*>(seq_len_dev));
 }
 
+static fqkv::QuantCtl quant_ctl(const DeviceState& ds) {
+  return fqkv::QuantCtl{ds.sm_count * std::max(1, ds.occ_quantize), ds.status, g_timeout_ns.load()};
+}
+
 static int run_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
                              int64_t D, int64_t cap, int64_t pos_host, const int32_t* pos_dev,
                              fqkv_stream_t stream) {
@@ -658,7 +664,7 @@ static int run_quantize_into(bool int4, const void* X, void* codes, void* scales
   DeviceState* ds = nullptr;
   if (int rc = device_state(&ds)) return rc;
   cudaError_t e = fqkv::launch_quantize_into(int4, X, codes, scales, groups, T, int(D), cap, pos_host,
-                                             reinterpret_cast<const int*>(pos_dev), ds->sm_count,
+                                             reinterpret_cast<const int*>(pos_dev), quant_ctl(*ds),
                                              reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
   return FQKV_OK;
@@ -717,7 +723,7 @@ static int run_quantize(bool int4, const void* X, void* codes, void* scales, int
   DeviceState* ds = nullptr;
   if (int rc = device_state(&ds)) return rc;
   cudaError_t e =
-      fqkv::launch_quantize(int4, X, codes, scales, rows, int(D), ds->sm_count, reinterpret_cast<cudaStream_t>(stream));
+      fqkv::launch_quantize(int4, X, codes, scales, rows, int(D), quant_ctl(*ds), reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
   return FQKV_OK;
 }

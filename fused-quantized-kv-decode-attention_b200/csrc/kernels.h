@@ -155,13 +155,23 @@ cudaError_t launch_tp_wait(const unsigned long long* counters, int world, unsign
 // chained to the preceding launch by programmatic dependent launch.
 cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream);
 
-cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D, int sm_count,
-                            cudaStream_t stream);
+// Per-token quantizers (quantize.cu).  ctas: the persistent grid's size limit
+// (resident CTAs of the staged kernel); status / timeout_ns: the bounded waits
+// of its shared-memory ring.  quantize_kernel_prepare sets the staged kernel's
+// dynamic shared-memory opt-in on the current device and returns its CTAs per SM.
+struct QuantCtl {
+  int ctas;
+  int* status;
+  unsigned long long timeout_ns;
+};
+cudaError_t quantize_kernel_prepare(int* ctas_per_sm);
+cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,
+                            const QuantCtl& ctl, cudaStream_t stream);
 // Quantize groups x T tokens [groups, T, D] into a cache [groups, cap, D]
 // (int4: [groups, cap, D/2]) at positions pos .. pos+T-1 of every group, pos =
 // *pos_dev if given else pos_host; D in {64, 128}; X 16-byte aligned.
 cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
-                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, int sm_count,
+                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, const QuantCtl& ctl,
                                  cudaStream_t stream);
 
 }  // namespace fqkv

@@ -29,8 +29,8 @@
 // (all-zero / tiny tokens, non-finite inputs) take the IEEE __fdiv_rn path
 // with the clamp and the NaN rule.
 //
-// HBM-bound: a persistent grid; each lane keeps 16-byte loads of kUnroll
-// tokens in flight (streaming, evict-first), D/8 lanes per token.
+// HBM-bound: a persistent grid whose CTAs stream 16 KiB tiles of tokens into
+// a shared-memory ring with bulk copies (quantize_tma_kernel below).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -104,50 +104,146 @@ struct QuantPlace {
   const int* pos_dev;
 };
 
-// Tokens whose 16-byte loads each lane of the quantizer keeps in flight.
-constexpr int kUnroll = 3;
+// Staged quantizer (D in {64, 128, 256}, X 16-byte aligned).  A persistent grid;
+// in every CTA one producer thread streams 16 KiB tiles of consecutive tokens
+// (8192 / D of them) into a 4-stage shared-memory ring with 1-D bulk copies
+// completing on mbarriers, and 8 consumer warps quantize each tile: D/16 lanes
+// per token, 16 elements per lane (two 16-byte shared-memory reads), so the
+// per-token amax reduction and scale are shared by 16 elements.  Codes leave by
+// plain 8-byte (int8) / 4-byte (int4) streaming stores, scales by 2-byte
+// stores.  The exact quotients use the packed fp32x2 multiply and FMAs of
+// sm_100 (the same IEEE operations as the scalar ones, two lanes at a time).
+constexpr int kQConsumerWarps = 8;
+constexpr int kQThreads = 32 * (kQConsumerWarps + 1);
+constexpr int kQStages = 4;
+constexpr int kQTileBytes = 16384;
+constexpr size_t kQSmemBytes = 128 + size_t(kQStages) * kQTileBytes + 2 * kQStages * sizeof(uint64_t);
 
+__device__ __forceinline__ unsigned long long f32x2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f32x2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f32x2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f32x2_fma(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
 
-// Vectorised path: D in {64, 128, 256}; LPR = D/8 lanes per token, each with 8
-// consecutive elements.  Persistent: warp w handles tokens w*RPW + j + i*stride.
+// Codes of the fp16 pair h for a normal fp16 scale s (ns2 = (-s, -s), y2 = (1/s~, 1/s~)):
+// quot_fast on both lanes, then code_pair_bits.
+__device__ __forceinline__ uint32_t code_pair_fast(__half2 h, unsigned long long ns2, unsigned long long y2) {
+  const float2 f = __half22float2(h);
+  const unsigned long long x2 = f32x2_pack(f.x, f.y);
+  const unsigned long long q0 = f32x2_mul(x2, y2);
+  const unsigned long long q1 = f32x2_fma(f32x2_fma(ns2, q0, x2), y2, q0);
+  float lo, hi;
+  f32x2_unpack(q1, lo, hi);
+  return code_pair_bits(lo, hi);
+}
+
 template <bool kInt4, int D, bool kPlace>
-__global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __restrict__ X, void* __restrict__ codes,
-                                                           __half* __restrict__ scales, int64_t rows,
-                                                           QuantPlace pl) {
-  constexpr int LPR = D / 8;
-  constexpr int RPW = 32 / LPR;
+__global__ void __launch_bounds__(kQThreads, 3)
+    quantize_tma_kernel(const __half* __restrict__ X, void* __restrict__ codes, __half* __restrict__ scales,
+                        int64_t rows, QuantPlace pl, WaitCtl wc) {
+  constexpr int kTok = kQTileBytes / (2 * D);  // tokens per tile
+  constexpr int kLPT = D / 16;                  // lanes per token
+  constexpr int kTPW = 32 / kLPT;               // tokens per warp and pass
+  constexpr int kPass = kTok / (kQConsumerWarps * kTPW);
   constexpr int Q = kInt4 ? 7 : 127;
+  static_assert(kPass == 2, "two passes of the consumer warps per tile");
+  extern __shared__ uint8_t qsmem_raw[];
+  uint8_t* smem = qsmem_raw + ((uint32_t(128) - (smem_u32(qsmem_raw) & 127u)) & 127u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kQStages) * kQTileBytes);
+  uint64_t* empty = full + kQStages;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int c = lane % LPR;
-  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  const int64_t stride = warps * RPW;  // tokens covered by one pass of all warps
-  const int64_t pos0 = kPlace ? (pl.pos_dev ? int64_t(*pl.pos_dev) : pl.pos_host) : 0;
-  for (int64_t wbase = ((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * RPW; wbase < rows;
-       wbase += kUnroll * stride) {  // warp-uniform: every lane takes part in the shuffles below
-    uint4 raw[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t row = wbase + lane / LPR + u * stride;
-      raw[u] = row < rows ? __ldcs(reinterpret_cast<const uint4*>(X + row * D + 8 * c)) : make_uint4(0, 0, 0, 0);
+  const int64_t ntiles = (rows + kTok - 1) / kTok;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kQConsumerWarps);
     }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------ producer
+  if (warp == kQConsumerWarps) {
+    if (lane != 0) return;
+    int it = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int st = it % kQStages;
+      if (it >= kQStages) {
+        if (*reinterpret_cast<volatile int*>(&abort_flag) ||
+            !mbar_wait(&empty[st], ((it / kQStages) - 1) & 1, wc, kDevTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+      }
+      const int64_t t0 = t * kTok;
+      const uint32_t bytes = uint32_t(rows - t0 < kTok ? rows - t0 : kTok) * (2 * D);
+      mbar_arrive_expect_tx(&full[st], bytes);
+      bulk_g2s(smem + size_t(st) * kQTileBytes, X + t0 * D, bytes, &full[st]);
+    }
+    if (!ok) {
+      for (int j = (it > kQStages ? it - kQStages : 0); j < it; ++j)
+        mbar_wait(&full[j % kQStages], (j / kQStages) & 1, wc, kDevTimeoutDrain);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int c = lane % kLPT;  // 16-element chunk of the token
+  const int tl = lane / kLPT;  // token slot of the warp
+  const int64_t pos0 = kPlace ? (pl.pos_dev ? int64_t(*pl.pos_dev) : pl.pos_host) : 0;
+  int it = 0;
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+    const int st = it % kQStages;
+    const bool ok = mbar_wait(&full[st], (it / kQStages) & 1, wc, kDevTimeoutFull) &&
+                    !*reinterpret_cast<volatile int*>(&abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) abort_flag = 1;
+      break;
+    }
+    const uint8_t* tile = smem + size_t(st) * kQTileBytes;
+    const int64_t t0 = t * kTok;
+    const int nt = int(rows - t0 < kTok ? rows - t0 : kTok);
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t row = wbase + lane / LPR + u * stride;
-      if (wbase + u * stride >= rows) break;  // warp-uniform
-      const __half2* h2 = reinterpret_cast<const __half2*>(&raw[u]);
-      // amax in fp16 (exact), NaN-propagating like torch.amax, reduced over the token's lanes
-      // as packed fp16 pairs: one shuffle per step carries both the maximum and any NaN
+    for (int p = 0; p < kPass; ++p) {
+      const int wtok = (p * kQConsumerWarps + warp) * kTPW;  // first token of this warp and pass
+      if (wtok >= nt) break;                                  // warp-uniform
+      const int tok = wtok + tl;
+      // tokens past nt (the last tile's tail) read stale tile bytes: computed, never stored
+      const uint4 ra = *reinterpret_cast<const uint4*>(tile + tok * (2 * D) + 32 * c);
+      const uint4 rb = *reinterpret_cast<const uint4*>(tile + tok * (2 * D) + 32 * c + 16);
+      __half2 h2[8];
+      *reinterpret_cast<uint4*>(&h2[0]) = ra;
+      *reinterpret_cast<uint4*>(&h2[4]) = rb;
+      // amax in fp16 (exact), NaN-propagating like torch.amax, as packed pairs
       __half2 m2 = __habs2(h2[0]);
 #pragma unroll
-      for (int i = 1; i < 4; ++i) m2 = __hmax2_nan(m2, __habs2(h2[i]));
+      for (int i = 1; i < 8; ++i) m2 = __hmax2_nan(m2, __habs2(h2[i]));
 #pragma unroll
-      for (int off = 1; off < LPR; off <<= 1) m2 = __hmax2_nan(m2, __shfl_xor_sync(0xffffffffu, m2, off));
+      for (int off = 1; off < kLPT; off <<= 1) m2 = __hmax2_nan(m2, __shfl_xor_sync(0xffffffffu, m2, off));
       m2 = __hmax2_nan(m2, __lowhigh2highlow(m2));
       const bool nan = __hisnan(__low2half(m2));
-      const float amax = __low2float(m2);
-      const __half sh = quant_scale_fast<Q>(amax, nan);
+      const __half sh = quant_scale_fast<Q>(__low2float(m2), nan);
       const float sc = __half2float(sh);
-      if (row >= rows) continue;
+      if (tok >= nt) continue;
+      const int64_t row = t0 + tok;
       int64_t orow = row;
       if constexpr (kPlace) {  // append into a cache: group row / T, position pos0 + row % T
         const int64_t pos = pos0 + row % pl.T;
@@ -156,32 +252,42 @@ __global__ void __launch_bounds__(256, 4) quantize_vec_kernel(const __half* __re
       }
       if (c == 0) scales[orow] = sh;
       // cb[i]: codes of elements 2i (byte 0) and 2i + 1 (byte 2)
-      uint32_t cb[4];
+      uint32_t cb[8];
       if (normal_fp16_scale(sc)) {
         const float y = rcp_approx(sc);
+        const unsigned long long y2 = f32x2_pack(y, y), ns2 = f32x2_pack(-sc, -sc);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(h2[i]);
-          cb[i] = code_pair_bits(quot_fast(f.x, sc, y), quot_fast(f.y, sc, y));
-        }
+        for (int i = 0; i < 8; ++i) cb[i] = code_pair_fast(h2[i], ns2, y2);
       } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 8; ++i) {
           const float2 f = __half22float2(h2[i]);
           cb[i] = (uint32_t(quant_code<Q>(f.x, sc)) & 0xFFu) | ((uint32_t(quant_code<Q>(f.y, sc)) & 0xFFu) << 16);
         }
       }
-      const uint32_t w0 = __byte_perm(cb[0], cb[1], 0x6420u);  // elements 0..3, one byte each
-      const uint32_t w1 = __byte_perm(cb[2], cb[3], 0x6420u);  // elements 4..7
-      if (kInt4) {
+      uint32_t w[4];  // elements 4i .. 4i + 3, one byte each
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = __byte_perm(cb[2 * i], cb[2 * i + 1], 0x6420u);
+      if constexpr (kInt4) {
         // byte t = (code[2t] & 0xF) | (code[2t+1] << 4): even elements from bytes 0/2, odd from 1/3
-        const uint32_t ev = __byte_perm(w0, w1, 0x6420u) & 0x0F0F0F0Fu;
-        const uint32_t od = (__byte_perm(w0, w1, 0x7531u) << 4) & 0xF0F0F0F0u;
-        __stcs(reinterpret_cast<unsigned int*>(codes) + (orow * D) / 8 + c, ev | od);
+        uint32_t pk[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const uint32_t ev = __byte_perm(w[2 * i], w[2 * i + 1], 0x6420u) & 0x0F0F0F0Fu;
+          const uint32_t od = (__byte_perm(w[2 * i], w[2 * i + 1], 0x7531u) << 4) & 0xF0F0F0F0u;
+          pk[i] = ev | od;
+        }
+        unsigned int* dst = reinterpret_cast<unsigned int*>(codes) + (orow * D) / 8 + 2 * c;
+        __stcs(dst, pk[0]);
+        __stcs(dst + 1, pk[1]);
       } else {
-        __stcs(reinterpret_cast<uint2*>(codes) + (orow * D) / 8 + c, make_uint2(w0, w1));
+        uint2* dst = reinterpret_cast<uint2*>(codes) + (orow * D) / 8 + 2 * c;
+        __stcs(dst, make_uint2(w[0], w[1]));
+        __stcs(dst + 1, make_uint2(w[2], w[3]));
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
   }
 }
 
@@ -222,30 +328,43 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const __half* __r
   }
 }
 
-// Persistent grid of the vectorised quantizer: enough 256-thread CTAs for every
-// token once (kUnroll tokens per lane), at most 4 per SM (64 registers per thread).
-int64_t quant_blocks(int64_t rows, int D, int sm_count) {
-  const int64_t warps_needed = (rows * (D / 8) + 31) / 32;
-  const int64_t blocks = (warps_needed + kUnroll * 8 - 1) / (kUnroll * 8);
-  return std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count) * 4));
+template <bool kInt4, int D, bool kPlace>
+cudaError_t launch_qt(const __half* x, void* codes, __half* sc, int64_t rows, const QuantPlace& pl,
+                      const QuantCtl& ctl, cudaStream_t stream) {
+  const int64_t ntiles = (rows * 2 * D + kQTileBytes - 1) / kQTileBytes;
+  const unsigned blocks = unsigned(std::max<int64_t>(1, std::min<int64_t>(ntiles, ctl.ctas)));
+  const WaitCtl wc{ctl.status, ctl.timeout_ns};
+  quantize_tma_kernel<kInt4, D, kPlace><<<blocks, kQThreads, kQSmemBytes, stream>>>(x, codes, sc, rows, pl, wc);
+  return cudaGetLastError();
+}
+
+template <bool kInt4, bool kPlace>
+cudaError_t launch_qt_d(const __half* x, void* codes, __half* sc, int64_t rows, int D, const QuantPlace& pl,
+                        const QuantCtl& ctl, cudaStream_t stream) {
+  if (D == 64) return launch_qt<kInt4, 64, kPlace>(x, codes, sc, rows, pl, ctl, stream);
+  if (D == 128) return launch_qt<kInt4, 128, kPlace>(x, codes, sc, rows, pl, ctl, stream);
+  return launch_qt<kInt4, 256, kPlace>(x, codes, sc, rows, pl, ctl, stream);
+}
+
+template <bool kInt4, int D, bool kPlace>
+cudaError_t prepare_qt() {
+  return cudaFuncSetAttribute(quantize_tma_kernel<kInt4, D, kPlace>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(kQSmemBytes));
 }
 
 template <bool kInt4>
-cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int D, int sm_count, cudaStream_t stream) {
+cudaError_t launch_q(const void* X, void* codes, void* scales, int64_t rows, int D, const QuantCtl& ctl,
+                     cudaStream_t stream) {
   const __half* x = static_cast<const __half*>(X);
   __half* sc = static_cast<__half*>(scales);
   const bool aligned = (reinterpret_cast<uintptr_t>(X) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(codes) % (kInt4 ? 4 : 8) == 0);
   if (aligned && (D == 64 || D == 128 || D == 256)) {
-    const unsigned blocks = unsigned(quant_blocks(rows, D, sm_count));
     const QuantPlace pl{rows, rows, 0, nullptr};
-    if (D == 64) quantize_vec_kernel<kInt4, 64, false><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else if (D == 128) quantize_vec_kernel<kInt4, 128, false><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<kInt4, 256, false><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-  } else {
-    const int64_t blocks = (rows * 32 + 255) / 256;
-    quantize_generic_kernel<kInt4><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, D);
+    return launch_qt_d<kInt4, false>(x, codes, sc, rows, D, pl, ctl, stream);
   }
+  const int64_t blocks = (rows * 32 + 255) / 256;
+  quantize_generic_kernel<kInt4><<<dim3(unsigned(blocks)), 256, 0, stream>>>(x, codes, sc, rows, D);
   return cudaGetLastError();
 }
 
@@ -384,28 +503,32 @@ cudaError_t launch_rope_append(bool bf16, bool int8_cache, const void* qkv, int6
                   : launch_rope_append_t<__half, 64>(a, int8_cache, stream);
 }
 
+cudaError_t quantize_kernel_prepare(int* ctas_per_sm) {
+  cudaError_t e = cudaSuccess;
+  for (cudaError_t r : {prepare_qt<false, 64, false>(), prepare_qt<false, 128, false>(), prepare_qt<false, 256, false>(),
+                        prepare_qt<true, 64, false>(), prepare_qt<true, 128, false>(), prepare_qt<true, 256, false>(),
+                        prepare_qt<false, 64, true>(), prepare_qt<false, 128, true>(), prepare_qt<false, 256, true>(),
+                        prepare_qt<true, 64, true>(), prepare_qt<true, 128, true>(), prepare_qt<true, 256, true>()})
+    if (e == cudaSuccess) e = r;
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, quantize_tma_kernel<false, 128, false>, kQThreads,
+                                                       kQSmemBytes);
+}
+
 cudaError_t launch_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,
-                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, int sm_count,
+                                 int D, int64_t cap, int64_t pos_host, const int* pos_dev, const QuantCtl& ctl,
                                  cudaStream_t stream) {
   const __half* x = static_cast<const __half*>(X);
   __half* sc = static_cast<__half*>(scales);
-  const int64_t rows = groups * T;
   const QuantPlace pl{T, cap, pos_host, pos_dev};
-  const unsigned blocks = unsigned(quant_blocks(rows, D, sm_count));
-  if (D == 64) {
-    if (int4) quantize_vec_kernel<true, 64, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<false, 64, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-  } else {
-    if (int4) quantize_vec_kernel<true, 128, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-    else quantize_vec_kernel<false, 128, true><<<blocks, 256, 0, stream>>>(x, codes, sc, rows, pl);
-  }
-  return cudaGetLastError();
+  return int4 ? launch_qt_d<true, true>(x, codes, sc, groups * T, D, pl, ctl, stream)
+              : launch_qt_d<false, true>(x, codes, sc, groups * T, D, pl, ctl, stream);
 }
 
-cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D, int sm_count,
-                            cudaStream_t stream) {
-  return int4 ? launch_q<true>(X, codes, scales, rows, D, sm_count, stream)
-              : launch_q<false>(X, codes, scales, rows, D, sm_count, stream);
+cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,
+                            const QuantCtl& ctl, cudaStream_t stream) {
+  return int4 ? launch_q<true>(X, codes, scales, rows, D, ctl, stream)
+              : launch_q<false>(X, codes, scales, rows, D, ctl, stream);
 }
 
 }  // namespace fqkv
