@@ -136,7 +136,7 @@ def dominant_kernel(w: dict, plan) -> str:
     """The library kernel(s) that take (nearly) all of a call's device time for workload `w` under `plan`."""
     k, D = w["kind"], w["D"]
     if k in ("quant8", "quant4"):
-        return "quantize_vec_kernel<int4>" if k == "quant4" else "quantize_vec_kernel<int8>"
+        return "quantize_tma_kernel<int4>" if k == "quant4" else "quantize_tma_kernel<int8>"
     names = {0: f"decode_f16_kernel<{D},{'1' if plan[1] else '0'}>", 1: f"decode_quant_kernel<false,{D}>",
              2: f"decode_quant_kernel<true,{D}>", 3: f"decode_qtc_kernel<{D},false,false>",
              4: f"decode_qtc_kernel<{D},true,true>"}
