@@ -379,9 +379,9 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         uint32_t vwd[C::kWords];
         lane_words<C::kLaneBytes>(vt + kl * C::kRowBytes + C::kLaneBytes * c, vwd);
         if (kInt4) {
-          // nibble n of word w is dim 8w + n.  One logic op leaves the nibble pair
-          // (n, n+4) in offset binary as fp16 subnormals s*(code+8) * 2^-24, s = 1
-          // or 16 (exact; the FMA takes them as they are); p/16 pairs with the
+          // nibble n of word w is dim 8w + n.  After one xor per word, one mask leaves
+          // the nibble pair (n, n+4) in offset binary as fp16 subnormals
+          // s*(code+8) * 2^-24, s = 1 or 16 (exact; the FMA takes them as they are); p/16 pairs with the
           // s = 16 halves.  The offset, 8 * 2^-24 * sum(p) per dimension, leaves
           // once per unit through bias_lo / bias_hi.
           const uint16_t ph16 = __half_as_ushort(__float2half_rn(pv * 0.0625f));
@@ -389,12 +389,14 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
           add_half(bias_hi, ph16);
 #pragma unroll
           for (int w = 0; w < C::kWords; ++w) {
-            const uint32_t x = vwd[w];
+            // one xor turns all eight nibbles to offset binary, so every field below is a
+            // single-constant mask (a mask and an xor constant together cost two logic ops)
+            const uint32_t x = vwd[w] ^ 0x88888888u;
             const uint32_t y = x >> 8;
-            const uint32_t a04 = (x & 0x000F000Fu) ^ 0x00080008u;
-            const uint32_t a15 = (x & 0x00F000F0u) ^ 0x00800080u;
-            const uint32_t a26 = (y & 0x000F000Fu) ^ 0x00080008u;
-            const uint32_t a37 = (y & 0x00F000F0u) ^ 0x00800080u;
+            const uint32_t a04 = x & 0x000F000Fu;
+            const uint32_t a15 = x & 0x00F000F0u;
+            const uint32_t a26 = y & 0x000F000Fu;
+            const uint32_t a37 = y & 0x00F000F0u;
             float* od = &o[(8 * w) % kDPL];
             fma_pair(od[0], od[4], a04, ph);
             fma_pair(od[1], od[5], a15, ph16);
