@@ -192,6 +192,9 @@ __device__ __forceinline__ uint32_t code_pair(uint32_t p) {
 }
 constexpr uint32_t kI8A = 0x64806480u, kI8B = 0xFF00FF00u;    // whole byte: int8 code
 
+// The low nibble of every byte as the unsigned byte code + 8, in one logic op.
+__device__ __forceinline__ uint32_t low_nibbles_offset(uint32_t x) { return xor_and<0x08080808u, 0x0F0F0F0Fu>(x); }
+
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
   return (uint32_t(a) & 0xFFu) | ((uint32_t(b) & 0xFFu) << 8) | ((uint32_t(c) & 0xFFu) << 16) |
          (uint32_t(d) << 24);
@@ -548,9 +551,8 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
               int acch[4] = {0, 0, 0, 0};
 #pragma unroll
               for (int kk = 0; kk < KS / 2; ++kk) {
-                const uint32_t al[4] = {(kw[0][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu, (kw[1][2 * kk] ^ 0x08080808u) & 0x0F0F0F0Fu,
-                                        (kw[0][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu,
-                                        (kw[1][2 * kk + 1] ^ 0x08080808u) & 0x0F0F0F0Fu};
+                const uint32_t al[4] = {low_nibbles_offset(kw[0][2 * kk]), low_nibbles_offset(kw[1][2 * kk]),
+                                        low_nibbles_offset(kw[0][2 * kk + 1]), low_nibbles_offset(kw[1][2 * kk + 1])};
                 const uint32_t ah[4] = {kw[0][2 * kk] & 0xF0F0F0F0u, kw[1][2 * kk] & 0xF0F0F0F0u,
                                         kw[0][2 * kk + 1] & 0xF0F0F0F0u, kw[1][2 * kk + 1] & 0xF0F0F0F0u};
                 mma_i8_16832<true, false>(acc, al, qa[kk][0], qa[kk][1]);
@@ -585,7 +587,7 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
 #pragma unroll
             for (int kk = 0; kk < KS / 2; ++kk) {
               const uint32_t w0 = kw[2 * kk], w1 = kw[2 * kk + 1];
-              mma_i8_16832<false, true>(acc, qa[kk], (w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu);
+              mma_i8_16832<false, true>(acc, qa[kk], low_nibbles_offset(w0), low_nibbles_offset(w1));
               mma_i8_16832<false, false>(acch, qa[KS / 2 + kk], w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u);
             }
             // 16 * (low sum - 8 sum q) + high sum (a multiple of 16); hf carries the 1/16
@@ -676,8 +678,8 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
             const uint32_t w1 = __byte_perm(vr[sg][0], vr[sg][1], 0x7531u);
             const uint32_t w2 = __byte_perm(vr[sg][2], vr[sg][3], 0x6420u);
             const uint32_t w3 = __byte_perm(vr[sg][2], vr[sg][3], 0x7531u);
-            const uint32_t al[4] = {(w0 ^ 0x08080808u) & 0x0F0F0F0Fu, (w1 ^ 0x08080808u) & 0x0F0F0F0Fu,
-                                    (w2 ^ 0x08080808u) & 0x0F0F0F0Fu, (w3 ^ 0x08080808u) & 0x0F0F0F0Fu};
+            const uint32_t al[4] = {low_nibbles_offset(w0), low_nibbles_offset(w1), low_nibbles_offset(w2),
+                                    low_nibbles_offset(w3)};
             const uint32_t ah[4] = {w0 & 0xF0F0F0F0u, w1 & 0xF0F0F0F0u, w2 & 0xF0F0F0F0u, w3 & 0xF0F0F0F0u};
             mma_i8_16832<true, false>(oi[sg], al, pb0, pb1);
             mma_i8_16832<false, false>(oi[NSEG + sg], ah, pb0, pb1);

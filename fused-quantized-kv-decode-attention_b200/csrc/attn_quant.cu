@@ -321,9 +321,8 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
           int ahe = 0, aho = 0, ale = 0, alo = 0;
 #pragma unroll
           for (int w = 0; w < C::kWords; ++w) {
-            const uint32_t x = kwd[w] ^ 0x88888888u;
-            const uint32_t ev = x & 0x0F0F0F0Fu;  // (code + 8) of even dims
-            const uint32_t od = x & 0xF0F0F0F0u;  // 16 * (code + 8) of odd dims
+            const uint32_t ev = xor_and<0x88888888u, 0x0F0F0F0Fu>(kwd[w]);  // (code + 8) of even dims
+            const uint32_t od = xor_and<0x88888888u, 0xF0F0F0F0u>(kwd[w]);  // 16 * (code + 8) of odd dims
             ahe = dp4a_su(qh[(2 * w) % kPW], ev, ahe);
             aho = dp4a_su(qh[(2 * w + 1) % kPW], od, aho);
             ale = dp4a_uu(ql[(2 * w) % kPW], ev, ale);
@@ -379,8 +378,8 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
         uint32_t vwd[C::kWords];
         lane_words<C::kLaneBytes>(vt + kl * C::kRowBytes + C::kLaneBytes * c, vwd);
         if (kInt4) {
-          // nibble n of word w is dim 8w + n.  After one xor per word, one mask leaves
-          // the nibble pair (n, n+4) in offset binary as fp16 subnormals
+          // nibble n of word w is dim 8w + n.  One logic op leaves the nibble pair
+          // (n, n+4) in offset binary as fp16 subnormals
           // s*(code+8) * 2^-24, s = 1 or 16 (exact; the FMA takes them as they are); p/16 pairs with the
           // s = 16 halves.  The offset, 8 * 2^-24 * sum(p) per dimension, leaves
           // once per unit through bias_lo / bias_hi.
@@ -389,14 +388,13 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
           add_half(bias_hi, ph16);
 #pragma unroll
           for (int w = 0; w < C::kWords; ++w) {
-            // one xor turns all eight nibbles to offset binary, so every field below is a
-            // single-constant mask (a mask and an xor constant together cost two logic ops)
-            const uint32_t x = vwd[w] ^ 0x88888888u;
+            // each field to offset binary in one logic op (xor and mask with register constants)
+            const uint32_t x = vwd[w];
             const uint32_t y = x >> 8;
-            const uint32_t a04 = x & 0x000F000Fu;
-            const uint32_t a15 = x & 0x00F000F0u;
-            const uint32_t a26 = y & 0x000F000Fu;
-            const uint32_t a37 = y & 0x00F000F0u;
+            const uint32_t a04 = xor_and<0x00080008u, 0x000F000Fu>(x);
+            const uint32_t a15 = xor_and<0x00800080u, 0x00F000F0u>(x);
+            const uint32_t a26 = xor_and<0x00080008u, 0x000F000Fu>(y);
+            const uint32_t a37 = xor_and<0x00800080u, 0x00F000F0u>(y);
             float* od = &o[(8 * w) % kDPL];
             fma_pair(od[0], od[4], a04, ph);
             fma_pair(od[1], od[5], a15, ph16);

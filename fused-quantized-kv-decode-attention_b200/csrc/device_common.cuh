@@ -191,6 +191,15 @@ __device__ __forceinline__ float frame_for(float v, float& k) {
   return __int_as_float((127 + 127 + 13 - e) << 23);
 }
 
+// (x ^ A) & B in one logic op.  The constants are register operands: as two immediates the
+// expression takes two instructions (a logic op carries at most one immediate).
+template <uint32_t A, uint32_t B>
+__device__ __forceinline__ uint32_t xor_and(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(r) : "r"(x), "r"(A), "r"(B));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
