@@ -644,7 +644,8 @@ int fqkv_decode_attn_gqa_int8_kvcache(const void* q, const void* Kq, const void*
 }
 
 static fqkv::QuantCtl quant_ctl(const DeviceState& ds) {
-  return fqkv::QuantCtl{ds.sm_count * std::max(1, ds.occ_quantize), ds.status, g_timeout_ns.load()};
+  return fqkv::QuantCtl{ds.sm_count * std::max(1, ds.occ_quantize), ds.status, g_timeout_ns.load(),
+                        g_debug_skip_loads.load()};
 }
 
 static int run_quantize_into(bool int4, const void* X, void* codes, void* scales, int64_t groups, int64_t T,

@@ -157,12 +157,13 @@ cudaError_t launch_combine(const DecodeLaunch& a, cudaStream_t stream);
 
 // Per-token quantizers (quantize.cu).  ctas: the persistent grid's size limit
 // (resident CTAs of the staged kernel); status / timeout_ns: the bounded waits
-// of its shared-memory ring.  quantize_kernel_prepare sets the staged kernel's
+// of its shared-memory ring; debug_skip_loads: the failure-path test hook.  quantize_kernel_prepare sets the staged kernel's
 // dynamic shared-memory opt-in on the current device and returns its CTAs per SM.
 struct QuantCtl {
   int ctas;
   int* status;
   unsigned long long timeout_ns;
+  int debug_skip_loads;  // test hook: the producer issues nothing
 };
 cudaError_t quantize_kernel_prepare(int* ctas_per_sm);
 cudaError_t launch_quantize(bool int4, const void* X, void* codes, void* scales, int64_t rows, int D,

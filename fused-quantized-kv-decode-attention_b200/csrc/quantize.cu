@@ -154,7 +154,7 @@ __device__ __forceinline__ uint32_t code_pair_fast(__half2 h, unsigned long long
 template <bool kInt4, int D, bool kPlace>
 __global__ void __launch_bounds__(kQThreads, 3)
     quantize_tma_kernel(const __half* __restrict__ X, void* __restrict__ codes, __half* __restrict__ scales,
-                        int64_t rows, QuantPlace pl, WaitCtl wc) {
+                        int64_t rows, QuantPlace pl, WaitCtl wc, int debug_skip_loads) {
   constexpr int kTok = kQTileBytes / (2 * D);  // tokens per tile
   constexpr int kLPT = D / 16;                  // lanes per token
   constexpr int kTPW = 32 / kLPT;               // tokens per warp and pass
@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kQThreads, 3)
 
   // ------------------------------------------------------------ producer
   if (warp == kQConsumerWarps) {
-    if (lane != 0) return;
+    if (lane != 0 || debug_skip_loads) return;
     int it = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
@@ -334,7 +334,8 @@ cudaError_t launch_qt(const __half* x, void* codes, __half* sc, int64_t rows, co
   const int64_t ntiles = (rows * 2 * D + kQTileBytes - 1) / kQTileBytes;
   const unsigned blocks = unsigned(std::max<int64_t>(1, std::min<int64_t>(ntiles, ctl.ctas)));
   const WaitCtl wc{ctl.status, ctl.timeout_ns};
-  quantize_tma_kernel<kInt4, D, kPlace><<<blocks, kQThreads, kQSmemBytes, stream>>>(x, codes, sc, rows, pl, wc);
+  quantize_tma_kernel<kInt4, D, kPlace><<<blocks, kQThreads, kQSmemBytes, stream>>>(x, codes, sc, rows, pl, wc,
+                                                                                    ctl.debug_skip_loads);
   return cudaGetLastError();
 }
 

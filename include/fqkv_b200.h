@@ -67,11 +67,12 @@ int fqkv_device_status(int* status_out, int clear);
  * default 2000).  Intended for tests of the failure path. */
 void fqkv_set_wait_timeout_ms(uint32_t ms);
 
-/* Test hook for the failure path: while enabled, decode launches issue no
- * tile loads, so every in-kernel wait for a tile runs out after the wait
- * limit; the kernel then unwinds (no load is in flight), records status 61 in
- * the device status word and returns, leaving the context usable.  Outputs of
- * such launches are undefined.  Never enable it outside tests. */
+/* Test hook for the failure path: while enabled, decode launches and the
+ * staged quantizers (D = 64, 128, 256) issue no tile loads, so every in-kernel
+ * wait for a tile runs out after the wait limit; the kernel then unwinds (no
+ * load is in flight), records status 61 in the device status word and
+ * returns, leaving the context usable.  Outputs of such launches are
+ * undefined.  Never enable it outside tests. */
 void fqkv_debug_skip_loads(int enable);
 
 /* How split plans of the fp16 and the int8 GQA kernels merge their splits

@@ -1,7 +1,7 @@
 """Failure detection without a GPU fault.
 
-Every mbarrier wait in the decode kernels is bounded.  The test hook
-``fqkv_debug_skip_loads`` makes the producer warp issue no tile loads, so the
+Every mbarrier wait in the decode kernels and the staged quantizers is bounded.
+The test hook ``fqkv_debug_skip_loads`` makes the producer issue no tile loads, so the
 consumers' waits for a tile run out after a short limit (a flag that nothing
 sets).  The kernel must unwind on its own, record status 61 in the device
 status word, and leave the CUDA context usable: the next normal launch
@@ -15,6 +15,7 @@ import pytest
 import torch
 
 from oracle import attention as oatt
+from oracle import quant as oq
 
 pytestmark = pytest.mark.gpu
 
@@ -25,18 +26,31 @@ def _status(fqkv, clear=0):
     return st.value
 
 
-@pytest.mark.parametrize("kind", ["gqa", "int8", "int4", "gqa_int8", "gqa_int8_cluster", "gqa_int8_cluster_long"])
+@pytest.mark.parametrize("kind", ["gqa", "int8", "int4", "gqa_int8", "gqa_int8_cluster", "gqa_int8_cluster_long",
+                                  "qpt", "quant_int4"])
 def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
     """A pipeline whose tiles never arrive: every bounded wait gives up, the kernel unwinds by itself
     (in the cluster-merge forms every thread still passes both cluster barriers), status 61 is
     recorded, and the context stays usable.  The "gqa" shape (N = 300) runs the fp16 cluster merge;
-    the int8 cluster cases run its one-group (N = 300) and two-group (N = 4096) forms."""
+    the int8 cluster cases run its one-group (N = 300) and two-group (N = 4096) forms; "qpt" and
+    "quant_int4" stall the staged quantizers' shared-memory ring."""
     lib = fqkv.native.lib()
     g = torch.Generator().manual_seed(5)
     B, Hq, Hkv, N, D = 2, 8, 2, 4096 if kind == "gqa_int8_cluster_long" else 300, 128
     q = torch.randn(B, Hq, D, generator=g).half().cuda()
     K = torch.randn(B, Hkv, N, D, generator=g).half().cuda()
     V = torch.randn(B, Hkv, N, D, generator=g).half().cuda()
+    # quantized inputs are made before the hook is on (the quantizers honour it too)
+    if kind == "int8":
+        Kq, Ks = fqkv.qpt(K.view(B * Hkv, N, D))
+        Vq, Vs = fqkv.qpt(V.view(B * Hkv, N, D))
+    elif kind == "int4":
+        Kp, Ks = fqkv.quant_int4_per_token(K.view(B * Hkv, N, D))
+        Vp, Vs = fqkv.quant_int4_per_token(V.view(B * Hkv, N, D))
+    elif kind.startswith("gqa_int8"):
+        Kq, Ks = fqkv.qpt(K)
+        Vq, Vs = fqkv.qpt(V)
+    torch.cuda.synchronize()
     assert _status(fqkv, clear=1) == 0
     lib.fqkv_set_wait_timeout_ms(50)
     lib.fqkv_debug_skip_loads(1)
@@ -44,16 +58,14 @@ def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
         if kind == "gqa":
             fqkv.decode_attn_gqa(q, K, V, 8)
         elif kind == "int8":
-            Kq, Ks = fqkv.qpt(K.view(B * Hkv, N, D))
-            Vq, Vs = fqkv.qpt(V.view(B * Hkv, N, D))
             fqkv.decode_attn_int8_mw(q[:, :Hkv].reshape(B * Hkv, D).contiguous(), Kq, Vq, Ks, Vs, 8)
         elif kind == "int4":  # tensor-core quantized kernel, one head per KV row
-            Kp, Ks = fqkv.quant_int4_per_token(K.view(B * Hkv, N, D))
-            Vp, Vs = fqkv.quant_int4_per_token(V.view(B * Hkv, N, D))
             fqkv.decode_attn_int4(q[:, :Hkv].reshape(B * Hkv, D).contiguous(), Kp, Vp, Ks, Vs, 8)
+        elif kind == "qpt":
+            fqkv.qpt(K)
+        elif kind == "quant_int4":
+            fqkv.quant_int4_per_token(K)
         else:  # tensor-core quantized kernel, several heads per KV row (forced: its cluster-merge form)
-            Kq, Ks = fqkv.qpt(K)
-            Vq, Vs = fqkv.qpt(V)
             if kind.startswith("gqa_int8_cluster"):
                 fqkv.native.check(lib.fqkv_set_split_mode(fqkv.native.SPLIT_CLUSTER), "split mode")
             fqkv.decode_attn_gqa_int8(q, Kq, Vq, Ks, Vs)
@@ -67,6 +79,10 @@ def test_stalled_pipeline_times_out_and_context_survives(fqkv, kind):
     out = fqkv.decode_attn_gqa(q, K, V, 8)        # the context is still healthy
     ref = oatt.decode_attention_gqa(q.cpu().numpy(), K.cpu().numpy(), V.cpu().numpy())
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-3, rtol=1e-2)
+    if kind in ("qpt", "quant_int4"):              # and the quantizer runs clean again
+        c, s = fqkv.qpt(K)
+        rc, rs = oq.quantize_int8_per_token(K.cpu().numpy())
+        assert np.array_equal(c.cpu().numpy(), rc)
     assert _status(fqkv) == 0
 
 
