@@ -355,7 +355,9 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   //    streaming and even where the split search alone would not split (D = 64, N = 512 / 640 /
   //    1024 / 2048: batch 1 4.76 -> 3.68, 5.42 -> 3.99, 5.68 -> 3.88, 6.38 -> 4.56; batch 4 5.56
   //    -> 4.21, 5.65 -> 4.65, 6.34 -> 4.90, 8.08 -> 7.25; batch 8 (unsplit plan) 7.82 -> 4.80,
-  //    6.90 -> 5.39, 8.10 -> 7.07, 10.16 -> 10.26), so it is taken up to N = 4096 at D = 64;
+  //    6.90 -> 5.39, 8.10 -> 7.07, 10.16 -> 10.26), so it is taken up to N = 4096 at D = 64, and
+  //    up to N = 8192 for a grid of at most 8 units (batch 1 with Hkv = 8: N = 8192 9.49 -> 8.60;
+  //    N = 16K 11.74 -> 12.58; batch 2 and 4 at N = 16K 15.7 -> 18.2 and 24.5 -> 25.7);
   //  * D = 128 up to N = 32K (batch 1, N = 2K / 16K / 32K / 64K: 7.21 -> 5.36, 16.99 -> 15.56,
   //    27.2 -> 26.4, 46.0 -> 47.4; batch 2: 8.75 -> 7.18, 25.8 -> 24.3, 44.8 -> 44.4, 83.0 -> 84.0;
   //    batch 3: 9.33 -> 8.77, 34.9 -> 33.0, 63.4 -> 61.3, 120.4 -> 116.8), and at any length when
@@ -365,7 +367,7 @@ void plan_geometry(DecodeLaunch& a, const DeviceState& ds, int64_t S_fixed, size
   //  * D = 64 longer contexts keep the combine: one CTA per SM streams too slowly there (batch 1,
   //    N=16K: 11.8 -> 12.6 us; B=4, N=64K: 83 -> 97 us).
   const int mode = g_split_mode.load();
-  const int64_t short_n = a.D == 128 ? 32768 : 4096;
+  const int64_t short_n = a.D == 128 ? 32768 : (units0 <= 8 ? 8192 : 4096);
   const bool f16 = a.fmt == KvFormat::F16;
   // int8 GQA (tensor-core kernel; its cluster form runs one CTA per SM with an 8-stage ring and one
   // or two consumer groups): the cluster merge up to N = 16K (N = 4096 from 64 units on), where it

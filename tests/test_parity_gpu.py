@@ -128,7 +128,8 @@ def test_gqa_bench_shape_sampled_rows(fqkv):
 # the reference's six cases (tests/test_kernels.py:59) plus larger S / N
 @pytest.mark.parametrize("N,D,S,W,CW", [(1024, 64, 8, 8, 4), (4096, 128, 16, 8, 4), (16384, 64, 64, 8, 8),
                                         (3, 128, 8, 4, 4), (1, 64, 4, 2, 4), (100, 64, 7, 4, 4),
-                                        (16384, 128, 64, 8, 8), (65536, 128, 128, 8, 8), (777, 128, 1, 8, 4)])
+                                        (16384, 128, 64, 8, 8), (65536, 128, 128, 8, 8), (777, 128, 1, 8, 4),
+                                        (8192, 64, 64, 8, 8)])
 def test_gqa_sk_fast(fqkv, N, D, S, W, CW):
     Hq, Hkv = 32, 8
     q, K, V = _randn(Hq, D, seed=40), _randn(Hkv, N, D, seed=41), _randn(Hkv, N, D, seed=42)
@@ -144,8 +145,8 @@ def test_gqa_sk_fast(fqkv, N, D, S, W, CW):
 # ------------------------------------------------------------------ properties
 def test_split_count_does_not_change_the_result(fqkv):
     """Same op with no workspace (one split) and with the preferred split-K plan (partials +
-    combine: at D = 64 batch 1 does not use the cluster merge)."""
-    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 64
+    combine: at D = 64 batch 1 past N = 8192 does not use the cluster merge)."""
+    B, Hq, Hkv, N, D = 1, 32, 8, 16384, 64
     q, K, V = (_randn(B, Hq, D, seed=50).cuda(), _randn(B, Hkv, N, D, seed=51).cuda(),
                _randn(B, Hkv, N, D, seed=52).cuda())
     lib = fqkv.native.lib()
@@ -184,8 +185,8 @@ def test_cuda_graph_capture_and_side_stream(fqkv):
 
 def test_split_launches_on_two_streams_at_once(fqkv):
     """Split launches (partial kernel + combine) in flight on two streams at once, each with its own workspace
-    (D = 64: batch 1 splits into partials + combine there)."""
-    B, Hq, Hkv, N, D = 1, 32, 8, 8192, 64
+    (D = 64: batch 1 past N = 8192 splits into partials + combine there)."""
+    B, Hq, Hkv, N, D = 1, 32, 8, 16384, 64
     assert fqkv.workspace_bytes("fp16", B, Hq, Hkv, N, D) > 0
     inputs = [(_randn(B, Hq, D, seed=100 + i).cuda(), _randn(B, Hkv, N, D, seed=110 + i).cuda(),
                _randn(B, Hkv, N, D, seed=120 + i).cuda()) for i in range(2)]
@@ -622,6 +623,13 @@ def test_split_plans_pick_the_cluster_merge_where_it_fits(fqkv):
             assert out[1] == out[0] >= 2, (B, N, list(out), fits64)
     fqkv.native.check(lib.fqkv_decode_plan(0, 1, 32, 8, 16384, 64, 1 << 30, out), "plan")
     assert out[0] > 1 and out[1] == 0, list(out)
+    # a grid of at most 8 units (batch 1) at D = 64 takes the cluster merge up to N = 8192
+    fits64 = [c for c in range(2, min(16, sm // 8) + 1) if max_clusters_64[c] >= 8]
+    fqkv.native.check(lib.fqkv_decode_plan(0, 1, 32, 8, 8192, 64, 1 << 30, out), "plan")
+    if fits64:
+        assert out[1] == out[0] >= 2, (list(out), fits64)
+    fqkv.native.check(lib.fqkv_decode_plan(0, 2, 32, 8, 8192, 64, 1 << 30, out), "plan")
+    assert out[1] == 0, list(out)
 
 
 @pytest.mark.parametrize("scale", [1e-4, 1e-3, 1e2, "ramp"])
