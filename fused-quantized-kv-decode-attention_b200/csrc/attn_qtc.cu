@@ -30,9 +30,11 @@
 //  * Several heads (int8): O^T += V^T (P * Vscale)^T on the fp16 tensor cores
 //    (m16n8k16): the A operand pairs one dimension of two consecutive keys,
 //    built in registers from the codes (a byte permute of the two keys' words,
-//    one three-input logic op forming an fp16 with the code in its mantissa,
-//    one exact fp16 subtraction); the B operand is the fp16 probabilities
-//    times the key's V scale, taken directly from the score accumulators.
+//    one three-input logic op forming the exact fp16 1152 + code); the B
+//    operand is the fp16 probabilities times the key's V scale, taken directly
+//    from the score accumulators.  The 1152 offset leaves once per unit:
+//    1152 times the per-head sum of the same B operand, which one extra MMA
+//    of an all-ones A tile accumulates per 16 keys.
 //    Rows of O^T are head dimensions, columns the group's heads.
 //  * One head (int4): the same product on the integer tensor cores
 //    (m16n8k32): V bytes arrive transposed by ldmatrix.trans plus two byte
@@ -179,18 +181,28 @@ __device__ __forceinline__ void mma_i8_16832(int (&d)[4], const uint32_t (&a)[4]
   }
 }
 
-// f(p) = B ? A : (p ^ A) bitwise, then an exact fp16x2 subtraction of A: with
-// p = {x.b, -, y.b, -} (byte b of the two keys' words) this turns the chosen
-// code field of each half into an exact fp16 (A holds 0x64 in the high byte of
-// each half, the field's sign-flip bit in the low byte; B marks constant bits).
+// f(p) = B ? A : (p ^ A) bitwise: with p = {x.b, -, y.b, -} (byte b of the two keys' words) each
+// half becomes an exact fp16 1024 + 128 + code (A holds 0x64 in the high byte of each half, the
+// code byte's sign-flip bit in the low byte; B marks the bits taken from A).  The int8 GQA P.V
+// multiplies these and removes 1152 * sum(P) once per unit -- sum(P) accumulated from the same
+// fp16 B operand, four mixed-precision adds per 16 keys -- instead of one fp16 subtraction per
+// code pair.
 template <uint32_t A, uint32_t B>
-__device__ __forceinline__ uint32_t code_pair(uint32_t p) {
+__device__ __forceinline__ uint32_t code_pair_offset(uint32_t p) {
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0x9c;" : "=r"(r) : "r"(p), "r"(A), "r"(B));
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(r), "r"(A));
   return r;
 }
 constexpr uint32_t kI8A = 0x64806480u, kI8B = 0xFF00FF00u;    // whole byte: int8 code
+constexpr float kI8Offset = 1152.f;
+
+// acc += both halves of an fp16 pair, exactly (mixed-precision FMAs by 1.0)
+__device__ __forceinline__ void add_half2(float& acc, uint32_t h2) {
+  asm("{\n\t.reg .f16 a, b, one;\n\tmov.b32 {a, b}, %1;\n\tmov.b16 one, 0x3C00;\n\t"
+      "fma.rn.f32.f16 %0, a, one, %0;\n\tfma.rn.f32.f16 %0, b, one, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(h2));
+}
 
 // The low nibble of every byte as the unsigned byte code + 8, in one logic op.
 __device__ __forceinline__ uint32_t low_nibbles_offset(uint32_t x) { return xor_and<0x08080808u, 0x0F0F0F0Fu>(x); }
@@ -482,7 +494,8 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
       }
     }
 
-    float o[MT][4];   // several heads: O^T in fp32
+    float o[MT][4];   // several heads: O^T in fp32 (codes carried as 1152 + code)
+    float pe = 0.f;   // several heads: this lane's sum of the fp16 B operand (head g)
     int oi[8][4];     // one head: the frame's integer O^T (see g1_flush)
     int bsum = 0, ftiles = 0;
     float ps = 0.f, inv_ps = 0.f;  // one head: the frame's fixed-point scale of P * vs and 1 / it
@@ -734,6 +747,7 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
               o[i][2] *= a_lo;
               o[i][3] *= a_hi;
             }
+            pe *= alpha * ratio;  // this lane's head is g
           }
           const float mu = ((m_run == -INFINITY) ? 0.f : m_run) - vk;  // ex2(s - mu) = p * vsc
           uint32_t pb[NJ];
@@ -754,12 +768,15 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
               const int w0 = i >> 2, w1 = (MT + i) >> 2;
               const uint32_t s0 = uint32_t(i & 3) * 0x1111u + sel_base;
               const uint32_t s1 = uint32_t((MT + i) & 3) * 0x1111u + sel_base;
-              const uint32_t a0 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w0], vw[kp][1][w0], s0));
-              const uint32_t a1 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][0][w1], vw[kp][1][w1], s1));
-              const uint32_t a2 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w0], vw[kp][3][w0], s0));
-              const uint32_t a3 = code_pair<kI8A, kI8B>(__byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1));
+              const uint32_t a0 = code_pair_offset<kI8A, kI8B>(__byte_perm(vw[kp][0][w0], vw[kp][1][w0], s0));
+              const uint32_t a1 = code_pair_offset<kI8A, kI8B>(__byte_perm(vw[kp][0][w1], vw[kp][1][w1], s1));
+              const uint32_t a2 = code_pair_offset<kI8A, kI8B>(__byte_perm(vw[kp][2][w0], vw[kp][3][w0], s0));
+              const uint32_t a3 = code_pair_offset<kI8A, kI8B>(__byte_perm(vw[kp][2][w1], vw[kp][3][w1], s1));
               mma_16816(o[i], a0, a1, a2, a3, pb[2 * kp], pb[2 * kp + 1]);
             }
+            // B holds head g's keys 2t, 2t+1 (pb[2kp]) and 2t+8, 2t+9 (pb[2kp+1]) of the k-step
+            add_half2(pe, pb[2 * kp]);
+            add_half2(pe, pb[2 * kp + 1]);
           }
         }
       };
@@ -786,6 +803,14 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
     }
     const int ct = threadIdx.x;
     const size_t row_base = size_t(uc.b) * a.Hq + h0;
+    // several heads: 1152 * sum(P) of the heads 2t, 2t + 1 whose columns this thread holds
+    float off_lo = 0.f, off_hi = 0.f;
+    if constexpr (!G1) {
+      pe += __shfl_xor_sync(0xffffffffu, pe, 1);
+      pe += __shfl_xor_sync(0xffffffffu, pe, 2);  // head g's sum over the warp's keys
+      off_lo = kI8Offset * __shfl_sync(0xffffffffu, pe, (2 * t) * 4);
+      off_hi = kI8Offset * __shfl_sync(0xffffffffu, pe, (2 * t + 1) * 4);
+    }
     for (int hp = 0; hp < gvalid; hp += MH) {
       if constexpr (!G1) {  // one head: the warp's O is in shared memory already
 #pragma unroll
@@ -797,9 +822,11 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
             float val[D / 8];
             const float inv_vsc = 1.f / vsc;  // leave the V-scale frame (a power of two: exact)
 #pragma unroll
+            const float off = e ? off_hi : off_lo;  // the codes' 1152 offset times sum(P) of the head
+#pragma unroll
             for (int i = 0; i < MT; ++i) {
-              val[i] = o[i][e] * inv_vsc;
-              val[MT + i] = o[i][2 + e] * inv_vsc;
+              val[i] = (o[i][e] - off) * inv_vsc;
+              val[MT + i] = (o[i][2 + e] - off) * inv_vsc;
             }
             float* dst = &sm_o[(warp * MH + gl) * D + g * (D / 8)];
 #pragma unroll
