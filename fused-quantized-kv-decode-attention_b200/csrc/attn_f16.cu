@@ -40,6 +40,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include "device_common.cuh"
 #include "kernels.h"
@@ -261,69 +262,84 @@ __global__ void __launch_bounds__(F16Cfg<D, kCl>::kThr) decode_f16_kernel(const 
       if (!alive) continue;
       const uint32_t sk = ring + uint32_t(st) * C::kStageBytes;
       const uint32_t sv = sk + C::kTileBytes;
+      // One tile of this warp's 16 keys; kMask adds the per-key bound checks and V masks that only
+      // the last (partial) tile of a unit needs.
+      auto tile = [&](auto mask_tag) {
+        constexpr bool kMask = decltype(mask_tag)::value;
 
-      // ---- S = Q K^T for this warp's 16 keys (two n8 tiles)
-      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // ---- S = Q K^T for this warp's 16 keys (two n8 tiles)
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const int row = r0 + ((mi >> 1) << 3) + rr;
-        const int chunk = 2 * kk + (mi & 1);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(sk + swz(row, chunk), b0, b1, b2, b3);
-        mma_16816(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
-        mma_16816(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
-      }
-
-      // ---- online softmax (log2 domain); row g, keys k0 + r0 + 8j + 2t + e
-      float mx = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = k0 + r0 + 8 * j + 2 * t + e;
-          const float v = (key < hi) ? sc[j][e] * csc : -INFINITY;
-          sc[j][e] = v;
-          mx = fmaxf(mx, v);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int row = r0 + ((mi >> 1) << 3) + rr;
+          const int chunk = 2 * kk + (mi & 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(sk + swz(row, chunk), b0, b1, b2, b3);
+          mma_16816(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+          mma_16816(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
         }
-      }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_run, mx);
-      if (__any_sync(0xffffffffu, m_new > m_run)) {
-        const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
-#pragma unroll
-        for (int j = 0; j < D / 8; ++j) {
-          o[j][0] *= alpha;
-          o[j][1] *= alpha;
-        }
-        l_run *= alpha;
-        m_run = m_new;
-      }
-      const float mu = (m_run == -INFINITY) ? 0.f : m_run;
-      const float p00 = ex2(sc[0][0] - mu), p01 = ex2(sc[0][1] - mu);
-      const float p10 = ex2(sc[1][0] - mu), p11 = ex2(sc[1][1] - mu);
-      l_run += (p00 + p01) + (p10 + p11);
-      const uint32_t pa0 = pack_half2(p00, p01);
-      const uint32_t pa2 = pack_half2(p10, p11);
 
-      // ---- O += P V  (V^T fragments via ldmatrix.trans).  This lane's B registers
-      // b0/b2 hold keys r0 + 2t, +1 and b1/b3 keys r0 + 8 + 2t, +9 (the columns of
-      // its P registers).  Past the valid length a KV cache may hold anything
-      // (a torch.empty tail): p = 0 there, but 0 * inf / NaN is NaN, so the V
-      // halves of keys past `hi` are masked to zero (all-ones masks on full
-      // tiles; one AND per B register, no extra registers or spills).
-      const int kb = k0 + r0 + 2 * t;
-      const uint32_t vm0 = (kb < hi ? 0x0000ffffu : 0u) | (kb + 1 < hi ? 0xffff0000u : 0u);
-      const uint32_t vm1 = (kb + 8 < hi ? 0x0000ffffu : 0u) | (kb + 9 < hi ? 0xffff0000u : 0u);
+        // ---- online softmax (log2 domain); row g, keys k0 + r0 + 8j + 2t + e
+        float mx = -INFINITY;
 #pragma unroll
-      for (int pp = 0; pp < D / 16; ++pp) {
-        const int row = r0 + ((mi & 1) << 3) + rr;
-        const int chunk = 2 * pp + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(sv + swz(row, chunk), b0, b1, b2, b3);
-        mma_16816(o[2 * pp], pa0, 0u, pa2, 0u, b0 & vm0, b1 & vm1);
-        mma_16816(o[2 * pp + 1], pa0, 0u, pa2, 0u, b2 & vm0, b3 & vm1);
-      }
+        for (int j = 0; j < 2; ++j) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = k0 + r0 + 8 * j + 2 * t + e;
+            const float v = (!kMask || key < hi) ? sc[j][e] * csc : -INFINITY;
+            sc[j][e] = v;
+            mx = fmaxf(mx, v);
+          }
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        if (__any_sync(0xffffffffu, m_new > m_run)) {
+          const float alpha = (m_new == -INFINITY) ? 1.f : ex2(m_run - m_new);
+#pragma unroll
+          for (int j = 0; j < D / 8; ++j) {
+            o[j][0] *= alpha;
+            o[j][1] *= alpha;
+          }
+          l_run *= alpha;
+          m_run = m_new;
+        }
+        const float mu = (m_run == -INFINITY) ? 0.f : m_run;
+        const float p00 = ex2(sc[0][0] - mu), p01 = ex2(sc[0][1] - mu);
+        const float p10 = ex2(sc[1][0] - mu), p11 = ex2(sc[1][1] - mu);
+        l_run += (p00 + p01) + (p10 + p11);
+        const uint32_t pa0 = pack_half2(p00, p01);
+        const uint32_t pa2 = pack_half2(p10, p11);
+
+        // ---- O += P V  (V^T fragments via ldmatrix.trans).  This lane's B registers
+        // b0/b2 hold keys r0 + 2t, +1 and b1/b3 keys r0 + 8 + 2t, +9 (the columns of
+        // its P registers).  Past the valid length a KV cache may hold anything
+        // (a torch.empty tail): p = 0 there, but 0 * inf / NaN is NaN, so in the last
+        // tile the V halves of keys past `hi` are masked to zero (one AND per B register).
+        uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
+        if constexpr (kMask) {
+          const int kb = k0 + r0 + 2 * t;
+          vm0 = (kb < hi ? 0x0000ffffu : 0u) | (kb + 1 < hi ? 0xffff0000u : 0u);
+          vm1 = (kb + 8 < hi ? 0x0000ffffu : 0u) | (kb + 9 < hi ? 0xffff0000u : 0u);
+        }
+#pragma unroll
+        for (int pp = 0; pp < D / 16; ++pp) {
+          const int row = r0 + ((mi & 1) << 3) + rr;
+          const int chunk = 2 * pp + (mi >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(sv + swz(row, chunk), b0, b1, b2, b3);
+          if constexpr (kMask) {
+            b0 &= vm0;
+            b1 &= vm1;
+            b2 &= vm0;
+            b3 &= vm1;
+          }
+          mma_16816(o[2 * pp], pa0, 0u, pa2, 0u, b0, b1);
+          mma_16816(o[2 * pp + 1], pa0, 0u, pa2, 0u, b2, b3);
+        }
+      };
+      if (k0 + kTK <= hi) tile(std::false_type{});
+      else tile(std::true_type{});
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
