@@ -824,6 +824,20 @@ int fqkv_gemv(int32_t model_dtype, int32_t x_dtype, const void* x, const void* W
   return FQKV_OK;
 }
 
+int fqkv_gemv_swiglu(int32_t model_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B,
+                     int64_t I, int64_t K, fqkv_stream_t stream) {
+  if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (B < 1 || B > 4 || I < 1 || I > INT32_MAX / 4 || K < 256 || K % 256 != 0 || K > 16384)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "gemv_swiglu: need 1 <= B <= 4, I >= 1, K a multiple of 256 in [256, 16384]");
+  if (!x || !W || !y) return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(x, 16) || !aligned(W, 16) || !aligned(y, 2) || (bias && !aligned(bias, 2)))
+    return fail(FQKV_ERR_MISALIGNED, "gemv_swiglu: x and W must be 16-byte aligned");
+  cudaError_t e = fqkv::launch_gemv_swiglu(model_dtype == 1, x, W, bias, y, int(B), int(I), int(K),
+                                           reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gemv_swiglu launch");
+  return FQKV_OK;
+}
+
 size_t fqkv_argmax_scratch_bytes(int64_t rows) { return rows > 0 ? fqkv::argmax_scratch_bytes(rows) : 0; }
 
 int fqkv_argmax(int32_t model_dtype, const void* logits, int64_t rows, int64_t V, void* scratch, int64_t* idx,

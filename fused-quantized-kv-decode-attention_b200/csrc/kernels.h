@@ -143,6 +143,9 @@ cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, in
                             cudaStream_t stream);
 cudaError_t launch_gemv(bool bf16, bool x_f16, const void* x, const void* W, const void* bias, void* y, int B, int N,
                         int K, cudaStream_t stream);
+// SwiGLU of a concatenated [gate | up] projection W [2I, K] (bias [2I] or null): y [B, I].
+cudaError_t launch_gemv_swiglu(bool bf16, const void* x, const void* W, const void* bias, void* y, int B, int I, int K,
+                               cudaStream_t stream);
 size_t argmax_scratch_bytes(int64_t rows);
 cudaError_t launch_argmax(bool bf16, const void* logits, int64_t rows, int V, void* scratch, int64_t* out,
                           cudaStream_t stream);

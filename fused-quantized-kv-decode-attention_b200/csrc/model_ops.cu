@@ -217,18 +217,24 @@ __global__ void __launch_bounds__(256) silu_mul_vec_kernel(const T* __restrict__
 // staged in shared memory; the WPR slice sums of a row are added in a fixed
 // order.
 // K % 256 == 0, rows 16-byte aligned.
+// kSwi (SwiGLU of a concatenated [gate | up] projection, W [2N, K]): a warp owns
+// the gate row n and the up row N + n and writes y[b, n] = T(T(silu(g)) * u),
+// g and u the two projections rounded to T -- the same values as the GEMV of
+// both halves followed by the separate SwiGLU kernel, in one launch.
 constexpr int kGemvWarps = 8;
-template <typename T, int B, int RPW, int WPR>
+template <typename T, int B, int RPW, int WPR, bool kSwi = false>
 __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __restrict__ x, const T* __restrict__ W,
                                                                const T* __restrict__ bias, T* __restrict__ y, int N,
                                                                int K, bool x_f16) {
+  static_assert(!kSwi || (RPW == 2 && WPR == 1), "SwiGLU: one output (a gate and an up row) per warp");
   extern __shared__ uint4 xs[];  // [B][K/8] chunks
   __shared__ float red[kGemvWarps][RPW][B];
   constexpr int kGroups = kGemvWarps / WPR;  // row groups per CTA
   const int kc = K / 8;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int n0 = (blockIdx.x * kGroups + warp / WPR) * RPW;
+  // first output row of this warp; its weight rows are n0 + r, or n0 and N + n0 for SwiGLU
+  const int n0 = (blockIdx.x * kGroups + warp / WPR) * (kSwi ? 1 : RPW);
   const int kcw = kc / WPR;                  // chunks of this warp's K slice
   const int c_lo = (warp % WPR) * kcw, c_hi = c_lo + kcw;
   constexpr int U = 8;  // chunks per lane per pass: a 2048-element slice is one pass
@@ -241,7 +247,8 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int cc = c + 32 * u;
-        if (cc < c_hi && n0 + r < N) wv[r][u] = reinterpret_cast<const uint4*>(W + int64_t(n0 + r) * K)[cc];
+        const int wr = kSwi ? n0 + r * N : n0 + r;
+        if (cc < c_hi && (kSwi ? n0 : n0 + r) < N) wv[r][u] = reinterpret_cast<const uint4*>(W + int64_t(wr) * K)[cc];
         else wv[r][u] = make_uint4(0, 0, 0, 0);
       }
   };
@@ -301,7 +308,17 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
       for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
       acc[r][b] = v;
     }
-  if constexpr (WPR == 1) {
+  if constexpr (kSwi) {
+    if (lane == 0 && n0 < N) {
+      const float bg = bias ? ld<T>(bias, n0) : 0.f, bu = bias ? ld<T>(bias, N + n0) : 0.f;
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const float g = rnd<T>(acc[0][b] + bg);
+        const float s = rnd<T>(g / (1.f + expf(-g)));
+        y[int64_t(b) * N + n0] = cvt<T>(s * rnd<T>(acc[1][b] + bu));
+      }
+    }
+  } else if constexpr (WPR == 1) {
     if (lane == 0) {
 #pragma unroll
       for (int r = 0; r < RPW; ++r) {
@@ -334,13 +351,13 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
   }
 }
 
-template <typename T, int B, int RPW, int WPR>
+template <typename T, int B, int RPW, int WPR, bool kSwi = false>
 cudaError_t launch_gemv_k(const void* x, const void* W, const void* bias, void* y, int N, int K, bool x_f16,
                           cudaStream_t stream) {
   const size_t smem = size_t(B) * K * sizeof(T);
-  constexpr int kRowsPerCta = kGemvWarps / WPR * RPW;
+  constexpr int kRowsPerCta = kGemvWarps / WPR * (kSwi ? 1 : RPW);  // output rows per CTA
   const unsigned blocks = unsigned((N + kRowsPerCta - 1) / kRowsPerCta);
-  auto fn = gemv_kernel<T, B, RPW, WPR>;
+  auto fn = gemv_kernel<T, B, RPW, WPR, kSwi>;
   // dynamic + static (the slice sums) shared memory above the 48 KB default needs the opt-in
   if (smem + sizeof(float) * kGemvWarps * RPW * B > 48 * 1024)
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -381,6 +398,17 @@ cudaError_t launch_gemv_b(const void* x, const void* W, const void* bias, void* 
     case 2: return launch_gemv_t<T, 2>(x, W, bias, y, N, K, x_f16, stream);
     case 3: return launch_gemv_t<T, 3>(x, W, bias, y, N, K, x_f16, stream);
     default: return launch_gemv_t<T, 4>(x, W, bias, y, N, K, x_f16, stream);
+  }
+}
+
+template <typename T>
+cudaError_t launch_gemv_swiglu_b(const void* x, const void* W, const void* bias, void* y, int B, int I, int K,
+                                 cudaStream_t stream) {
+  switch (B) {
+    case 1: return launch_gemv_k<T, 1, 2, 1, true>(x, W, bias, y, I, K, false, stream);
+    case 2: return launch_gemv_k<T, 2, 2, 1, true>(x, W, bias, y, I, K, false, stream);
+    case 3: return launch_gemv_k<T, 3, 2, 1, true>(x, W, bias, y, I, K, false, stream);
+    default: return launch_gemv_k<T, 4, 2, 1, true>(x, W, bias, y, I, K, false, stream);
   }
 }
 
@@ -506,6 +534,12 @@ cudaError_t launch_gemv(bool bf16, bool x_f16, const void* x, const void* W, con
                         int K, cudaStream_t stream) {
   return bf16 ? launch_gemv_b<__nv_bfloat16>(x, W, bias, y, B, N, K, x_f16, stream)
               : launch_gemv_b<__half>(x, W, bias, y, B, N, K, true, stream);
+}
+
+cudaError_t launch_gemv_swiglu(bool bf16, const void* x, const void* W, const void* bias, void* y, int B, int I, int K,
+                               cudaStream_t stream) {
+  return bf16 ? launch_gemv_swiglu_b<__nv_bfloat16>(x, W, bias, y, B, I, K, stream)
+              : launch_gemv_swiglu_b<__half>(x, W, bias, y, B, I, K, stream);
 }
 
 cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void* w, void* y, int64_t rows, int H,

@@ -647,6 +647,38 @@ def gemv(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = None,
     return out
 
 
+def gemv_swiglu(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """A SwiGLU MLP's gate/up projection and the SwiGLU in one launch (small batch).
+
+    x [B, K] (B <= 4), W [2I, K] = [gate_proj.weight; up_proj.weight], bias [2I] or None, all in
+    the model dtype; returns y [B, I] = silu(g) * u with g, u the projections rounded to the model
+    dtype -- the same values as ``silu_mul(gemv(x, W, bias), y)``.
+    """
+    op = "gemv_swiglu"
+    ts = dict(x=x, W=W) if bias is None else dict(x=x, W=W, bias=bias)
+    dev = _require_cuda(op, *ts.values())
+    if W.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", "W must be fp16 or bf16")
+    _require_dtype(op, "model dtype", W.dtype, **ts)
+    _require_contig(op, **ts)
+    if x.dim() != 2 or W.dim() != 2 or x.shape[1] != W.shape[1] or W.shape[0] % 2 \
+            or (bias is not None and bias.shape != (W.shape[0],)):
+        _fail(op, "shape", "x [B, K], W [2I, K], bias [2I]")
+    B, K = x.shape
+    I = W.shape[0] // 2
+    if out is None:
+        out = torch.empty(B, I, dtype=W.dtype, device=dev)
+    elif out.shape != (B, I) or out.dtype != W.dtype or not out.is_contiguous():
+        _fail(op, "out", "out must be a contiguous [B, I] tensor in the model dtype")
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_gemv_swiglu(1 if W.dtype == torch.bfloat16 else 0, x.data_ptr(), W.data_ptr(),
+                                            bias.data_ptr() if bias is not None else None, out.data_ptr(), B, I, K,
+                                            _stream(dev))
+    _native.check(rc, f"launch: {op}")
+    return out
+
+
 def argmax_rows(logits: torch.Tensor, scratch: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Greedy choice per row: logits [rows, V] (fp16 / bf16) -> int64 [rows], as torch.argmax(-1).
 

@@ -290,6 +290,18 @@ int fqkv_silu_mul(int32_t model_dtype, const void* gu, void* y, int64_t rows, in
 int fqkv_gemv(int32_t model_dtype, int32_t x_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B,
               int64_t N, int64_t K, fqkv_stream_t stream);
 
+/* The gate/up projection of a SwiGLU MLP and the SwiGLU in one launch: W
+ * [2I, K] is the concatenation [gate_proj.weight; up_proj.weight] (bias [2I]
+ * the concatenated biases, or null), y [B, I] = T(T(silu(g)) * u) with g, u
+ * the two projections of x [B, K] rounded to the model dtype T -- the values
+ * of fqkv_gemv on W followed by fqkv_silu_mul, without the [B, 2I]
+ * intermediate or the second launch.  Same sizes, alignment and launch
+ * behaviour as fqkv_gemv (x in the model dtype).  No counterpart in the
+ * reference (it replaces the Llama MLP's gate/up linear and act_fn * up in
+ * the decode step, transformers LlamaMLP.forward). */
+int fqkv_gemv_swiglu(int32_t model_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B,
+                     int64_t I, int64_t K, fqkv_stream_t stream);
+
 /* Greedy token choice: idx [rows] int64 = argmax over each row of logits
  * [rows, V] (model dtype), first index of the maximum, NaN largest (as
  * torch.argmax).  `scratch` holds fqkv_argmax_scratch_bytes(rows) bytes,

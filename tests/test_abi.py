@@ -112,7 +112,7 @@ def test_workspace_query_without_gpu_is_zero(fqkv):
 
 
 def test_decode_step_kernels_reject_bad_arguments(fqkv):
-    """The decode-step entries (GEMV, argmax, SwiGLU, add+RMSNorm) validate before launching."""
+    """The decode-step entries (GEMV, GEMV + SwiGLU, argmax, SwiGLU, add+RMSNorm) validate before launching."""
     bad, mis, ok = fqkv.native.ERR_INVALID_ARGUMENT, fqkv.native.ERR_MISALIGNED, fqkv.native.OK
     # GEMV: batch above 4, K not a multiple of 256, bf16 activations with fp16 weights, misaligned weights
     assert _call(fqkv, "fqkv_gemv", 1, 1, P, P, None, P, 5, 16, 256, None)[0] == bad
@@ -130,6 +130,11 @@ def test_decode_step_kernels_reject_bad_arguments(fqkv):
     assert 0 < lib.fqkv_argmax_scratch_bytes(1) < lib.fqkv_argmax_scratch_bytes(64)
     # SwiGLU: a row stride shorter than the gate and up halves
     assert _call(fqkv, "fqkv_silu_mul", 1, P, P, 2, 100, 150, None)[0] == bad
+    # GEMV + SwiGLU: batch above 4, K not a multiple of 256, unknown dtype, misaligned x
+    assert _call(fqkv, "fqkv_gemv_swiglu", 1, P, P, None, P, 5, 16, 256, None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv_swiglu", 1, P, P, None, P, 1, 16, 300, None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv_swiglu", 2, P, P, None, P, 1, 16, 256, None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv_swiglu", 1, P3, P, None, P, 1, 16, 256, None)[0] == mis
     # add + RMSNorm: hidden size above 8192, odd address
     assert _call(fqkv, "fqkv_add_rmsnorm", 1, P, None, P, P, 2, 9000, 1e-5, None)[0] == bad
     assert _call(fqkv, "fqkv_add_rmsnorm", 1, ctypes.c_void_p(17), None, P, P, 2, 64, 1e-5, None)[0] == mis

@@ -281,6 +281,35 @@ def test_gemv_matches_fp32_projection(fqkv, dtype, B, N, K):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("B,I,K,bias", [(1, 8192, 2048, False), (4, 300, 2048, True), (2, 77, 512, True),
+                                         (3, 1000, 4096, False)])
+def test_gemv_swiglu_equals_gemv_then_silu_mul(fqkv, dtype, B, I, K, bias):
+    """The fused gate/up GEMV + SwiGLU: bit-identical to the GEMV of [gate; up] followed by the SwiGLU
+    kernel (the same per-row dot products and roundings) wherever that GEMV runs one warp per row
+    (K <= 2048, or any K at B > 1); at B = 1 with K > 2048 the plain GEMV sums K-slices in another
+    order, so there it is checked within one output rounding.  And against the fp32 reference of
+    silu(x Wg^T + bg) * (x Wu^T + bu)."""
+    torch.manual_seed(B * 7 + I)
+    x = torch.randn(B, K, device="cuda").to(dtype)
+    W = (torch.randn(2 * I, K, device="cuda") * 0.05).to(dtype)
+    b = torch.randn(2 * I, device="cuda").to(dtype) if bias else None
+    got = fqkv.gemv_swiglu(x, W, b)
+    assert got.shape == (B, I) and got.dtype == dtype
+    two = torch.empty(B, I, device="cuda", dtype=dtype)
+    fqkv.silu_mul(fqkv.gemv(x, W, b), two)
+    if K <= 2048 or B > 1:
+        assert torch.equal(got, two)
+    else:
+        assert ((got.float() - two.float()).abs() <= 2 * torch.finfo(dtype).eps * two.float().abs() + 1e-6).all()
+    g = x.float() @ W[:I].float().t() + (b[:I].float() if bias else 0)
+    u = x.float() @ W[I:].float().t() + (b[I:].float() if bias else 0)
+    ref = torch.nn.functional.silu(g) * u
+    tol = 4 * torch.finfo(dtype).eps * ref.abs() + 1e-3 * ref.abs().max()
+    assert ((got.float() - ref).abs() <= tol).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("rows,V", [(1, 128256), (4, 32000), (64, 128256), (3, 100), (2, 1), (2, 16), (300, 1000)])
 def test_argmax_rows_matches_torch(fqkv, dtype, rows, V):
     """Multi-CTA argmax: the same index as torch.argmax, ties to the first index, reusable scratch."""
