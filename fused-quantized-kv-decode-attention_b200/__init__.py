@@ -25,6 +25,7 @@ from .ops import (
     quant_int4_per_token,
     add_rmsnorm,
     gemv,
+    gemv_rope_append,
     gemv_swiglu,
     quantize_into_cache,
     rope_qkv_append,
@@ -45,6 +46,7 @@ __all__ = [
     "rope_qkv_append",
     "add_rmsnorm",
     "gemv",
+    "gemv_rope_append",
     "gemv_swiglu",
     "silu_mul",
     "decode_attn_kvcache_tp",

@@ -71,6 +71,8 @@ SIGNATURES = {
     "fqkv_silu_mul": (_INT, [ctypes.c_int32, _P, _P, _I64, _I64, _I64, _P]),
     "fqkv_gemv": (_INT, [ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "fqkv_gemv_swiglu": (_INT, [ctypes.c_int32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "fqkv_gemv_rope_append": (_INT, [ctypes.c_int32, _P, _P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P,
+                                     _I64, _I64, _I64, _I64, _P]),
     "fqkv_argmax_scratch_bytes": (_SZ, [_I64]),
     "fqkv_argmax": (_INT, [ctypes.c_int32, _P, _I64, _I64, _P, _P, _P]),
     "fqkv_decode_attn_kvcache_out": (_INT, [ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,

@@ -838,6 +838,45 @@ int fqkv_gemv_swiglu(int32_t model_dtype, const void* x, const void* W, const vo
   return FQKV_OK;
 }
 
+int fqkv_gemv_rope_append(int32_t model_dtype, const void* x, const void* W, const void* bias, int64_t K,
+                          const void* cos_table, const void* sin_table, int64_t table_rows, int64_t pos_host,
+                          const int32_t* pos_dev, void* q_out, void* k_cache, void* v_cache, int64_t Hq, int64_t Hkv,
+                          int64_t D, int64_t cap, fqkv_stream_t stream) {
+  if (model_dtype != 0 && model_dtype != 1) return fail(FQKV_ERR_INVALID_ARGUMENT, "model_dtype: 0 (f16) or 1 (bf16)");
+  if (int rc = check_D(D)) return rc;
+  if (K < 256 || K % 256 != 0 || K > 16384)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "gemv_rope_append: K must be a multiple of 256 in [256, 16384]");
+  if (Hq < 1 || Hkv < 1 || Hq % Hkv != 0 || Hq + 2 * Hkv > 4096 || cap < 1 || cap > INT32_MAX || table_rows < 1)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "gemv_rope_append: bad sizes (Hq=%lld Hkv=%lld cap=%lld table_rows=%lld)",
+                (long long)Hq, (long long)Hkv, (long long)cap, (long long)table_rows);
+  if (!pos_dev && (pos_host < 0 || pos_host >= table_rows))
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "pos %lld outside the rotary table (%lld rows)", (long long)pos_host,
+                (long long)table_rows);
+  if (!x || !W || !cos_table || !sin_table || !q_out || !k_cache || !v_cache)
+    return fail(FQKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(x, 16) || !aligned(W, 16) || (bias && !aligned(bias, 2)) || !aligned(cos_table, 2) ||
+      !aligned(sin_table, 2) || !aligned(q_out, 2) || !aligned(k_cache, 2) || !aligned(v_cache, 2) ||
+      (pos_dev && !aligned(pos_dev, 4)))
+    return fail(FQKV_ERR_MISALIGNED, "gemv_rope_append: x and W must be 16-byte aligned");
+  fqkv::GemvRope rp;
+  rp.cos_t = cos_table;
+  rp.sin_t = sin_table;
+  rp.table_rows = table_rows;
+  rp.pos_host = pos_host;
+  rp.pos_dev = reinterpret_cast<const int*>(pos_dev);
+  rp.q_out = static_cast<__half*>(q_out);
+  rp.k_cache = static_cast<__half*>(k_cache);
+  rp.v_cache = static_cast<__half*>(v_cache);
+  rp.Hq = int(Hq);
+  rp.Hkv = int(Hkv);
+  rp.D = int(D);
+  rp.cap = int(cap);
+  cudaError_t e = fqkv::launch_gemv_rope_append(model_dtype == 1, x, W, bias, int(K), rp,
+                                                reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gemv_rope_append launch");
+  return FQKV_OK;
+}
+
 size_t fqkv_argmax_scratch_bytes(int64_t rows) { return rows > 0 ? fqkv::argmax_scratch_bytes(rows) : 0; }
 
 int fqkv_argmax(int32_t model_dtype, const void* logits, int64_t rows, int64_t V, void* scratch, int64_t* idx,

@@ -143,6 +143,21 @@ cudaError_t launch_silu_mul(bool bf16, const void* gu, void* y, int64_t rows, in
                             cudaStream_t stream);
 cudaError_t launch_gemv(bool bf16, bool x_f16, const void* x, const void* W, const void* bias, void* y, int B, int N,
                         int K, cudaStream_t stream);
+// The batch-1 fused q/k/v projection with RoPE, the fp16 cast of q and the append of k / v to an
+// fp16 cache [Hkv, cap, D] at position *pos_dev (or pos_host) in its epilogue (model_ops.cu).
+struct GemvRope {
+  const void* cos_t = nullptr;  // [table_rows, D] in the model dtype
+  const void* sin_t = nullptr;
+  int64_t table_rows = 0;
+  int64_t pos_host = 0;
+  const int* pos_dev = nullptr;
+  __half* q_out = nullptr;      // [Hq, D]
+  __half* k_cache = nullptr;    // [Hkv, cap, D]
+  __half* v_cache = nullptr;
+  int Hq = 0, Hkv = 0, D = 0, cap = 0;
+};
+cudaError_t launch_gemv_rope_append(bool bf16, const void* x, const void* W, const void* bias, int K,
+                                    const GemvRope& rp, cudaStream_t stream);
 // SwiGLU of a concatenated [gate | up] projection W [2I, K] (bias [2I] or null): y [B, I].
 cudaError_t launch_gemv_swiglu(bool bf16, const void* x, const void* W, const void* bias, void* y, int B, int I, int K,
                                cudaStream_t stream);

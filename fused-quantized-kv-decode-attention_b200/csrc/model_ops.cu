@@ -217,24 +217,38 @@ __global__ void __launch_bounds__(256) silu_mul_vec_kernel(const T* __restrict__
 // staged in shared memory; the WPR slice sums of a row are added in a fixed
 // order.
 // K % 256 == 0, rows 16-byte aligned.
-// kSwi (SwiGLU of a concatenated [gate | up] projection, W [2N, K]): a warp owns
-// the gate row n and the up row N + n and writes y[b, n] = T(T(silu(g)) * u),
-// g and u the two projections rounded to T -- the same values as the GEMV of
-// both halves followed by the separate SwiGLU kernel, in one launch.
+// Epilogues (kEpi):
+//  * kEpiSwiGLU (a concatenated [gate | up] projection, W [2N, K]): a warp owns
+//    the gate row n and the up row N + n and writes y[b, n] = T(T(silu(g)) * u),
+//    g and u the two projections rounded to T -- the same values as the GEMV of
+//    both halves followed by the separate SwiGLU kernel, in one launch.
+//  * kEpiRope (batch 1, the fused q/k/v projection of a decode step, N = (Hq +
+//    2 Hkv) D rows): a warp owns rows i and i + D/2 of one head -- a rotate-half
+//    pair -- and applies RoPE to q and k heads, casts to fp16 and writes q to
+//    q_out and k / v into the fp16 cache at the step's position: the values of
+//    the GEMV followed by rope_append_kernel (see quantize.cu), in one launch.
 constexpr int kGemvWarps = 8;
-template <typename T, int B, int RPW, int WPR, bool kSwi = false>
+constexpr int kEpiPlain = 0, kEpiSwiGLU = 1, kEpiRope = 2;
+template <typename T, int B, int RPW, int WPR, int kEpi = kEpiPlain>
 __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __restrict__ x, const T* __restrict__ W,
                                                                const T* __restrict__ bias, T* __restrict__ y, int N,
-                                                               int K, bool x_f16) {
-  static_assert(!kSwi || (RPW == 2 && WPR == 1), "SwiGLU: one output (a gate and an up row) per warp");
+                                                               int K, bool x_f16, const GemvRope rp) {
+  constexpr bool kSwi = kEpi == kEpiSwiGLU;
+  constexpr bool kRope = kEpi == kEpiRope;
+  static_assert(kEpi == kEpiPlain || (RPW == 2 && WPR == 1), "paired epilogues: two rows per warp");
+  static_assert(!kRope || B == 1, "the RoPE epilogue serves batch 1");
   extern __shared__ uint4 xs[];  // [B][K/8] chunks
   __shared__ float red[kGemvWarps][RPW][B];
   constexpr int kGroups = kGemvWarps / WPR;  // row groups per CTA
   const int kc = K / 8;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  // first output row of this warp; its weight rows are n0 + r, or n0 and N + n0 for SwiGLU
-  const int n0 = (blockIdx.x * kGroups + warp / WPR) * (kSwi ? 1 : RPW);
+  // first weight row of this warp; its rows are n0 + r, or n0 and N + n0 (SwiGLU), or n0 and n0 + D/2
+  // (RoPE: head n0 / D, rotate-half pair i, i + D/2)
+  const int gw = blockIdx.x * kGroups + warp / WPR;
+  const int half = kRope ? rp.D / 2 : 0;
+  const int n0 = kSwi ? gw : kRope ? (gw / half) * rp.D + gw % half : gw * RPW;
+  const bool warp_live = kSwi ? n0 < N : kRope ? 2 * gw < N : n0 < N;
   const int kcw = kc / WPR;                  // chunks of this warp's K slice
   const int c_lo = (warp % WPR) * kcw, c_hi = c_lo + kcw;
   constexpr int U = 8;  // chunks per lane per pass: a 2048-element slice is one pass
@@ -247,8 +261,9 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int cc = c + 32 * u;
-        const int wr = kSwi ? n0 + r * N : n0 + r;
-        if (cc < c_hi && (kSwi ? n0 : n0 + r) < N) wv[r][u] = reinterpret_cast<const uint4*>(W + int64_t(wr) * K)[cc];
+        const int wr = kSwi ? n0 + r * N : kRope ? n0 + r * half : n0 + r;
+        const bool live = kEpi == kEpiPlain ? n0 + r < N : warp_live;
+        if (cc < c_hi && live) wv[r][u] = reinterpret_cast<const uint4*>(W + int64_t(wr) * K)[cc];
         else wv[r][u] = make_uint4(0, 0, 0, 0);
       }
   };
@@ -278,7 +293,7 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
-  if (n0 < N) {
+  if (warp_live) {
     for (int c = c_lo + lane; c < c_hi; c += 32 * U) {
       if (c != c_lo + lane) load_w(c);
 #pragma unroll
@@ -308,7 +323,34 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
       for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
       acc[r][b] = v;
     }
-  if constexpr (kSwi) {
+  if constexpr (kRope) {
+    const int64_t pos = rp.pos_dev ? int64_t(*rp.pos_dev) : rp.pos_host;
+    if (lane == 0 && warp_live && pos >= 0 && pos < rp.table_rows) {
+      const int head = n0 / rp.D, i = n0 % rp.D;
+      float lo = rnd<T>(acc[0][0] + (bias ? ld<T>(bias, n0) : 0.f));
+      float hi = rnd<T>(acc[1][0] + (bias ? ld<T>(bias, n0 + half) : 0.f));
+      if (head < rp.Hq + rp.Hkv) {  // q and k heads: out = T(T(x cos) + T(rotate_half(x) sin))
+        const T* c = static_cast<const T*>(rp.cos_t) + pos * rp.D;
+        const T* sn = static_cast<const T*>(rp.sin_t) + pos * rp.D;
+        const float rl = rnd<T>(rnd<T>(lo * ld<T>(c, i)) + rnd<T>(-hi * ld<T>(sn, i)));
+        const float rh = rnd<T>(rnd<T>(hi * ld<T>(c, i + half)) + rnd<T>(lo * ld<T>(sn, i + half)));
+        lo = rl;
+        hi = rh;
+      }
+      __half* dst = nullptr;
+      if (head < rp.Hq) {
+        dst = rp.q_out + int64_t(head) * rp.D;
+      } else if (pos < rp.cap) {
+        const bool is_v = head >= rp.Hq + rp.Hkv;
+        const int kh = head - rp.Hq - (is_v ? rp.Hkv : 0);
+        dst = (is_v ? rp.v_cache : rp.k_cache) + (int64_t(kh) * rp.cap + pos) * rp.D;
+      }
+      if (dst) {
+        dst[i] = __float2half_rn(lo);  // x.to(float16)
+        dst[i + half] = __float2half_rn(hi);
+      }
+    }
+  } else if constexpr (kSwi) {
     if (lane == 0 && n0 < N) {
       const float bg = bias ? ld<T>(bias, n0) : 0.f, bu = bias ? ld<T>(bias, N + n0) : 0.f;
 #pragma unroll
@@ -351,13 +393,14 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const void* __res
   }
 }
 
-template <typename T, int B, int RPW, int WPR, bool kSwi = false>
+template <typename T, int B, int RPW, int WPR, int kEpi = kEpiPlain>
 cudaError_t launch_gemv_k(const void* x, const void* W, const void* bias, void* y, int N, int K, bool x_f16,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const GemvRope& rp = GemvRope{}) {
   const size_t smem = size_t(B) * K * sizeof(T);
-  constexpr int kRowsPerCta = kGemvWarps / WPR * (kSwi ? 1 : RPW);  // output rows per CTA
+  // rows of N per CTA (SwiGLU: outputs, each two weight rows)
+  constexpr int kRowsPerCta = kGemvWarps / WPR * (kEpi == kEpiSwiGLU ? 1 : RPW);
   const unsigned blocks = unsigned((N + kRowsPerCta - 1) / kRowsPerCta);
-  auto fn = gemv_kernel<T, B, RPW, WPR, kSwi>;
+  auto fn = gemv_kernel<T, B, RPW, WPR, kEpi>;
   // dynamic + static (the slice sums) shared memory above the 48 KB default needs the opt-in
   if (smem + sizeof(float) * kGemvWarps * RPW * B > 48 * 1024)
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -366,9 +409,9 @@ cudaError_t launch_gemv_k(const void* x, const void* W, const void* bias, void* 
   // 976, 1000 -> 1108 us).
   if constexpr (B == 1)
     return launch_pdl(fn, dim3(blocks), dim3(32 * kGemvWarps), smem, stream, x, static_cast<const T*>(W),
-                      static_cast<const T*>(bias), static_cast<T*>(y), N, K, x_f16);
+                      static_cast<const T*>(bias), static_cast<T*>(y), N, K, x_f16, rp);
   fn<<<blocks, 32 * kGemvWarps, smem, stream>>>(x, static_cast<const T*>(W), static_cast<const T*>(bias),
-                                               static_cast<T*>(y), N, K, x_f16);
+                                               static_cast<T*>(y), N, K, x_f16, rp);
   return cudaGetLastError();
 }
 
@@ -405,10 +448,10 @@ template <typename T>
 cudaError_t launch_gemv_swiglu_b(const void* x, const void* W, const void* bias, void* y, int B, int I, int K,
                                  cudaStream_t stream) {
   switch (B) {
-    case 1: return launch_gemv_k<T, 1, 2, 1, true>(x, W, bias, y, I, K, false, stream);
-    case 2: return launch_gemv_k<T, 2, 2, 1, true>(x, W, bias, y, I, K, false, stream);
-    case 3: return launch_gemv_k<T, 3, 2, 1, true>(x, W, bias, y, I, K, false, stream);
-    default: return launch_gemv_k<T, 4, 2, 1, true>(x, W, bias, y, I, K, false, stream);
+    case 1: return launch_gemv_k<T, 1, 2, 1, kEpiSwiGLU>(x, W, bias, y, I, K, false, stream);
+    case 2: return launch_gemv_k<T, 2, 2, 1, kEpiSwiGLU>(x, W, bias, y, I, K, false, stream);
+    case 3: return launch_gemv_k<T, 3, 2, 1, kEpiSwiGLU>(x, W, bias, y, I, K, false, stream);
+    default: return launch_gemv_k<T, 4, 2, 1, kEpiSwiGLU>(x, W, bias, y, I, K, false, stream);
   }
 }
 
@@ -540,6 +583,13 @@ cudaError_t launch_gemv_swiglu(bool bf16, const void* x, const void* W, const vo
                                cudaStream_t stream) {
   return bf16 ? launch_gemv_swiglu_b<__nv_bfloat16>(x, W, bias, y, B, I, K, stream)
               : launch_gemv_swiglu_b<__half>(x, W, bias, y, B, I, K, stream);
+}
+
+cudaError_t launch_gemv_rope_append(bool bf16, const void* x, const void* W, const void* bias, int K,
+                                    const GemvRope& rp, cudaStream_t stream) {
+  const int N = (rp.Hq + 2 * rp.Hkv) * rp.D;
+  return bf16 ? launch_gemv_k<__nv_bfloat16, 1, 2, 1, kEpiRope>(x, W, bias, nullptr, N, K, false, stream, rp)
+              : launch_gemv_k<__half, 1, 2, 1, kEpiRope>(x, W, bias, nullptr, N, K, false, stream, rp);
 }
 
 cudaError_t launch_add_rmsnorm(bool bf16, void* h, const void* delta, const void* w, void* y, int64_t rows, int H,

@@ -28,7 +28,9 @@
   concatenated gate/up weights plus :func:`ops.silu_mul` and the down GEMM
   (LlamaRMSNorm / SwiGLU arithmetic; only the fp32 sum of squares is
   reduced in a different order); at batch 1 the gate/up projection and the
-  SwiGLU are one :func:`ops.gemv_swiglu` launch.
+  SwiGLU are one :func:`ops.gemv_swiglu` launch, and with an fp16 cache the
+  q/k/v projection, RoPE and the cache append one :func:`ops.gemv_rope_append`
+  launch.
 
   With ``tp_group`` (a ``torch.distributed`` group, NCCL on GPUs) the decoder
   is tensor-parallel by KV head: each rank keeps the q/k/v projection rows, the
@@ -340,10 +342,17 @@ class GraphDecoder:
         ops.add_rmsnorm(h, None, layers[0].input_layernorm.weight, x, layers[0].input_layernorm.variance_epsilon)
         for li, layer in enumerate(layers):
             attn = layer.self_attn
-            qkv = ops.gemv(x, self.wqkv[li], self.bqkv[li]) if self.small_b else F.linear(x, self.wqkv[li], self.bqkv[li])
-            ks = self.ks[li] if self.kv_dtype == "int8" else None
-            vs = self.vs[li] if self.kv_dtype == "int8" else None
-            ops.rope_qkv_append(qkv, self.cos_t, self.sin_t, self.pos32, self.q16, self.kc[li], self.vc[li], ks, vs)
+            if B == 1 and self.small_b and self.kv_dtype != "int8":
+                # q/k/v GEMV with RoPE, the fp16 cast of q and the cache append in its epilogue
+                ops.gemv_rope_append(x, self.wqkv[li], self.bqkv[li], self.cos_t, self.sin_t, self.pos32, self.q16,
+                                     self.kc[li], self.vc[li])
+            else:
+                qkv = (ops.gemv(x, self.wqkv[li], self.bqkv[li]) if self.small_b
+                       else F.linear(x, self.wqkv[li], self.bqkv[li]))
+                ks = self.ks[li] if self.kv_dtype == "int8" else None
+                vs = self.vs[li] if self.kv_dtype == "int8" else None
+                ops.rope_qkv_append(qkv, self.cos_t, self.sin_t, self.pos32, self.q16, self.kc[li], self.vc[li],
+                                    ks, vs)
             self._attend(li, self.q16)
             if self.xchg is not None:
                 self.xchg.wait()

@@ -679,6 +679,51 @@ def gemv_swiglu(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = No
     return out
 
 
+def gemv_rope_append(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None, cos_table: torch.Tensor,
+                     sin_table: torch.Tensor, pos, q_out: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> None:
+    """Batch-1 q/k/v projection with RoPE, q -> fp16 and the k / v cache append in one launch.
+
+    x [1, Hidden], W [(Hq + 2 Hkv) D, Hidden] (the concatenated q/k/v weights), bias or None, the
+    rotary tables [rows, D] -- all in the model dtype; ``pos`` an int or a CUDA int32 tensor;
+    q_out [1, Hq, D] fp16; K / V [1, Hkv, cap, D] fp16 caches.  The same values as
+    ``rope_qkv_append(gemv(x, W, bias), cos_table, sin_table, pos, q_out, K, V)``.
+    """
+    op = "gemv_rope_append"
+    ts = dict(x=x, W=W, cos_table=cos_table, sin_table=sin_table)
+    if bias is not None:
+        ts["bias"] = bias
+    dev = _require_cuda(op, *ts.values(), q_out, K, V)
+    if W.dtype not in (torch.float16, torch.bfloat16):
+        _fail(op, "dtype", "W must be fp16 or bf16")
+    _require_dtype(op, "model dtype", W.dtype, **ts)
+    _require_dtype(op, "fp16", torch.float16, q_out=q_out, K=K, V=V)
+    _require_contig(op, **ts)
+    _require_contig(op, q_out=q_out, K=K, V=V)
+    if x.dim() != 2 or x.shape[0] != 1 or q_out.dim() != 3 or q_out.shape[0] != 1 or K.dim() != 4 or K.shape[0] != 1:
+        _fail(op, "shape", "x [1, Hidden], q_out [1, Hq, D], K / V [1, Hkv, cap, D]")
+    _, Hq, D = q_out.shape
+    _, Hkv, cap, _ = K.shape
+    _require_D(op, D)
+    _require_shape(op, "V", V, (1, Hkv, cap, D))
+    if W.dim() != 2 or W.shape != ((Hq + 2 * Hkv) * D, x.shape[1]) or (bias is not None and bias.shape != (W.shape[0],)):
+        _fail(op, "shape", f"W must be [(Hq + 2 Hkv) D = {(Hq + 2 * Hkv) * D}, {x.shape[1]}], bias [{W.shape[0]}]")
+    if cos_table.dim() != 2 or cos_table.shape[1] != D or sin_table.shape != cos_table.shape:
+        _fail(op, "shape", "cos_table / sin_table must be [rows, D]")
+    if isinstance(pos, torch.Tensor):
+        if pos.device != dev or pos.dtype != torch.int32 or pos.numel() < 1:
+            _fail(op, "pos", "a tensor pos must be a CUDA int32 tensor on the inputs' device")
+        pos_host, pos_ptr = 0, pos.data_ptr()
+    else:
+        pos_host, pos_ptr = int(pos), None
+    with _DeviceGuard(dev):
+        rc = _native.lib().fqkv_gemv_rope_append(
+            1 if W.dtype == torch.bfloat16 else 0, x.data_ptr(), W.data_ptr(),
+            bias.data_ptr() if bias is not None else None, x.shape[1], cos_table.data_ptr(), sin_table.data_ptr(),
+            cos_table.shape[0], pos_host, pos_ptr, q_out.data_ptr(), K.data_ptr(), V.data_ptr(), Hq, Hkv, D, cap,
+            _stream(dev))
+    _native.check(rc, f"launch: {op}")
+
+
 def argmax_rows(logits: torch.Tensor, scratch: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Greedy choice per row: logits [rows, V] (fp16 / bf16) -> int64 [rows], as torch.argmax(-1).
 

@@ -302,6 +302,24 @@ int fqkv_gemv(int32_t model_dtype, int32_t x_dtype, const void* x, const void* W
 int fqkv_gemv_swiglu(int32_t model_dtype, const void* x, const void* W, const void* bias, void* y, int64_t B,
                      int64_t I, int64_t K, fqkv_stream_t stream);
 
+/* Batch-1 decode-step attention prologue in one launch: the fused q/k/v
+ * projection y = x W^T (+ bias) of one token (x [K], W [(Hq + 2 Hkv) D, K] =
+ * [q_proj; k_proj; v_proj] weights, model dtype), then in its epilogue what
+ * fqkv_rope_qkv_append does for an fp16 cache: RoPE of the q and k heads from
+ * the model's rotary tables [table_rows, D] at position pos (*pos_dev when
+ * given, else pos_host), the cast to fp16, q into q_out [Hq, D] and k / v
+ * into the caches [Hkv, cap, D] at row pos (not written when pos >= cap).
+ * The values equal fqkv_gemv followed by fqkv_rope_qkv_append.  D is 64 or
+ * 128, K a multiple of 256 in [256, 16384]; x and W 16-byte aligned.
+ * Launched with programmatic dependent launch like fqkv_gemv at B = 1 (W and
+ * bias must not be written by a kernel that may still be running).  No
+ * counterpart in the reference (it replaces the q/k/v linears,
+ * apply_rotary_pos_emb and the cache update of the decode step). */
+int fqkv_gemv_rope_append(int32_t model_dtype, const void* x, const void* W, const void* bias, int64_t K,
+                          const void* cos_table, const void* sin_table, int64_t table_rows, int64_t pos_host,
+                          const int32_t* pos_dev, void* q_out, void* k_cache, void* v_cache, int64_t Hq, int64_t Hkv,
+                          int64_t D, int64_t cap, fqkv_stream_t stream);
+
 /* Greedy token choice: idx [rows] int64 = argmax over each row of logits
  * [rows, V] (model dtype), first index of the maximum, NaN largest (as
  * torch.argmax).  `scratch` holds fqkv_argmax_scratch_bytes(rows) bytes,

@@ -112,7 +112,8 @@ def test_workspace_query_without_gpu_is_zero(fqkv):
 
 
 def test_decode_step_kernels_reject_bad_arguments(fqkv):
-    """The decode-step entries (GEMV, GEMV + SwiGLU, argmax, SwiGLU, add+RMSNorm) validate before launching."""
+    """The decode-step entries (GEMV, GEMV + SwiGLU, GEMV + RoPE + append, argmax, SwiGLU, add+RMSNorm)
+    validate before launching."""
     bad, mis, ok = fqkv.native.ERR_INVALID_ARGUMENT, fqkv.native.ERR_MISALIGNED, fqkv.native.OK
     # GEMV: batch above 4, K not a multiple of 256, bf16 activations with fp16 weights, misaligned weights
     assert _call(fqkv, "fqkv_gemv", 1, 1, P, P, None, P, 5, 16, 256, None)[0] == bad
@@ -135,6 +136,15 @@ def test_decode_step_kernels_reject_bad_arguments(fqkv):
     assert _call(fqkv, "fqkv_gemv_swiglu", 1, P, P, None, P, 1, 16, 300, None)[0] == bad
     assert _call(fqkv, "fqkv_gemv_swiglu", 2, P, P, None, P, 1, 16, 256, None)[0] == bad
     assert _call(fqkv, "fqkv_gemv_swiglu", 1, P3, P, None, P, 1, 16, 256, None)[0] == mis
+    # GEMV + RoPE + append: head size 96, K not a multiple of 256, position outside the table, misaligned W
+    assert _call(fqkv, "fqkv_gemv_rope_append", 1, P, P, None, 256, P, P, 10, 0, None, P, P, P, 8, 2, 96, 10,
+                 None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv_rope_append", 1, P, P, None, 300, P, P, 10, 0, None, P, P, P, 8, 2, 64, 10,
+                 None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv_rope_append", 1, P, P, None, 256, P, P, 10, 10, None, P, P, P, 8, 2, 64, 10,
+                 None)[0] == bad
+    assert _call(fqkv, "fqkv_gemv_rope_append", 1, P, P3, None, 256, P, P, 10, 0, None, P, P, P, 8, 2, 64, 10,
+                 None)[0] == mis
     # add + RMSNorm: hidden size above 8192, odd address
     assert _call(fqkv, "fqkv_add_rmsnorm", 1, P, None, P, P, 2, 9000, 1e-5, None)[0] == bad
     assert _call(fqkv, "fqkv_add_rmsnorm", 1, ctypes.c_void_p(17), None, P, P, 2, 64, 1e-5, None)[0] == mis

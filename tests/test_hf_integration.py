@@ -171,6 +171,38 @@ def test_rope_qkv_append_bit_exact(fqkv, dtype, kv):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("D,bias", [(64, False), (128, True)])
+def test_gemv_rope_append_equals_gemv_then_rope_append(fqkv, dtype, D, bias):
+    """The batch-1 q/k/v GEMV with RoPE, q cast and fp16 cache append in its epilogue: the same q and
+    cache rows as the GEMV followed by rope_qkv_append (itself bit-exact with transformers' RoPE), with
+    a device or host position; a position past the cache writes q only."""
+    torch.manual_seed(D + bias)
+    Hq, Hkv, Hid, cap, rows = 8, 2, 512, 40, 64
+    x = torch.randn(1, Hid, device="cuda").to(dtype)
+    W = (torch.randn((Hq + 2 * Hkv) * D, Hid, device="cuda") * 0.05).to(dtype)
+    b = torch.randn(W.shape[0], device="cuda").to(dtype) if bias else None
+    ang = torch.arange(rows, device="cuda")[:, None] * torch.linspace(0.01, 1.0, D // 2, device="cuda")[None]
+    cos_t = torch.cat([ang.cos(), ang.cos()], 1).to(dtype).contiguous()
+    sin_t = torch.cat([ang.sin(), ang.sin()], 1).to(dtype).contiguous()
+    for pos in (torch.tensor([7], dtype=torch.int32, device="cuda"), 39, 45):
+        outs = []
+        for fused in (True, False):
+            q = torch.full((1, Hq, D), float("nan"), dtype=torch.float16, device="cuda")
+            K = torch.zeros(1, Hkv, cap, D, dtype=torch.float16, device="cuda")
+            V = torch.zeros_like(K)
+            if fused:
+                fqkv.gemv_rope_append(x, W, b, cos_t, sin_t, pos, q, K, V)
+            else:
+                fqkv.rope_qkv_append(fqkv.gemv(x, W, b), cos_t, sin_t, pos, q, K, V)
+            outs.append((q, K, V))
+        (qf, Kf, Vf), (qr, Kr, Vr) = outs
+        assert torch.equal(qf, qr) and torch.equal(Kf, Kr) and torch.equal(Vf, Vr), pos
+        if pos == 45:   # past the cache: q written, the cache untouched
+            assert torch.isfinite(qf).all() and not Kf.any() and not Vf.any()
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("kv", ["fp16", "int8"])
 def test_graph_decoder_fused_prologue_equals_hf_ops(fqkv, kv):
     """GraphDecoder with the fused RoPE/append prologue gives the same logits, bit for bit,
