@@ -203,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
 
   // ------------------------------------------------------------ consumers
   constexpr int kDPL = C::kDimsPerLane;
+  constexpr bool kPairSplit = kInt4 && C::kL == 2;  // int4 at D = 64: two lanes per key row
   constexpr int kPW = kInt4 ? 2 * C::kWords : C::kWords;  // q plane words per lane
   const int c = lane % C::kL;          // 32-byte chunk of the key row
   const int j = lane / C::kL;          // key slot
@@ -292,6 +293,113 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
     // the lane's o and l leave the frame (/ vsc) before the cross-lane reduction.
     float vsc = 1099511627776.f, vk = 40.f;  // 2^40: any nonzero fp16 V scale lowers it on its first tile
     float vthr = 1.4901161193847656e-8f;     // 2^14 / vsc = 2^-26
+
+    // int4 at D = 64: the two lanes of a key row split the per-key scalar work -- lane c scales,
+    // exponentiates and packs the probabilities of its keys sp = c and c + 2 of the four, and the
+    // pair trades the partial dot products and the packed fp16 (p, p/16) by shuffles; l and the
+    // offset sums then cover only a lane's own keys and are added across the pair per unit.
+    auto tile_pair = [&](const uint8_t* base, int st, int k0, auto mask_tag) {
+      constexpr bool kMask = decltype(mask_tag)::value;
+      const uint8_t* kt = base;
+      const uint8_t* vt = base + C::kTileBytes;
+      const __half* kst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes) + stage_off[st][0];
+      const __half* vst = reinterpret_cast<const __half*>(base + 2 * C::kTileBytes + C::kScaleBytes) + stage_off[st][1];
+      float vso[2];  // V scales of this lane's own keys (sp = 2i + c)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int kl = kw + j + C::kKPS * (2 * i + c);
+        vso[i] = (!kMask || (k0 + kl) < hi) ? __half2float(vst[kl]) : 0.f;
+      }
+      float vmax = fmaxf(vso[0], vso[1]);
+      int accp[4];  // this lane's half of every key's integer dot product
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        const int kl = kw + j + C::kKPS * sp;
+        uint32_t kwd[C::kWords];
+        lane_words<C::kLaneBytes>(kt + kl * C::kRowBytes + C::kLaneBytes * c, kwd);
+        int ahe = 0, aho = 0, ale = 0, alo = 0;
+#pragma unroll
+        for (int w = 0; w < C::kWords; ++w) {
+          const uint32_t ev = xor_and<0x88888888u, 0x0F0F0F0Fu>(kwd[w]);  // (code + 8) of even dims
+          const uint32_t od = xor_and<0x88888888u, 0xF0F0F0F0u>(kwd[w]);  // 16 * (code + 8) of odd dims
+          ahe = dp4a_su(qh[(2 * w) % kPW], ev, ahe);
+          aho = dp4a_su(qh[(2 * w + 1) % kPW], od, aho);
+          ale = dp4a_uu(ql[(2 * w) % kPW], ev, ale);
+          alo = dp4a_uu(ql[(2 * w + 1) % kPW], od, alo);
+        }
+        accp[sp] = (ahe * 16 + aho) * 256 + (ale * 16 + alo) - qbias;
+      }
+      float sco[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        // one shuffle per two keys: each lane sends its half of the partner's own key
+        const int recv = __shfl_xor_sync(0xffffffffu, c ? accp[2 * i] : accp[2 * i + 1], 1);
+        const int acc = (c ? accp[2 * i + 1] : accp[2 * i]) + recv;
+        const int kl = kw + j + C::kKPS * (2 * i + c);
+        const float sv = float(acc) * (__half2float(kst[kl]) * qscale_unit);
+        sco[i] = (!kMask || (k0 + kl) < hi) ? sv : -INFINITY;
+      }
+      float mx = fmaxf(sco[0], sco[1]);
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_run, mx);
+      if (__any_sync(0xffffffffu, m_new > m_run || vmax > vthr)) {
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, off));
+        const bool grow_v = vmax > vthr;  // rare: the V frame must move down
+        const float alpha = m_new > m_run ? ex2(m_run - m_new) : 1.f;
+        float nk = vk;
+        const float nsc = grow_v ? frame_for(vmax, nk) : vsc;
+        const float f = alpha * (nsc / vsc);  // the frame ratio is a power of two: exact
+#pragma unroll
+        for (int d = 0; d < kDPL; ++d) o[d] *= f;
+        l_run *= f;
+        bias_lo *= f;
+        bias_hi *= f;
+        m_run = m_new;
+        vsc = nsc;
+        vk = nk;
+        vthr = 16384.f / nsc;  // a power of two: exact
+      }
+      const float mu = ((m_run == -INFINITY) ? 0.f : m_run) - vk;  // ex2(s - mu) = p * vsc
+      uint32_t pw[2];  // own keys: fp16 p * vscale (low half) and p * vscale / 16 (high half)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float p = ex2(sco[i] - mu);
+        l_run += p;
+        const float pv = p * vso[i];
+        const uint16_t ph = __half_as_ushort(__float2half_rn(pv));
+        const uint16_t ph16 = __half_as_ushort(__float2half_rn(pv * 0.0625f));
+        add_half(bias_lo, ph);
+        add_half(bias_hi, ph16);
+        pw[i] = uint32_t(ph) | (uint32_t(ph16) << 16);
+      }
+      const uint32_t pr[2] = {__shfl_xor_sync(0xffffffffu, pw[0], 1), __shfl_xor_sync(0xffffffffu, pw[1], 1)};
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        const int kl = kw + j + C::kKPS * sp;
+        const int i = sp >> 1;
+        const uint32_t pk = ((sp & 1) == c) ? pw[i] : pr[i];
+        const uint16_t ph = uint16_t(pk & 0xFFFFu), ph16 = uint16_t(pk >> 16);
+        uint32_t vwd[C::kWords];
+        lane_words<C::kLaneBytes>(vt + kl * C::kRowBytes + C::kLaneBytes * c, vwd);
+        // nibble fields as in the tile below: offset-binary fp16 subnormals, p/16 with the s = 16 halves
+#pragma unroll
+        for (int w = 0; w < C::kWords; ++w) {
+          const uint32_t x = vwd[w];
+          const uint32_t y = x >> 8;
+          const uint32_t a04 = xor_and<0x00080008u, 0x000F000Fu>(x);
+          const uint32_t a15 = xor_and<0x00800080u, 0x00F000F0u>(x);
+          const uint32_t a26 = xor_and<0x00080008u, 0x000F000Fu>(y);
+          const uint32_t a37 = xor_and<0x00800080u, 0x00F000F0u>(y);
+          float* od = &o[(8 * w) % kDPL];
+          fma_pair(od[0], od[4], a04, ph);
+          fma_pair(od[1], od[5], a15, ph16);
+          fma_pair(od[2], od[6], a26, ph);
+          fma_pair(od[3], od[7], a37, ph16);
+        }
+      }
+    };
 
     // One tile of this warp's keys; kMask adds the per-key bound checks that
     // only the last (partial) tile of a unit needs.
@@ -428,12 +536,22 @@ __global__ void __launch_bounds__(kThreads, QCfg<kInt4, D>::kMinBlocks)
       }
       if (!alive) continue;
       const uint8_t* base = smem + size_t(st) * C::kStageBytes;
-      if (k0 + C::kTK <= hi) tile(base, st, k0, std::false_type{});
-      else tile(base, st, k0, std::true_type{});
+      if constexpr (kPairSplit) {
+        if (k0 + C::kTK <= hi) tile_pair(base, st, k0, std::false_type{});
+        else tile_pair(base, st, k0, std::true_type{});
+      } else {
+        if (k0 + C::kTK <= hi) tile(base, st, k0, std::false_type{});
+        else tile(base, st, k0, std::true_type{});
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
 
+    if constexpr (kPairSplit) {  // l and the offset sums covered this lane's own keys only
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+      bias_lo += __shfl_xor_sync(0xffffffffu, bias_lo, 1);
+      bias_hi += __shfl_xor_sync(0xffffffffu, bias_hi, 1);
+    }
     // scale the subnormal fields back, remove their offset (int4: + 8; int8: + 128) and leave
     // the lane's V-scale frame
     const float inv_vsc = 1.f / vsc;  // a power of two: exact
