@@ -485,9 +485,10 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
         qa[kk][3] = pack_s8x4(lv[4], lv[5], lv[6], lv[7]);
         if constexpr (G1) {
           // one head: q is the B operand of S^T = K Q^T; columns 2c / 2c + 1 = hi / lo plane for
-          // c = 0, 1, 2, so the lanes t = 0, 1, 2 of a group all hold the same scores (columns 6, 7 zero)
-          const uint32_t b0 = g < 6 ? ((g & 1) ? qa[kk][1] : qa[kk][0]) : 0u;
-          const uint32_t b1 = g < 6 ? ((g & 1) ? qa[kk][3] : qa[kk][2]) : 0u;
+          // c = 0 .. 3, so the four lanes t of a group all hold the same scores (and lane t finishes
+          // the score, probability and fixed-point word of the group's key t, see below)
+          const uint32_t b0 = (g & 1) ? qa[kk][1] : qa[kk][0];
+          const uint32_t b1 = (g & 1) ? qa[kk][3] : qa[kk][2];
           qa[kk][0] = b0;
           qa[kk][1] = b1;
         }
@@ -544,7 +545,12 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
         float sc[NJ][2];
         bool valid[NJ][2];
         float mx = -INFINITY;
+        // one head: lane t of a group finishes the group's key t (k-slot 4g + t)
+        int own_si = 0, own_key = 0;
+        bool own_ok = false;
+        float own_sc = -INFINITY;
         if constexpr (G1) {
+          static_assert(!G1 || KP == 2, "one head: four keys per lane group and tile");
 #pragma unroll
           for (int mt = 0; mt < KP; ++mt) {
             uint32_t kw[2][KB / 4];  // keys r0 + g1_key(g, 2mt) and r0 + g1_key(g, 2mt + 1)
@@ -574,16 +580,15 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
 #pragma unroll
               for (int e = 0; e < 4; ++e) acc[e] = 16 * acc[e] + acch[e];
             }
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int key = r0 + g1_key(g, 2 * mt + e);
-              valid[2 * mt][e] = t < 3 && (!kMask || (k0 + key) < hi);
-              const int si = acc[2 * e] * 256 + acc[2 * e + 1] - (I4 ? qbias : 0);
-              const float s = float(si) * (__half2float(kst[key]) * hf);
-              sc[2 * mt][e] = valid[2 * mt][e] ? s : -INFINITY;
-              mx = fmaxf(mx, sc[2 * mt][e]);
-            }
+            // the group's keys 2mt (rows g) and 2mt + 1 (rows g + 8): lane t keeps key t's sum
+            const int si0 = acc[0] * 256 + acc[1] - (I4 ? qbias : 0);
+            const int si1 = acc[2] * 256 + acc[3] - (I4 ? qbias : 0);
+            if ((t >> 1) == mt) own_si = (t & 1) ? si1 : si0;
           }
+          own_key = r0 + g1_key(g, t);
+          own_ok = !kMask || (k0 + own_key) < hi;
+          own_sc = own_ok ? float(own_si) * (__half2float(kst[own_key]) * hf) : -INFINITY;
+          mx = own_sc;
         } else {
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
@@ -626,9 +631,7 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
 #pragma unroll
           for (int sg = 0; sg < NSEG; ++sg)
             ldmatrix_x4_trans(vt_s + (v_row_off ^ uint32_t(sg << 4)), vr[sg][0], vr[sg][1], vr[sg][2], vr[sg][3]);
-          float vs4[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) vs4[i] = __half2float(vst[r0 + g1_key(g, i)]);
+          const float vs_own = __half2float(vst[own_key]);
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[st]);  // everything this warp needs is in registers
 
@@ -636,7 +639,8 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
           // p * vs above the fixed-point range (or a full frame) the scale; either ends the frame
           // (lane-local tests and a vote; the warp-wide maxima only when a frame ends)
           if (__any_sync(0xffffffffu, mx > m_run + kG1Headroom)) {
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // lanes t < 3 hold the same scores
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // lane t holds key t's score
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
@@ -646,18 +650,14 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
             m_run = mx;
             ftiles = 0;
           }
-          float pv[4];
-          float pvm = 0.f;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const bool v_ok = valid[2 * (i >> 1)][i & 1];
-            const float pr = v_ok ? ex2(sc[2 * (i >> 1)][i & 1] - m_run) : 0.f;
-            l_run += pr;
-            pv[i] = v_ok ? pr * vs4[i] : 0.f;
-            pvm = fmaxf(pvm, pv[i]);
-          }
+          // this lane's key only (l sums the four lanes per unit)
+          const float pr = own_ok ? ex2(own_sc - m_run) : 0.f;
+          l_run += pr;
+          const float pv_own = own_ok ? pr * vs_own : 0.f;
+          float pvm = pv_own;
           if (__any_sync(0xffffffffu, pvm * ps > kG1VLim || (ps == 0.f && pvm > 0.f)) || ftiles >= kG1FrameTiles) {
             pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 1));
+            pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 2));
             pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 4));
             pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 8));
             pvm = fmaxf(pvm, __shfl_xor_sync(0xffffffffu, pvm, 16));
@@ -673,9 +673,11 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
 
           // ---- P in three planes; lane t < 3 packs plane t of its four keys (k-slots 4g + i)
           // and spreads them as the B operand (column c = plane c, c < 3)
+          // each lane forms its key's fixed-point word, then every lane gathers the group's four
+          const uint32_t fw_own = __float_as_uint(fmaf(pv_own, ps, kG1Magic));
           uint32_t fw[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) fw[i] = __float_as_uint(fmaf(pv[i], ps, kG1Magic));
+          for (int i = 0; i < 4; ++i) fw[i] = __shfl_sync(0xffffffffu, fw_own, (lane & ~3) | i);
           const uint32_t px = __byte_perm(fw[0], fw[1], psel);
           const uint32_t py = __byte_perm(fw[2], fw[3], psel);
           const uint32_t pw = (__byte_perm(px, py, 0x5410u) ^ pxor) & pmask;
@@ -786,9 +788,11 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
 
     // ---- unit epilogue: merge the 4 warps' (m, l, O) per head
     if constexpr (G1) {
-      // one head: the last frame joins the fp32 O; the lanes t < 3 of a group summed the
-      // same keys, so l is the sum over the groups
+      // one head: the last frame joins the fp32 O; each lane summed the probabilities of its
+      // group's key t, so l is the sum over all lanes
       g1_flush<NSEG>(oi, bsum, so, 1.f, inv_ps, g, t);
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);  // the four lanes of a group: one key each
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 4);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
       l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
