@@ -539,9 +539,9 @@ __global__ void __launch_bounds__(QtcCfg<D, I4, G1, kCl>::kThr, QtcCfg<D, I4, G1
 
         // ---- scores of this warp's KPW keys (rows r0 ..) in integers.
         // Several heads: S = Q K^T, n-tile j holds keys 8j + 2t + e of head g.
-        // One head (G1): S^T = K Q^T, m-tile j/2 holds (rows g / g + 8) keys
-        // g1_key(g, j + 0 / 1) in lanes t < 3 (columns 2t / 2t + 1: hi / lo
-        // plane); sc[j][e] is key g1_key(g, j + e) for even j (odd j unused).
+        // One head (G1): S^T = K Q^T, m-tile mt holds (rows g / g + 8) keys
+        // g1_key(g, 2mt + 0 / 1) in every lane t of group g (columns 2t / 2t + 1:
+        // hi / lo plane); lane t keeps key g1_key(g, t) only (own_*).
         float sc[NJ][2];
         bool valid[NJ][2];
         float mx = -INFINITY;
