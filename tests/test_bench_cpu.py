@@ -59,3 +59,13 @@ def test_committed_traffic_reports_its_source(bench):
     traffic, source = bench.committed_traffic("gqa")
     assert traffic is None or traffic > 0
     assert isinstance(source, str) and source
+
+
+def test_committed_traffic_covers_the_algorithmic_bytes(bench):
+    """Every committed DRAM-traffic figure is within 1 % of, or above, its workload's algorithmic bytes
+    (every byte is read or written at least once; well above would mean re-reads), and names its source."""
+    for name in ("gqa", "int8", "int8_b2048", "int4", "int4_b2048", "gqa_int8", "qpt", "quant_int4"):
+        traffic, source = bench.committed_traffic(name)
+        assert traffic is not None and source, name
+        alg = bench.algorithmic_bytes(bench.WORKLOADS[name])
+        assert 0.99 * alg <= traffic <= 1.05 * alg, (name, traffic, alg)
